@@ -1,0 +1,363 @@
+// Channels-last conv1d as an implicit GEMM on tcgen05, with SnakeBeta on load and bias +
+// residual in the epilogue.
+//
+// The B200 form of tts-nn's fused `nlc_conv_f32` (crates/tts-nn/src/nlcconv.rs:15-198 and
+// crates/tts-nn/src/nlc.rs:40-132): the tap gather happens inside the GEMM, so no im2col matrix
+// exists. GEMM view: M = output positions (128 per CTA), N = output channels (<= 512 per CTA,
+// the whole TMEM as 128 x 512 f32), K = taps x input channels.
+//
+// For each 64-channel block, one TMA load brings a "halo" of R = 128 + (k-1)*dil input rows
+// into shared memory in the no-swizzle K-major core-matrix layout: slab g (8 channels) holds
+// row r at byte r*16, slabs R*16 bytes apart. In that layout row r is simply 16*r bytes from
+// the start, so the A operand of tap t is the same halo with the descriptor's start moved by
+// t*dil*16 bytes: all k taps read one load, and SnakeBeta is applied once per halo element
+// (in place, by the four transform warps) rather than once per tap. Rows before 0 or past
+// len are zero-filled by TMA, and snake(0) = 0, so padding matches the reference's
+// pad-then-activate order.
+//
+// Warp roles (224 threads): warp 0 lane 0 issues the weight tiles (B ring), warp 1 lane 0 the
+// MMAs, warps 2..5 issue the halos (A ring), apply the snake and run the epilogue, warp 6 is
+// spare. Every wait is bounded; a wait that gives up sets an error flag the host reads.
+#include <algorithm>
+#include <mutex>
+
+#include "tts_common.cuh"
+#include "tts_internal.h"
+
+namespace tts {
+
+namespace {
+
+constexpr int kRows = 128;      // output positions per CTA
+constexpr int kCB = 64;         // input channels per halo
+constexpr int kAStages = 3;     // halo ring
+constexpr int kBStages = 2;     // weight-tile ring
+constexpr int kThreads = 224;
+
+struct ConvArgs {
+  int b, len, cin, cout, k, dil, pad_left;
+  int cout_cta;  // output channels per CTA (<= 512)
+  int nh, nper;  // MMAs per K step and N of each
+  int R;         // halo rows (multiple of 8)
+  int tmem_cols;
+  const float* bias;
+  const float* alpha;
+  const float* brecip;
+  const __half* res;
+  __half* y;
+  int* err;
+};
+
+__device__ __forceinline__ void snake8(uint4& u, const float* alpha, const float* brecip) {
+  __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float2 f = __half22float2(h[q]);
+    const float s0 = sinf(__ldg(alpha + 2 * q) * f.x);
+    const float s1 = sinf(__ldg(alpha + 2 * q + 1) * f.y);
+    f.x = f.x + __ldg(brecip + 2 * q) * (s0 * s0);
+    f.y = f.y + __ldg(brecip + 2 * q + 1) * (s1 * s1);
+    h[q] = __floats2half2_rn(f.x, f.y);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_nlc_kernel(const __grid_constant__ CUtensorMap tmX,
+                    const __grid_constant__ CUtensorMap tmW, const ConvArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int l0 = blockIdx.x * kRows;
+  const int bb = blockIdx.y;
+  const int co0 = blockIdx.z * a.cout_cta;
+  const int ncb = a.cin / kCB;
+  const uint32_t a_bytes = uint32_t(a.R) * kCB * 2;        // 8 slabs x R rows x 16 B
+  const uint32_t b_bytes = uint32_t(a.cout_cta) * kCB * 2;  // cout_cta rows x 128 B
+  uint8_t* a_base = smem;
+  uint8_t* b_base = smem + kAStages * a_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + kBStages * b_bytes);
+  uint64_t* full_a = bars;
+  uint64_t* ready_a = bars + kAStages;
+  uint64_t* empty_a = bars + 2 * kAStages;
+  uint64_t* full_b = bars + 3 * kAStages;
+  uint64_t* empty_b = full_b + kBStages;
+  uint64_t* done = empty_b + kBStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kAStages; ++s) {
+      mbar_init(&full_a[s], 1);
+      mbar_init(&ready_a[s], 128);
+      mbar_init(&empty_a[s], 1);
+    }
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(&full_b[s], 1);
+      mbar_init(&empty_b[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmW);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, a.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  const int nsteps = ncb * a.k;
+  if (warp == 0 && lane == 0) {
+    // ---------------- weight tiles: step i = (cb, tap) -> W[co0 .., tap*cin + cb*64 ..]
+    for (int i = 0; i < nsteps; ++i) {
+      const int s = i % kBStages;
+      if (i >= kBStages && !mbar_wait(&empty_b[s], ((i / kBStages) + 1) & 1)) {
+        atomicOr(a.err, 16);
+        break;
+      }
+      const int cb = i / a.k, t = i % a.k;
+      uint8_t* dst = b_base + s * b_bytes;
+      mbar_arrive_expect_tx(&full_b[s], b_bytes);
+      for (int h = 0; h < a.nh; ++h)
+        tma_load_2d(dst + h * a.nper * 128, &tmW, &full_b[s], t * a.cin + cb * kCB,
+                    co0 + h * a.nper);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    const uint32_t idesc = idesc_f16_f32(kRows, a.nper);
+    const uint32_t slab = uint32_t(a.R) * 16;
+    bool ok = true;
+    for (int cb = 0; cb < ncb && ok; ++cb) {
+      const int sa = cb % kAStages;
+      if (!mbar_wait(&ready_a[sa], (cb / kAStages) & 1)) {
+        atomicOr(a.err, 32);
+        break;
+      }
+      const uint32_t ha = smem_u32(a_base + sa * a_bytes);
+      for (int t = 0; t < a.k; ++t) {
+        const int i = cb * a.k + t;
+        const int sb = i % kBStages;
+        if (!mbar_wait(&full_b[sb], (i / kBStages) & 1)) {
+          atomicOr(a.err, 64);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t hb = smem_u32(b_base + sb * b_bytes);
+#pragma unroll
+        for (int kk = 0; kk < kCB / 16; ++kk) {
+          const uint64_t ad = desc_k_interleave(ha + 2 * kk * slab + t * a.dil * 16, slab);
+          for (int h = 0; h < a.nh; ++h) {
+            const uint64_t bd = desc_k_sw128(hb + h * a.nper * 128 + kk * 32);
+            umma_f16(tmem + h * a.nper, ad, bd, idesc, (i | kk) != 0);
+          }
+        }
+        umma_commit(&empty_b[sb]);
+      }
+      umma_commit(&empty_a[sa]);
+    }
+    umma_commit(done);
+  } else if (warp >= 2 && warp <= 5) {
+    // ---------------- halos: load, snake in place, hand to the MMA
+    const int tt = threadIdx.x - 64;  // 0..127
+    auto issue = [&](int cb) {
+      const int s = cb % kAStages;
+      if (cb >= kAStages && !mbar_wait(&empty_a[s], ((cb / kAStages) + 1) & 1)) {
+        atomicOr(a.err, 128);
+        return;
+      }
+      mbar_arrive_expect_tx(&full_a[s], a_bytes);
+      tma_load_4d(a_base + s * a_bytes, &tmX, &full_a[s], 0, l0 - a.pad_left, cb * (kCB / 8), bb);
+    };
+    if (tt == 0)
+      for (int cb = 0; cb < std::min(ncb, kAStages - 1); ++cb) issue(cb);
+    for (int cb = 0; cb < ncb; ++cb) {
+      const int s = cb % kAStages;
+      if (!mbar_wait(&full_a[s], (cb / kAStages) & 1)) {
+        if (tt == 0) atomicOr(a.err, 256);
+      }
+      if (a.alpha) {
+        uint8_t* halo = a_base + s * a_bytes;
+        const int chunks = 8 * a.R;
+        for (int c = tt; c < chunks; c += 128) {
+          const int g = c / a.R;
+          const int ch = cb * kCB + g * 8;
+          uint4* p = reinterpret_cast<uint4*>(halo) + c;
+          uint4 u = *p;
+          snake8(u, a.alpha + ch, a.brecip + ch);
+          *p = u;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      }
+      mbar_arrive(&ready_a[s]);
+      if (tt == 0 && cb + kAStages - 1 < ncb) issue(cb + kAStages - 1);
+    }
+  }
+  __syncwarp();
+
+  // ---------------- epilogue (warps 2..5: TMEM lane quadrant = warp % 4)
+  if (warp >= 2 && warp <= 5) {
+    if (!mbar_wait(done, 0) && lane == 0) atomicOr(a.err, 512);
+    tc_fence_after();
+    const int quad = warp & 3;
+    const int l = l0 + quad * 32 + lane;
+    const bool live = l < a.len;
+    const size_t row = ((size_t)bb * a.len + (live ? l : 0)) * a.cout + co0;
+    for (int c0 = 0; c0 < a.cout_cta; c0 += 16) {
+      float v[16];
+      tmem_ld16(tmem + (uint32_t(quad * 32) << 16) + c0, v);
+      if (!live) continue;
+      if (a.bias) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] += __ldg(a.bias + co0 + c0 + i);
+      }
+      if (a.res) {
+        const uint4* rp = reinterpret_cast<const uint4*>(a.res + row + c0);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint4 u = rp[hh];
+          const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __half22float2(h2[q]);
+            v[hh * 8 + 2 * q] += f.x;
+            v[hh * 8 + 2 * q + 1] += f.y;
+          }
+        }
+      }
+      uint4 o[2];
+      __half2* oh = reinterpret_cast<__half2*>(o);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) oh[q] = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
+      uint4* yp = reinterpret_cast<uint4*>(a.y + row + c0);
+      yp[0] = o[0];
+      yp[1] = o[1];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, a.tmem_cols);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 conv_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+}  // namespace
+
+bool conv_supported(const ConvRequest& r, std::string* why) {
+  auto no = [&](const char* s) {
+    if (why) *why = s;
+    return false;
+  };
+  if (r.b < 1 || r.len < 1) return no("empty input");
+  if (r.cin < kCB || r.cin % kCB) return no("cin must be a positive multiple of 64");
+  if (r.cout < 32 || r.cout % 32) return no("cout must be a positive multiple of 32");
+  if (r.cout > 512 && r.cout % 512) return no("cout above 512 must be a multiple of 512");
+  if (r.k < 1 || r.dil < 1) return no("k and dilation must be >= 1");
+  if ((r.k - 1) * r.dil > 128) return no("(k - 1) * dilation must be <= 128");
+  if (r.pad_left < 0 || r.pad_left > (r.k - 1) * r.dil)
+    return no("pad_left must be in 0..(k-1)*dilation");
+  return true;
+}
+
+cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* err) {
+  (void)device;
+  std::string why;
+  if (!conv_supported(r, &why)) {
+    set_error("conv1d: " + why);
+    return cudaErrorInvalidValue;
+  }
+  auto fn = conv_encode_fn();
+  if (!fn) {
+    set_error("conv1d: cuTensorMapEncodeTiled unavailable");
+    return cudaErrorInvalidValue;
+  }
+  ConvArgs a{};
+  a.b = r.b;
+  a.len = r.len;
+  a.cin = r.cin;
+  a.cout = r.cout;
+  a.k = r.k;
+  a.dil = r.dil;
+  a.pad_left = r.pad_left;
+  a.cout_cta = std::min(r.cout, 512);
+  a.nh = a.cout_cta > 256 ? 2 : 1;
+  a.nper = a.cout_cta / a.nh;
+  a.R = (kRows + (r.k - 1) * r.dil + 7) / 8 * 8;
+  a.tmem_cols = 32;
+  while (a.tmem_cols < a.cout_cta) a.tmem_cols *= 2;
+  a.bias = r.bias;
+  a.alpha = r.alpha;
+  a.brecip = r.brecip;
+  a.res = r.res;
+  a.y = r.y;
+  a.err = err;
+
+  // Halo map over x [b][len][cin]: dims (8 channels, len, cin/8 slabs, b). The box
+  // {8, R, 8, 1} lands as [slab][row][8 ch], the core-matrix layout the MMA reads.
+  CUtensorMap tmX, tmW;
+  {
+    cuuint64_t dims[4] = {8, cuuint64_t(r.len), cuuint64_t(r.cin / 8), cuuint64_t(r.b)};
+    cuuint64_t strides[3] = {cuuint64_t(r.cin) * 2, 16, cuuint64_t(r.len) * r.cin * 2};
+    cuuint32_t box[4] = {8, cuuint32_t(a.R), 8, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (fn(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<__half*>(r.x), dims, strides, box,
+           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+      set_error("conv1d: halo tensor map rejected");
+      return cudaErrorInvalidValue;
+    }
+  }
+  if (!make_tmap_2d_f16(&tmW, r.w, uint64_t(r.k) * r.cin, uint64_t(r.cout),
+                        uint64_t(r.k) * r.cin * 2, kCB, a.nper, true)) {
+    set_error("conv1d: weight tensor map rejected");
+    return cudaErrorInvalidValue;
+  }
+  const size_t smem = size_t(kAStages) * a.R * kCB * 2 + size_t(kBStages) * a.cout_cta * kCB * 2 +
+                      1024 + 256;
+  {
+    // The opt-in shared-memory limit is a per-device function attribute.
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !done[dev]) {
+      cudaFuncSetAttribute(conv_nlc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      done[dev] = true;
+    }
+  }
+  if (smem > 227 * 1024) {
+    set_error("conv1d: shared memory plan exceeds 227 KB");
+    return cudaErrorInvalidValue;
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((r.len + kRows - 1) / kRows, r.b, r.cout / a.cout_cta);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = r.pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, conv_nlc_kernel, tmX, tmW, a);
+}
+
+}  // namespace tts

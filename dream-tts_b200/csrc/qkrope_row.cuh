@@ -1,0 +1,72 @@
+// QK-norm + RoPE + paged KV append for one (lane, head) row of 128 values held by a warp,
+// four per thread (thread t owns dims 4t .. 4t+3).
+//
+// Restates crates/qwen3tts/src/qwen3.rs:358-394 (rms_norm over the head dim, then
+// candle_nn::rotary_emb::rope's rotate_half form: dims i and i + 64 rotate together) and
+// crates/tts-nn/src/qkrope.rs:26-69 (the fused kernel writes k and v as f16 into the cache at
+// the lane's position). Used by the QKV GEMM's epilogue and by the standalone op.
+#pragma once
+#include "tts_common.cuh"
+#include "tts_internal.h"
+
+namespace tts {
+
+// head < heads: q head -> q_out (f32). heads <= head < heads + n_kv: k head -> K page.
+// Otherwise: v head -> V page (no norm, no rotation).
+__device__ __forceinline__ void qkrope_row(const QkRopeArgs& q, int head, int j, int lane,
+                                           float v[4]) {
+  // Positions and page numbers are device data: a row outside the RoPE table, the lane's
+  // block table or the pool is skipped and flagged, never written out of bounds.
+  // (j, head) is the same for the whole warp, so the early return is warp-uniform.
+  const int pos = q.positions[j];
+  if (pos < 0 || pos >= q.rope_len || pos >= q.max_blocks * q.block_size) {
+    if (lane == 0 && q.err) atomicOr(q.err, 256);
+    return;
+  }
+  int blk = 0;
+  const int off = pos % q.block_size;
+  if (head >= q.heads) {
+    blk = q.block_table[(size_t)j * q.max_blocks + pos / q.block_size];
+    if (blk < 0 || blk >= q.num_blocks) {
+      if (lane == 0 && q.err) atomicOr(q.err, 256);
+      return;
+    }
+  }
+  if (head < q.heads + q.n_kv) {
+    const float* w = q.norms + (head < q.heads ? 0 : 128) + 4 * lane;
+    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+    ss = warp_sum(ss);
+    const float rms = sqrtf(ss / 128.0f + q.eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = v[i] / rms * w[i];
+    float pr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pr[i] = __shfl_xor_sync(0xffffffffu, v[i], 16);
+    const int fi = (lane & 15) * 4;
+    const float* ct = q.cos_t + (size_t)pos * 64 + fi;
+    const float* st = q.sin_t + (size_t)pos * 64 + fi;
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      o[i] = lane < 16 ? v[i] * ct[i] - pr[i] * st[i] : v[i] * ct[i] + pr[i] * st[i];
+    if (head < q.heads) {
+      float4* dst =
+          reinterpret_cast<float4*>(q.q_out + ((size_t)j * q.heads + head) * 128 + 4 * lane);
+      *dst = make_float4(o[0], o[1], o[2], o[3]);
+    } else {
+      const int h = head - q.heads;
+      __half2* dst = reinterpret_cast<__half2*>(
+          q.k_pool + (((size_t)blk * q.n_kv + h) * q.block_size + off) * 128 + 4 * lane);
+      dst[0] = __floats2half2_rn(o[0], o[1]);
+      dst[1] = __floats2half2_rn(o[2], o[3]);
+    }
+  } else {
+    const int h = head - q.heads - q.n_kv;
+    __half2* dst = reinterpret_cast<__half2*>(
+        q.v_pool + (((size_t)blk * q.n_kv + h) * q.block_size + off) * 128 + 4 * lane);
+    dst[0] = __floats2half2_rn(v[0], v[1]);
+    dst[1] = __floats2half2_rn(v[2], v[3]);
+  }
+}
+
+}  // namespace tts

@@ -1,0 +1,670 @@
+// C ABI (include/tts_cuda.h) and the native runtime around the kernels: context and scratch
+// ownership, argument checks, the decoder stack, the decode step and its CUDA graph.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/tts_cuda.h"
+#include "tts_internal.h"
+
+namespace tts {
+
+namespace {
+thread_local std::string g_err;
+thread_local long long g_launches = 0;
+}  // namespace
+
+void set_error(const std::string& msg) { g_err = msg; }
+const char* last_error() { return g_err.c_str(); }
+
+int num_sms(int device) {
+  static int cache[64] = {0};
+  if (device < 0 || device >= 64) return 148;
+  if (!cache[device]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+}  // namespace tts
+
+using namespace tts;
+
+struct tts_ctx {
+  int device = 0;
+  int max_lanes = 0;
+  Workspace gemm;
+  AttnWorkspace attn;
+  int* err_host = nullptr;
+};
+
+struct tts_stack {
+  tts_ctx* ctx = nullptr;
+  tts_stack_geometry geo{};
+  std::vector<tts_layer_weights> layers;
+  const float* final_norm = nullptr;
+  const __half* heads = nullptr;
+  const __half* embed = nullptr;
+  // device buffers owned by the stack
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  float* h = nullptr;         // residual stream [max_lanes][dim]
+  __half* xn = nullptr;       // normed activations as the next GEMM's x [max_lanes][max(dim, q)]
+  float* q = nullptr;         // [max_lanes][heads][head_dim]
+  __half* attn = nullptr;     // [max_lanes][heads * head_dim]
+  __half* act = nullptr;      // [max_lanes][ffn]
+  float* x_next = nullptr;    // [max_lanes][dim]
+  unsigned long long* keys = nullptr;  // [max_lanes][codebooks]
+};
+
+struct tts_graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  long long kernels = 0;
+};
+
+namespace rt {
+
+tts_status fail(tts_status s, const std::string& msg) {
+  set_error(msg);
+  return s;
+}
+
+tts_status cuda_status(cudaError_t e, const char* op) {
+  if (e == cudaSuccess) return TTS_OK;
+  if (e == cudaErrorInvalidValue && g_err.size() && g_err.find(op) != std::string::npos)
+    return TTS_ERR_UNSUPPORTED_SHAPE;
+  set_error(std::string(op) + ": " + cudaGetErrorString(e));
+  return e == cudaErrorMemoryAllocation ? TTS_ERR_OOM : TTS_ERR_CUDA;
+}
+
+// Every launch goes through here so the launch counter is exact.
+tts_status counted(cudaError_t e, const char* op) {
+  if (e == cudaSuccess) ++g_launches;
+  return cuda_status(e, op);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+template <class T>
+cudaError_t dmalloc(T** p, size_t bytes) {
+  return cudaMalloc(reinterpret_cast<void**>(p), bytes);
+}
+
+__global__ void interleave_gate_up_kernel(const __half* gate, const __half* up, int ffn, int dim,
+                                          __half* out) {
+  // out row r: tile t = r / 128, within-tile i = r % 128; i < 64 -> gate row t*64+i,
+  // else up row t*64 + (i - 64).
+  const long total = 2L * ffn * dim / 8;
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total;
+       e += (long)gridDim.x * blockDim.x) {
+    const long el = e * 8;
+    const long r = el / dim, c = el % dim;
+    const long t = r / 128, i = r % 128;
+    const __half* src = i < 64 ? gate + (t * 64 + i) * dim + c : up + (t * 64 + (i - 64)) * dim + c;
+    *reinterpret_cast<uint4*>(out + el) = *reinterpret_cast<const uint4*>(src);
+  }
+}
+
+}  // namespace rt
+using namespace rt;
+
+extern "C" {
+
+int tts_abi_version(void) { return TTS_CUDA_ABI_VERSION; }
+const char* tts_last_error(void) { return g_err.c_str(); }
+long long tts_launch_count(int reset) {
+  const long long n = g_launches;
+  if (reset) g_launches = 0;
+  return n;
+}
+
+tts_status tts_ctx_create(int device, int max_lanes, tts_ctx** out) {
+  if (!out) return fail(TTS_ERR_INVALID_ARG, "ctx_create: out is NULL");
+  if (max_lanes < 1 || max_lanes > 512)
+    return fail(TTS_ERR_INVALID_ARG, "ctx_create: max_lanes must be in 1..512");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+    return fail(TTS_ERR_CUDA, "ctx_create: no such CUDA device");
+  DeviceGuard g(device);
+  cudaDeviceProp prop{};
+  cudaGetDeviceProperties(&prop, device);
+  if (prop.major != 10)
+    return fail(TTS_ERR_CUDA, "ctx_create: this library is built for sm_100a (B200)");
+  auto* c = new tts_ctx();
+  c->device = device;
+  c->max_lanes = max_lanes;
+  const int slots = std::max(512, 2 * num_sms(device));
+  c->gemm.ws_bytes = size_t(slots) * max_lanes * 128 * sizeof(float);
+  c->gemm.n_counters = 4096;
+  const int max_span = 8192, n_kv = 8, gqa = 2;
+  c->attn.part_bytes = attn_part_bytes(max_lanes, n_kv, gqa, max_span);
+  c->attn.n_counters = max_lanes * 64;
+  cudaError_t e = dmalloc(&c->gemm.ws, c->gemm.ws_bytes);
+  if (e == cudaSuccess) e = dmalloc(&c->gemm.counters, c->gemm.n_counters * sizeof(unsigned));
+  if (e == cudaSuccess) e = dmalloc(&c->gemm.err, 16);
+  if (e == cudaSuccess) e = dmalloc(&c->attn.part, c->attn.part_bytes);
+  if (e == cudaSuccess) e = dmalloc(&c->attn.counters, c->attn.n_counters * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(c->gemm.counters, 0, c->gemm.n_counters * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(c->attn.counters, 0, c->attn.n_counters * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(c->gemm.err, 0, 16);
+  if (e == cudaSuccess) e = cudaMallocHost(reinterpret_cast<void**>(&c->err_host), 16);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    tts_ctx_destroy(c);
+    return cuda_status(e, "ctx_create");
+  }
+  *out = c;
+  return TTS_OK;
+}
+
+tts_status tts_ctx_destroy(tts_ctx* c) {
+  if (!c) return TTS_OK;
+  DeviceGuard g(c->device);
+  cudaFree(c->gemm.ws);
+  cudaFree(c->gemm.counters);
+  cudaFree(c->gemm.err);
+  cudaFree(c->attn.part);
+  cudaFree(c->attn.counters);
+  if (c->err_host) cudaFreeHost(c->err_host);
+  delete c;
+  return TTS_OK;
+}
+
+tts_status tts_ctx_check(tts_ctx* c, void* stream) {
+  if (!c) return fail(TTS_ERR_INVALID_ARG, "ctx_check: ctx is NULL");
+  DeviceGuard g(c->device);
+  cudaError_t e = cudaMemcpyAsync(c->err_host, c->gemm.err, sizeof(int), cudaMemcpyDeviceToHost,
+                                  S(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(S(stream));
+  if (e != cudaSuccess) return cuda_status(e, "ctx_check");
+  if (c->err_host[0]) {
+    const int code = c->err_host[0];
+    cudaMemsetAsync(c->gemm.err, 0, sizeof(int), S(stream));
+    cudaStreamSynchronize(S(stream));
+    return fail(TTS_ERR_TIMEOUT, "device wait gave up (code " + std::to_string(code) +
+                                     "): results of the affected launches are not valid");
+  }
+  return TTS_OK;
+}
+
+tts_status tts_proj_forward(tts_ctx* c, const void* x, int m, int k, const void* w, int n,
+                            int epilogue, void* y, int ldy, void* stream) {
+  if (!c || !x || !w || !y) return fail(TTS_ERR_INVALID_ARG, "proj: NULL argument");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y))
+    return fail(TTS_ERR_INVALID_ARG, "proj: pointers must be 16-byte aligned");
+  if (epilogue < TTS_EPI_F32 || epilogue > TTS_EPI_SWIGLU_F16)
+    return fail(TTS_ERR_INVALID_ARG, "proj: unknown epilogue");
+  std::string why;
+  if (!gemm_supported(m, k, n, epilogue, &why))
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "proj: " + why);
+  if (m > c->max_lanes)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "proj: m exceeds the context's max_lanes");
+  DeviceGuard g(c->device);
+  GemmRequest r;
+  r.w = static_cast<const __half*>(w);
+  r.x = static_cast<const __half*>(x);
+  r.m = m;
+  r.k = k;
+  r.n = n;
+  r.epi = epilogue;
+  r.y = y;
+  r.ldy = ldy;
+  r.pdl = false;
+  return counted(launch_gemm(r, c->gemm, S(stream), c->device), "proj");
+}
+
+tts_status tts_interleave_gate_up(tts_ctx* c, const void* gate, const void* up, int ffn, int dim,
+                                  void* out, void* stream) {
+  if (!c || !gate || !up || !out) return fail(TTS_ERR_INVALID_ARG, "interleave: NULL argument");
+  if (ffn % 64 || dim % 8)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "interleave: ffn % 64 and dim % 8 must be 0");
+  DeviceGuard g(c->device);
+  interleave_gate_up_kernel<<<1184, 256, 0, S(stream)>>>(static_cast<const __half*>(gate),
+                                                        static_cast<const __half*>(up), ffn,
+                                                        dim, static_cast<__half*>(out));
+  return counted(cudaGetLastError(), "interleave");
+}
+
+tts_status tts_rms_norm(tts_ctx* c, const float* x, const float* w, int rows, int dim, float eps,
+                        float* y32, void* y16, void* stream) {
+  if (!c || !x || !w || (!y32 && !y16)) return fail(TTS_ERR_INVALID_ARG, "rms_norm: NULL argument");
+  DeviceGuard g(c->device);
+  return counted(launch_rms_norm(x, w, rows, dim, eps, y32, static_cast<__half*>(y16), nullptr, 0,
+                                 false, S(stream)),
+                 "rms_norm");
+}
+
+tts_status tts_swiglu_mul(tts_ctx* c, const float* gate, const float* up, long n, void* y,
+                          int y_f16, void* stream) {
+  if (!c || !gate || !up || !y) return fail(TTS_ERR_INVALID_ARG, "swiglu_mul: NULL argument");
+  DeviceGuard g(c->device);
+  return counted(launch_swiglu(gate, up, y, y_f16 != 0, n, S(stream)), "swiglu_mul");
+}
+
+tts_status tts_snake_beta_nlc(tts_ctx* c, const void* x, int x_f16, const float* alpha,
+                              const float* brecip, long rows, int chan, void* y, int y_f16,
+                              void* stream) {
+  if (!c || !x || !alpha || !brecip || !y)
+    return fail(TTS_ERR_INVALID_ARG, "snake_beta_nlc: NULL argument");
+  DeviceGuard g(c->device);
+  return counted(launch_snake(x, x_f16 != 0, alpha, brecip, rows, chan, y, y_f16 != 0, S(stream)),
+                 "snake_beta");
+}
+
+static bool kv_ok(const tts_kv_cache* kv, std::string* why) {
+  if (!kv || !kv->k_pages || !kv->v_pages || !kv->block_table) {
+    *why = "kv cache pointers are NULL";
+    return false;
+  }
+  if (kv->head_dim != 128) {
+    *why = "head_dim must be 128";
+    return false;
+  }
+  if (kv->block_size < 1 || kv->max_blocks < 1 || kv->n_kv < 1) {
+    *why = "empty kv cache geometry";
+    return false;
+  }
+  return true;
+}
+
+tts_status tts_qk_rope_append(tts_ctx* c, const float* qkv, int lanes, int heads,
+                              const float* norms, const float* cos_t, const float* sin_t,
+                              int rope_len, const int* positions, const tts_kv_cache* kv,
+                              float eps, float* q_out, void* stream) {
+  std::string why;
+  if (!c || !qkv || !norms || !cos_t || !sin_t || !positions || !q_out)
+    return fail(TTS_ERR_INVALID_ARG, "qk_rope: NULL argument");
+  if (!kv_ok(kv, &why)) return fail(TTS_ERR_INVALID_ARG, "qk_rope: " + why);
+  if (lanes < 1 || heads < 1) return fail(TTS_ERR_INVALID_ARG, "qk_rope: empty shape");
+  DeviceGuard g(c->device);
+  QkRopeArgs a;
+  a.norms = norms;
+  a.cos_t = cos_t;
+  a.sin_t = sin_t;
+  a.positions = positions;
+  a.block_table = kv->block_table;
+  a.max_blocks = kv->max_blocks;
+  a.block_size = kv->block_size;
+  a.num_blocks = kv->num_blocks;
+  a.rope_len = rope_len;
+  a.err = c->gemm.err;
+  a.k_pool = static_cast<__half*>(kv->k_pages);
+  a.v_pool = static_cast<__half*>(kv->v_pages);
+  a.q_out = q_out;
+  a.heads = heads;
+  a.n_kv = kv->n_kv;
+  a.eps = eps;
+  return counted(launch_qk_rope(qkv, a, lanes, false, S(stream)), "qk_rope");
+}
+
+tts_status tts_decode_attention(tts_ctx* c, const float* q, int lanes, int gqa,
+                                const tts_kv_cache* kv, const int* spans, int max_span,
+                                int window, void* out, int out_f16, void* stream) {
+  std::string why;
+  if (!c || !q || !spans || !out) return fail(TTS_ERR_INVALID_ARG, "decode_attention: NULL argument");
+  if (!kv_ok(kv, &why)) return fail(TTS_ERR_INVALID_ARG, "decode_attention: " + why);
+  if (gqa != 1 && gqa != 2)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "decode_attention: gqa must be 1 or 2");
+  if (lanes < 1 || lanes > c->max_lanes || max_span < 1 || max_span > 8192)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE,
+                "decode_attention: lanes must be in 1..max_lanes and max_span in 1..8192");
+  DeviceGuard g(c->device);
+  AttnRequest r;
+  r.q = q;
+  r.k_pool = static_cast<const __half*>(kv->k_pages);
+  r.v_pool = static_cast<const __half*>(kv->v_pages);
+  r.block_table = kv->block_table;
+  r.max_blocks = kv->max_blocks;
+  r.block_size = kv->block_size;
+  r.num_blocks = kv->num_blocks;
+  r.err = c->gemm.err;
+  r.spans = spans;
+  r.span_add = 0;
+  r.max_span = max_span;
+  r.window = window;
+  r.lanes = lanes;
+  r.n_kv = kv->n_kv;
+  r.gqa = gqa;
+  r.out = out;
+  r.out_f16 = out_f16 != 0;
+  r.pdl = false;
+  return counted(launch_attn(r, c->attn, S(stream)), "decode_attention");
+}
+
+tts_status tts_argmax(tts_ctx* c, const float* logits, int rows, int n,
+                      const unsigned char* banned, unsigned int* out, void* stream) {
+  if (!c || !logits || !out) return fail(TTS_ERR_INVALID_ARG, "argmax: NULL argument");
+  if (rows < 1 || n < 1) return fail(TTS_ERR_INVALID_ARG, "argmax: empty shape");
+  DeviceGuard g(c->device);
+  return counted(launch_argmax(logits, rows, n, banned, out, S(stream)), "argmax");
+}
+
+tts_status tts_conv1d_nlc(tts_ctx* c, const void* x, int b, int len, int cin, const void* w,
+                          int cout, int k, int dilation, int pad_left, const float* bias,
+                          const float* alpha, const float* brecip, const void* res, void* y,
+                          void* stream) {
+  if (!c || !x || !w || !y) return fail(TTS_ERR_INVALID_ARG, "conv1d: NULL argument");
+  if ((alpha == nullptr) != (brecip == nullptr))
+    return fail(TTS_ERR_INVALID_ARG, "conv1d: alpha and brecip come together");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (res && !aligned16(res)))
+    return fail(TTS_ERR_INVALID_ARG, "conv1d: pointers must be 16-byte aligned");
+  ConvRequest r;
+  r.x = static_cast<const __half*>(x);
+  r.w = static_cast<const __half*>(w);
+  r.bias = bias;
+  r.alpha = alpha;
+  r.brecip = brecip;
+  r.res = static_cast<const __half*>(res);
+  r.y = static_cast<__half*>(y);
+  r.b = b;
+  r.len = len;
+  r.cin = cin;
+  r.cout = cout;
+  r.k = k;
+  r.dil = dilation;
+  r.pad_left = pad_left;
+  std::string why;
+  if (!conv_supported(r, &why)) return fail(TTS_ERR_UNSUPPORTED_SHAPE, "conv1d: " + why);
+  DeviceGuard g(c->device);
+  return counted(launch_conv(r, S(stream), c->device, c->gemm.err), "conv1d");
+}
+
+// ---------------------------------------------------------------- stack
+
+tts_status tts_stack_create(tts_ctx* c, const tts_stack_geometry* geo, tts_stack** out) {
+  if (!c || !geo || !out) return fail(TTS_ERR_INVALID_ARG, "stack_create: NULL argument");
+  const tts_stack_geometry& gm = *geo;
+  if (gm.head_dim != 128 || gm.dim % 128 || gm.ffn % 64 || gm.layers < 1 || gm.heads < 1 ||
+      gm.n_kv < 1 || gm.heads % gm.n_kv || (gm.heads / gm.n_kv) > 2 || gm.rope_len < 1)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE,
+                "stack_create: need head_dim 128, dim % 128 == 0, ffn % 64 == 0, gqa 1 or 2");
+  if (gm.codebooks < 0 || gm.codebooks > 64 || (gm.codebooks && gm.vocab % 128))
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "stack_create: 0..64 codebooks, vocab % 128 == 0");
+  DeviceGuard g(c->device);
+  auto* s = new tts_stack();
+  s->ctx = c;
+  s->geo = gm;
+  s->layers.resize(gm.layers);
+  const int L = c->max_lanes;
+  const int qw = gm.heads * gm.head_dim;
+  // RoPE table in f64, rounded to f32 (crates/tts-nn/src/lib.rs:1178-1205).
+  std::vector<float> cs(size_t(gm.rope_len) * 64), sn(size_t(gm.rope_len) * 64);
+  for (int t = 0; t < gm.rope_len; ++t)
+    for (int i = 0; i < 64; ++i) {
+      const double freq = 1.0 / std::pow(gm.rope_base, 2.0 * double(i) / 128.0);
+      const double ph = double(t) * freq;
+      cs[size_t(t) * 64 + i] = float(std::cos(ph));
+      sn[size_t(t) * 64 + i] = float(std::sin(ph));
+    }
+  cudaError_t e = dmalloc(&s->rope_cos, cs.size() * 4);
+  if (e == cudaSuccess) e = dmalloc(&s->rope_sin, sn.size() * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(s->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(s->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = dmalloc(&s->h, size_t(L) * gm.dim * 4);
+  if (e == cudaSuccess) e = dmalloc(&s->xn, size_t(L) * std::max(gm.dim, qw) * 2);
+  if (e == cudaSuccess) e = dmalloc(&s->q, size_t(L) * qw * 4);
+  if (e == cudaSuccess) e = dmalloc(&s->attn, size_t(L) * qw * 2);
+  if (e == cudaSuccess) e = dmalloc(&s->act, size_t(L) * gm.ffn * 2);
+  if (e == cudaSuccess) e = dmalloc(&s->x_next, size_t(L) * gm.dim * 4);
+  if (e == cudaSuccess) e = dmalloc(&s->keys, size_t(L) * std::max(1, gm.codebooks) * 8);
+  if (e == cudaSuccess) e = cudaMemset(s->keys, 0, size_t(L) * std::max(1, gm.codebooks) * 8);
+  if (e == cudaSuccess) e = cudaMemset(s->x_next, 0, size_t(L) * gm.dim * 4);
+  if (e != cudaSuccess) {
+    tts_stack_destroy(s);
+    return cuda_status(e, "stack_create");
+  }
+  *out = s;
+  return TTS_OK;
+}
+
+tts_status tts_stack_set_layer(tts_stack* s, int layer, const tts_layer_weights* w) {
+  if (!s || !w) return fail(TTS_ERR_INVALID_ARG, "stack_set_layer: NULL argument");
+  if (layer < 0 || layer >= s->geo.layers)
+    return fail(TTS_ERR_INVALID_ARG, "stack_set_layer: layer out of range");
+  if (!w->attn_norm || !w->ffn_norm || !w->wqkv || !w->qk_norms || !w->wo || !w->w_gate_up ||
+      !w->w_down)
+    return fail(TTS_ERR_INVALID_ARG, "stack_set_layer: every weight is required");
+  s->layers[layer] = *w;
+  return TTS_OK;
+}
+
+tts_status tts_stack_set_head(tts_stack* s, const float* final_norm, const void* heads,
+                              const void* embed) {
+  if (!s || !final_norm) return fail(TTS_ERR_INVALID_ARG, "stack_set_head: final_norm is required");
+  s->final_norm = final_norm;
+  s->heads = static_cast<const __half*>(heads);
+  s->embed = static_cast<const __half*>(embed);
+  return TTS_OK;
+}
+
+tts_status tts_stack_destroy(tts_stack* s) {
+  if (!s) return TTS_OK;
+  DeviceGuard g(s->ctx->device);
+  cudaFree(s->rope_cos);
+  cudaFree(s->rope_sin);
+  cudaFree(s->h);
+  cudaFree(s->xn);
+  cudaFree(s->q);
+  cudaFree(s->attn);
+  cudaFree(s->act);
+  cudaFree(s->x_next);
+  cudaFree(s->keys);
+  delete s;
+  return TTS_OK;
+}
+
+static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const float* x,
+                            float* h_out, float* logits, unsigned int* codes, cudaStream_t cs) {
+  const tts_stack_geometry& gm = s->geo;
+  tts_ctx* c = s->ctx;
+  if (!st || !st->positions || !st->block_table || !st->k_pages || !st->v_pages)
+    return fail(TTS_ERR_INVALID_ARG, "decode_step: state pointers are NULL");
+  const int B = st->lanes;
+  if (B < 1 || B > c->max_lanes)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "decode_step: lanes must be in 1..max_lanes");
+  if (st->max_span < 1 || st->max_span > std::min(8192, gm.rope_len))
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "decode_step: max_span must be in 1..min(8192, rope_len)");
+  for (int l = 0; l < gm.layers; ++l)
+    if (!s->layers[l].wqkv) return fail(TTS_ERR_INVALID_ARG, "decode_step: layer weights not set");
+  if (!s->final_norm) return fail(TTS_ERR_INVALID_ARG, "decode_step: final norm not set");
+  if ((logits || codes) && !s->heads)
+    return fail(TTS_ERR_INVALID_ARG, "decode_step: logits/codes need codebook heads");
+
+  const int D = gm.dim, qw = gm.heads * gm.head_dim, nqkv = (gm.heads + 2 * gm.n_kv) * 128;
+  const size_t layer_pages = size_t(st->num_blocks) * gm.n_kv * st->block_size * 128;
+  tts_status rc;
+#define TTS_TRY(expr, op)                     \
+  do {                                        \
+    if ((rc = counted((expr), op)) != TTS_OK) \
+      return rc;                              \
+  } while (0)
+
+  const float* src = x ? x : s->x_next;
+  if ((rc = cuda_status(cudaMemcpyAsync(s->h, src, size_t(B) * D * 4, cudaMemcpyDeviceToDevice, cs),
+                        "decode_step")) != TTS_OK)
+    return rc;
+
+  for (int l = 0; l < gm.layers; ++l) {
+    const tts_layer_weights& w = s->layers[l];
+    __half* kp = static_cast<__half*>(st->k_pages) + layer_pages * l;
+    __half* vp = static_cast<__half*>(st->v_pages) + layer_pages * l;
+    // attention block (qwen3.rs:339-451)
+    TTS_TRY(launch_rms_norm(s->h, w.attn_norm, B, D, gm.eps, nullptr, s->xn, nullptr, 0, true, cs),
+            "rms_norm");
+    GemmRequest r;
+    r.w = static_cast<const __half*>(w.wqkv);
+    r.x = s->xn;
+    r.m = B;
+    r.k = D;
+    r.n = nqkv;
+    r.epi = EPI_QKROPE;
+    r.qk.norms = w.qk_norms;
+    r.qk.cos_t = s->rope_cos;
+    r.qk.sin_t = s->rope_sin;
+    r.qk.positions = st->positions;
+    r.qk.block_table = st->block_table;
+    r.qk.max_blocks = st->max_blocks;
+    r.qk.block_size = st->block_size;
+    r.qk.num_blocks = st->num_blocks;
+    r.qk.rope_len = gm.rope_len;
+    r.qk.err = c->gemm.err;
+    r.qk.k_pool = kp;
+    r.qk.v_pool = vp;
+    r.qk.q_out = s->q;
+    r.qk.heads = gm.heads;
+    r.qk.n_kv = gm.n_kv;
+    r.qk.eps = gm.eps;
+    TTS_TRY(launch_gemm(r, c->gemm, cs, c->device), "proj");
+    AttnRequest ar;
+    ar.q = s->q;
+    ar.k_pool = kp;
+    ar.v_pool = vp;
+    ar.block_table = st->block_table;
+    ar.max_blocks = st->max_blocks;
+    ar.block_size = st->block_size;
+    ar.num_blocks = st->num_blocks;
+    ar.err = c->gemm.err;
+    ar.spans = st->positions;
+    ar.span_add = 1;
+    ar.max_span = st->max_span;
+    ar.window = 0;
+    ar.lanes = B;
+    ar.n_kv = gm.n_kv;
+    ar.gqa = gm.heads / gm.n_kv;
+    ar.out = s->attn;
+    ar.out_f16 = true;
+    TTS_TRY(launch_attn(ar, c->attn, cs), "decode_attention");
+    GemmRequest o;
+    o.w = static_cast<const __half*>(w.wo);
+    o.x = s->attn;
+    o.m = B;
+    o.k = qw;
+    o.n = D;
+    o.epi = EPI_RESIDUAL;
+    o.y = s->h;
+    TTS_TRY(launch_gemm(o, c->gemm, cs, c->device), "proj");
+    // feed-forward block (qwen3.rs:453-463)
+    TTS_TRY(launch_rms_norm(s->h, w.ffn_norm, B, D, gm.eps, nullptr, s->xn, nullptr, 0, true, cs),
+            "rms_norm");
+    GemmRequest gu;
+    gu.w = static_cast<const __half*>(w.w_gate_up);
+    gu.x = s->xn;
+    gu.m = B;
+    gu.k = D;
+    gu.n = 2 * gm.ffn;
+    gu.epi = EPI_SWIGLU;
+    gu.y = s->act;
+    TTS_TRY(launch_gemm(gu, c->gemm, cs, c->device), "proj");
+    GemmRequest dn;
+    dn.w = static_cast<const __half*>(w.w_down);
+    dn.x = s->act;
+    dn.m = B;
+    dn.k = gm.ffn;
+    dn.n = D;
+    dn.epi = EPI_RESIDUAL;
+    dn.y = s->h;
+    TTS_TRY(launch_gemm(dn, c->gemm, cs, c->device), "proj");
+  }
+  // final norm (qwen3.rs:466), heads + greedy pick, next input
+  const int nkeys = s->heads ? B * gm.codebooks : 0;
+  TTS_TRY(launch_rms_norm(s->h, s->final_norm, B, D, gm.eps, h_out, s->xn, s->heads ? s->keys : nullptr,
+                          nkeys, true, cs),
+          "rms_norm");
+  if (s->heads) {
+    GemmRequest hd;
+    hd.w = s->heads;
+    hd.x = s->xn;
+    hd.m = B;
+    hd.k = D;
+    hd.n = gm.codebooks * gm.vocab;
+    hd.epi = EPI_ARGMAX;
+    hd.y = logits;
+    hd.argmax_keys = s->keys;
+    hd.vocab = gm.vocab;
+    TTS_TRY(launch_gemm(hd, c->gemm, cs, c->device), "proj");
+    TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, s->embed, D, codes,
+                                 s->embed ? s->x_next : nullptr, nullptr, true, cs),
+            "keys_to_codes");
+  }
+  TTS_TRY(launch_advance_positions(st->positions, B, true, cs), "advance_positions");
+#undef TTS_TRY
+  return TTS_OK;
+}
+
+tts_status tts_stack_decode_step(tts_stack* s, const tts_decode_state* st, const float* x,
+                                 float* h_out, float* logits, unsigned int* codes, void* stream) {
+  if (!s) return fail(TTS_ERR_INVALID_ARG, "decode_step: stack is NULL");
+  DeviceGuard g(s->ctx->device);
+  return step_impl(s, st, x, h_out, logits, codes, S(stream));
+}
+
+tts_status tts_stack_graph_capture(tts_stack* s, const tts_decode_state* st, const float* x,
+                                   float* h_out, float* logits, unsigned int* codes, void* stream,
+                                   tts_graph** out) {
+  if (!s || !out) return fail(TTS_ERR_INVALID_ARG, "graph_capture: NULL argument");
+  if (!stream) return fail(TTS_ERR_INVALID_ARG, "graph_capture: needs a non-legacy stream");
+  DeviceGuard g(s->ctx->device);
+  cudaStream_t cs = S(stream);
+  const long long before = g_launches;
+  cudaError_t e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return cuda_status(e, "graph_capture");
+  tts_status rc = step_impl(s, st, x, h_out, logits, codes, cs);
+  cudaGraph_t graph = nullptr;
+  e = cudaStreamEndCapture(cs, &graph);
+  const long long kernels = g_launches - before;
+  g_launches = before;  // capture launches nothing
+  if (rc != TTS_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return cuda_status(e, "graph_capture");
+  auto* gr = new tts_graph();
+  gr->graph = graph;
+  gr->kernels = kernels;
+  e = cudaGraphInstantiate(&gr->exec, graph, 0);
+  if (e != cudaSuccess) {
+    tts_graph_destroy(gr);
+    return cuda_status(e, "graph_capture");
+  }
+  *out = gr;
+  return TTS_OK;
+}
+
+tts_status tts_graph_launch(tts_graph* g, void* stream) {
+  if (!g) return fail(TTS_ERR_INVALID_ARG, "graph_launch: NULL graph");
+  cudaError_t e = cudaGraphLaunch(g->exec, S(stream));
+  if (e == cudaSuccess) g_launches += g->kernels;
+  return cuda_status(e, "graph_launch");
+}
+
+tts_status tts_graph_destroy(tts_graph* g) {
+  if (!g) return TTS_OK;
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  if (g->graph) cudaGraphDestroy(g->graph);
+  delete g;
+  return TTS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,141 @@
+// Internal C++ interface between the kernel files and the C ABI in runtime.cu.
+#pragma once
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace tts {
+
+// ------------------------------------------------------------------ errors
+void set_error(const std::string& msg);
+const char* last_error();
+
+// ------------------------------------------------------------------ device properties
+int num_sms(int device);
+
+// ------------------------------------------------------------------ decode GEMM
+enum Epilogue : int {
+  EPI_F32 = 0,       // y[m, n] f32
+  EPI_F16 = 1,       // y[m, n] f16
+  EPI_RESIDUAL = 2,  // y[m, n] f32 += acc
+  EPI_SWIGLU = 3,    // W rows interleaved per 128-row tile: 64 gate then 64 up; y[m, n/2] f16
+  EPI_QKROPE = 4,    // QK-norm + RoPE + paged KV append per 128-row head tile
+  EPI_ARGMAX = 5,    // greedy pick per (row, codebook); optional f32 logits in y
+};
+
+struct QkRopeArgs {
+  const float* norms = nullptr;  // [2][128]: q weight (1/sqrt(hd) folded in), k weight
+  const float* cos_t = nullptr;  // [positions][64]
+  const float* sin_t = nullptr;
+  const int* positions = nullptr;    // [lanes] position written this step
+  const int* block_table = nullptr;  // [lanes][max_blocks]
+  int max_blocks = 0;
+  int block_size = 0;
+  int num_blocks = 0;        // pages in the pool; out-of-range table entries are skipped
+  int rope_len = 0;          // rows of cos_t/sin_t; positions outside are skipped
+  int* err = nullptr;        // set (bit 8) when a table entry or position is out of range
+  __half* k_pool = nullptr;  // this layer's K pages [num_blocks][n_kv][block_size][128]
+  __half* v_pool = nullptr;
+  float* q_out = nullptr;  // [lanes][heads][128]
+  int heads = 0;
+  int n_kv = 0;
+  float eps = 1e-6f;
+};
+
+struct GemmRequest {
+  const __half* w = nullptr;  // [n][k] (out-major, K contiguous)
+  const __half* x = nullptr;  // [m][k]
+  int m = 0, k = 0, n = 0;
+  int epi = EPI_F32;
+  void* y = nullptr;
+  int ldy = 0;  // elements between rows of y (0 = natural width)
+  QkRopeArgs qk;
+  unsigned long long* argmax_keys = nullptr;  // [m][codebooks]
+  int vocab = 0;
+  bool pdl = true;
+  int force_splits = 0;  // 0 = automatic
+};
+
+struct Workspace {
+  float* ws = nullptr;  // split-K partials
+  size_t ws_bytes = 0;
+  unsigned* counters = nullptr;  // per-tile arrival counters (zero between launches)
+  int n_counters = 0;
+  int* err = nullptr;  // device error flags (bounded waits that gave up)
+};
+
+bool gemm_supported(int m, int k, int n, int epi, std::string* why);
+cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t st, int device);
+
+// ------------------------------------------------------------------ decode attention
+struct AttnRequest {
+  const float* q = nullptr;  // [lanes][n_kv*gqa][128] f32, scale folded in
+  const __half* k_pool = nullptr;  // layer view [num_blocks][n_kv][block_size][128]
+  const __half* v_pool = nullptr;
+  const int* block_table = nullptr;  // [lanes][max_blocks]
+  int max_blocks = 0;
+  int block_size = 0;
+  int num_blocks = 0;
+  int* err = nullptr;
+  const int* spans = nullptr;  // [lanes]; span of lane i = spans[i] + span_add
+  int span_add = 0;
+  int max_span = 0;  // upper bound of any span (sizes the grid)
+  int window = 0;    // 0 = none; else positions < span - window are masked
+  int lanes = 0, n_kv = 0, gqa = 0;
+  void* out = nullptr;  // [lanes][n_kv*gqa*128]
+  bool out_f16 = true;
+  bool pdl = true;
+};
+struct AttnWorkspace {
+  float* part = nullptr;
+  size_t part_bytes = 0;
+  unsigned* counters = nullptr;
+  int n_counters = 0;
+};
+size_t attn_part_bytes(int lanes, int n_kv, int gqa, int max_span);
+cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream_t st);
+
+// ------------------------------------------------------------------ small kernels
+cudaError_t launch_rms_norm(const float* x, const float* w, int rows, int dim, float eps,
+                            float* y32, __half* y16, unsigned long long* zero_keys, int n_keys,
+                            bool pdl, cudaStream_t st);
+cudaError_t launch_qk_rope(const float* qkv, const QkRopeArgs& a, int lanes, bool pdl,
+                           cudaStream_t st);
+cudaError_t launch_swiglu(const float* g, const float* u, void* y, bool y_f16, long n,
+                          cudaStream_t st);
+cudaError_t launch_snake(const void* x, bool x_f16, const float* alpha, const float* brecip,
+                         long rows, int chan, void* y, bool y_f16, cudaStream_t st);
+cudaError_t launch_argmax(const float* logits, int rows, int n, const uint8_t* banned,
+                          uint32_t* out, cudaStream_t st);
+cudaError_t launch_keys_to_codes(const unsigned long long* keys, int rows, int codebooks,
+                                 int vocab, const __half* embed, int dim, uint32_t* codes,
+                                 float* x_next, unsigned long long* keys_reset, bool pdl,
+                                 cudaStream_t st);
+cudaError_t launch_advance_positions(int* positions, int lanes, bool pdl, cudaStream_t st);
+cudaError_t launch_cast_f32_f16(const float* x, __half* y, long n, cudaStream_t st);
+
+// ------------------------------------------------------------------ codec conv
+struct ConvRequest {
+  const __half* x = nullptr;  // [b][len][cin] channels-last
+  const __half* w = nullptr;  // [cout][k][cin] (K-major per output channel)
+  const float* bias = nullptr;    // [cout] or null
+  const float* alpha = nullptr;   // snake on load: [cin] or null
+  const float* brecip = nullptr;  // [cin]
+  const __half* res = nullptr;    // [b][len][cout] or null
+  __half* y = nullptr;            // [b][len][cout]
+  int b = 0, len = 0, cin = 0, cout = 0, k = 0, dil = 1, pad_left = 0;
+  bool pdl = false;
+};
+bool conv_supported(const ConvRequest& r, std::string* why);
+cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* err);
+
+// ------------------------------------------------------------------ TMA descriptor encode
+bool make_tmap_2d_f16(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer,
+                      uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                      bool swizzle128);
+
+}  // namespace tts

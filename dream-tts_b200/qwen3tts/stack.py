@@ -1,0 +1,205 @@
+"""The qwen3 decoder stack and its decode-time state on B200.
+
+Mirrors crates/qwen3tts/src/qwen3.rs: `Geometry`, `Stack` (layer weights, final norm, RoPE
+tables) and `State` (the KV cache and how many positions each lane holds). The cache is paged:
+K and V pools of fixed-size pages shared by every lane of a group, a block table per lane, and
+a position per lane, all device-resident, so lanes of different lengths step together and a
+finished lane gives its pages back without touching the others (the reference's contiguous
+per-batch cache can only narrow a finished tail, qwen3.rs:198-211).
+
+The decode step itself runs in native code (libtts_cuda.so, tts_stack_decode_step); this
+module owns the tensors and hands pointers across the C ABI.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import torch
+
+import ttsnn
+from ttsnn import _lib as L
+from ttsnn._ctx import ctx, ptr, stream
+
+
+@dataclass
+class Geometry:
+    """Layer shape (crates/qwen3tts/src/qwen3.rs:15-39) plus the talker's codebook heads."""
+    dim: int = 2048
+    layers: int = 28
+    heads: int = 16
+    n_kv: int = 8
+    head_dim: int = 128
+    ffn: int = 6144
+    eps: float = 1e-6
+    rope_base: float = 1e6
+    rope_len: int = 4096
+    codebooks: int = 16
+    vocab: int = 2048
+
+    @property
+    def gqa(self) -> int:
+        return self.heads // self.n_kv
+
+    def c_struct(self) -> L.StackGeometry:
+        return L.StackGeometry(self.dim, self.layers, self.heads, self.n_kv, self.head_dim,
+                               self.ffn, self.eps, self.rope_base, self.rope_len,
+                               self.codebooks, self.vocab)
+
+
+@dataclass
+class LayerTensors:
+    """One layer on the device, in the layout the kernels take (qwen3.rs:61-119 does the same
+    folding at load: q/k/v concatenated, 1/sqrt(head_dim) folded into the q norm)."""
+    attn_norm: torch.Tensor  # f32 [dim]
+    ffn_norm: torch.Tensor   # f32 [dim]
+    wqkv: torch.Tensor       # f16 [(heads + 2 n_kv) * hd, dim]
+    qk_norms: torch.Tensor   # f32 [2, hd]
+    wo: torch.Tensor         # f16 [dim, heads * hd]
+    w_gate_up: torch.Tensor  # f16 [2 ffn, dim], tile-interleaved
+    w_down: torch.Tensor     # f16 [dim, ffn]
+
+    @classmethod
+    def load(cls, q_proj, k_proj, v_proj, o_proj, gate, up, down, attn_norm, ffn_norm, q_norm,
+             k_norm, head_dim: int = 128) -> "LayerTensors":
+        """From checkpoint-layout tensors ([out, in] projections), as Layer::load does."""
+        dev = q_proj.device
+        wqkv = torch.cat([q_proj, k_proj, v_proj], 0).to(torch.float16).contiguous()
+        qn = q_norm.to(torch.float32) * (1.0 / head_dim ** 0.5)
+        return cls(attn_norm.to(dev, torch.float32).contiguous(),
+                   ffn_norm.to(dev, torch.float32).contiguous(), wqkv,
+                   torch.stack([qn, k_norm.to(torch.float32)]).to(dev).contiguous(),
+                   o_proj.to(torch.float16).contiguous(),
+                   ttsnn.interleave_gate_up(gate, up), down.to(torch.float16).contiguous())
+
+
+class PagedKv:
+    """KV pages for one group of lanes: pools f16 [layers][num_blocks][n_kv][block_size][128],
+    block table int32 [lanes][max_blocks], positions int32 [lanes] (each lane's cached length).
+    Pages come from a host-side free list when a lane is admitted."""
+
+    def __init__(self, geo: Geometry, lanes: int, num_blocks: int, block_size: int,
+                 max_blocks: int, device: torch.device | str = "cuda"):
+        self.geo = geo
+        self.lanes = lanes
+        self.block_size = block_size
+        self.num_blocks = num_blocks
+        self.max_blocks = max_blocks
+        shape = (geo.layers, num_blocks, geo.n_kv, block_size, geo.head_dim)
+        self.k = torch.zeros(shape, dtype=torch.float16, device=device)
+        self.v = torch.zeros(shape, dtype=torch.float16, device=device)
+        self.table = torch.zeros(lanes, max_blocks, dtype=torch.int32, device=device)
+        self.positions = torch.zeros(lanes, dtype=torch.int32, device=device)
+        self._free = list(range(num_blocks - 1, -1, -1))
+        self._owned: dict[int, list[int]] = {}
+
+    def admit(self, lane: int, capacity: int, length: int = 0) -> list[int]:
+        """Give `lane` pages for `capacity` positions; it holds `length` of them already."""
+        need = -(-capacity // self.block_size)
+        if need > self.max_blocks:
+            raise ValueError(f"lane needs {need} pages, the table holds {self.max_blocks}")
+        if need > len(self._free):
+            raise MemoryError("KV pool exhausted")
+        self.release(lane)
+        pages = [self._free.pop() for _ in range(need)]
+        self._owned[lane] = pages
+        row = torch.zeros(self.max_blocks, dtype=torch.int32)
+        row[:need] = torch.tensor(pages, dtype=torch.int32)
+        self.table[lane].copy_(row)
+        self.positions[lane] = length
+        return pages
+
+    def release(self, lane: int) -> None:
+        for p in self._owned.pop(lane, []):
+            self._free.append(p)
+
+    def free_pages(self) -> int:
+        return len(self._free)
+
+    def state(self, lanes: int | None = None, max_span: int | None = None) -> L.DecodeState:
+        n = self.lanes if lanes is None else lanes
+        ms = max_span if max_span is not None else self.max_blocks * self.block_size
+        return L.DecodeState(n, self.positions.data_ptr(), self.table.data_ptr(),
+                             self.max_blocks, self.block_size, self.num_blocks,
+                             self.k.data_ptr(), self.v.data_ptr(), ms)
+
+
+class Graph:
+    """A captured decode step, replayed with `replay()` (one tts_graph_launch)."""
+
+    def __init__(self, handle: C.c_void_p, keep: list):
+        self.handle = handle
+        self._keep = keep
+
+    def replay(self) -> None:
+        L.call("tts_graph_launch", self.handle, stream())
+
+    def __del__(self):
+        try:
+            if self.handle:
+                L.load().tts_graph_destroy(self.handle)
+                self.handle = None
+        except Exception:
+            pass
+
+
+class Stack:
+    """`Stack` of crates/qwen3tts/src/qwen3.rs:214-467 with the talker's heads, on B200."""
+
+    def __init__(self, geo: Geometry, layers: list[LayerTensors], final_norm: torch.Tensor,
+                 heads: torch.Tensor | None = None, embed: torch.Tensor | None = None):
+        if len(layers) != geo.layers:
+            raise ValueError(f"{len(layers)} layers for geometry with {geo.layers}")
+        self.geo = geo
+        self.layers = layers
+        self.device = layers[0].wqkv.device
+        self.final_norm = final_norm.to(self.device, torch.float32).contiguous()
+        self.heads = None if heads is None else heads.to(torch.float16).contiguous()
+        self.embed = None if embed is None else embed.to(torch.float16).contiguous()
+        self._ctx = ctx(self.device.index)
+        h = C.c_void_p()
+        g = geo.c_struct()
+        L.call("tts_stack_create", self._ctx, C.byref(g), C.byref(h))
+        self.handle = h
+        for i, lt in enumerate(layers):
+            w = L.LayerWeights(lt.attn_norm.data_ptr(), lt.ffn_norm.data_ptr(),
+                               lt.wqkv.data_ptr(), lt.qk_norms.data_ptr(), lt.wo.data_ptr(),
+                               lt.w_gate_up.data_ptr(), lt.w_down.data_ptr())
+            L.call("tts_stack_set_layer", h, i, C.byref(w))
+        L.call("tts_stack_set_head", h, ptr(self.final_norm), ptr(self.heads), ptr(self.embed))
+
+    def weight_bytes(self) -> int:
+        n = 0
+        for lt in self.layers:
+            n += sum(t.numel() * t.element_size() for t in
+                     (lt.wqkv, lt.wo, lt.w_gate_up, lt.w_down))
+        if self.heads is not None:
+            n += self.heads.numel() * 2
+        return n
+
+    def decode_step(self, kv: PagedKv, x: torch.Tensor | None = None, lanes: int | None = None,
+                    h_out: torch.Tensor | None = None, logits: torch.Tensor | None = None,
+                    codes: torch.Tensor | None = None, max_span: int | None = None) -> None:
+        """One step for `lanes` lanes (default all): writes each lane's K/V at its position,
+        advances the positions, and fills the optional outputs."""
+        st = kv.state(lanes, max_span)
+        L.call("tts_stack_decode_step", self.handle, C.byref(st), ptr(x), ptr(h_out),
+               ptr(logits), ptr(codes), stream())
+
+    def capture(self, kv: PagedKv, x: torch.Tensor | None = None, lanes: int | None = None,
+                h_out: torch.Tensor | None = None, logits: torch.Tensor | None = None,
+                codes: torch.Tensor | None = None, max_span: int | None = None) -> Graph:
+        """The same step as a CUDA graph on the current (non-default) stream."""
+        st = kv.state(lanes, max_span)
+        g = C.c_void_p()
+        L.call("tts_stack_graph_capture", self.handle, C.byref(st), ptr(x), ptr(h_out),
+               ptr(logits), ptr(codes), stream(), C.byref(g))
+        return Graph(g, [kv, x, h_out, logits, codes])
+
+    def __del__(self):
+        try:
+            if getattr(self, "handle", None):
+                L.load().tts_stack_destroy(self.handle)
+                self.handle = None
+        except Exception:
+            pass

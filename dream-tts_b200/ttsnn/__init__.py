@@ -1,0 +1,114 @@
+"""tts-nn on B200: the operator surface crates/qwen3tts calls, backed by sm_100a kernels.
+
+Names, argument meanings and error behaviour follow the reference crate `tts-nn`
+(crates/tts-nn/src/lib.rs and its op modules); tensors are torch CUDA tensors, and every op
+runs through the C ABI of libtts_cuda.so (include/tts_cuda.h). Nothing here computes on the
+CPU: a shape the kernels do not take raises TtsError(UNSUPPORTED_SHAPE).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib as L
+from ._ctx import check, ctx, ctx_of, launch_count, ptr, stream
+from ._lib import TtsError
+from . import attn, fused, nlc, qkrope, topk  # noqa: F401  (submodules mirror tts-nn's)
+
+__all__ = ["Proj", "rms_norm", "rope_table_f32", "abs_and_rel", "TtsError", "check", "ctx",
+           "launch_count", "attn", "fused", "nlc", "qkrope", "topk"]
+
+
+class Proj:
+    """`Proj::Half` (crates/tts-nn/src/lib.rs:388-401, 510-533): f16 weight, f32 in and out.
+
+    The weight stays in the checkpoint's `[out, in]` layout, which is the K-major operand the
+    tcgen05 GEMM wants (the reference transposes to `[in, out]` at load instead,
+    lib.rs:473-489). `forward` casts x to f16 (lib.rs:517) and accumulates in f32, like the
+    reference's skinny kernel (skinny.rs:155-165).
+    """
+
+    def __init__(self, w_out_in: torch.Tensor):
+        if w_out_in.dim() != 2:
+            raise ValueError("Proj: weight must be [out, in]")
+        self.w = w_out_in.to(torch.float16).contiguous()
+        self.n, self.k = self.w.shape
+
+    @classmethod
+    def from_tensor(cls, t: torch.Tensor, device: torch.device | None = None) -> "Proj":
+        return cls(t.to(device or t.device))
+
+    def forward(self, x: torch.Tensor, epilogue: int = L.EPI_F32,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+        if x.shape[-1] != self.k:
+            raise ValueError(f"Proj: input width {x.shape[-1]} != {self.k}")
+        lead = x.shape[:-1]
+        rows = math.prod(lead) if lead else 1
+        h = x.to(torch.float16).reshape(rows, self.k).contiguous()
+        if epilogue == L.EPI_F32:
+            y = out if out is not None else torch.empty(rows, self.n, device=x.device,
+                                                        dtype=torch.float32)
+        elif epilogue == L.EPI_F16:
+            y = out if out is not None else torch.empty(rows, self.n, device=x.device,
+                                                        dtype=torch.float16)
+        elif epilogue == L.EPI_RESIDUAL_F32:
+            if out is None:
+                raise ValueError("Proj: the residual epilogue needs `out` (the residual stream)")
+            y = out
+        elif epilogue == L.EPI_SWIGLU_F16:
+            y = out if out is not None else torch.empty(rows, self.n // 2, device=x.device,
+                                                        dtype=torch.float16)
+        else:
+            raise ValueError("Proj: unknown epilogue")
+        L.call("tts_proj_forward", ctx_of(x), ptr(h), rows, self.k, ptr(self.w), self.n,
+               epilogue, ptr(y), 0, stream())
+        return y.reshape(*lead, y.shape[-1]) if epilogue != L.EPI_RESIDUAL_F32 else y
+
+    __call__ = forward
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """`[ffn, dim]` gate and up -> `[2 ffn, dim]` in the SwiGLU epilogue's tile order."""
+    ffn, dim = gate.shape
+    g = gate.to(torch.float16).contiguous()
+    u = up.to(torch.float16).contiguous()
+    out = torch.empty(2 * ffn, dim, device=gate.device, dtype=torch.float16)
+    L.call("tts_interleave_gate_up", ctx_of(g), ptr(g), ptr(u), ffn, dim, ptr(out), stream())
+    return out
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+             out_f16: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm over the last dim in f32 (crates/tts-nn/src/lib.rs:1001-1003)."""
+    dim = x.shape[-1]
+    xf = x.to(torch.float32).contiguous()
+    w = weight.to(torch.float32).contiguous()
+    if w.numel() != dim:
+        raise ValueError(f"rms_norm: weight has {w.numel()} elements for width {dim}")
+    y = torch.empty_like(xf)
+    L.call("tts_rms_norm", ctx_of(xf), ptr(xf), ptr(w), xf.numel() // dim, dim, float(eps),
+           ptr(y), ptr(out_f16), stream())
+    return y
+
+
+def rope_table_f32(length: int, head_dim: int, base: float,
+                   device: torch.device | str = "cuda") -> tuple[torch.Tensor, torch.Tensor]:
+    """Half-split RoPE tables `[length, head_dim/2]`, phases in f64 rounded to f32
+    (crates/tts-nn/src/lib.rs:1178-1205)."""
+    half = head_dim // 2
+    i = torch.arange(half, dtype=torch.float64)
+    freq = 1.0 / torch.pow(torch.tensor(base, dtype=torch.float64), 2.0 * i / head_dim)
+    t = torch.arange(length, dtype=torch.float64)[:, None]
+    ph = t * freq[None, :]
+    return (torch.cos(ph).to(torch.float32).to(device),
+            torch.sin(ph).to(torch.float32).to(device))
+
+
+def abs_and_rel(a: torch.Tensor, b: torch.Tensor) -> tuple[float, float]:
+    """Max abs difference and that difference over b's peak magnitude (lib.rs:1239-1248)."""
+    a = a.detach().to(torch.float32).flatten().cpu()
+    b = b.detach().to(torch.float32).flatten().cpu()
+    d = (a - b).abs().max().item() if a.numel() else 0.0
+    s = b.abs().max().item() if b.numel() else 0.0
+    return d, (d / s if s > 0 else 0.0)

@@ -1,0 +1,115 @@
+"""ctypes binding of libtts_cuda.so (the C ABI declared in include/tts_cuda.h).
+
+Loading fails loudly when the library has not been built: there is no other implementation
+behind these functions.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libtts_cuda.so")
+
+TTS_OK = 0
+STATUS = {0: "OK", 1: "INVALID_ARG", 2: "UNSUPPORTED_SHAPE", 3: "CUDA", 4: "TIMEOUT", 5: "OOM"}
+
+EPI_F32, EPI_F16, EPI_RESIDUAL_F32, EPI_SWIGLU_F16 = 0, 1, 2, 3
+
+
+class TtsError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+class KvCache(C.Structure):
+    _fields_ = [("k_pages", C.c_void_p), ("v_pages", C.c_void_p), ("block_table", C.c_void_p),
+                ("max_blocks", C.c_int), ("block_size", C.c_int), ("num_blocks", C.c_int),
+                ("n_kv", C.c_int), ("head_dim", C.c_int)]
+
+
+class StackGeometry(C.Structure):
+    _fields_ = [("dim", C.c_int), ("layers", C.c_int), ("heads", C.c_int), ("n_kv", C.c_int),
+                ("head_dim", C.c_int), ("ffn", C.c_int), ("eps", C.c_float),
+                ("rope_base", C.c_double), ("rope_len", C.c_int), ("codebooks", C.c_int),
+                ("vocab", C.c_int)]
+
+
+class LayerWeights(C.Structure):
+    _fields_ = [("attn_norm", C.c_void_p), ("ffn_norm", C.c_void_p), ("wqkv", C.c_void_p),
+                ("qk_norms", C.c_void_p), ("wo", C.c_void_p), ("w_gate_up", C.c_void_p),
+                ("w_down", C.c_void_p)]
+
+
+class DecodeState(C.Structure):
+    _fields_ = [("lanes", C.c_int), ("positions", C.c_void_p), ("block_table", C.c_void_p),
+                ("max_blocks", C.c_int), ("block_size", C.c_int), ("num_blocks", C.c_int),
+                ("k_pages", C.c_void_p), ("v_pages", C.c_void_p), ("max_span", C.c_int)]
+
+
+P = C.c_void_p
+I = C.c_int
+L = C.c_long
+F = C.c_float
+
+# name -> argtypes; every function returns tts_status (int) unless listed in _RESTYPE.
+SIGNATURES = {
+    "tts_abi_version": [],
+    "tts_last_error": [],
+    "tts_launch_count": [I],
+    "tts_ctx_create": [I, I, C.POINTER(P)],
+    "tts_ctx_destroy": [P],
+    "tts_ctx_check": [P, P],
+    "tts_proj_forward": [P, P, I, I, P, I, I, P, I, P],
+    "tts_interleave_gate_up": [P, P, P, I, I, P, P],
+    "tts_rms_norm": [P, P, P, I, I, F, P, P, P],
+    "tts_swiglu_mul": [P, P, P, L, P, I, P],
+    "tts_snake_beta_nlc": [P, P, I, P, P, L, I, P, I, P],
+    "tts_qk_rope_append": [P, P, I, I, P, P, P, I, P, C.POINTER(KvCache), F, P, P],
+    "tts_decode_attention": [P, P, I, I, C.POINTER(KvCache), P, I, I, P, I, P],
+    "tts_argmax": [P, P, I, I, P, P, P],
+    "tts_conv1d_nlc": [P, P, I, I, I, P, I, I, I, I, P, P, P, P, P, P],
+    "tts_stack_create": [P, C.POINTER(StackGeometry), C.POINTER(P)],
+    "tts_stack_set_layer": [P, I, C.POINTER(LayerWeights)],
+    "tts_stack_set_head": [P, P, P, P],
+    "tts_stack_destroy": [P],
+    "tts_stack_decode_step": [P, C.POINTER(DecodeState), P, P, P, P, P],
+    "tts_stack_graph_capture": [P, C.POINTER(DecodeState), P, P, P, P, P, C.POINTER(P)],
+    "tts_graph_launch": [P, P],
+    "tts_graph_destroy": [P],
+}
+_RESTYPE = {"tts_last_error": C.c_char_p, "tts_launch_count": C.c_longlong}
+
+_lib = None
+
+
+def load() -> C.CDLL:
+    """The loaded library; raises if it was never built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python dream-tts_b200/build.py` "
+                "(there is no fallback implementation)")
+        lib = C.CDLL(LIB_PATH)
+        for name, args in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = _RESTYPE.get(name, C.c_int)
+        _lib = lib
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    """Calls a tts_status-returning entry point and raises TtsError on failure."""
+    lib = load()
+    rc = getattr(lib, name)(*args)
+    if rc != TTS_OK:
+        msg = lib.tts_last_error()
+        raise TtsError(rc, msg.decode() if msg else name)
+
+
+def last_error() -> str:
+    msg = load().tts_last_error()
+    return msg.decode() if msg else ""

@@ -1,0 +1,233 @@
+/*
+ * tts_cuda.h — C ABI of the B200 (sm_100a) backend for dream-tts's qwen3tts hot path.
+ *
+ * Each entry point stands in for one operator of the `tts-nn` crate that crates/qwen3tts calls
+ * (the reference's plugin surface: candle CustomOps with cpu_fwd/metal_fwd arms), or for the
+ * qwen3tts decode step built from them. The citation above each declaration names the
+ * reference interface it replaces (paths within the dream-tts project).
+ *
+ * Conventions
+ *  - Plain C types only. Every device pointer is caller-owned, 16-byte aligned, row-major and
+ *    contiguous unless stated; `stream` is a cudaStream_t passed as void* (NULL = legacy).
+ *  - f16 buffers are IEEE binary16 (`void*`), f32 buffers `float*`.
+ *  - Calls are stream-ordered and return without synchronising. A context serialises its
+ *    scratch buffers: use one stream per context (the reference's dispatcher is single-stream
+ *    too, crates/tts-nn/src/lib.rs:76-88).
+ *  - Every function returns a tts_status; on failure tts_last_error() (thread-local) names the
+ *    operator and the violated constraint, the way the reference's `bail!`s do. There is no
+ *    CPU fallback: a shape the kernels do not take returns TTS_ERR_UNSUPPORTED_SHAPE.
+ */
+#ifndef TTS_CUDA_H
+#define TTS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TTS_CUDA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TTS_API __attribute__((visibility("default")))
+#else
+#define TTS_API
+#endif
+
+typedef enum tts_status {
+  TTS_OK = 0,
+  TTS_ERR_INVALID_ARG = 1,
+  TTS_ERR_UNSUPPORTED_SHAPE = 2,
+  TTS_ERR_CUDA = 3,
+  TTS_ERR_TIMEOUT = 4, /* a bounded device-side wait gave up; results are not valid */
+  TTS_ERR_OOM = 5
+} tts_status;
+
+typedef struct tts_ctx tts_ctx;
+typedef struct tts_stack tts_stack;
+typedef struct tts_graph tts_graph;
+
+TTS_API int tts_abi_version(void);
+/* Last error message of the calling thread ("" when none). */
+TTS_API const char* tts_last_error(void);
+
+/* One context per device (and per host thread driving it). Allocates the split-K and
+ * attention scratch for up to `max_lanes` rows. Replaces the candle Device the reference opens
+ * in crates/qwen3tts/src/engine.rs:529-533. */
+TTS_API tts_status tts_ctx_create(int device, int max_lanes, tts_ctx** out);
+TTS_API tts_status tts_ctx_destroy(tts_ctx* ctx);
+/* Synchronises `stream` and reports TTS_ERR_TIMEOUT if any kernel's bounded wait gave up
+ * since the last check (then clears the flag). */
+TTS_API tts_status tts_ctx_check(tts_ctx* ctx, void* stream);
+
+/* ---------------------------------------------------------------- projections
+ * Proj::forward for Proj::Half: crates/tts-nn/src/lib.rs:510-533, via skinny::matmul
+ * (crates/tts-nn/src/skinny.rs:155-165) and matmul_2d (lib.rs:438-459).
+ * y = x[m, k] (f16) . w[n, k]^T (f16, the checkpoint's [out, in] layout), f32 accumulate.
+ * m in 1..512, k % 64 == 0, n % 128 == 0. `epilogue`:
+ *   TTS_EPI_F32          y f32 [m][ldy]
+ *   TTS_EPI_F16          y f16 [m][ldy]
+ *   TTS_EPI_RESIDUAL_F32 y f32 [m][ldy] += x.w^T   (qwen3.rs:451 and :463, h += proj)
+ *   TTS_EPI_SWIGLU_F16   w is a gate/up pair interleaved by tts_interleave_gate_up;
+ *                        y f16 [m][n/2] = silu(gate) * up  (fused.rs:289-386)
+ * ldy = 0 means the natural row width. */
+typedef enum tts_epilogue {
+  TTS_EPI_F32 = 0,
+  TTS_EPI_F16 = 1,
+  TTS_EPI_RESIDUAL_F32 = 2,
+  TTS_EPI_SWIGLU_F16 = 3
+} tts_epilogue;
+TTS_API tts_status tts_proj_forward(tts_ctx* ctx, const void* x_f16, int m, int k, const void* w_f16,
+                            int n, int epilogue, void* y, int ldy, void* stream);
+
+/* Gate and up projections [ffn][dim] each -> one [2 ffn][dim] weight whose 128-row tiles hold
+ * 64 gate rows then the same 64 up rows, the layout TTS_EPI_SWIGLU_F16 consumes. Load-time
+ * step, the counterpart of the q/k/v concatenation in crates/qwen3tts/src/qwen3.rs:70-77. */
+TTS_API tts_status tts_interleave_gate_up(tts_ctx* ctx, const void* gate_f16, const void* up_f16,
+                                  int ffn, int dim, void* out_f16, void* stream);
+
+/* ---------------------------------------------------------------- norms and elementwise
+ * rms_norm: crates/tts-nn/src/lib.rs:1001-1003. y = x / sqrt(mean(x^2) + eps) * w over the
+ * last dim, f32 math; either output may be NULL. dim % 4 == 0. */
+TTS_API tts_status tts_rms_norm(tts_ctx* ctx, const float* x, const float* w, int rows, int dim,
+                        float eps, float* y_f32, void* y_f16, void* stream);
+
+/* fused::swiglu_mul: crates/tts-nn/src/fused.rs:289-386. y = silu(gate) * up. */
+TTS_API tts_status tts_swiglu_mul(tts_ctx* ctx, const float* gate, const float* up, long n, void* y,
+                          int y_f16, void* stream);
+
+/* fused::snake_beta_nlc: crates/tts-nn/src/fused.rs:526-663. Channels-last [rows][chan],
+ * y = x + brecip[c] * sin(alpha[c] * x)^2 in f32; x and y f16 or f32. chan % 8 == 0. */
+TTS_API tts_status tts_snake_beta_nlc(tts_ctx* ctx, const void* x, int x_f16, const float* alpha,
+                              const float* brecip, long rows, int chan, void* y, int y_f16,
+                              void* stream);
+
+/* ---------------------------------------------------------------- attention and KV cache
+ * A paged KV cache for one layer: K and V pages f16 [num_blocks][n_kv][block_size][head_dim];
+ * block_table [lanes][max_blocks] maps a lane's logical block (position / block_size) to a
+ * page. The reference's contiguous per-lane cache [b][n_kv][cap][head_dim]
+ * (crates/qwen3tts/src/qwen3.rs:122-212) is the case block_size = cap, block_table[i] = {i}. */
+typedef struct tts_kv_cache {
+  void* k_pages;
+  void* v_pages;
+  const int* block_table;
+  int max_blocks;
+  int block_size;
+  int num_blocks;
+  int n_kv;
+  int head_dim; /* must be 128 */
+} tts_kv_cache;
+
+/* qkrope::apply: crates/tts-nn/src/qkrope.rs:26-69 (composed form qwen3.rs:358-394).
+ * qkv f32 [lanes][(heads + 2 n_kv) * 128]; norms f32 [2][128] (q weight with 1/sqrt(128)
+ * folded in, then k weight); cos/sin f32 [rope_len][64]; positions [lanes] is the position
+ * each lane writes. Writes q f32 [lanes][heads][128] and K/V (f16) into the pages. Rows whose
+ * position or page is out of range are skipped and reported by tts_ctx_check. */
+TTS_API tts_status tts_qk_rope_append(tts_ctx* ctx, const float* qkv, int lanes, int heads,
+                                      const float* norms, const float* cos_t,
+                                      const float* sin_t, int rope_len, const int* positions,
+                                      const tts_kv_cache* kv, float eps, float* q_out,
+                                      void* stream);
+
+/* attn::decode_attention: crates/tts-nn/src/attn.rs:22-73. q f32 [lanes][n_kv * gqa][128]
+ * with the scale folded in; lane i attends positions [wstart_i, spans[i]) where
+ * wstart_i = max(0, spans[i] - window) (window 0 = none). max_span bounds every spans[i].
+ * out [lanes][n_kv * gqa * 128], f16 or f32. gqa in {1, 2}. */
+TTS_API tts_status tts_decode_attention(tts_ctx* ctx, const float* q, int lanes, int gqa,
+                                const tts_kv_cache* kv, const int* spans, int max_span,
+                                int window, void* out, int out_f16, void* stream);
+
+/* ---------------------------------------------------------------- sampling
+ * Greedy pick of sample_with_u: crates/qwen3tts/src/talker.rs:154-189. banned[n] (nullable)
+ * marks ids forced to -inf; ties go to the highest index (Rust's max_by). */
+TTS_API tts_status tts_argmax(tts_ctx* ctx, const float* logits, int rows, int n,
+                      const unsigned char* banned, unsigned int* out, void* stream);
+
+/* ---------------------------------------------------------------- codec convolution
+ * nlc::causal_conv1d and nlc::snake_conv_residual: crates/tts-nn/src/nlc.rs:40-132 via the
+ * NlcConv kernel (crates/tts-nn/src/nlcconv.rs:15-198), extended with pad_left so the centred
+ * form (crates/tts-nn/src/lib.rs:736-767) is the same call.
+ * y[b, l, co] = bias[co] + sum_t sum_ci s(x)[b, l + t*dil - pad_left, ci] * w[co, t, ci]
+ *               (+ res[b, l, co]),   rows outside [0, len) read as zero,
+ * s(x) = x + brecip * sin(alpha * x)^2 when alpha is given (SnakeBeta on load), else x.
+ * x, res, y f16 channels-last; w f16 [cout][k][cin]; bias/alpha/brecip f32 (nullable).
+ * cin % 64 == 0, cout % 128 == 0 and <= 512, k * dil <= 128. */
+TTS_API tts_status tts_conv1d_nlc(tts_ctx* ctx, const void* x_f16, int b, int len, int cin,
+                          const void* w_f16, int cout, int k, int dilation, int pad_left,
+                          const float* bias, const float* alpha, const float* brecip,
+                          const void* res_f16, void* y_f16, void* stream);
+
+/* ---------------------------------------------------------------- decoder stack
+ * The qwen3 decoder stack (crates/qwen3tts/src/qwen3.rs:15-467): geometry, per-layer weights
+ * (caller-owned device memory, referenced not copied) and the decode step at t == 1. */
+typedef struct tts_stack_geometry {
+  int dim, layers, heads, n_kv, head_dim, ffn;
+  float eps;
+  double rope_base;
+  int rope_len;  /* positions the RoPE table covers */
+  int codebooks; /* heads after the final norm (0 = none) */
+  int vocab;     /* ids per codebook head, multiple of 128 */
+} tts_stack_geometry;
+
+typedef struct tts_layer_weights {
+  const float* attn_norm; /* [dim] */
+  const float* ffn_norm;  /* [dim] */
+  const void* wqkv;       /* f16 [(heads + 2 n_kv) * head_dim][dim], q/k/v rows concatenated */
+  const float* qk_norms;  /* [2][head_dim]: q_norm * 1/sqrt(head_dim), k_norm (qwen3.rs:82-87) */
+  const void* wo;         /* f16 [dim][heads * head_dim] */
+  const void* w_gate_up;  /* f16 [2 ffn][dim] from tts_interleave_gate_up */
+  const void* w_down;     /* f16 [dim][ffn] */
+} tts_layer_weights;
+
+TTS_API tts_status tts_stack_create(tts_ctx* ctx, const tts_stack_geometry* geo, tts_stack** out);
+TTS_API tts_status tts_stack_set_layer(tts_stack* s, int layer, const tts_layer_weights* w);
+/* final_norm f32 [dim]; heads f16 [codebooks * vocab][dim] (NULL = none); embed f16
+ * [codebooks][vocab][dim] (NULL = none), the tables whose rows for the picked codes are summed
+ * into the next step's input. */
+TTS_API tts_status tts_stack_set_head(tts_stack* s, const float* final_norm, const void* heads_f16,
+                              const void* embed_f16);
+TTS_API tts_status tts_stack_destroy(tts_stack* s);
+
+/* Decode-time cache state of one group of lanes, all layers: pages f16
+ * [layers][num_blocks][n_kv][block_size][head_dim]. positions[lanes] (device) is each lane's
+ * cached length; the step writes there and then advances it by one. max_span bounds
+ * positions[i] + 1 for as long as a captured graph is replayed. */
+typedef struct tts_decode_state {
+  int lanes;
+  int* positions;
+  const int* block_table;
+  int max_blocks;
+  int block_size;
+  int num_blocks;
+  void* k_pages;
+  void* v_pages;
+  int max_span;
+} tts_decode_state;
+
+/* One talker decode step: Stack::forward at t == 1 (qwen3.rs:294-467, the whole layer loop and
+ * the final norm), then the codebook heads and a greedy pick per head (talker.rs:956-998), then
+ * the sum of the picked codes' embedding rows as the next input (talker.rs:1019-1023, 528-550).
+ * x f32 [lanes][dim], or NULL to continue from the previous step's embedding sum. Outputs
+ * (nullable): h_out f32 [lanes][dim] normed hidden; logits f32 [lanes][codebooks * vocab];
+ * codes u32 [lanes][codebooks]. */
+TTS_API tts_status tts_stack_decode_step(tts_stack* s, const tts_decode_state* st, const float* x,
+                                 float* h_out, float* logits, unsigned int* codes, void* stream);
+
+/* The same step captured once into a CUDA graph (stream must not be the legacy stream) and
+ * replayed with tts_graph_launch. Pointers are baked in at capture. */
+TTS_API tts_status tts_stack_graph_capture(tts_stack* s, const tts_decode_state* st, const float* x,
+                                   float* h_out, float* logits, unsigned int* codes,
+                                   void* stream, tts_graph** out);
+TTS_API tts_status tts_graph_launch(tts_graph* g, void* stream);
+TTS_API tts_status tts_graph_destroy(tts_graph* g);
+
+/* Kernel launches made by the calling thread through this library since the last call
+ * (observability: the bench reports it). */
+TTS_API long long tts_launch_count(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TTS_CUDA_H */

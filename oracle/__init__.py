@@ -1,0 +1,263 @@
+"""CPU oracle for the qwen3tts hot path — TEST INFRASTRUCTURE ONLY.
+
+Python face of oracle/oracle.c (a plain-C restatement of the reference's CPU arithmetic) plus
+the compositions the reference builds from those ops: the decoder layer's decode step
+(crates/qwen3tts/src/qwen3.rs:294-467), the greedy head pick, and the codec residual block.
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use this package; the
+product library never links or calls it.
+
+PARITY UNPINNED: the reference ships no golden vectors for these ops and cannot be built or
+run here (Rust, no toolchain, no checkpoint). The restatement is cross-checked against
+independent PyTorch-CPU formulas and the structural identities of the reference's own tests
+(tests/test_oracle.py); tests/golden/ pins it against regressions.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "liboracle.so")
+_lib = None
+
+f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
+i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+u32p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
+u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+
+
+def build() -> str:
+    src = os.path.join(HERE, "oracle.c")
+    if not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(src):
+        subprocess.run(["make", "-s", "-C", HERE, "liboracle.so"], check=True)
+    return LIB
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        build()
+        L = C.CDLL(LIB)
+        L.orc_proj.argtypes = [u16p, u16p, f32p, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.orc_rms_norm.argtypes = [f32p, f32p, f32p, C.c_int64, C.c_int, C.c_float]
+        L.orc_rope_table.argtypes = [C.c_int, C.c_int, C.c_double, f32p, f32p]
+        L.orc_qk_rope.argtypes = [f32p, f32p, f32p, f32p, i32p, C.c_int, C.c_int, C.c_int,
+                                  C.c_int, C.c_float, f32p, f32p, f32p]
+        L.orc_decode_attention.argtypes = [f32p, u16p, u16p, i32p, i32p, C.c_int, C.c_int,
+                                           C.c_int, C.c_int, C.c_int, f32p]
+        L.orc_swiglu.argtypes = [f32p, f32p, f32p, C.c_int64]
+        L.orc_snake_beta.argtypes = [f32p, f32p, f32p, f32p, C.c_int64, C.c_int]
+        L.orc_conv1d_nlc.argtypes = [f32p, f32p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                     f32p] + [C.c_int] * 7
+        L.orc_argmax.argtypes = [f32p, C.c_void_p, u32p, C.c_int, C.c_int]
+        L.orc_num_threads.restype = C.c_int
+        L.orc_set_threads.argtypes = [C.c_int]
+        _lib = L
+    return _lib
+
+
+def threads() -> int:
+    return lib().orc_num_threads()
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(int(n))
+
+
+# ---------------------------------------------------------------- f16 helpers
+def f16_bits(x: np.ndarray) -> np.ndarray:
+    """f32 -> IEEE binary16 bit patterns (round to nearest even)."""
+    return np.ascontiguousarray(np.asarray(x, dtype=np.float32).astype(np.float16).view(np.uint16))
+
+
+def f16_value(bits: np.ndarray) -> np.ndarray:
+    return np.asarray(bits, dtype=np.uint16).view(np.float16).astype(np.float32)
+
+
+def _c(a, dt=np.float32):
+    return np.ascontiguousarray(a, dtype=dt)
+
+
+# ---------------------------------------------------------------- ops (oracle.c)
+def proj(x_f32: np.ndarray, w_bits: np.ndarray, round_f16: bool = False) -> np.ndarray:
+    """Proj::Half: f16(x) . W^T with W `[n, k]` f16 bits; f32 accumulate."""
+    lead = x_f32.shape[:-1]
+    k = x_f32.shape[-1]
+    n = w_bits.shape[0]
+    xb = f16_bits(x_f32.reshape(-1, k))
+    y = np.empty((xb.shape[0], n), np.float32)
+    lib().orc_proj(xb, _c(w_bits, np.uint16), y, xb.shape[0], k, n, 1 if round_f16 else 0)
+    return y.reshape(*lead, n)
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    x = _c(x)
+    y = np.empty_like(x)
+    lib().orc_rms_norm(x, _c(w), y, x.size // x.shape[-1], x.shape[-1], float(eps))
+    return y
+
+
+def rope_table(length: int, hd: int, base: float) -> tuple[np.ndarray, np.ndarray]:
+    c = np.empty((length, hd // 2), np.float32)
+    s = np.empty((length, hd // 2), np.float32)
+    lib().orc_rope_table(int(length), int(hd), float(base), c, s)
+    return c, s
+
+
+def qk_rope(qkv: np.ndarray, norms: np.ndarray, cos: np.ndarray, sin: np.ndarray,
+            pos: np.ndarray, heads: int, n_kv: int, eps: float, hd: int = 128):
+    b = qkv.shape[0]
+    q = np.empty((b, heads, hd), np.float32)
+    k = np.empty((b, n_kv, hd), np.float32)
+    v = np.empty((b, n_kv, hd), np.float32)
+    lib().orc_qk_rope(_c(qkv), _c(norms), _c(cos), _c(sin), _c(pos, np.int32), b, heads, n_kv,
+                      hd, float(eps), q, k, v)
+    return q, k, v
+
+
+def decode_attention(q: np.ndarray, k_bits: np.ndarray, v_bits: np.ndarray, span, wstart):
+    """q `[b, n_kv, gqa, hd]` f32; caches `[b, n_kv, cap, hd]` f16 bits; span/wstart per lane."""
+    b, n_kv, gqa, hd = q.shape
+    cap = k_bits.shape[2]
+    sp = np.broadcast_to(np.asarray(span, np.int32), (b,)).copy()
+    ws = np.broadcast_to(np.asarray(wstart, np.int32), (b,)).copy()
+    out = np.empty_like(_c(q))
+    lib().orc_decode_attention(_c(q), _c(k_bits, np.uint16), _c(v_bits, np.uint16), sp, ws, b,
+                               n_kv, gqa, hd, cap, out)
+    return out
+
+
+def swiglu(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    g = _c(g)
+    y = np.empty_like(g)
+    lib().orc_swiglu(g, _c(u), y, g.size)
+    return y
+
+
+def snake_beta(x: np.ndarray, alpha: np.ndarray, brecip: np.ndarray) -> np.ndarray:
+    x = _c(x)
+    y = np.empty_like(x)
+    c = x.shape[-1]
+    lib().orc_snake_beta(x, _c(alpha), _c(brecip), y, x.size // c, c)
+    return y
+
+
+def _vp(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def conv1d_nlc(x: np.ndarray, w_tap: np.ndarray, bias=None, dilation: int = 1,
+               pad_left: int | None = None, snake=None, res=None) -> np.ndarray:
+    """x `[b, L, cin]`, w_tap `[k, cin, cout]`; pad_left defaults to causal (k-1)*dilation."""
+    b, length, cin = x.shape
+    k, _, cout = w_tap.shape
+    if pad_left is None:
+        pad_left = (k - 1) * dilation
+    x = _c(x)
+    w = _c(w_tap)
+    keep = [None if a is None else _c(a) for a in
+            (bias, None if snake is None else snake[0], None if snake is None else snake[1], res)]
+    y = np.empty((b, length, cout), np.float32)
+    lib().orc_conv1d_nlc(x, w, *[_vp(a) for a in keep], y, b, length, cin, cout, k,
+                         int(dilation), int(pad_left))
+    return y
+
+
+def argmax(logits: np.ndarray, banned: np.ndarray | None = None) -> np.ndarray:
+    x = _c(logits)
+    n = x.shape[-1]
+    rows = x.size // n
+    out = np.empty(rows, np.uint32)
+    bb = None if banned is None else _c(banned, np.uint8)
+    lib().orc_argmax(x, _vp(bb), out, rows, n)
+    return out.reshape(x.shape[:-1])
+
+
+# ---------------------------------------------------------------- compositions
+@dataclass
+class Geometry:
+    dim: int = 2048
+    layers: int = 28
+    heads: int = 16
+    n_kv: int = 8
+    head_dim: int = 128
+    ffn: int = 6144
+    eps: float = 1e-6
+    rope_base: float = 1e6
+    codebooks: int = 16
+    vocab: int = 2048
+
+
+@dataclass
+class Layer:
+    """One decoder layer's weights as the reference holds them after load (qwen3.rs:61-119):
+    projection weights f16 bits `[out, in]`, norms f32, qk_norms `[2, hd]` with the q weight
+    already scaled by 1/sqrt(hd) (qwen3.rs:82-87)."""
+    attn_norm: np.ndarray
+    ffn_norm: np.ndarray
+    wqkv: np.ndarray
+    qk_norms: np.ndarray
+    wo: np.ndarray
+    gate: np.ndarray
+    up: np.ndarray
+    down: np.ndarray
+
+
+def decode_step(x: np.ndarray, layers: list[Layer], final_norm: np.ndarray, kcache: list,
+                vcache: list, pos: np.ndarray, cos: np.ndarray, sin: np.ndarray, g: Geometry,
+                round_f16: bool = False) -> np.ndarray:
+    """Stack::forward at t == 1 (crates/qwen3tts/src/qwen3.rs:294-467), composed CPU form
+    (:358-394), with a per-lane position. kcache/vcache: per layer `[b, n_kv, cap, hd]` f16
+    bits, updated in place at each lane's position. Returns the final-normed hidden f32."""
+    b = x.shape[0]
+    gqa = g.heads // g.n_kv
+    h = _c(x).copy()
+    pos = np.asarray(pos, np.int32)
+    lanes = np.arange(b)
+    for li, L in enumerate(layers):
+        normed = rms_norm(h, L.attn_norm, g.eps)
+        qkv = proj(normed, L.wqkv, round_f16)
+        q, k, v = qk_rope(qkv, L.qk_norms, cos, sin, pos, g.heads, g.n_kv, g.eps, g.head_dim)
+        kcache[li][lanes, :, pos, :] = f16_bits(k)
+        vcache[li][lanes, :, pos, :] = f16_bits(v)
+        att = decode_attention(q.reshape(b, g.n_kv, gqa, g.head_dim), kcache[li], vcache[li],
+                               pos + 1, 0)
+        h = h + proj(att.reshape(b, g.heads * g.head_dim), L.wo, round_f16)
+        normed = rms_norm(h, L.ffn_norm, g.eps)
+        tail = swiglu(proj(normed, L.gate, round_f16), proj(normed, L.up, round_f16))
+        h = h + proj(tail, L.down, round_f16)
+    return rms_norm(h, final_norm, g.eps)
+
+
+def heads_pick(hidden: np.ndarray, heads_bits: np.ndarray, g: Geometry):
+    """Codebook heads `[codebooks * vocab, dim]` f16 and the greedy pick per head."""
+    logits = proj(hidden, heads_bits)
+    b = hidden.shape[0]
+    codes = argmax(logits.reshape(b, g.codebooks, g.vocab))
+    return logits, codes
+
+
+def embed_sum(codes: np.ndarray, embed_bits: np.ndarray) -> np.ndarray:
+    """Sum over codebooks of each picked code's embedding row (talker.rs:528-550)."""
+    cb = embed_bits.shape[0]
+    rows = [f16_value(embed_bits[q][codes[:, q]]) for q in range(cb)]
+    out = np.zeros_like(rows[0])
+    for r in rows:
+        out = out + r
+    return out
+
+
+def snake_residual_block(x: np.ndarray, convs, dilations=(1, 3, 9), same: bool = True):
+    """The config's codec residual block, channels-last: for each dilation,
+    x = x + conv_d(snake_d(x)) with k = 7 ("same" padding when `same`, else causal).
+    convs: list of (w_tap [k, c, c], bias [c], alpha [c], brecip [c])."""
+    for (w, bias, alpha, brecip), d in zip(convs, dilations):
+        k = w.shape[0]
+        pad = (k - 1) * d // 2 if same else (k - 1) * d
+        x = conv1d_nlc(x, w, bias, d, pad, snake=(alpha, brecip), res=x)
+    return x

@@ -1,0 +1,171 @@
+"""Per-operator parity on a B200: each C-ABI op against the CPU oracle on the same seeded
+inputs. Shapes follow the reference's own tests (cited per test). Tolerances are stated per
+test; BASELINE's bar for f16 ops is max relative error <= 2e-2."""
+import numpy as np
+import pytest
+import torch
+
+from _model import dev_f16, dev_f32
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    s = np.abs(b).max()
+    return float(np.abs(a - b).max() / s) if s > 0 else float(np.abs(a - b).max())
+
+
+def np_(t):
+    return t.detach().float().cpu().numpy()
+
+
+# crates/tts-nn/src/skinny.rs:181-189 shapes, plus the lane counts of the sweep (1..384)
+SHAPES = [(48, 2048, 4096), (48, 2048, 6144), (48, 6144, 2048), (48, 1024, 3072), (40, 3072, 1024),
+          (32, 1024, 2048), (8, 1024, 4096), (1, 2048, 2048), (128, 2048, 2048), (256, 1024, 1024),
+          (384, 2048, 1024), (17, 512, 384)]
+
+
+@pytest.mark.parametrize("m,k,n", SHAPES)
+def test_proj_f32(tt, orc, m, k, n):
+    rng = np.random.default_rng(m * 7 + k + n)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    w = orc.f16_bits(rng.standard_normal((n, k), dtype=np.float32) * 0.02)
+    want = orc.proj(x, w)
+    got = tt.Proj(dev_f16(w)).forward(dev_f32(x))
+    torch.cuda.synchronize()
+    tt.check()
+    # f16 inputs, f32 accumulation on both sides: only the summation order differs
+    assert rel(np_(got), want) < 1e-4, (m, k, n)
+
+
+def test_proj_epilogues(tt, orc):
+    from ttsnn import _lib as L
+    rng = np.random.default_rng(11)
+    m, k, n = 48, 2048, 1024
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    w = orc.f16_bits(rng.standard_normal((n, k), dtype=np.float32) * 0.02)
+    want = orc.proj(x, w)
+    P = tt.Proj(dev_f16(w))
+    y16 = P.forward(dev_f32(x), L.EPI_F16)
+    assert y16.dtype == torch.float16 and rel(np_(y16), want) < 2e-3
+    h0 = rng.standard_normal((m, n), dtype=np.float32)
+    h = dev_f32(h0)
+    P.forward(dev_f32(x), L.EPI_RESIDUAL_F32, out=h)
+    assert rel(np_(h), h0 + want) < 1e-5
+    # SwiGLU: gate/up interleaved per 128-row tile
+    g = orc.f16_bits(rng.standard_normal((512, k), dtype=np.float32) * 0.02)
+    u = orc.f16_bits(rng.standard_normal((512, k), dtype=np.float32) * 0.02)
+    gu = tt.interleave_gate_up(dev_f16(g), dev_f16(u))
+    act = tt.Proj(gu).forward(dev_f32(x), L.EPI_SWIGLU_F16)
+    want_act = orc.swiglu(orc.proj(x, g), orc.proj(x, u))
+    assert act.shape == (m, 512) and rel(np_(act), want_act) < 2e-3
+    tt.check()
+
+
+def test_proj_declines_unsupported(tt):
+    P = tt.Proj(torch.zeros(100, 64, dtype=torch.float16, device="cuda"))
+    with pytest.raises(tt.TtsError) as e:
+        P.forward(torch.zeros(4, 64, device="cuda"))
+    assert "n must be" in str(e.value)
+
+
+def test_rms_norm(tt, orc):
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((48, 2048), dtype=np.float32)
+    w = rng.uniform(0.5, 1.5, 2048).astype(np.float32)
+    got = tt.rms_norm(dev_f32(x), dev_f32(w), 1e-6)
+    assert rel(np_(got), orc.rms_norm(x, w, 1e-6)) < 1e-6
+
+
+@pytest.mark.parametrize("b,start,off", [(8, 37, 2), (4, 0, 1), (48, 1000, 0)])
+def test_qk_rope_lane_window(tt, orc, b, start, off):
+    # crates/tts-nn/src/qkrope.rs:191-260: a lane window of a larger cache; nothing outside it
+    # is written.
+    heads, n_kv, cap, eps = 16, 8, 1100, 1e-6
+    rng = np.random.default_rng(b + start)
+    cos, sin = orc.rope_table(cap, 128, 1e6)
+    norms = rng.uniform(0.5, 1.5, (2, 128)).astype(np.float32)
+    qkv = rng.standard_normal((b, (heads + 2 * n_kv) * 128), dtype=np.float32)
+    kc = torch.zeros(b + 3, n_kv, cap, 128, dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    q, _ = tt.qkrope.apply(dev_f32(qkv).reshape(b, 1, -1), dev_f32(norms), dev_f32(cos), dev_f32(sin),
+                           kc[off:off + b], vc[off:off + b], heads, start, eps)
+    wq, wk, wv = orc.qk_rope(qkv, norms, cos, sin, np.full(b, start, np.int32), heads, n_kv, eps)
+    assert rel(np_(q).reshape(b, heads, 128), wq) < 1e-5
+    assert rel(np_(kc[off:off + b, :, start]), wk) < 1e-3
+    assert rel(np_(vc[off:off + b, :, start]), wv) < 1e-3
+    outside = kc[:off].abs().sum() + kc[off + b:].abs().sum() + vc[:off].abs().sum() + vc[off + b:].abs().sum()
+    assert outside.item() == 0.0
+    assert kc[off:off + b, :, :start].abs().sum().item() == 0.0
+    tt.check()
+
+
+@pytest.mark.parametrize("b,n_kv,gqa,cap,span,wstart",
+                         [(48, 8, 2, 400, 250, 0), (40, 8, 2, 17, 3, 0), (8, 8, 2, 300, 211, 90),
+                          (4, 8, 1, 64, 33, 0), (6, 8, 2, 2100, 2050, 0)])
+def test_decode_attention_ref_shapes(tt, orc, b, n_kv, gqa, cap, span, wstart):
+    # crates/tts-nn/src/attn.rs:402-433 shapes (+ one multi-chunk span); reference bound 1e-5
+    rng = np.random.default_rng(span)
+    q = rng.standard_normal((b, n_kv, gqa, 128), dtype=np.float32) * 0.1
+    kb = orc.f16_bits(rng.standard_normal((b, n_kv, cap, 128), dtype=np.float32))
+    vb = orc.f16_bits(rng.standard_normal((b, n_kv, cap, 128), dtype=np.float32))
+    want = orc.decode_attention(q, kb, vb, span, wstart)
+    got = tt.attn.decode_attention(dev_f32(q), dev_f16(kb), dev_f16(vb), span, wstart)
+    assert rel(np_(got), want) < 1e-5
+    tt.check()
+
+
+def test_decode_attention_paged_ragged(tt, orc):
+    """Per-lane spans (1..1100) over shuffled pages; one call serves every lane."""
+    from ttsnn import _lib as L
+    lanes, n_kv, gqa, bs = 24, 8, 2, 32
+    rng = np.random.default_rng(5)
+    spans = np.concatenate([[1, 2, 31, 32, 33, 256, 257, 1100], rng.integers(1, 1100, lanes - 8)]).astype(np.int32)
+    cap = 1120
+    per = cap // bs
+    q = rng.standard_normal((lanes, n_kv * gqa, 128), dtype=np.float32) * 0.1
+    kb = orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
+    vb = orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
+    nb = lanes * per + 5
+    order = rng.permutation(nb)
+    table = order[:lanes * per].reshape(lanes, per).astype(np.int32)
+    def pages(c):
+        p = c.reshape(lanes, n_kv, per, bs, 128).transpose(0, 2, 1, 3, 4).reshape(-1, n_kv, bs, 128)
+        host = np.zeros((nb, n_kv, bs, 128), np.uint16)
+        host[table.reshape(-1)] = p
+        return dev_f16(host)
+    kp, vp = pages(kb), pages(vb)
+    tdev = torch.from_numpy(table).cuda()
+    kv = L.KvCache(kp.data_ptr(), vp.data_ptr(), tdev.data_ptr(), per, bs, nb, n_kv, 128)
+    got = tt.attn.decode_attention_paged(dev_f32(q), kv, torch.from_numpy(spans).cuda(), 1100,
+                                         out_f16=False)
+    want = orc.decode_attention(q.reshape(lanes, n_kv, gqa, 128), kb, vb, spans, 0)
+    assert rel(np_(got), want.reshape(lanes, -1)) < 1e-5
+    tt.check()
+
+
+def test_swiglu_snake_argmax(tt, orc):
+    rng = np.random.default_rng(9)
+    g = rng.standard_normal(48 * 6144, dtype=np.float32) * 3
+    u = rng.standard_normal(48 * 6144, dtype=np.float32)
+    assert rel(np_(tt.fused.swiglu_mul(dev_f32(g), dev_f32(u))), orc.swiglu(g, u)) < 1e-6
+    x = rng.standard_normal((4000, 512), dtype=np.float32)
+    a = np.exp(rng.uniform(-1, 1, 512)).astype(np.float32)
+    br = (1.0 / a).astype(np.float32)
+    want = orc.snake_beta(x, a, br)
+    assert rel(np_(tt.fused.snake_beta_nlc(dev_f32(x), dev_f32(a), dev_f32(br))), want) < 1e-6
+    x16 = orc.f16_value(orc.f16_bits(x))
+    got16 = tt.fused.snake_beta_nlc(dev_f32(x16).half(), dev_f32(a), dev_f32(br))
+    assert got16.dtype == torch.float16 and rel(np_(got16), orc.snake_beta(x16, a, br)) < 2e-3
+    logits = np.array([[1.0, 3.0, 3.0, 2.0], [5.0, 1.0, 5.0, 5.0]], np.float32)
+    assert tt.topk.argmax(dev_f32(logits)).tolist() == [2, 3]
+    banned = torch.tensor([0, 0, 1, 1], dtype=torch.uint8, device="cuda")
+    assert tt.topk.argmax(dev_f32(logits), banned).tolist() == [1, 0]
+    big = rng.standard_normal((48, 3072), dtype=np.float32)
+    mask = np.zeros(3072, np.uint8)
+    mask[2048:] = 1
+    mask[2150] = 0
+    assert np.array_equal(tt.topk.argmax(dev_f32(big), torch.from_numpy(mask).cuda()).cpu().numpy(),
+                          orc.argmax(big, mask).astype(np.int32))

@@ -1,0 +1,217 @@
+"""The CPU oracle against independent PyTorch-CPU formulas of the same ops, and against the
+structural identities the reference's own tests assert. No GPU."""
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    s = np.abs(b).max()
+    return float(np.abs(a - b).max() / s) if s > 0 else float(np.abs(a - b).max())
+
+
+def test_f16_roundtrip(orc):
+    x = np.array([0.0, 1.0, -2.5, 65504.0, 1e-8, 3.14159], np.float32)
+    bits = orc.f16_bits(x)
+    assert np.array_equal(bits, torch.from_numpy(x).to(torch.float16).view(torch.int16).numpy().view(np.uint16))
+
+
+@pytest.mark.parametrize("m,k,n", [(48, 2048, 6144), (40, 3072, 1024), (8, 1024, 4096), (1, 128, 256)])
+def test_proj_vs_torch(orc, m, k, n):
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    w = orc.f16_bits(rng.standard_normal((n, k), dtype=np.float32) * 0.02)
+    got = orc.proj(x, w)
+    xt = torch.from_numpy(orc.f16_value(orc.f16_bits(x))).double()
+    wt = torch.from_numpy(orc.f16_value(w)).double()
+    want = (xt @ wt.T).numpy()
+    assert rel(got, want) < 1e-5
+    # the CPU arm rounds the product to f16 (crates/tts-nn/src/lib.rs:528): within f16 resolution
+    assert rel(orc.proj(x, w, round_f16=True), want) < 2e-3
+
+
+def test_rms_norm_vs_torch(orc):
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((48, 2048), dtype=np.float32)
+    w = rng.uniform(0.5, 1.5, 2048).astype(np.float32)
+    got = orc.rms_norm(x, w, 1e-6)
+    want = F.rms_norm(torch.from_numpy(x).double(), (2048,), torch.from_numpy(w).double(), 1e-6)
+    assert rel(got, want.numpy()) < 1e-6
+
+
+def test_rope_table_f64(orc):
+    c, s = orc.rope_table(1024, 128, 1e6)
+    i = np.arange(64, dtype=np.float64)
+    freq = 1.0 / np.power(1e6, 2.0 * i / 128)
+    ph = np.arange(1024, dtype=np.float64)[:, None] * freq[None]
+    assert np.array_equal(c, np.cos(ph).astype(np.float32))
+    assert np.array_equal(s, np.sin(ph).astype(np.float32))
+
+
+def rotate_half_rope(x, cos, sin):
+    x1, x2 = x[..., :64], x[..., 64:]
+    c = torch.cat([cos, cos], -1)
+    s = torch.cat([sin, sin], -1)
+    return x * c + torch.cat([-x2, x1], -1) * s
+
+
+def test_qk_rope_vs_torch(orc):
+    rng = np.random.default_rng(2)
+    b, heads, n_kv = 8, 16, 8
+    qkv = rng.standard_normal((b, (heads + 2 * n_kv) * 128), dtype=np.float32)
+    norms = rng.uniform(0.5, 1.5, (2, 128)).astype(np.float32)
+    cos, sin = orc.rope_table(1100, 128, 1e6)
+    pos = rng.integers(0, 1024, b).astype(np.int32)
+    q, k, v = orc.qk_rope(qkv, norms, cos, sin, pos, heads, n_kv, 1e-6)
+    t = torch.from_numpy(qkv).double().reshape(b, heads + 2 * n_kv, 128)
+    c = torch.from_numpy(cos[pos]).double()[:, None]
+    s = torch.from_numpy(sin[pos]).double()[:, None]
+    qn = F.rms_norm(t[:, :heads], (128,), torch.from_numpy(norms[0]).double(), 1e-6)
+    kn = F.rms_norm(t[:, heads:heads + n_kv], (128,), torch.from_numpy(norms[1]).double(), 1e-6)
+    assert rel(q, rotate_half_rope(qn, c, s).numpy()) < 1e-5
+    assert rel(k, rotate_half_rope(kn, c, s).numpy()) < 1e-5
+    assert np.array_equal(v, qkv.reshape(b, -1, 128)[:, heads + n_kv:])
+
+
+@pytest.mark.parametrize("b,n_kv,gqa,cap,span,wstart",
+                         [(48, 8, 2, 400, 250, 0), (40, 8, 2, 17, 3, 0), (8, 8, 2, 300, 211, 90),
+                          (4, 8, 1, 64, 33, 0)])
+def test_decode_attention_vs_sdpa(orc, b, n_kv, gqa, cap, span, wstart):
+    # the reference's own attention test shapes (crates/tts-nn/src/attn.rs:408-413)
+    rng = np.random.default_rng(3)
+    q = (rng.standard_normal((b, n_kv, gqa, 128), dtype=np.float32) * 0.1)
+    kb = orc.f16_bits(rng.standard_normal((b, n_kv, cap, 128), dtype=np.float32))
+    vb = orc.f16_bits(rng.standard_normal((b, n_kv, cap, 128), dtype=np.float32))
+    got = orc.decode_attention(q, kb, vb, span, wstart)
+    K = torch.from_numpy(orc.f16_value(kb)).double()[:, :, wstart:span]
+    V = torch.from_numpy(orc.f16_value(vb)).double()[:, :, wstart:span]
+    Q = torch.from_numpy(q).double()
+    want = F.scaled_dot_product_attention(Q, K, V, scale=1.0)
+    assert rel(got, want.numpy()) < 1e-5
+
+
+def test_swiglu_and_snake_vs_torch(orc):
+    rng = np.random.default_rng(4)
+    g = rng.standard_normal(10000, dtype=np.float32) * 3
+    u = rng.standard_normal(10000, dtype=np.float32)
+    assert rel(orc.swiglu(g, u), (F.silu(torch.from_numpy(g).double()) * torch.from_numpy(u).double()).numpy()) < 1e-6
+    x = rng.standard_normal((300, 96), dtype=np.float32)
+    a = np.exp(rng.uniform(-1, 1, 96)).astype(np.float32)
+    br = (1.0 / a).astype(np.float32)
+    xt = torch.from_numpy(x).double()
+    want = xt + torch.from_numpy(br).double() * torch.sin(torch.from_numpy(a).double() * xt) ** 2
+    assert rel(orc.snake_beta(x, a, br), want.numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("cin,cout,length,k,dil,same", [(8, 12, 40, 7, 1, False), (16, 16, 33, 7, 3, False),
+                                                        (6, 9, 20, 1, 1, False), (16, 16, 50, 7, 9, True),
+                                                        (32, 24, 64, 7, 3, True)])
+def test_conv_vs_torch(orc, cin, cout, length, k, dil, same):
+    # channels-last vs channel-major (crates/tts-nn/src/nlc.rs:293-330)
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((2, cin, length), dtype=np.float32)
+    w = (rng.standard_normal((cout, cin, k), dtype=np.float32) * 0.1)
+    bias = (rng.standard_normal(cout, dtype=np.float32) * 0.1)
+    pad = (k - 1) * dil // 2 if same else (k - 1) * dil
+    xt = torch.from_numpy(x).double()
+    xp = F.pad(xt, (pad, (k - 1) * dil - pad))
+    want = F.conv1d(xp, torch.from_numpy(w).double(), torch.from_numpy(bias).double(), dilation=dil)
+    got = orc.conv1d_nlc(np.ascontiguousarray(x.transpose(0, 2, 1)), np.ascontiguousarray(w.transpose(2, 1, 0)),
+                         bias, dil, pad)
+    assert rel(got.transpose(0, 2, 1), want.numpy()) < 1e-5
+
+
+def test_snake_conv_residual_vs_composed(orc):
+    # crates/tts-nn/src/nlc.rs:263-288: fused snake-conv-residual == snake -> conv -> + res
+    rng = np.random.default_rng(6)
+    x = rng.standard_normal((1, 500, 32), dtype=np.float32)
+    res = rng.standard_normal((1, 500, 32), dtype=np.float32)
+    w = (rng.standard_normal((7, 32, 32), dtype=np.float32) / np.sqrt(7 * 32)).astype(np.float32)
+    b = (rng.standard_normal(32, dtype=np.float32) * 0.1)
+    a = rng.uniform(0.5, 2.0, 32).astype(np.float32)
+    br = rng.uniform(0.2, 1.5, 32).astype(np.float32)
+    got = orc.conv1d_nlc(x, w, b, 3, None, snake=(a, br), res=res)
+    want = orc.conv1d_nlc(orc.snake_beta(x, a, br), w, b, 3) + res
+    assert rel(got, want) < 1e-6
+
+
+@pytest.mark.parametrize("cin,cout,length,stride,mult", [(8, 6, 12, 2, 1), (8, 6, 12, 2, 2), (12, 8, 9, 5, 2),
+                                                         (10, 7, 11, 3, 2), (9, 5, 7, 4, 1)])
+def test_transposed_conv_is_reversed_tap_causal_conv(orc, cin, cout, length, stride, mult):
+    # crates/tts-nn/src/nlc.rs:164-174 and its test at :331-364: a transposed conv with
+    # kernel m*stride equals a causal conv over m reversed tap groups, phases interleaved.
+    import sys, os
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(__file__)), "dream-tts_b200"))
+    from ttsnn import nlc
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((1, cin, length), dtype=np.float32)
+    w = rng.standard_normal((cin, cout, mult * stride), dtype=np.float32) * 0.1
+    bias = rng.standard_normal(cout, dtype=np.float32) * 0.1
+    full = F.conv_transpose1d(torch.from_numpy(x).double(), torch.from_numpy(w).double(),
+                              torch.from_numpy(bias).double(), stride=stride)
+    want = full[..., :length * stride]  # causal: drop the trailing k - stride
+    tap = nlc.transpose_tap_weight(torch.from_numpy(w), stride).numpy()
+    tb = nlc.transpose_bias(torch.from_numpy(bias), stride).numpy()
+    y = orc.conv1d_nlc(np.ascontiguousarray(x.transpose(0, 2, 1)), tap, tb, 1)
+    got = y.reshape(1, length * stride, cout).transpose(0, 2, 1)
+    assert rel(got, want.numpy()) < 1e-5
+
+
+def test_argmax_ties_and_banned(orc):
+    logits = np.array([[1.0, 3.0, 3.0, 2.0], [5.0, 1.0, 5.0, 5.0]], np.float32)
+    assert orc.argmax(logits).tolist() == [2, 3]  # last of equal maxima (Rust max_by)
+    banned = np.array([0, 0, 1, 1], np.uint8)
+    assert orc.argmax(logits, banned).tolist() == [1, 0]
+
+
+def test_decode_step_vs_torch(orc):
+    """A 2-layer Qwen3 decode step against a float64 PyTorch re-derivation."""
+    from _model import make_talker
+    g, layers, final, kc, vc, pos, x = make_talker(orc, lanes=4, layers=2, dim=256, heads=4,
+                                                   n_kv=2, ffn=512, cap=40, seed=8)
+    cos, sin = orc.rope_table(64, 128, g.rope_base)
+    kc2 = [a.copy() for a in kc]
+    vc2 = [a.copy() for a in vc]
+    got = orc.decode_step(x, layers, final, kc, vc, pos, cos, sin, g)
+    want = torch_decode_step(orc, x, layers, final, kc2, vc2, pos, cos, sin, g)
+    assert rel(got, want) < 1e-4
+    # the caches agree (f16 of an f32 vs of an f64 value can differ by one ulp)
+    for li in range(2):
+        for a, b in ((kc[li], kc2[li]), (vc[li], vc2[li])):
+            assert rel(orc.f16_value(a), orc.f16_value(b)) < 2e-3
+
+
+def torch_decode_step(orc, x, layers, final, kc, vc, pos, cos, sin, g):
+    T = lambda a: torch.from_numpy(np.asarray(a)).double()
+    W = lambda bits: T(orc.f16_value(bits))
+    f16 = lambda t: t.float().half().double()
+    b = x.shape[0]
+    h = T(x)
+    gqa = g.heads // g.n_kv
+    for li, L in enumerate(layers):
+        xn = F.rms_norm(h, (g.dim,), T(L.attn_norm), g.eps)
+        qkv = f16(xn) @ W(L.wqkv).T
+        t = qkv.reshape(b, -1, 128)
+        c = T(cos[pos])[:, None]
+        s = T(sin[pos])[:, None]
+        q = rotate_half_rope(F.rms_norm(t[:, :g.heads], (128,), T(L.qk_norms[0]), g.eps), c, s)
+        k = rotate_half_rope(F.rms_norm(t[:, g.heads:g.heads + g.n_kv], (128,), T(L.qk_norms[1]), g.eps), c, s)
+        v = t[:, g.heads + g.n_kv:]
+        out = torch.zeros(b, g.heads * 128, dtype=torch.float64)
+        for i in range(b):
+            kc[li][i, :, pos[i]] = orc.f16_bits(k[i].numpy())
+            vc[li][i, :, pos[i]] = orc.f16_bits(v[i].numpy())
+            K = W(kc[li][i, :, :pos[i] + 1])
+            V = W(vc[li][i, :, :pos[i] + 1])
+            Q = q[i].reshape(g.n_kv, gqa, 128)
+            o = F.scaled_dot_product_attention(Q, K, V, scale=1.0)
+            out[i] = o.reshape(-1)
+        h = h + f16(out) @ W(L.wo).T
+        xn = F.rms_norm(h, (g.dim,), T(L.ffn_norm), g.eps)
+        gate = f16(xn) @ W(L.gate).T
+        up = f16(xn) @ W(L.up).T
+        h = h + f16(F.silu(gate) * up) @ W(L.down).T
+    return F.rms_norm(h, (g.dim,), T(final), g.eps).numpy()
