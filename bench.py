@@ -1,0 +1,372 @@
+"""Benchmark: qwen3tts talker decode on B200 — codec frames/s at 48 lanes.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+One step = one talker decode step for 48 lanes: 28 Qwen3 layers (dim 2048, 16/8 heads,
+head_dim 128, SwiGLU 6144, f16 weights ~N(0, 0.02), RMSNorm, RoPE theta 1e6, paged KV with
+lane lengths ~U[64, 1024]), the final norm, 16 codebook heads x 2048 with a greedy pick, and the
+next input as the sum of the picked codes' embedding rows. Every lane emits one 12.5 Hz codec
+frame per step, so frames/s = lanes x steps/s. The step runs as one captured CUDA graph.
+
+Under torchrun each rank drives its own GPU with its own 48 lanes (data parallel, weights
+replicated, no collective on the data path): `value` is frames/s over all ranks, timed on the
+device as the max over ranks. `--impl reference` times the CPU restatement of the reference's
+CPU path (oracle/, the only runnable form of the reference here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "dream-tts_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "codec frames/sec (48-lane decode, whole box)"
+UNIT = "frames/s"
+LANES, LAYERS, DIM, HEADS, N_KV, HD, FFN, CB, VOCAB = 48, 28, 2048, 16, 8, 128, 6144, 16, 2048
+BLOCK = 32
+KV_LO, KV_HI = 64, 1024
+WORKLOAD = ("config[2]: full talker decode step, 28 layers, hidden 2048, 16q/8kv heads x 128, "
+            "SwiGLU 6144, f16 weights N(0,0.02), 16 codebook heads x 2048, greedy; 48 lanes, "
+            "KV lengths U[64,1024] seed 0, paged (32-position pages)")
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def kv_lengths(seed=0):
+    return np.random.default_rng(seed).integers(KV_LO, KV_HI + 1, LANES).astype(np.int32)
+
+
+# ---------------------------------------------------------------- reference (CPU) arm
+def cpu_sample(layers_sample=4, threads=None, seed=0, reps=1):
+    """The oracle's decode step on `layers_sample` of the 28 layers at 48 lanes with the
+    workload's KV lengths, plus the heads and greedy pick; returns seconds per full step
+    (layer time scaled to 28 layers) and the sample description."""
+    import oracle as orc
+    if threads:
+        orc.set_threads(threads)
+    rng = np.random.default_rng(seed)
+    g = orc.Geometry(layers=layers_sample)
+    lengths = kv_lengths(seed)
+    cap = int(lengths.max()) + 2
+    from tests._model import make_layer  # seeded synthetic weights, same distributions
+    Ls = [make_layer(orc, rng, g) for _ in range(layers_sample)]
+    final = np.ones(DIM, np.float32)
+    kc = [orc.f16_bits(rng.standard_normal((LANES, N_KV, cap, HD), dtype=np.float32)) for _ in range(layers_sample)]
+    vc = [orc.f16_bits(rng.standard_normal((LANES, N_KV, cap, HD), dtype=np.float32)) for _ in range(layers_sample)]
+    heads = orc.f16_bits(rng.standard_normal((CB * VOCAB, DIM), dtype=np.float32) * 0.02)
+    x = rng.standard_normal((LANES, DIM), dtype=np.float32)
+    cos, sin = orc.rope_table(cap + 64, HD, 1e6)
+    best_layers, best_heads = float("inf"), float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        h = orc.decode_step(x, Ls, final, kc, vc, lengths, cos, sin, g)
+        t1 = time.perf_counter()
+        orc.heads_pick(h, heads, orc.Geometry())
+        t2 = time.perf_counter()
+        best_layers = min(best_layers, t1 - t0)
+        best_heads = min(best_heads, t2 - t1)
+    per_step = best_layers * (LAYERS / layers_sample) + best_heads
+    sample = (f"{layers_sample} of 28 layers + heads at 48 lanes, KV lengths U[64,1024]; layer time "
+              f"scaled x{LAYERS / layers_sample:g} to a full step")
+    return per_step, sample, orc.threads()
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    cores = os.cpu_count() or 1
+    per_steps = []
+    sample = ""
+    for _ in range(args.warmup):
+        cpu_sample(threads=cores)
+    for _ in range(args.steps):
+        t, sample, used = cpu_sample(threads=cores)
+        per_steps.append(t)
+    sec = statistics.median(per_steps)
+    value = LANES / sec
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "parallelism": "host cores"},
+            "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": used, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- B200 arm
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index, path):
+        self.path = path
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [c.strip() for c in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def build_device_talker(device, seed=0, extra_positions=256):
+    import torch
+    import ttsnn
+    from qwen3tts import Geometry, LayerTensors, PagedKv, Stack
+    gen = torch.Generator(device=device).manual_seed(seed)
+
+    def w(n, k):
+        return (torch.randn(n, k, generator=gen, device=device) * 0.02).half()
+
+    geo = Geometry(dim=DIM, layers=LAYERS, heads=HEADS, n_kv=N_KV, head_dim=HD, ffn=FFN,
+                   rope_len=KV_HI + extra_positions + 64, codebooks=CB, vocab=VOCAB)
+    ones = torch.ones(DIM, device=device)
+    qk = torch.stack([torch.full((HD,), 1.0 / HD ** 0.5, device=device), torch.ones(HD, device=device)])
+    layers = []
+    for _ in range(LAYERS):
+        layers.append(LayerTensors(ones, ones, w((HEADS + 2 * N_KV) * HD, DIM), qk.contiguous(),
+                                   w(DIM, HEADS * HD), ttsnn.interleave_gate_up(w(FFN, DIM), w(FFN, DIM)),
+                                   w(DIM, FFN)))
+    heads = w(CB * VOCAB, DIM)
+    embed = (torch.randn(CB, VOCAB, DIM, generator=gen, device=device) * 0.02).half()
+    stack = Stack(geo, layers, ones, heads, embed)
+    lengths = kv_lengths(seed)
+    cap = KV_HI + extra_positions
+    per_lane = -(-cap // BLOCK)
+    kv = PagedKv(geo, LANES, LANES * per_lane, BLOCK, per_lane, device)
+    for i in range(LANES):
+        kv.admit(i, cap, int(lengths[i]))
+    for li in range(LAYERS):
+        kv.k[li].normal_(generator=gen)
+        kv.v[li].normal_(generator=gen)
+    return stack, kv, lengths, cap
+
+
+def time_dominant_gemm(stack, device, reps=3):
+    """The gate/up GEMM (SwiGLU epilogue) alone, over the 28 layers' weights in turn (1.4 GB, so
+    nothing is served from L2): CUDA-event time per launch on the launching stream."""
+    import torch
+    import ttsnn
+    from ttsnn import _lib as L
+    x = torch.randn(LANES, DIM, device=device)
+    projs = [ttsnn.Proj(lt.w_gate_up) for lt in stack.layers]
+    out = torch.empty(LANES, FFN, device=device, dtype=torch.float16)
+    for p in projs:
+        p.forward(x, L.EPI_SWIGLU_F16, out=out)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x16 = x.half()
+    e0.record(s)
+    for _ in range(reps):
+        for p in projs:
+            L.call("tts_proj_forward", ttsnn.ctx(), ttsnn.ptr(x16), LANES, DIM, ttsnn.ptr(p.w),
+                   2 * FFN, L.EPI_SWIGLU_F16, ttsnn.ptr(out), 0, ttsnn.stream())
+    e1.record(s)
+    torch.cuda.synchronize()
+    per = e0.elapsed_time(e1) / (reps * len(projs)) * 1e-3
+    bytes_ = 2 * FFN * DIM * 2 + LANES * DIM * 2 + LANES * FFN * 2
+    return per, bytes_
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
+    import ttsnn
+    from ttsnn import _lib as L
+
+    steps, warmup = args.steps, args.warmup
+    stack, kv, lengths, cap = build_device_talker(device, seed=rank, extra_positions=2 * (steps + warmup) + 16)
+    stream = torch.cuda.Stream(device)
+    codes = torch.zeros(LANES, CB, dtype=torch.int32, device=device)
+    x_dev = torch.empty(LANES, DIM, device=device)
+    x_host = torch.randn(LANES, DIM).pin_memory()
+    codes_host = torch.empty(LANES, CB, dtype=torch.int32).pin_memory()
+    max_span = cap
+    with torch.cuda.stream(stream):
+        x_dev.copy_(x_host, non_blocking=True)
+        stack.decode_step(kv, x_dev, codes=codes, max_span=max_span)  # seeds the embedding input
+        graph = stack.capture(kv, None, codes=codes, max_span=max_span)
+        graph_e2e = stack.capture(kv, x_dev, codes=codes, max_span=max_span)
+    stream.synchronize()
+    ttsnn.check(local)
+    pos0 = kv.positions.clone()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-resident timing (graph replays, inputs already in HBM)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            graph.replay()
+    stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local, os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
+                    if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/clocks_rank{rank}.csv")
+    ttsnn.launch_count(reset=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    stream.synchronize()
+    launches = ttsnn.launch_count()
+    clk = clocks.stop()
+    barrier()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ttsnn.check(local)
+
+    # ---- end to end through the public API: pinned host input in, codes out, every step
+    barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            x_dev.copy_(x_host, non_blocking=True)
+            graph_e2e.replay()
+            codes_host.copy_(codes, non_blocking=True)
+            stream.synchronize()
+        e2.record(stream)
+        for _ in range(steps):
+            x_dev.copy_(x_host, non_blocking=True)
+            graph_e2e.replay()
+            codes_host.copy_(codes, non_blocking=True)
+            stream.synchronize()  # the host reads the codes before the next step, as the engine does
+        e3.record(stream)
+    stream.synchronize()
+    t2 = torch.tensor([e2.elapsed_time(e3)], device=device)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t2.item())
+    ttsnn.check(local)
+
+    # ---- roofline of the dominant kernel and of the whole step
+    hbm, peak_kind = peaks()
+    gemm_s, gemm_bytes = time_dominant_gemm(stack, device)
+    weights = stack.weight_bytes()
+    mean_len = float(lengths.mean()) + warmup + steps / 2.0 + 1
+    kv_bytes = LAYERS * N_KV * HD * 2 * 2 * LANES * mean_len
+    step_bytes = weights + kv_bytes + CB * LANES * DIM * 2
+    step_s = ms_max / steps * 1e-3
+
+    if rank == 0:
+        value = world * LANES * steps / (ms_max * 1e-3)
+        e2e_value = world * LANES * steps / (e2e_ms * 1e-3)
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            cpu_t, sample, used = cpu_sample(threads=os.cpu_count())
+            cpu = {"value": round(LANES / cpu_t, 3), "unit": UNIT, "cores": used, "kind": "port",
+                   "sample": sample}
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": steps, "warmup": warmup, "ms_per_step": round(ms_max / steps, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "lanes_per_gpu": LANES, "global_lanes": LANES * world,
+                       "parallelism": f"dp{world} (replicated weights, lanes sharded per GPU)",
+                       "l2": "inputs larger than L2: each step streams 2.95 GB of weights and ~3 GB of KV"},
+            "roofline": {"bound": "hbm", "kernel": "gemm_decode (gate/up, SwiGLU epilogue)",
+                         "achieved": round(gemm_bytes / gemm_s / 1e9, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(gemm_bytes / gemm_s / 1e9 / hbm, 4),
+                         "traffic": None, "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": gemm_bytes,
+                         "launch_us": round(gemm_s * 1e6, 2)},
+            "roofline_step": {"bound": "hbm", "achieved": round(step_bytes / step_s / 1e9, 1),
+                              "peak": hbm, "unit": "GB/s",
+                              "frac": round(step_bytes / step_s / 1e9 / hbm, 4),
+                              "algorithmic_bytes_per_step": int(step_bytes)},
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": LANES * DIM * 4, "d2h_bytes_per_step": LANES * CB * 4},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    del graph, graph_e2e
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
