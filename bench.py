@@ -58,38 +58,44 @@ def kv_lengths(seed=0):
 
 
 # ---------------------------------------------------------------- reference (CPU) arm
-def cpu_sample(layers_sample=4, threads=None, seed=0, reps=1):
+class CpuSample:
     """The oracle's decode step on `layers_sample` of the 28 layers at 48 lanes with the
-    workload's KV lengths, plus the heads and greedy pick; returns seconds per full step
-    (layer time scaled to 28 layers) and the sample description."""
-    import oracle as orc
-    if threads:
-        orc.set_threads(threads)
-    rng = np.random.default_rng(seed)
-    g = orc.Geometry(layers=layers_sample)
-    lengths = kv_lengths(seed)
-    cap = int(lengths.max()) + 2
-    from tests._model import make_layer  # seeded synthetic weights, same distributions
-    Ls = [make_layer(orc, rng, g) for _ in range(layers_sample)]
-    final = np.ones(DIM, np.float32)
-    kc = [orc.f16_bits(rng.standard_normal((LANES, N_KV, cap, HD), dtype=np.float32)) for _ in range(layers_sample)]
-    vc = [orc.f16_bits(rng.standard_normal((LANES, N_KV, cap, HD), dtype=np.float32)) for _ in range(layers_sample)]
-    heads = orc.f16_bits(rng.standard_normal((CB * VOCAB, DIM), dtype=np.float32) * 0.02)
-    x = rng.standard_normal((LANES, DIM), dtype=np.float32)
-    cos, sin = orc.rope_table(cap + 64, HD, 1e6)
-    best_layers, best_heads = float("inf"), float("inf")
-    for _ in range(reps):
+    workload's KV lengths, plus the heads and the greedy pick. `time()` returns seconds per full
+    step: the layer time scaled to 28 layers, plus the heads."""
+
+    def __init__(self, layers_sample=4, threads=None, seed=0):
+        import oracle as orc
+        self.orc = orc
+        if threads:
+            orc.set_threads(threads)
+        rng = np.random.default_rng(seed)
+        self.layers_sample = layers_sample
+        self.g = orc.Geometry(layers=layers_sample)
+        self.lengths = kv_lengths(seed)
+        cap = int(self.lengths.max()) + 2
+        self.layers = [orc.synthetic_layer(rng, self.g) for _ in range(layers_sample)]
+        self.final = np.ones(DIM, np.float32)
+        shape = (LANES, N_KV, cap, HD)
+        self.kc = [orc.f16_bits(rng.standard_normal(shape, dtype=np.float32)) for _ in range(layers_sample)]
+        self.vc = [orc.f16_bits(rng.standard_normal(shape, dtype=np.float32)) for _ in range(layers_sample)]
+        self.heads = orc.f16_bits(rng.standard_normal((CB * VOCAB, DIM), dtype=np.float32) * 0.02)
+        self.x = rng.standard_normal((LANES, DIM), dtype=np.float32)
+        self.cos, self.sin = orc.rope_table(cap + 64, HD, 1e6)
+        self.sample = (f"{layers_sample} of 28 layers + heads at 48 lanes, KV lengths U[64,1024]; "
+                       f"layer time scaled x{LAYERS / layers_sample:g} to a full step")
+
+    def threads(self):
+        return self.orc.threads()
+
+    def time(self):
+        orc = self.orc
         t0 = time.perf_counter()
-        h = orc.decode_step(x, Ls, final, kc, vc, lengths, cos, sin, g)
+        h = orc.decode_step(self.x, self.layers, self.final, self.kc, self.vc, self.lengths,
+                            self.cos, self.sin, self.g)
         t1 = time.perf_counter()
-        orc.heads_pick(h, heads, orc.Geometry())
+        orc.heads_pick(h, self.heads, orc.Geometry())
         t2 = time.perf_counter()
-        best_layers = min(best_layers, t1 - t0)
-        best_heads = min(best_heads, t2 - t1)
-    per_step = best_layers * (LAYERS / layers_sample) + best_heads
-    sample = (f"{layers_sample} of 28 layers + heads at 48 lanes, KV lengths U[64,1024]; layer time "
-              f"scaled x{LAYERS / layers_sample:g} to a full step")
-    return per_step, sample, orc.threads()
+        return (t1 - t0) * (LAYERS / self.layers_sample) + (t2 - t1)
 
 
 def run_reference(args):
@@ -97,14 +103,12 @@ def run_reference(args):
     if rank != 0:
         return 0
     cores = os.cpu_count() or 1
-    per_steps = []
-    sample = ""
-    for _ in range(args.warmup):
-        cpu_sample(threads=cores)
-    for _ in range(args.steps):
-        t, sample, used = cpu_sample(threads=cores)
-        per_steps.append(t)
+    cs = CpuSample(threads=cores)
+    for _ in range(min(args.warmup, 1)):
+        cs.time()
+    per_steps = [cs.time() for _ in range(args.steps)]
     sec = statistics.median(per_steps)
+    sample, used = cs.sample, cs.threads()
     value = LANES / sec
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -219,6 +223,101 @@ def time_dominant_gemm(stack, device, reps=3):
     return per, bytes_
 
 
+def bf16_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def build_codec_block(device, b=8, t=24000, c=512, seed=0):
+    """BASELINE config[1]: x [8, 512, 24000] f16 ~N(0,1) held channels-last [8, 24000, 512];
+    per dilation 1, 3, 9: x = x + conv_k7(snake(x)) with 'same' padding, alpha = exp(U(-1,1)),
+    Snake's 1/alpha, weights ~N(0, 0.02), bias 0."""
+    import torch
+    import ttsnn
+    gen = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(b, t, c, generator=gen, device=device).half()
+    convs = []
+    for d in (1, 3, 9):
+        w_tap = torch.randn(7, c, c, generator=gen, device=device) * 0.02
+        alpha = torch.exp(torch.rand(c, generator=gen, device=device) * 2 - 1)
+        convs.append((ttsnn.nlc.device_weight(w_tap), torch.zeros(c, device=device), alpha,
+                      1.0 / alpha, d))
+    return x, convs
+
+
+def codec_block(x, convs, bufs):
+    import ttsnn
+    cur = x
+    for i, (w, bias, alpha, brecip, d) in enumerate(convs):
+        out = bufs[i % 2]
+        ttsnn.nlc.conv1d(cur, w, bias, d, 3 * d, snake=(alpha, brecip), res=cur, out=out)
+        cur = out
+    return cur
+
+
+def time_codec_block(device, reps=5):
+    import torch
+    x, convs = build_codec_block(device)
+    bufs = [torch.empty_like(x), torch.empty_like(x)]
+    codec_block(x, convs, bufs)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(reps):
+        codec_block(x, convs, bufs)
+    e1.record(s)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) * 1e-3 / reps
+    b, t, c = x.shape
+    flops = 3 * 2 * b * t * c * c * 7
+    return sec, flops
+
+
+def run_kernel_case(args):
+    """Small standalone cases of one kernel, for ncu captures (a few launches, < 1 GB)."""
+    import torch
+    import ttsnn
+    from ttsnn import _lib as L
+    device = torch.device("cuda", 0)
+    if args.kernel == "gemm":
+        gen = torch.Generator(device=device).manual_seed(0)
+        ws = [ttsnn.interleave_gate_up((torch.randn(FFN, DIM, generator=gen, device=device) * 0.02).half(),
+                                       (torch.randn(FFN, DIM, generator=gen, device=device) * 0.02).half())
+              for _ in range(4)]
+        x = torch.randn(LANES, DIM, device=device)
+        out = torch.empty(LANES, FFN, device=device, dtype=torch.float16)
+        for i in range(8):
+            ttsnn.Proj(ws[i % 4]).forward(x, L.EPI_SWIGLU_F16, out=out)
+    elif args.kernel == "attn":
+        from qwen3tts import Geometry, PagedKv
+        geo = Geometry(layers=1)
+        lengths = kv_lengths(0)
+        per = -(-KV_HI // BLOCK) + 1
+        kv = PagedKv(geo, LANES, LANES * per, BLOCK, per, device)
+        for i in range(LANES):
+            kv.admit(i, per * BLOCK, int(lengths[i]))
+        kv.k.normal_()
+        kv.v.normal_()
+        q = torch.randn(LANES, HEADS, HD, device=device) * 0.1
+        st = L.KvCache(kv.k.data_ptr(), kv.v.data_ptr(), kv.table.data_ptr(), per, BLOCK,
+                       kv.num_blocks, N_KV, HD)
+        for _ in range(4):
+            ttsnn.attn.decode_attention_paged(q, st, kv.positions, per * BLOCK)
+    elif args.kernel == "conv":
+        x, convs = build_codec_block(device)
+        bufs = [torch.empty_like(x), torch.empty_like(x)]
+        codec_block(x, convs, bufs)
+    torch.cuda.synchronize()
+    ttsnn.check(0)
+    print(json.dumps({"kernel_case": args.kernel, "ok": True}))
+    return 0
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -312,14 +411,19 @@ def run_b200(args):
     step_bytes = weights + kv_bytes + CB * LANES * DIM * 2
     step_s = ms_max / steps * 1e-3
 
+    codec_s, codec_flops = time_codec_block(device)
+    tpeak, tpeak_kind = bf16_peak()
+
     if rank == 0:
         value = world * LANES * steps / (ms_max * 1e-3)
         e2e_value = world * LANES * steps / (e2e_ms * 1e-3)
         cpu = None
         if world == 1 and not args.no_cpu:
-            cpu_t, sample, used = cpu_sample(threads=os.cpu_count())
-            cpu = {"value": round(LANES / cpu_t, 3), "unit": UNIT, "cores": used, "kind": "port",
-                   "sample": sample}
+            cs = CpuSample(threads=os.cpu_count())
+            cs.time()
+            cpu_t = statistics.median([cs.time() for _ in range(3)])
+            cpu = {"value": round(LANES / cpu_t, 3), "unit": UNIT, "cores": cs.threads(),
+                   "kind": "port", "sample": cs.sample}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
             "steps": steps, "warmup": warmup, "ms_per_step": round(ms_max / steps, 4),
@@ -340,6 +444,13 @@ def run_b200(args):
                               "algorithmic_bytes_per_step": int(step_bytes)},
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                     "h2d_bytes_per_step": LANES * DIM * 4, "d2h_bytes_per_step": LANES * CB * 4},
+            "codec_block": {"workload": "config[1]: [8,512,24000] f16, snake + 3 x conv 512->512 k7 "
+                                        "d1/3/9 'same' + residual, implicit GEMM on tcgen05",
+                            "ms": round(codec_s * 1e3, 3), "bound": "tensor",
+                            "achieved": round(codec_flops / codec_s / 1e12, 1), "unit": "TFLOP/s",
+                            "peak": tpeak, "frac": round(codec_flops / codec_s / 1e12 / tpeak, 4),
+                            "peak_source": tpeak_kind + " dense bf16 (f16 runs at the same rate)",
+                            "flops_per_block": codec_flops},
             "gpu_launches": int(launches),
             "clocks": clk,
         }
@@ -360,11 +471,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--kernel", choices=["gemm", "attn", "conv"],
+                    help="run a small standalone case of one kernel (for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.kernel:
+        return run_kernel_case(args)
     return run_b200(args)
 
 

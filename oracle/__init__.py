@@ -208,6 +208,24 @@ class Layer:
     down: np.ndarray
 
 
+def synthetic_layer(rng: np.random.Generator, g: Geometry) -> Layer:
+    """Seeded random-init layer with the distributions BASELINE's configs name: projections
+    ~N(0, 0.02) as f16, norm weights near 1, 1/sqrt(head_dim) folded into the q norm."""
+    dim, hd = g.dim, g.head_dim
+    nq = (g.heads + 2 * g.n_kv) * hd
+
+    def w(n, k):
+        return f16_bits(rng.standard_normal((n, k), dtype=np.float32) * 0.02)
+
+    qn = rng.uniform(0.8, 1.2, hd).astype(np.float32) / np.sqrt(hd)
+    kn = rng.uniform(0.8, 1.2, hd).astype(np.float32)
+    return Layer(attn_norm=rng.uniform(0.8, 1.2, dim).astype(np.float32),
+                 ffn_norm=rng.uniform(0.8, 1.2, dim).astype(np.float32),
+                 wqkv=w(nq, dim), qk_norms=np.stack([qn, kn]).astype(np.float32),
+                 wo=w(dim, g.heads * hd), gate=w(g.ffn, dim), up=w(g.ffn, dim),
+                 down=w(dim, g.ffn))
+
+
 def decode_step(x: np.ndarray, layers: list[Layer], final_norm: np.ndarray, kcache: list,
                 vcache: list, pos: np.ndarray, cos: np.ndarray, sin: np.ndarray, g: Geometry,
                 round_f16: bool = False) -> np.ndarray:

@@ -9,24 +9,7 @@ import numpy as np
 
 
 def make_layer(orc, rng, g):
-    dim, hd = g.dim, g.head_dim
-    nq = (g.heads + 2 * g.n_kv) * hd
-
-    def w(n, k):
-        return orc.f16_bits(rng.standard_normal((n, k), dtype=np.float32) * 0.02)
-
-    qn = rng.uniform(0.8, 1.2, hd).astype(np.float32) / np.sqrt(hd)
-    kn = rng.uniform(0.8, 1.2, hd).astype(np.float32)
-    return orc.Layer(
-        attn_norm=rng.uniform(0.8, 1.2, dim).astype(np.float32),
-        ffn_norm=rng.uniform(0.8, 1.2, dim).astype(np.float32),
-        wqkv=w(nq, dim),
-        qk_norms=np.stack([qn, kn]).astype(np.float32),
-        wo=w(dim, g.heads * hd),
-        gate=w(g.ffn, dim),
-        up=w(g.ffn, dim),
-        down=w(dim, g.ffn),
-    )
+    return orc.synthetic_layer(rng, g)
 
 
 def make_talker(orc, lanes, layers, dim, heads, n_kv, ffn, cap, seed, codebooks=0, vocab=0,
