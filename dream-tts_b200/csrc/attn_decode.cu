@@ -13,6 +13,7 @@
 // across half-warps in shared memory, and, when a lane's span needs several chunks, written as
 // partials that the last CTA of that (lane, kv head) merges in chunk order (deterministic).
 #include <cstdio>
+#include <mutex>
 
 #include "tts_common.cuh"
 #include "tts_internal.h"
@@ -258,6 +259,15 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
 
 }  // namespace
 
+// Scratch for launch_attn_static: the split-KV partials followed by the per-(lane, kv head)
+// arrival counters, in one fixed device array so that callers which must not allocate device
+// memory can still run the attention. Every GPU that loads the library holds this array until
+// the process exits. All calls share it and it keeps the last call's contents, so the counters
+// are cleared on every call, and calls that overlap on the GPU (two streams, two threads) race.
+constexpr size_t kStaticPartBytes = size_t(4) << 20;  // 4 MiB of partials
+constexpr int kStaticCounters = 4096;                  // lanes * n_kv
+static __device__ __align__(256) unsigned char g_attn_static_scratch[kStaticPartBytes + kStaticCounters * sizeof(unsigned)];
+
 size_t attn_part_bytes(int lanes, int n_kv, int gqa, int max_span) {
   const int chunks = (max_span + kChunk - 1) / kChunk;
   return size_t(lanes) * n_kv * chunks * gqa * 130 * sizeof(float);
@@ -310,6 +320,56 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
   cfg.numAttrs = 1;
   if (r.gqa == 2) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<2>, a);
   return cudaLaunchKernelEx(&cfg, attn_decode_kernel<1>, a);
+}
+
+size_t attn_static_part_limit() { return kStaticPartBytes; }
+int attn_static_counter_limit() { return kStaticCounters; }
+
+cudaError_t launch_attn_static(const AttnRequest& r, cudaStream_t st) {
+  if (attn_part_bytes(r.lanes, r.n_kv, r.gqa, r.max_span) > kStaticPartBytes ||
+      r.lanes * r.n_kv > kStaticCounters) {
+    set_error("decode_attention_static: lanes x kv heads x chunks of max_span need " +
+              std::to_string(attn_part_bytes(r.lanes, r.n_kv, r.gqa, r.max_span)) +
+              " bytes of partials (limit " + std::to_string(kStaticPartBytes) +
+              ") and lanes x kv heads <= " + std::to_string(kStaticCounters));
+    return cudaErrorInvalidValue;
+  }
+  // The host-side name of the array is not a device address: resolve it once per device, with
+  // that device current, and pass the resolved pointer to the kernel.
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) {
+    set_error("decode_attention_static: device index out of range");
+    return cudaErrorInvalidValue;
+  }
+  static std::mutex mu;
+  static void* scratch[64] = {nullptr};
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!scratch[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
+      if (e != cudaSuccess) {
+        set_error(std::string("decode_attention_static: cudaGetSymbolAddress failed: ") +
+                  cudaGetErrorString(e));
+        return e;
+      }
+      scratch[dev] = p;
+    }
+    base = scratch[dev];
+  }
+  AttnWorkspace w;
+  w.part = static_cast<float*>(base);
+  w.part_bytes = kStaticPartBytes;
+  w.counters = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(base) + kStaticPartBytes);
+  w.n_counters = kStaticCounters;
+  // The counters must start at zero; a previous call leaves them at zero, but one that was cut
+  // short (a bounded wait that gave up elsewhere in the stream) may not, so clear them here.
+  e = cudaMemsetAsync(w.counters, 0, size_t(r.lanes) * r.n_kv * sizeof(unsigned), st);
+  if (e != cudaSuccess) return e;
+  return launch_attn(r, w, st);
 }
 
 }  // namespace tts

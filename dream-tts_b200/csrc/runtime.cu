@@ -353,6 +353,40 @@ tts_status tts_decode_attention(tts_ctx* c, const float* q, int lanes, int gqa,
   return counted(launch_attn(r, c->attn, S(stream)), "decode_attention");
 }
 
+tts_status tts_decode_attention_static(const float* q, int lanes, int gqa,
+                                       const tts_kv_cache* kv, const int* spans, int max_span,
+                                       int window, void* out, int out_f16, void* stream) {
+  std::string why;
+  if (!q || !spans || !out)
+    return fail(TTS_ERR_INVALID_ARG, "decode_attention_static: NULL argument");
+  if (!kv_ok(kv, &why)) return fail(TTS_ERR_INVALID_ARG, "decode_attention_static: " + why);
+  if (gqa != 1 && gqa != 2)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "decode_attention_static: gqa must be 1 or 2");
+  if (lanes < 1 || max_span < 1 || max_span > 8192)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE,
+                "decode_attention_static: lanes must be >= 1 and max_span in 1..8192");
+  AttnRequest r;
+  r.q = q;
+  r.k_pool = static_cast<const __half*>(kv->k_pages);
+  r.v_pool = static_cast<const __half*>(kv->v_pages);
+  r.block_table = kv->block_table;
+  r.max_blocks = kv->max_blocks;
+  r.block_size = kv->block_size;
+  r.num_blocks = kv->num_blocks;
+  r.err = nullptr;
+  r.spans = spans;
+  r.span_add = 0;
+  r.max_span = max_span;
+  r.window = window;
+  r.lanes = lanes;
+  r.n_kv = kv->n_kv;
+  r.gqa = gqa;
+  r.out = out;
+  r.out_f16 = out_f16 != 0;
+  r.pdl = false;
+  return counted(launch_attn_static(r, S(stream)), "decode_attention_static");
+}
+
 tts_status tts_argmax(tts_ctx* c, const float* logits, int rows, int n,
                       const unsigned char* banned, unsigned int* out, void* stream) {
   if (!c || !logits || !out) return fail(TTS_ERR_INVALID_ARG, "argmax: NULL argument");

@@ -98,6 +98,10 @@ struct AttnWorkspace {
 };
 size_t attn_part_bytes(int lanes, int n_kv, int gqa, int max_span);
 cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream_t st);
+// The same attention with its scratch in a fixed device array (no allocation anywhere).
+cudaError_t launch_attn_static(const AttnRequest& r, cudaStream_t st);
+size_t attn_static_part_limit();
+int attn_static_counter_limit();
 
 // ------------------------------------------------------------------ small kernels
 cudaError_t launch_rms_norm(const float* x, const float* w, int rows, int dim, float eps,

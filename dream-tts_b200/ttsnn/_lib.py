@@ -68,6 +68,7 @@ SIGNATURES = {
     "tts_snake_beta_nlc": [P, P, I, P, P, L, I, P, I, P],
     "tts_qk_rope_append": [P, P, I, I, P, P, P, I, P, C.POINTER(KvCache), F, P, P],
     "tts_decode_attention": [P, P, I, I, C.POINTER(KvCache), P, I, I, P, I, P],
+    "tts_decode_attention_static": [P, I, I, C.POINTER(KvCache), P, I, I, P, I, P],
     "tts_argmax": [P, P, I, I, P, P, P],
     "tts_conv1d_nlc": [P, P, I, I, I, P, I, I, I, I, P, P, P, P, P, P],
     "tts_stack_create": [P, C.POINTER(StackGeometry), C.POINTER(P)],

@@ -138,6 +138,25 @@ TTS_API tts_status tts_decode_attention(tts_ctx* ctx, const float* q, int lanes,
                                 const tts_kv_cache* kv, const int* spans, int max_span,
                                 int window, void* out, int out_f16, void* stream);
 
+/* No counterpart in the reference. The same decode attention (same kernel, same results as
+ * tts_decode_attention) for callers that cannot allocate device memory: a real-time audio or
+ * streaming thread, where cudaMalloc/cudaFree may synchronise the whole device and take
+ * unbounded time, or a host engine that reserves all device memory up front in its own arena
+ * and cannot let a library allocate behind its back. It needs no tts_ctx (creating one
+ * allocates) and calls no allocator: its scratch is one fixed device array inside the library,
+ * 4 MiB of split-KV partials plus 4096 arrival counters, which every GPU that loads the library
+ * holds until the process exits. Limits: lanes * n_kv * ceil(max_span / 256) * gqa * 520 bytes
+ * must fit in 4 MiB (e.g. 48 lanes x 8 kv heads x gqa 2 up to max_span 2048) and
+ * lanes * n_kv <= 4096; larger requests return TTS_ERR_UNSUPPORTED_SHAPE. The first call on a
+ * device looks up the array's device address with that device current, so make the first call
+ * before any stream capture. All calls share the array and it keeps the last call's contents:
+ * the counters are cleared at the start of every call, and calls that overlap on the GPU (two
+ * streams or threads at once) race. Out-of-range pages are masked, not reported. */
+TTS_API tts_status tts_decode_attention_static(const float* q, int lanes, int gqa,
+                                               const tts_kv_cache* kv, const int* spans,
+                                               int max_span, int window, void* out,
+                                               int out_f16, void* stream);
+
 /* ---------------------------------------------------------------- sampling
  * Greedy pick of sample_with_u: crates/qwen3tts/src/talker.rs:154-189. banned[n] (nullable)
  * marks ids forced to -inf; ties go to the highest index (Rust's max_by). */
