@@ -178,9 +178,10 @@ def build_device_talker(device, seed=0, extra_positions=256):
     qk = torch.stack([torch.full((HD,), 1.0 / HD ** 0.5, device=device), torch.ones(HD, device=device)])
     layers = []
     for _ in range(LAYERS):
-        layers.append(LayerTensors(ones, ones, w((HEADS + 2 * N_KV) * HD, DIM), qk.contiguous(),
-                                   w(DIM, HEADS * HD), ttsnn.interleave_gate_up(w(FFN, DIM), w(FFN, DIM)),
-                                   w(DIM, FFN)))
+        layers.append(LayerTensors.from_plain(ones, ones, w((HEADS + 2 * N_KV) * HD, DIM), qk,
+                                              w(DIM, HEADS * HD),
+                                              ttsnn.interleave_gate_up(w(FFN, DIM), w(FFN, DIM)),
+                                              w(DIM, FFN)))
     heads = w(CB * VOCAB, DIM)
     embed = (torch.randn(CB, VOCAB, DIM, generator=gen, device=device) * 0.02).half()
     stack = Stack(geo, layers, ones, heads, embed)
@@ -203,7 +204,9 @@ def time_dominant_gemm(stack, device, reps=3):
     import ttsnn
     from ttsnn import _lib as L
     x = torch.randn(LANES, DIM, device=device)
-    projs = [ttsnn.Proj(lt.w_gate_up) for lt in stack.layers]
+    projs = [ttsnn.Proj(lt.w_gate_up, packed=False) for lt in stack.layers]
+    for p in projs:  # the stack's weights are already packed
+        p.packed = True
     out = torch.empty(LANES, FFN, device=device, dtype=torch.float16)
     for p in projs:
         p.forward(x, L.EPI_SWIGLU_F16, out=out)
@@ -214,8 +217,8 @@ def time_dominant_gemm(stack, device, reps=3):
     e0.record(s)
     for _ in range(reps):
         for p in projs:
-            L.call("tts_proj_forward", ttsnn.ctx(), ttsnn.ptr(x16), LANES, DIM, ttsnn.ptr(p.w),
-                   2 * FFN, L.EPI_SWIGLU_F16, ttsnn.ptr(out), 0, ttsnn.stream())
+            L.call("tts_proj_forward_packed", ttsnn.ctx(), ttsnn.ptr(x16), LANES, DIM,
+                   ttsnn.ptr(p.w), 2 * FFN, L.EPI_SWIGLU_F16, ttsnn.ptr(out), 0, ttsnn.stream())
     e1.record(s)
     torch.cuda.synchronize()
     per = e0.elapsed_time(e1) / (reps * len(projs)) * 1e-3

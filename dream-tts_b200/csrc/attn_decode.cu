@@ -6,12 +6,15 @@
 // (the reference uses one span for the whole batch) let lanes of different lengths share a
 // step, which is what a paged cache is for.
 //
-// Work unit: one CTA per (chunk of kChunk positions, kv head, lane). Both query heads of a kv
-// head are served from one read of each K/V row. Inside a CTA, eight half-warps each take 32
-// consecutive positions; each of their 16 lanes owns 8 of the 128 dims (one 16-byte load per
-// row). Scores, the running max and the exp-rescaled sums are kept per half-warp, combined
-// across half-warps in shared memory, and, when a lane's span needs several chunks, written as
-// partials that the last CTA of that (lane, kv head) merges in chunk order (deterministic).
+// Work unit: one CTA per (chunk of 128 positions, kv head, lane). Both query heads of a kv head
+// are served from one read of each K/V row. The CTA first stages its chunk's K and V rows
+// (64 KB) into shared memory with bulk async copies completing on one mbarrier, so the whole
+// chunk is in flight at once and three CTAs per SM keep ~192 KB of reads outstanding. Then
+// eight half-warps each take 16 consecutive positions; each of their 16 lanes owns 8 of the 128
+// dims (one 16-byte shared load per row). Scores, the running max and the exp-rescaled sums
+// are kept per half-warp, combined across half-warps in shared memory, and, when a lane's span
+// needs several chunks, written as partials that the last CTA of that (lane, kv head) merges in
+// chunk order (deterministic).
 #include <cstdio>
 #include <mutex>
 
@@ -22,10 +25,12 @@ namespace tts {
 
 namespace {
 
-constexpr int kChunk = 256;  // positions per CTA
+constexpr int kChunk = 128;  // positions per CTA
 constexpr int kHalfWarps = 8;
-constexpr int kPerHalf = kChunk / kHalfWarps;  // 32
+constexpr int kPerHalf = kChunk / kHalfWarps;  // 16
 constexpr int kGroup = 8;                      // rows per inner iteration
+constexpr int kMaxPages = kChunk + 1;          // pages one chunk can touch (block_size 1)
+constexpr int kMaxChunks = 64;                 // 8192 positions
 
 struct AttnArgs {
   const float* q;
@@ -46,24 +51,34 @@ struct AttnArgs {
   int out_f16;
 };
 
-__device__ __forceinline__ void load8(const __half* p, float* f) {
-  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-  const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __half22float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
+// Dynamic shared memory of one CTA: the chunk's K and V rows (64 KB), the half-warp partials
+// and the merge scratch.
+struct AttnSmem {
+  __half k[kChunk][128];
+  __half v[kChunk][128];
+  float acc[kHalfWarps][2][128];
+  float m[kHalfWarps][2];
+  float l[kHalfWarps][2];
+  float cm[kMaxChunks][2];
+  float cl[kMaxChunks][2];
+  int page[kMaxPages];
+  uint64_t bar;
+  int last;
+};
+
+TTS_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 template <int GQA>
-__global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
-  __shared__ float sm_acc[kHalfWarps][GQA][128];
-  __shared__ float sm_m[kHalfWarps][GQA];
-  __shared__ float sm_l[kHalfWarps][GQA];
-  __shared__ int sm_last;
-
+__global__ void __launch_bounds__(128, 3) attn_decode_kernel(const AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  AttnSmem& S = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
+                                             ~uintptr_t(127));
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   pdl_launch_dependents();
   pdl_wait();
@@ -81,12 +96,56 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
   if (c >= nch) return;
   const int p0 = ws + c * kChunk;
   const int p1 = min(p0 + kChunk, span);
+  const int pg0 = p0 / a.bs, npg = (p1 - 1) / a.bs - pg0 + 1;
+  const int t = threadIdx.x;
 
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // ---- stage the chunk's K and V rows into shared memory with bulk copies (one barrier)
+  const int* bt = a.bt + (size_t)b * a.max_blocks;
+  for (int i = t; i < npg; i += 128) {
+    const int blk = bt[pg0 + i];
+    S.page[i] = (blk >= 0 && blk < a.num_blocks) ? blk : -1;
+  }
+  if (t == 0) {
+    mbar_init(&S.bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();  // barrier initialised, page table visible
+  if (t < 32) {
+    // warp 0, converged: one elected lane arms the barrier with the chunk's byte count, then
+    // each lane issues the copies of its pages
+    uint32_t bytes = 0;
+    for (int i = t; i < npg; i += 32) {
+      const int r0 = max(p0, (pg0 + i) * a.bs), r1 = min(p1, (pg0 + i + 1) * a.bs);
+      if (S.page[i] >= 0) bytes += uint32_t(r1 - r0) * 512u;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+    if (elect_one()) mbar_arrive_expect_tx(&S.bar, bytes);
+    __syncwarp();
+    for (int i = t; i < npg; i += 32) {
+      if (S.page[i] < 0) continue;
+      const int r0 = max(p0, (pg0 + i) * a.bs), r1 = min(p1, (pg0 + i + 1) * a.bs);
+      const size_t src = (((size_t)S.page[i] * a.n_kv + h) * a.bs + (r0 - (pg0 + i) * a.bs)) * 128;
+      bulk_g2s(&S.k[r0 - p0][0], a.k + src, uint32_t(r1 - r0) * 256u, &S.bar);
+      bulk_g2s(&S.v[r0 - p0][0], a.v + src, uint32_t(r1 - r0) * 256u, &S.bar);
+    }
+    __syncwarp();
+  }
+  // rows of pages outside the pool read as zero (and are reported)
+  for (int i = 0; i < npg; ++i) {
+    if (S.page[i] >= 0) continue;
+    const int r0 = max(p0, (pg0 + i) * a.bs), r1 = min(p1, (pg0 + i + 1) * a.bs);
+    if (t == 0 && a.err) atomicOr(a.err, 1024);
+    for (int e = t; e < (r1 - r0) * 16; e += 128) {
+      reinterpret_cast<uint4*>(&S.k[r0 - p0][0])[e] = make_uint4(0, 0, 0, 0);
+      reinterpret_cast<uint4*>(&S.v[r0 - p0][0])[e] = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  const int lane = t & 31, warp = t >> 5;
   const int hw = warp * 2 + (lane >> 4);
   const int j = lane & 15;
   const int heads = a.n_kv * GQA;
-
   float qv[GQA][8];
 #pragma unroll
   for (int g = 0; g < GQA; ++g) {
@@ -104,10 +163,12 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
 #pragma unroll
     for (int d = 0; d < 8; ++d) acc[g][d] = 0.f;
   }
+  __syncthreads();  // zero-filled rows visible
+  if (!mbar_wait(&S.bar, 0) && t == 0 && a.err) atomicOr(a.err, 2048);
 
-  const int* bt = a.bt + (size_t)b * a.max_blocks;
-  const int q0 = p0 + hw * kPerHalf;
-  const int q1 = min(q0 + kPerHalf, p1);
+  const int rows = p1 - p0;
+  const int q0 = hw * kPerHalf;
+  const int q1 = min(q0 + kPerHalf, rows);
   // The trip count is the same for both half-warps of a warp (their shuffles use the full
   // mask); rows past a half-warp's own range are masked instead.
   for (int it = 0; it < kPerHalf; it += kGroup) {
@@ -116,16 +177,23 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
     float kf[kGroup][8], vf[kGroup][8];
 #pragma unroll
     for (int u = 0; u < kGroup; ++u) {
-      const int p = pg + u;
-      const int blk = p < q1 ? bt[p / a.bs] : -1;
-      if (blk >= 0 && blk < a.num_blocks) {
-        const size_t row = (((size_t)blk * a.n_kv + h) * a.bs + (p % a.bs)) * 128 + 8 * j;
-        load8(a.k + row, kf[u]);
-        load8(a.v + row, vf[u]);
-      } else {
-        if (p < q1 && j == 0 && a.err) atomicOr(a.err, 1024);
+      // rows past this half-warp's range hold stale shared memory (possibly NaN patterns):
+      // read zeros instead, so a masked row contributes exactly nothing
+      const bool valid = pg + u < q1;
+      const int p = valid ? pg + u : 0;
+      uint4 ku = *reinterpret_cast<const uint4*>(&S.k[p][8 * j]);
+      uint4 vu = *reinterpret_cast<const uint4*>(&S.v[p][8 * j]);
+      if (!valid) ku = vu = make_uint4(0, 0, 0, 0);
+      const __half2* kh = reinterpret_cast<const __half2*>(&ku);
+      const __half2* vh = reinterpret_cast<const __half2*>(&vu);
 #pragma unroll
-        for (int d = 0; d < 8; ++d) kf[u][d] = vf[u][d] = 0.f;
+      for (int i = 0; i < 4; ++i) {
+        const float2 kk = __half22float2(kh[i]);
+        const float2 vv = __half22float2(vh[i]);
+        kf[u][2 * i] = kk.x;
+        kf[u][2 * i + 1] = kk.y;
+        vf[u][2 * i] = vv.x;
+        vf[u][2 * i + 1] = vv.y;
       }
     }
 #pragma unroll
@@ -133,14 +201,14 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
       float s[kGroup];
 #pragma unroll
       for (int u = 0; u < kGroup; ++u) {
-        float t = 0.f;
+        float tt = 0.f;
 #pragma unroll
-        for (int d = 0; d < 8; ++d) t += qv[g][d] * kf[u][d];
-        t += __shfl_xor_sync(0xffffffffu, t, 8);
-        t += __shfl_xor_sync(0xffffffffu, t, 4);
-        t += __shfl_xor_sync(0xffffffffu, t, 2);
-        t += __shfl_xor_sync(0xffffffffu, t, 1);
-        s[u] = (pg + u < q1) ? t : -INFINITY;
+        for (int d = 0; d < 8; ++d) tt += qv[g][d] * kf[u][d];
+        tt += __shfl_xor_sync(0xffffffffu, tt, 8);
+        tt += __shfl_xor_sync(0xffffffffu, tt, 4);
+        tt += __shfl_xor_sync(0xffffffffu, tt, 2);
+        tt += __shfl_xor_sync(0xffffffffu, tt, 1);
+        s[u] = (pg + u < q1) ? tt : -INFINITY;
       }
       float mx = s[0];
 #pragma unroll
@@ -163,39 +231,38 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
     }
   }
 
-  // combine the eight half-warps
+  // ---- combine the eight half-warps
 #pragma unroll
   for (int g = 0; g < GQA; ++g) {
 #pragma unroll
-    for (int d = 0; d < 8; ++d) sm_acc[hw][g][8 * j + d] = acc[g][d];
+    for (int d = 0; d < 8; ++d) S.acc[hw][g][8 * j + d] = acc[g][d];
     if (j == 0) {
-      sm_m[hw][g] = m[g];
-      sm_l[hw][g] = l[g];
+      S.m[hw][g] = m[g];
+      S.l[hw][g] = l[g];
     }
   }
   __syncthreads();
 
-  constexpr int kDims = 128 * GQA / 128;  // dims per thread: GQA
-  const int t = threadIdx.x;
-  const int base = (((size_t)b * a.n_kv + h) * a.max_chunks + c) * GQA;
+  constexpr int kDims = GQA;  // (g, d) outputs per thread
+  const size_t base = (((size_t)b * a.n_kv + h) * a.max_chunks + c) * GQA;
   float o[kDims], M[kDims], L[kDims];
   int gg[kDims], dd[kDims];
 #pragma unroll
   for (int e = 0; e < kDims; ++e) {
-    const int idx = t + e * 128;  // 0 .. 128*GQA-1
+    const int idx = t + e * 128;
     const int g = idx / 128, d = idx % 128;
     gg[e] = g;
     dd[e] = d;
     float mm = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kHalfWarps; ++w) mm = fmaxf(mm, sm_m[w][g]);
+    for (int w = 0; w < kHalfWarps; ++w) mm = fmaxf(mm, S.m[w][g]);
     float ll = 0.f, oo = 0.f;
 #pragma unroll
     for (int w = 0; w < kHalfWarps; ++w) {
-      if (sm_m[w][g] == -INFINITY) continue;
-      const float f = expf(sm_m[w][g] - mm);
-      ll += sm_l[w][g] * f;
-      oo += sm_acc[w][g][d] * f;
+      if (S.m[w][g] == -INFINITY) continue;
+      const float f = expf(S.m[w][g] - mm);
+      ll += S.l[w][g] * f;
+      oo += S.acc[w][g][d] * f;
     }
     o[e] = oo;
     M[e] = mm;
@@ -216,9 +283,11 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
     return;
   }
 
+  // ---- several chunks: write this chunk's partial; the last CTA to arrive merges them in
+  // chunk order (deterministic)
 #pragma unroll
   for (int e = 0; e < kDims; ++e) {
-    float* pp = a.part + (size_t)(base + gg[e]) * 130;
+    float* pp = a.part + (base + gg[e]) * 130;
     pp[dd[e]] = o[e];
     if (dd[e] == 0) {
       pp[128] = M[e];
@@ -229,23 +298,36 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const AttnArgs a) {
   __syncthreads();
   if (t == 0) {
     const unsigned prev = atomicAdd(&a.counters[b * a.n_kv + h], 1u);
-    sm_last = (prev == unsigned(nch - 1));
+    S.last = (prev == unsigned(nch - 1));
   }
   __syncthreads();
-  if (!sm_last) return;
+  if (!S.last) return;
   __threadfence();
+  const size_t pb = ((size_t)b * a.n_kv + h) * a.max_chunks * GQA;
+  for (int i = t; i < nch * GQA; i += 128) {
+    const float* pp = a.part + (pb + i) * 130;
+    S.cm[i / GQA][i % GQA] = __ldcg(pp + 128);
+    S.cl[i / GQA][i % GQA] = __ldcg(pp + 129);
+  }
+  __syncthreads();
 #pragma unroll
   for (int e = 0; e < kDims; ++e) {
     const int g = gg[e], d = dd[e];
-    const size_t pb = (((size_t)b * a.n_kv + h) * a.max_chunks) * GQA + g;
     float mm = -INFINITY;
-    for (int cc = 0; cc < nch; ++cc) mm = fmaxf(mm, __ldcg(a.part + (pb + (size_t)cc * GQA) * 130 + 128));
+    for (int cc = 0; cc < nch; ++cc) mm = fmaxf(mm, S.cm[cc][g]);
     float ll = 0.f, oo = 0.f;
-    for (int cc = 0; cc < nch; ++cc) {
-      const float* pp = a.part + (pb + (size_t)cc * GQA) * 130;
-      const float f = expf(__ldcg(pp + 128) - mm);
-      ll += __ldcg(pp + 129) * f;
-      oo += __ldcg(pp + d) * f;
+    for (int c0 = 0; c0 < nch; c0 += 4) {
+      float ov[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        ov[u] = (c0 + u < nch) ? __ldcg(a.part + (pb + (size_t)(c0 + u) * GQA + g) * 130 + d) : 0.f;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (c0 + u >= nch) break;
+        const float f = expf(S.cm[c0 + u][g] - mm);
+        ll += S.cl[c0 + u][g] * f;
+        oo += ov[u] * f;
+      }
     }
     const float r = oo / ll;
     const size_t oi = out_base + g * 128 + d;
@@ -283,6 +365,10 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
     return cudaErrorInvalidValue;
   }
   const int chunks = (r.max_span + kChunk - 1) / kChunk;
+  if (chunks > kMaxChunks) {
+    set_error("decode_attention: max_span exceeds 8192");
+    return cudaErrorInvalidValue;
+  }
   if (attn_part_bytes(r.lanes, r.n_kv, r.gqa, r.max_span) > w.part_bytes ||
       r.lanes * r.n_kv > w.n_counters) {
     set_error("decode_attention: workspace too small");
@@ -309,9 +395,22 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
   a.out_f16 = r.out_f16 ? 1 : 0;
 
   cudaLaunchConfig_t cfg{};
+  const size_t smem = sizeof(AttnSmem) + 128;
+  {
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !done[dev]) {
+      cudaFuncSetAttribute(attn_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      cudaFuncSetAttribute(attn_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      done[dev] = true;
+    }
+  }
   cfg.gridDim = dim3(chunks, r.n_kv, r.lanes);
   cfg.blockDim = dim3(128, 1, 1);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

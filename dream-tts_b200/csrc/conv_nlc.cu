@@ -112,69 +112,83 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_wait();
 
   const int nsteps = ncb * a.k;
-  if (warp == 0 && lane == 0) {
+  if (warp == 0) {
     // ---------------- weight tiles: step i = (cb, tap) -> W[co0 .., tap*cin + cb*64 ..]
+    // (converged warp, one elected lane issues)
     for (int i = 0; i < nsteps; ++i) {
       const int s = i % kBStages;
-      if (i >= kBStages && !mbar_wait(&empty_b[s], ((i / kBStages) + 1) & 1)) {
-        atomicOr(a.err, 16);
+      if (i >= kBStages && !mbar_wait_warp(&empty_b[s], ((i / kBStages) + 1) & 1)) {
+        if (lane == 0) atomicOr(a.err, 16);
         break;
       }
-      const int cb = i / a.k, t = i % a.k;
-      uint8_t* dst = b_base + s * b_bytes;
-      mbar_arrive_expect_tx(&full_b[s], b_bytes);
-      for (int h = 0; h < a.nh; ++h)
-        tma_load_2d(dst + h * a.nper * 128, &tmW, &full_b[s], t * a.cin + cb * kCB,
-                    co0 + h * a.nper);
+      if (elect_one()) {
+        const int cb = i / a.k, t = i % a.k;
+        uint8_t* dst = b_base + s * b_bytes;
+        mbar_arrive_expect_tx(&full_b[s], b_bytes);
+        for (int h = 0; h < a.nh; ++h)
+          tma_load_2d(dst + h * a.nper * 128, &tmW, &full_b[s], t * a.cin + cb * kCB,
+                      co0 + h * a.nper);
+      }
+      __syncwarp();
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (converged warp, one elected lane issues)
     const uint32_t idesc = idesc_f16_f32(kRows, a.nper);
     const uint32_t slab = uint32_t(a.R) * 16;
     bool ok = true;
     for (int cb = 0; cb < ncb && ok; ++cb) {
       const int sa = cb % kAStages;
-      if (!mbar_wait(&ready_a[sa], (cb / kAStages) & 1)) {
-        atomicOr(a.err, 32);
+      if (!mbar_wait_warp(&ready_a[sa], (cb / kAStages) & 1)) {
+        if (lane == 0) atomicOr(a.err, 32);
         break;
       }
       const uint32_t ha = smem_u32(a_base + sa * a_bytes);
       for (int t = 0; t < a.k; ++t) {
         const int i = cb * a.k + t;
         const int sb = i % kBStages;
-        if (!mbar_wait(&full_b[sb], (i / kBStages) & 1)) {
-          atomicOr(a.err, 64);
+        if (!mbar_wait_warp(&full_b[sb], (i / kBStages) & 1)) {
+          if (lane == 0) atomicOr(a.err, 64);
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t hb = smem_u32(b_base + sb * b_bytes);
+        if (elect_one()) {
+          const uint32_t hb = smem_u32(b_base + sb * b_bytes);
 #pragma unroll
-        for (int kk = 0; kk < kCB / 16; ++kk) {
-          const uint64_t ad = desc_k_interleave(ha + 2 * kk * slab + t * a.dil * 16, slab);
-          for (int h = 0; h < a.nh; ++h) {
-            const uint64_t bd = desc_k_sw128(hb + h * a.nper * 128 + kk * 32);
-            umma_f16(tmem + h * a.nper, ad, bd, idesc, (i | kk) != 0);
+          for (int kk = 0; kk < kCB / 16; ++kk) {
+            const uint64_t ad = desc_k_interleave(ha + 2 * kk * slab + t * a.dil * 16, slab);
+            for (int h = 0; h < a.nh; ++h) {
+              const uint64_t bd = desc_k_sw128(hb + h * a.nper * 128 + kk * 32);
+              umma_f16(tmem + h * a.nper, ad, bd, idesc, (i | kk) != 0);
+            }
           }
+          umma_commit(&empty_b[sb]);
         }
-        umma_commit(&empty_b[sb]);
+        __syncwarp();
       }
-      umma_commit(&empty_a[sa]);
+      if (ok) {
+        if (elect_one()) umma_commit(&empty_a[sa]);
+        __syncwarp();
+      }
     }
-    umma_commit(done);
+    if (elect_one()) umma_commit(done);
+    __syncwarp();
   } else if (warp >= 2 && warp <= 5) {
-    // ---------------- halos: load, snake in place, hand to the MMA
+    // ---------------- halos: load (warp 2, one elected lane), snake in place, hand to the MMA
     const int tt = threadIdx.x - 64;  // 0..127
-    auto issue = [&](int cb) {
+    auto issue = [&](int cb) {  // called by all of warp 2
       const int s = cb % kAStages;
-      if (cb >= kAStages && !mbar_wait(&empty_a[s], ((cb / kAStages) + 1) & 1)) {
-        atomicOr(a.err, 128);
+      if (cb >= kAStages && !mbar_wait_warp(&empty_a[s], ((cb / kAStages) + 1) & 1)) {
+        if (lane == 0) atomicOr(a.err, 128);
         return;
       }
-      mbar_arrive_expect_tx(&full_a[s], a_bytes);
-      tma_load_4d(a_base + s * a_bytes, &tmX, &full_a[s], 0, l0 - a.pad_left, cb * (kCB / 8), bb);
+      if (elect_one()) {
+        mbar_arrive_expect_tx(&full_a[s], a_bytes);
+        tma_load_4d(a_base + s * a_bytes, &tmX, &full_a[s], 0, l0 - a.pad_left, cb * (kCB / 8), bb);
+      }
+      __syncwarp();
     };
-    if (tt == 0)
+    if (warp == 2)
       for (int cb = 0; cb < std::min(ncb, kAStages - 1); ++cb) issue(cb);
     for (int cb = 0; cb < ncb; ++cb) {
       const int s = cb % kAStages;
@@ -195,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       }
       mbar_arrive(&ready_a[s]);
-      if (tt == 0 && cb + kAStages - 1 < ncb) issue(cb + kAStages - 1);
+      if (warp == 2 && cb + kAStages - 1 < ncb) issue(cb + kAStages - 1);
     }
   }
   __syncwarp();

@@ -9,15 +9,19 @@
 // contiguous range of 64-deep K blocks (split-K sized so the grid fills the SMs once).
 //   warp 0 lane 0  TMA producer: W tile (16 KB, 128B swizzle) + x tile per stage
 //   warp 1 lane 0  MMA issuer: 4 x tcgen05.mma (K = 16) per stage into TMEM
-//   all 4 warps    epilogue: TMEM -> registers -> split-K partials; the last CTA to arrive
-//                  on a tile sums the partials in split order (deterministic) and applies
-//                  the fused epilogue.
+//   all 4 warps    epilogue: TMEM -> this CTA's shared memory. The splits of one tile form a
+//                  thread-block cluster; after a cluster barrier each CTA reduces a slice of
+//                  the lanes by reading every split's partial over DSMEM in rank order
+//                  (deterministic, no global scratch) and applies the fused epilogue.
 // Weight loads for the first stages are issued before `griddepcontrol.wait`, so under
 // programmatic dependent launch they overlap the previous kernel's tail; only the x loads,
 // which read the previous kernel's output, wait.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "tts_common.cuh"
 #include "tts_internal.h"
@@ -35,11 +39,12 @@ struct GemmArgs {
   int m, k, n;
   int kb_total, splits, tiles;
   int groups, ng;  // token groups (<= 2) and MMA N per group (multiple of 16, <= 256)
-  int stages;
+  int packed;      // W tensor map is the packed [tiles * kb * 128][64] view
+  int stages;     // per pipeline
+  int pipes;      // independent producer/MMA pipelines per CTA
+  int acc_cols;   // TMEM columns per pipeline accumulator
   int tmem_cols;
   int epi;
-  float* ws;
-  unsigned* counters;
   int* err;
   void* y;
   int ldy;
@@ -126,7 +131,9 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& a, int tile, int j,
   }
 }
 
-__global__ void __launch_bounds__(128, 1)
+constexpr int kThreads = 256;  // 8 warps: 0..3 producers, 4..7 MMA issuers + epilogue
+
+__global__ void __launch_bounds__(kThreads, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmX, const GemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -139,27 +146,30 @@ __global__ void __launch_bounds__(128, 1)
   const int nkb = kb1 - kb0;
   const uint32_t x_bytes = uint32_t(a.groups * a.ng * 128);
   const uint32_t stage_bytes = kWBytes + x_bytes;
+  const int P = a.pipes, SP = a.stages;  // pipelines and stages per pipeline
 
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + a.stages * stage_bytes);
-  uint64_t* empty = full + a.stages;
-  uint64_t* done = empty + a.stages;
+  // P stage rings, reused after the main loop for the partial tile [m][128] f32; then barriers
+  const uint32_t body =
+      max(uint32_t(P * SP) * stage_bytes, uint32_t(a.m) * kTileM * 4u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + body);  // [P][SP]
+  uint64_t* empty = full + P * SP;                              // [P][SP]
+  uint64_t* done = empty + P * SP;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < a.stages; ++s) {
+    for (int s = 0; s < P * SP; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(done, 1);
+    mbar_init(done, P);
     fence_barrier_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
   }
-  if (warp == 1) {
+  if (warp == 4) {
     tmem_alloc(tmem_slot, a.tmem_cols);
     tmem_relinquish();
   }
@@ -170,103 +180,150 @@ __global__ void __launch_bounds__(128, 1)
 
   pdl_launch_dependents();
 
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer
-    const uint64_t pol_w = l2_policy_evict_first();
-    const int pre = nkb < a.stages ? nkb : a.stages;
-    for (int i = 0; i < pre; ++i) {
-      uint8_t* st = smem + i * stage_bytes;
-      mbar_arrive_expect_tx(&full[i], stage_bytes);
-      tma_load_2d_hint(st, &tmW, &full[i], (kb0 + i) * kBlockK, tile * kTileM, pol_w);
-    }
-    pdl_wait();  // x is the previous kernel's output
-    for (int i = 0; i < pre; ++i) {
-      uint8_t* st = smem + i * stage_bytes + kWBytes;
-      for (int g = 0; g < a.groups; ++g)
-        tma_load_2d(st + g * a.ng * 128, &tmX, &full[i], (kb0 + i) * kBlockK, g * a.ng);
-    }
-    for (int i = pre; i < nkb; ++i) {
-      const int s = i % a.stages;
-      if (!mbar_wait(&empty[s], ((i / a.stages) + 1) & 1)) {
-        atomicOr(a.err, 1);
-        break;
-      }
-      uint8_t* st = smem + s * stage_bytes;
-      mbar_arrive_expect_tx(&full[s], stage_bytes);
-      tma_load_2d_hint(st, &tmW, &full[s], (kb0 + i) * kBlockK, tile * kTileM, pol_w);
-      for (int g = 0; g < a.groups; ++g)
-        tma_load_2d(st + kWBytes + g * a.ng * 128, &tmX, &full[s], (kb0 + i) * kBlockK,
-                    g * a.ng);
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
-    const uint32_t idesc = idesc_f16_f32(kTileM, a.ng);
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % a.stages;
-      if (!mbar_wait(&full[s], (i / a.stages) & 1)) {
-        atomicOr(a.err, 2);
-        break;
-      }
-      tc_fence_after();
-      const uint32_t wa = smem_u32(smem + s * stage_bytes);
-      const uint32_t xa = wa + kWBytes;
-#pragma unroll
-      for (int kk = 0; kk < kBlockK / 16; ++kk) {
-        const uint64_t ad = desc_k_sw128(wa + kk * 32);
-        for (int g = 0; g < a.groups; ++g) {
-          const uint64_t bd = desc_k_sw128(xa + g * a.ng * 128 + kk * 32);
-          umma_f16(tmem + g * a.ng, ad, bd, idesc, (i | kk) != 0);
+  // Pipeline p streams k-blocks kb0 + p, kb0 + p + P, ... through its own SP stages into its
+  // own TMEM accumulator: P independent producer/MMA handshakes keep loads and MMAs
+  // overlapped (one pipeline alone serialises load latency and MMA latency per k-block).
+  if (warp < 4) {
+    const int pp = warp;
+    if (pp < P) {
+      // ---------------- TMA producer of pipeline pp (converged warp, one elected lane issues)
+      const uint64_t pol_w = l2_policy_evict_first();
+      const int cnt = nkb > pp ? (nkb - pp + P - 1) / P : 0;  // k-blocks of this pipeline
+      const int pre = cnt < SP ? cnt : SP;
+      uint8_t* ring = smem + size_t(pp) * SP * stage_bytes;
+      uint64_t* fl = full + pp * SP;
+      uint64_t* em = empty + pp * SP;
+      auto w_x = [&](int kb) { return a.packed ? 0 : kb * kBlockK; };
+      auto w_y = [&](int kb) { return a.packed ? (tile * a.kb_total + kb) * kTileM : tile * kTileM; };
+      if (elect_one()) {
+        for (int i = 0; i < pre; ++i) {
+          const int kb = kb0 + pp + i * P;
+          mbar_arrive_expect_tx(&fl[i], stage_bytes);
+          tma_load_2d_hint(ring + i * stage_bytes, &tmW, &fl[i], w_x(kb), w_y(kb), pol_w);
         }
       }
-      umma_commit(&empty[s]);
+      __syncwarp();
+      pdl_wait();  // x is the previous kernel's output
+      if (elect_one()) {
+        for (int i = 0; i < pre; ++i) {
+          const int kb = kb0 + pp + i * P;
+          uint8_t* st = ring + i * stage_bytes + kWBytes;
+          for (int g = 0; g < a.groups; ++g)
+            tma_load_2d(st + g * a.ng * 128, &tmX, &fl[i], kb * kBlockK, g * a.ng);
+        }
+      }
+      __syncwarp();
+      for (int i = pre; i < cnt; ++i) {
+        const int s = i % SP;
+        if (!mbar_wait_warp(&em[s], ((i / SP) + 1) & 1)) {
+          if (lane == 0) atomicOr(a.err, 1);
+          break;
+        }
+        if (elect_one()) {
+          const int kb = kb0 + pp + i * P;
+          uint8_t* st = ring + s * stage_bytes;
+          mbar_arrive_expect_tx(&fl[s], stage_bytes);
+          tma_load_2d_hint(st, &tmW, &fl[s], w_x(kb), w_y(kb), pol_w);
+          for (int g = 0; g < a.groups; ++g)
+            tma_load_2d(st + kWBytes + g * a.ng * 128, &tmX, &fl[s], kb * kBlockK, g * a.ng);
+        }
+        __syncwarp();
+      }
     }
-    umma_commit(done);
-  }
-  __syncwarp();
-
-  // ---------------- epilogue: TMEM -> split-K partials
-  const bool ok = mbar_wait(done, 0);
-  if (!ok && threadIdx.x == 64) atomicOr(a.err, 4);
-  tc_fence_after();
-  pdl_wait();
-  const int row = warp * 32 + lane;
-  float* part = a.ws + ((size_t)split * a.tiles + tile) * a.m * kTileM;
-  for (int c0 = 0; c0 < a.m; c0 += 16) {
-    float v[16];
-    tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + c0, v);
+  } else {
+    const int pp = warp - 4;
+    if (pp < P) {
+      // ---------------- MMA issuer of pipeline pp (converged warp, one elected lane issues)
+      const uint32_t idesc = idesc_f16_f32(kTileM, a.ng);
+      const int cnt = nkb > pp ? (nkb - pp + P - 1) / P : 0;
+      uint8_t* ring = smem + size_t(pp) * SP * stage_bytes;
+      uint64_t* fl = full + pp * SP;
+      uint64_t* em = empty + pp * SP;
+      const uint32_t acc = tmem + uint32_t(pp * a.acc_cols);
+      for (int i = 0; i < cnt; ++i) {
+        const int s = i % SP;
+        if (!mbar_wait_warp(&fl[s], (i / SP) & 1)) {
+          if (lane == 0) atomicOr(a.err, 2);
+          break;
+        }
+        tc_fence_after();
+        if (elect_one()) {
+          const uint32_t wa = smem_u32(ring + s * stage_bytes);
+          const uint32_t xa = wa + kWBytes;
 #pragma unroll
-    for (int jj = 0; jj < 16; ++jj) {
-      const int j = c0 + jj;
-      if (j < a.m) part[(size_t)j * kTileM + row] = v[jj];
+          for (int kk = 0; kk < kBlockK / 16; ++kk) {
+            const uint64_t ad = desc_k_sw128(wa + kk * 32);
+            for (int g = 0; g < a.groups; ++g) {
+              const uint64_t bd = desc_k_sw128(xa + g * a.ng * 128 + kk * 32);
+              umma_f16(acc + g * a.ng, ad, bd, idesc, (i | kk) != 0);
+            }
+          }
+          umma_commit(&em[s]);
+        }
+        __syncwarp();
+      }
+      if (elect_one()) umma_commit(done);  // no MMA issued: arrives at once (zero partial)
+      __syncwarp();
+    }
+  }
+
+  // ---------------- epilogue: sum the pipelines' accumulators (pipeline order) into this
+  // CTA's partial tile in shared memory. Warps 4..7 own TMEM lane quadrants 0..3.
+  const bool ok = mbar_wait(done, 0);
+  if (!ok && threadIdx.x == 128) atomicOr(a.err, 4);
+  tc_fence_after();
+  // Every TMA load was consumed by an MMA and every MMA has completed, so the stage buffers
+  // are free: the partial tile [m][128] f32 reuses them.
+  float* red = reinterpret_cast<float*>(smem);
+  if (warp >= 4) {
+    const int q = warp - 4;
+    const int row = q * 32 + lane;
+    for (int c0 = 0; c0 < a.m; c0 += 16) {
+      float v[16];
+      tmem_ld16(tmem + (uint32_t(q * 32) << 16) + c0, v);
+      for (int pp = 1; pp < P; ++pp) {
+        // a pipeline that issued nothing holds no accumulator
+        const int cnt = nkb > pp ? (nkb - pp + P - 1) / P : 0;
+        float u[16];
+        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(pp * a.acc_cols) + c0, u);
+        if (cnt > 0) {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) v[jj] += u[jj];
+        }
+      }
+      if (nkb == 0) {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) v[jj] = 0.f;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const int j = c0 + jj;
+        if (j < a.m) red[j * kTileM + row] = v[jj];
+      }
     }
   }
   tc_fence_before();
-  __threadfence();
-  __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, a.tmem_cols);
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&a.counters[tile], 1u);
-    *last_flag = (prev == unsigned(a.splits - 1));
-  }
-  __syncthreads();
-  if (!*last_flag) return;
-  __threadfence();
+  cluster_sync();
+  if (warp == 4) tmem_dealloc(tmem, a.tmem_cols);
+  pdl_wait();  // the epilogue reads and writes buffers earlier kernels use
 
-  // ---------------- last CTA on this tile: reduce in split order, fused epilogue
-  for (int j = warp; j < a.m; j += 4) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < a.splits; ++s) {
-      const float4 p = __ldcg(reinterpret_cast<const float4*>(
-                                  a.ws + (((size_t)s * a.tiles + tile) * a.m + j) * kTileM) +
-                              lane);
-      acc.x += p.x;
-      acc.y += p.y;
-      acc.z += p.z;
-      acc.w += p.w;
+  // ---------------- reduce this CTA's lanes across the cluster, in rank order
+  const uint32_t rank = cluster_rank();
+  const int S = a.splits;
+  const int nw = kThreads / 32;
+  for (int j = int(rank) + S * warp; j < a.m; j += nw * S) {
+    const float* src = red + j * kTileM + 4 * lane;
+    float4 acc4 = ld_dsmem_f4(src, 0);
+    for (int r = 1; r < S; ++r) {
+      const float4 p = ld_dsmem_f4(src, r);
+      acc4.x += p.x;
+      acc4.y += p.y;
+      acc4.z += p.z;
+      acc4.w += p.w;
     }
-    epilogue_row(a, tile, j, lane, acc);
+    epilogue_row(a, tile, j, lane, acc4);
   }
-  if (threadIdx.x == 0) a.counters[tile] = 0u;
+  cluster_sync();  // no CTA leaves while another may still read its shared memory
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -284,31 +341,88 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 struct Plan {
-  int groups, ng, stages, splits, tmem_cols;
+  int groups, ng, stages, pipes, acc_cols, splits, tmem_cols;
   size_t smem;
 };
 
+int env_int(const char* name, int fallback) {
+  const char* v = getenv(name);
+  if (!v || !*v) return fallback;
+  return atoi(v);
+}
+
+// Clusters of `splits` CTAs that can be resident at once for this shared-memory size, cached
+// per (device, splits, smem). 0 when the query fails.
+int max_active_clusters(int device, int splits, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, size_t>, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_tuple(device, splits, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaFuncSetAttribute(gemm_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1, splits, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = splits;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_decode_kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[key] = n;
+  return n;
+}
+
+// Tile plan for y[m, n] = x[m, k] W[n, k]^T. The grid is one wave: every CTA (and every
+// cluster of split-K CTAs) resident at once, so no tile waits for a second wave.
+// TTS_GEMM_STAGES / TTS_GEMM_SPLITS override the choice for A/B measurement.
 Plan plan_gemm(int m, int k, int n, int device, int force_splits) {
   Plan p{};
   const int pad = std::max(16, (m + 15) / 16 * 16);
   p.groups = (pad + 255) / 256;
   p.ng = ((pad + p.groups - 1) / p.groups + 15) / 16 * 16;
   const int cols = p.groups * p.ng;
+  p.acc_cols = 32;
+  while (p.acc_cols < cols) p.acc_cols *= 2;
+  // up to 4 pipelines, each with its own TMEM accumulator (512 columns in all)
+  p.pipes = std::max(1, std::min(4, 512 / p.acc_cols));
+  p.pipes = std::max(1, std::min(4, env_int("TTS_GEMM_PIPES", p.pipes)));
+  while (p.pipes > 1 && p.pipes * p.acc_cols > 512) --p.pipes;
   p.tmem_cols = 32;
-  while (p.tmem_cols < cols) p.tmem_cols *= 2;
+  while (p.tmem_cols < p.pipes * p.acc_cols) p.tmem_cols *= 2;
   const int stage = kWBytes + cols * 128;
-  // Two CTAs per SM when stages fit in ~100 KB: one drains its epilogue while the other
-  // streams; wide token counts take one CTA per SM with deeper stages.
-  const bool two = stage * 4 <= 100 * 1024;
-  const int budget = two ? 100 * 1024 : 200 * 1024;
-  p.stages = std::max(2, std::min(8, budget / stage));
-  p.smem = size_t(p.stages) * stage + 1024 + 256;
   const int tiles = n / kTileM;
+  const int sms = num_sms(device);
+  // Many tiles (the heads): two CTAs per SM, one stage per pipeline. Otherwise one CTA per SM
+  // with two stages per pipeline.
+  const bool two = tiles > sms;
+  const int budget = two ? 100 * 1024 : 200 * 1024;
+  p.stages = std::max(1, std::min(4, budget / (stage * p.pipes)));
+  p.stages = std::max(1, std::min(8, env_int("TTS_GEMM_STAGES", p.stages)));
+  while (p.stages > 1 && size_t(p.stages) * p.pipes * stage > 210 * 1024) --p.stages;
+  while (p.pipes > 1 && size_t(p.stages) * p.pipes * stage > 210 * 1024) --p.pipes;
+  const size_t red = size_t(m) * kTileM * sizeof(float);
+  const size_t rings = size_t(p.stages) * p.pipes * stage;
+  p.smem = std::max(rings, red) + 1024 + 512;
+
   const int kb = k / kBlockK;
-  const int slots = num_sms(device) * (two ? 2 : 1);
-  int s = std::max(1, slots / tiles);
-  s = std::min(s, std::max(1, kb / 2));
-  if (force_splits > 0) s = std::min(force_splits, kb);
+  int s = 1;
+  for (int c = std::min(8, kb); c >= 2; --c) {
+    if (tiles * c > sms) continue;
+    if (max_active_clusters(device, c, p.smem) < tiles) continue;
+    s = c;
+    break;
+  }
+  const int fs = force_splits > 0 ? force_splits : env_int("TTS_GEMM_SPLITS", 0);
+  if (fs > 0) s = std::min(std::min(fs, 8), kb);
   p.splits = s;
   return p;
 }
@@ -351,13 +465,16 @@ cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t
   }
   const Plan p = plan_gemm(r.m, r.k, r.n, device, r.force_splits);
   const int tiles = r.n / kTileM;
-  const size_t need = size_t(p.splits) * tiles * r.m * kTileM * sizeof(float);
-  if (need > wsp.ws_bytes || tiles > wsp.n_counters) {
-    set_error("proj: split-K workspace too small for this shape");
+  if (p.smem > 227 * 1024) {
+    set_error("proj: shared-memory plan exceeds 227 KB for this lane count");
     return cudaErrorInvalidValue;
   }
   CUtensorMap tmW, tmX;
-  if (!make_tmap_2d_f16(&tmW, r.w, r.k, r.n, uint64_t(r.k) * 2, kBlockK, kTileM, true) ||
+  const bool wmap_ok =
+      r.packed ? make_tmap_2d_f16(&tmW, r.w, kBlockK, uint64_t(r.n) / kTileM * (r.k / kBlockK) * kTileM,
+                                  kBlockK * 2, kBlockK, kTileM, true)
+               : make_tmap_2d_f16(&tmW, r.w, r.k, r.n, uint64_t(r.k) * 2, kBlockK, kTileM, true);
+  if (!wmap_ok ||
       !make_tmap_2d_f16(&tmX, r.x, r.k, r.m, uint64_t(r.k) * 2, kBlockK, p.ng, true)) {
     set_error("proj: cuTensorMapEncodeTiled failed (pointers must be 16-byte aligned)");
     return cudaErrorInvalidValue;
@@ -371,11 +488,12 @@ cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t
   a.tiles = tiles;
   a.groups = p.groups;
   a.ng = p.ng;
+  a.packed = r.packed ? 1 : 0;
   a.stages = p.stages;
+  a.pipes = p.pipes;
+  a.acc_cols = p.acc_cols;
   a.tmem_cols = p.tmem_cols;
   a.epi = r.epi;
-  a.ws = wsp.ws;
-  a.counters = wsp.counters;
   a.err = wsp.err;
   a.y = r.y;
   a.ldy = r.ldy > 0 ? r.ldy : (r.epi == EPI_SWIGLU ? r.n / 2 : r.n);
@@ -399,14 +517,18 @@ cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(tiles, p.splits, 1);
-  cfg.blockDim = dim3(128, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = p.smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = r.pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = p.splits;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.splits > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, gemm_decode_kernel, tmW, tmX, a);
 }
 

@@ -127,6 +127,23 @@ __global__ void interleave_gate_up_kernel(const __half* gate, const __half* up, 
   }
 }
 
+// w [n][k] -> [n/128][k/64][128][64]: each 128 x 64 tile one contiguous 16 KB block, a tile
+// row's k-blocks consecutive, so the GEMM streams its weights sequentially.
+__global__ void pack_weight_kernel(const __half* w, int n, int k, __half* out) {
+  const long total = long(n) * k / 8;
+  const int kb = k / 64;
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < total;
+       e += (long)gridDim.x * blockDim.x) {
+    const long el = e * 8;                  // element index in the packed layout
+    const long blk = el / (128 * 64);       // (tile, k-block) block
+    const int within = int(el % (128 * 64));
+    const int r = within / 64, c = within % 64;
+    const long t = blk / kb, b = blk % kb;
+    const __half* src = w + (t * 128 + r) * long(k) + b * 64 + c;
+    *reinterpret_cast<uint4*>(out + el) = *reinterpret_cast<const uint4*>(src);
+  }
+}
+
 }  // namespace rt
 using namespace rt;
 
@@ -155,18 +172,12 @@ tts_status tts_ctx_create(int device, int max_lanes, tts_ctx** out) {
   auto* c = new tts_ctx();
   c->device = device;
   c->max_lanes = max_lanes;
-  const int slots = std::max(512, 2 * num_sms(device));
-  c->gemm.ws_bytes = size_t(slots) * max_lanes * 128 * sizeof(float);
-  c->gemm.n_counters = 4096;
   const int max_span = 8192, n_kv = 8, gqa = 2;
   c->attn.part_bytes = attn_part_bytes(max_lanes, n_kv, gqa, max_span);
   c->attn.n_counters = max_lanes * 64;
-  cudaError_t e = dmalloc(&c->gemm.ws, c->gemm.ws_bytes);
-  if (e == cudaSuccess) e = dmalloc(&c->gemm.counters, c->gemm.n_counters * sizeof(unsigned));
-  if (e == cudaSuccess) e = dmalloc(&c->gemm.err, 16);
+  cudaError_t e = dmalloc(&c->gemm.err, 16);
   if (e == cudaSuccess) e = dmalloc(&c->attn.part, c->attn.part_bytes);
   if (e == cudaSuccess) e = dmalloc(&c->attn.counters, c->attn.n_counters * sizeof(unsigned));
-  if (e == cudaSuccess) e = cudaMemset(c->gemm.counters, 0, c->gemm.n_counters * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMemset(c->attn.counters, 0, c->attn.n_counters * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMemset(c->gemm.err, 0, 16);
   if (e == cudaSuccess) e = cudaMallocHost(reinterpret_cast<void**>(&c->err_host), 16);
@@ -182,8 +193,6 @@ tts_status tts_ctx_create(int device, int max_lanes, tts_ctx** out) {
 tts_status tts_ctx_destroy(tts_ctx* c) {
   if (!c) return TTS_OK;
   DeviceGuard g(c->device);
-  cudaFree(c->gemm.ws);
-  cudaFree(c->gemm.counters);
   cudaFree(c->gemm.err);
   cudaFree(c->attn.part);
   cudaFree(c->attn.counters);
@@ -245,6 +254,45 @@ tts_status tts_interleave_gate_up(tts_ctx* c, const void* gate, const void* up, 
                                                         static_cast<const __half*>(up), ffn,
                                                         dim, static_cast<__half*>(out));
   return counted(cudaGetLastError(), "interleave");
+}
+
+tts_status tts_weight_pack(tts_ctx* c, const void* w, int n, int k, void* out, void* stream) {
+  if (!c || !w || !out) return fail(TTS_ERR_INVALID_ARG, "weight_pack: NULL argument");
+  if (n < 128 || n % 128 || k < 64 || k % 64)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "weight_pack: n % 128 and k % 64 must be 0");
+  if (!aligned16(w) || !aligned16(out) || w == out)
+    return fail(TTS_ERR_INVALID_ARG, "weight_pack: 16-byte aligned, distinct buffers");
+  DeviceGuard g(c->device);
+  pack_weight_kernel<<<1184, 256, 0, S(stream)>>>(static_cast<const __half*>(w), n, k,
+                                                 static_cast<__half*>(out));
+  return counted(cudaGetLastError(), "weight_pack");
+}
+
+tts_status tts_proj_forward_packed(tts_ctx* c, const void* x, int m, int k, const void* w, int n,
+                                   int epilogue, void* y, int ldy, void* stream) {
+  if (!c || !x || !w || !y) return fail(TTS_ERR_INVALID_ARG, "proj: NULL argument");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y))
+    return fail(TTS_ERR_INVALID_ARG, "proj: pointers must be 16-byte aligned");
+  if (epilogue < TTS_EPI_F32 || epilogue > TTS_EPI_SWIGLU_F16)
+    return fail(TTS_ERR_INVALID_ARG, "proj: unknown epilogue");
+  std::string why;
+  if (!gemm_supported(m, k, n, epilogue, &why))
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "proj: " + why);
+  if (m > c->max_lanes)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "proj: m exceeds the context's max_lanes");
+  DeviceGuard g(c->device);
+  GemmRequest r;
+  r.w = static_cast<const __half*>(w);
+  r.packed = true;
+  r.x = static_cast<const __half*>(x);
+  r.m = m;
+  r.k = k;
+  r.n = n;
+  r.epi = epilogue;
+  r.y = y;
+  r.ldy = ldy;
+  r.pdl = false;
+  return counted(launch_gemm(r, c->gemm, S(stream), c->device), "proj");
 }
 
 tts_status tts_rms_norm(tts_ctx* c, const float* x, const float* w, int rows, int dim, float eps,
@@ -549,6 +597,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
             "rms_norm");
     GemmRequest r;
     r.w = static_cast<const __half*>(w.wqkv);
+    r.packed = true;
     r.x = s->xn;
     r.m = B;
     r.k = D;
@@ -592,6 +641,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     TTS_TRY(launch_attn(ar, c->attn, cs), "decode_attention");
     GemmRequest o;
     o.w = static_cast<const __half*>(w.wo);
+    o.packed = true;
     o.x = s->attn;
     o.m = B;
     o.k = qw;
@@ -604,6 +654,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
             "rms_norm");
     GemmRequest gu;
     gu.w = static_cast<const __half*>(w.w_gate_up);
+    gu.packed = true;
     gu.x = s->xn;
     gu.m = B;
     gu.k = D;
@@ -613,6 +664,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     TTS_TRY(launch_gemm(gu, c->gemm, cs, c->device), "proj");
     GemmRequest dn;
     dn.w = static_cast<const __half*>(w.w_down);
+    dn.packed = true;
     dn.x = s->act;
     dn.m = B;
     dn.k = gm.ffn;
@@ -629,6 +681,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
   if (s->heads) {
     GemmRequest hd;
     hd.w = s->heads;
+    hd.packed = true;
     hd.x = s->xn;
     hd.m = B;
     hd.k = D;

@@ -41,12 +41,42 @@ TTS_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: gives up after `limit` polls (each try_wait itself blocks for a
-// hardware-defined interval) and reports false, so no kernel can spin forever.
-TTS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit = (1u << 26)) {
-  for (uint32_t i = 0; i < limit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
+TTS_DEV uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: gives up after ~`limit_ns` of wall time (default 2 s) and reports false, so no
+// kernel can spin forever; the caller records an error flag the host reads.
+TTS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// One lane of a converged warp (elect.sync). Asynchronous tcgen05/TMA/bulk-copy issue belongs
+// to a converged warp with one elected lane: issued from a lone diverged lane, tcgen05.mma ran
+// several times slower on B200 (measured ~220 ns vs ~65 ns per 128x48x16 MMA).
+TTS_DEV bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
+      "elect.sync rx|px, %1;\n\t"
+      "@px mov.s32 %0, 1;\n\t}"
+      : "+r"(pred)
+      : "r"(0xffffffffu));
+  return pred != 0;
+}
+// Bounded wait by every lane of a warp with a warp-uniform result.
+TTS_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity);
+
+TTS_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+  const bool ok = mbar_wait(bar, parity);
+  return __all_sync(0xffffffffu, ok);
 }
 
 // ------------------------------------------------------------------ TMA
@@ -92,6 +122,30 @@ TTS_DEV uint64_t l2_policy_evict_last() {
 // ------------------------------------------------------------------ PDL
 TTS_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 TTS_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// ------------------------------------------------------------------ thread-block clusters
+TTS_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of all CTAs in the cluster; release/acquire orders shared-memory writes.
+TTS_DEV void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Reads 16 bytes at the same shared-memory offset in CTA `rank` of the cluster (DSMEM).
+TTS_DEV float4 ld_dsmem_f4(const void* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
 
 // ------------------------------------------------------------------ tcgen05
 // TMEM allocation is warp-collective; the allocated base address is written to smem.

@@ -47,7 +47,10 @@ struct QkRopeArgs {
 };
 
 struct GemmRequest {
-  const __half* w = nullptr;  // [n][k] (out-major, K contiguous)
+  // [n][k] (out-major, K contiguous), or packed: [n/128][k/64][128][64], each 128 x 64 tile
+  // one contiguous 16 KB block (tts_weight_pack)
+  const __half* w = nullptr;
+  bool packed = false;
   const __half* x = nullptr;  // [m][k]
   int m = 0, k = 0, n = 0;
   int epi = EPI_F32;
@@ -61,11 +64,7 @@ struct GemmRequest {
 };
 
 struct Workspace {
-  float* ws = nullptr;  // split-K partials
-  size_t ws_bytes = 0;
-  unsigned* counters = nullptr;  // per-tile arrival counters (zero between launches)
-  int n_counters = 0;
-  int* err = nullptr;  // device error flags (bounded waits that gave up)
+  int* err = nullptr;  // device error flags (bounded waits that gave up, out-of-range rows)
 };
 
 bool gemm_supported(int m, int k, int n, int epi, std::string* why);

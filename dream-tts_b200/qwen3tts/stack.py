@@ -50,7 +50,9 @@ class Geometry:
 @dataclass
 class LayerTensors:
     """One layer on the device, in the layout the kernels take (qwen3.rs:61-119 does the same
-    folding at load: q/k/v concatenated, 1/sqrt(head_dim) folded into the q norm)."""
+    folding at load: q/k/v concatenated, 1/sqrt(head_dim) folded into the q norm). Projection
+    weights are packed (`ttsnn.pack_weight`); build from plain `[out, in]` tensors with
+    `from_plain` or from checkpoint tensors with `load`."""
     attn_norm: torch.Tensor  # f32 [dim]
     ffn_norm: torch.Tensor   # f32 [dim]
     wqkv: torch.Tensor       # f16 [(heads + 2 n_kv) * hd, dim]
@@ -60,17 +62,23 @@ class LayerTensors:
     w_down: torch.Tensor     # f16 [dim, ffn]
 
     @classmethod
+    def from_plain(cls, attn_norm, ffn_norm, wqkv, qk_norms, wo, w_gate_up, w_down) -> "LayerTensors":
+        """From plain `[out, in]` f16 projections (gate/up already interleaved)."""
+        return cls(attn_norm.to(torch.float32).contiguous(), ffn_norm.to(torch.float32).contiguous(),
+                   ttsnn.pack_weight(wqkv), qk_norms.to(torch.float32).contiguous(),
+                   ttsnn.pack_weight(wo), ttsnn.pack_weight(w_gate_up), ttsnn.pack_weight(w_down))
+
+    @classmethod
     def load(cls, q_proj, k_proj, v_proj, o_proj, gate, up, down, attn_norm, ffn_norm, q_norm,
              k_norm, head_dim: int = 128) -> "LayerTensors":
         """From checkpoint-layout tensors ([out, in] projections), as Layer::load does."""
         dev = q_proj.device
         wqkv = torch.cat([q_proj, k_proj, v_proj], 0).to(torch.float16).contiguous()
         qn = q_norm.to(torch.float32) * (1.0 / head_dim ** 0.5)
-        return cls(attn_norm.to(dev, torch.float32).contiguous(),
-                   ffn_norm.to(dev, torch.float32).contiguous(), wqkv,
-                   torch.stack([qn, k_norm.to(torch.float32)]).to(dev).contiguous(),
-                   o_proj.to(torch.float16).contiguous(),
-                   ttsnn.interleave_gate_up(gate, up), down.to(torch.float16).contiguous())
+        return cls.from_plain(attn_norm.to(dev), ffn_norm.to(dev), wqkv,
+                              torch.stack([qn, k_norm.to(torch.float32)]).to(dev),
+                              o_proj.to(torch.float16), ttsnn.interleave_gate_up(gate, up),
+                              down.to(torch.float16))
 
 
 class PagedKv:
@@ -154,7 +162,8 @@ class Stack:
         self.layers = layers
         self.device = layers[0].wqkv.device
         self.final_norm = final_norm.to(self.device, torch.float32).contiguous()
-        self.heads = None if heads is None else heads.to(torch.float16).contiguous()
+        # heads `[codebooks * vocab, dim]` plain; packed here for the GEMM
+        self.heads = None if heads is None else ttsnn.pack_weight(heads)
         self.embed = None if embed is None else embed.to(torch.float16).contiguous()
         self._ctx = ctx(self.device.index)
         h = C.c_void_p()

@@ -16,7 +16,7 @@ from ._ctx import check, ctx, ctx_of, launch_count, ptr, stream
 from ._lib import TtsError
 from . import attn, fused, nlc, qkrope, topk  # noqa: F401  (submodules mirror tts-nn's)
 
-__all__ = ["Proj", "rms_norm", "rope_table_f32", "abs_and_rel", "TtsError", "check", "ctx",
+__all__ = ["Proj", "pack_weight", "interleave_gate_up", "rms_norm", "rope_table_f32", "abs_and_rel", "TtsError", "check", "ctx",
            "launch_count", "attn", "fused", "nlc", "qkrope", "topk"]
 
 
@@ -29,11 +29,14 @@ class Proj:
     reference's skinny kernel (skinny.rs:155-165).
     """
 
-    def __init__(self, w_out_in: torch.Tensor):
+    def __init__(self, w_out_in: torch.Tensor, packed: bool = True):
         if w_out_in.dim() != 2:
             raise ValueError("Proj: weight must be [out, in]")
-        self.w = w_out_in.to(torch.float16).contiguous()
-        self.n, self.k = self.w.shape
+        w = w_out_in.to(torch.float16).contiguous()
+        self.n, self.k = w.shape
+        # packed: each 128 x 64 tile the GEMM streams is one contiguous block (pack_weight)
+        self.packed = packed and self.n % 128 == 0 and self.k % 64 == 0
+        self.w = pack_weight(w) if self.packed else w
 
     @classmethod
     def from_tensor(cls, t: torch.Tensor, device: torch.device | None = None) -> "Proj":
@@ -61,11 +64,22 @@ class Proj:
                                                         dtype=torch.float16)
         else:
             raise ValueError("Proj: unknown epilogue")
-        L.call("tts_proj_forward", ctx_of(x), ptr(h), rows, self.k, ptr(self.w), self.n,
-               epilogue, ptr(y), 0, stream())
+        L.call("tts_proj_forward_packed" if self.packed else "tts_proj_forward", ctx_of(x),
+               ptr(h), rows, self.k, ptr(self.w), self.n, epilogue, ptr(y), 0, stream())
         return y.reshape(*lead, y.shape[-1]) if epilogue != L.EPI_RESIDUAL_F32 else y
 
     __call__ = forward
+
+
+def pack_weight(w: torch.Tensor) -> torch.Tensor:
+    """`[n, k]` f16 -> the decode GEMM's streaming layout `[n/128][k/64][128][64]` (returned
+    with shape `[n, k]`; only the element order differs). Load-time, like the reference's
+    host-side relayout of every projection (crates/tts-nn/src/lib.rs:1252-1298)."""
+    src = w.to(torch.float16).contiguous()
+    n, k = src.shape
+    out = torch.empty_like(src)
+    L.call("tts_weight_pack", ctx_of(src), ptr(src), n, k, ptr(out), stream())
+    return out
 
 
 def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:

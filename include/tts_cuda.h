@@ -81,6 +81,18 @@ typedef enum tts_epilogue {
 TTS_API tts_status tts_proj_forward(tts_ctx* ctx, const void* x_f16, int m, int k, const void* w_f16,
                             int n, int epilogue, void* y, int ldy, void* stream);
 
+/* Load-time weight layout for the decode GEMM: w [n][k] -> [n/128][k/64][128][64], so each
+ * 128 x 64 tile the kernel streams is one contiguous 16 KB block and a tile's k-blocks follow
+ * each other (DRAM reads stay sequential). The counterpart of the reference's host-side
+ * [out, in] -> [in, out] relayout at load (crates/tts-nn/src/lib.rs:473-489, 1252-1298).
+ * n % 128 == 0, k % 64 == 0; `out` must not alias `w`. */
+TTS_API tts_status tts_weight_pack(tts_ctx* ctx, const void* w_f16, int n, int k, void* out_f16,
+                                   void* stream);
+/* tts_proj_forward with a weight packed by tts_weight_pack. */
+TTS_API tts_status tts_proj_forward_packed(tts_ctx* ctx, const void* x_f16, int m, int k,
+                                           const void* w_packed, int n, int epilogue, void* y,
+                                           int ldy, void* stream);
+
 /* Gate and up projections [ffn][dim] each -> one [2 ffn][dim] weight whose 128-row tiles hold
  * 64 gate rows then the same 64 up rows, the layout TTS_EPI_SWIGLU_F16 consumes. Load-time
  * step, the counterpart of the q/k/v concatenation in crates/qwen3tts/src/qwen3.rs:70-77. */
@@ -145,8 +157,8 @@ TTS_API tts_status tts_decode_attention(tts_ctx* ctx, const float* q, int lanes,
  * and cannot let a library allocate behind its back. It needs no tts_ctx (creating one
  * allocates) and calls no allocator: its scratch is one fixed device array inside the library,
  * 4 MiB of split-KV partials plus 4096 arrival counters, which every GPU that loads the library
- * holds until the process exits. Limits: lanes * n_kv * ceil(max_span / 256) * gqa * 520 bytes
- * must fit in 4 MiB (e.g. 48 lanes x 8 kv heads x gqa 2 up to max_span 2048) and
+ * holds until the process exits. Limits: lanes * n_kv * ceil(max_span / 128) * gqa * 520 bytes
+ * must fit in 4 MiB (e.g. 48 lanes x 8 kv heads x gqa 2 up to max_span 1280) and
  * lanes * n_kv <= 4096; larger requests return TTS_ERR_UNSUPPORTED_SHAPE. The first call on a
  * device looks up the array's device address with that device current, so make the first call
  * before any stream capture. All calls share the array and it keeps the last call's contents:
@@ -192,6 +204,7 @@ typedef struct tts_stack_geometry {
 typedef struct tts_layer_weights {
   const float* attn_norm; /* [dim] */
   const float* ffn_norm;  /* [dim] */
+  /* projection weights are packed by tts_weight_pack */
   const void* wqkv;       /* f16 [(heads + 2 n_kv) * head_dim][dim], q/k/v rows concatenated */
   const float* qk_norms;  /* [2][head_dim]: q_norm * 1/sqrt(head_dim), k_norm (qwen3.rs:82-87) */
   const void* wo;         /* f16 [dim][heads * head_dim] */
@@ -201,7 +214,7 @@ typedef struct tts_layer_weights {
 
 TTS_API tts_status tts_stack_create(tts_ctx* ctx, const tts_stack_geometry* geo, tts_stack** out);
 TTS_API tts_status tts_stack_set_layer(tts_stack* s, int layer, const tts_layer_weights* w);
-/* final_norm f32 [dim]; heads f16 [codebooks * vocab][dim] (NULL = none); embed f16
+/* final_norm f32 [dim]; heads f16 [codebooks * vocab][dim] packed (NULL = none); embed f16
  * [codebooks][vocab][dim] (NULL = none), the tables whose rows for the picked codes are summed
  * into the next step's input. */
 TTS_API tts_status tts_stack_set_head(tts_stack* s, const float* final_norm, const void* heads_f16,

@@ -59,10 +59,10 @@ def device_stack(orc, g, layers, final, heads=None, embed=None, rope_len=4096):
                    vocab=g.vocab if heads is not None else 0)
     lts = []
     for L in layers:
-        lts.append(LayerTensors(dev_f32(L.attn_norm), dev_f32(L.ffn_norm), dev_f16(L.wqkv),
-                                dev_f32(L.qk_norms), dev_f16(L.wo),
-                                ttsnn.interleave_gate_up(dev_f16(L.gate), dev_f16(L.up)),
-                                dev_f16(L.down)))
+        lts.append(LayerTensors.from_plain(dev_f32(L.attn_norm), dev_f32(L.ffn_norm), dev_f16(L.wqkv),
+                                           dev_f32(L.qk_norms), dev_f16(L.wo),
+                                           ttsnn.interleave_gate_up(dev_f16(L.gate), dev_f16(L.up)),
+                                           dev_f16(L.down)))
     return Stack(geo, lts, dev_f32(final), None if heads is None else dev_f16(heads),
                  None if embed is None else dev_f16(embed))
 
