@@ -163,7 +163,7 @@ class Clocks:
                 "samples": len(rows)}
 
 
-def build_device_talker(device, seed=0, extra_positions=256):
+def build_device_talker(device, seed=0, extra_positions=256, lanes_override=None):
     import torch
     import ttsnn
     from qwen3tts import Geometry, LayerTensors, PagedKv, Stack
@@ -173,7 +173,7 @@ def build_device_talker(device, seed=0, extra_positions=256):
         return (torch.randn(n, k, generator=gen, device=device) * 0.02).half()
 
     geo = Geometry(dim=DIM, layers=LAYERS, heads=HEADS, n_kv=N_KV, head_dim=HD, ffn=FFN,
-                   rope_len=KV_HI + extra_positions + 64, codebooks=CB, vocab=VOCAB)
+                   rope_len=max(KV_HI + extra_positions + 64, 1600), codebooks=CB, vocab=VOCAB)
     ones = torch.ones(DIM, device=device)
     qk = torch.stack([torch.full((HD,), 1.0 / HD ** 0.5, device=device), torch.ones(HD, device=device)])
     layers = []
@@ -185,6 +185,8 @@ def build_device_talker(device, seed=0, extra_positions=256):
     heads = w(CB * VOCAB, DIM)
     embed = (torch.randn(CB, VOCAB, DIM, generator=gen, device=device) * 0.02).half()
     stack = Stack(geo, layers, ones, heads, embed)
+    if lanes_override == 0:
+        return stack, None, None, None
     lengths = kv_lengths(seed)
     cap = KV_HI + extra_positions
     per_lane = -(-cap // BLOCK)
@@ -279,6 +281,57 @@ def time_codec_block(device, reps=5):
     b, t, c = x.shape
     flops = 3 * 2 * b * t * c * c * 7
     return sec, flops
+
+
+def run_sweep(args):
+    """a document of segments with target lengths log-uniform in [40, 1200]
+    frames, grouped longest-first into runs of `--lanes` lanes, groups split over the ranks by
+    LPT (no collective on the data path), each rank decoding its shard with tail shedding
+    (`--refill` reuses finished lanes). frames/s = all frames / max over ranks of device time."""
+    import torch
+    import torch.distributed as dist
+    from qwen3tts.talker import Talker, plan_groups, shard_groups, synthetic_segments
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    n_segments = args.segments * world
+    segs = synthetic_segments(n_segments, seed=0)
+    groups = plan_groups(segs, args.lanes)
+    mine = shard_groups(groups, world)[rank]
+    queue = [s for g in mine for s in g]
+    stack, _, _, _ = build_device_talker(device, seed=0, extra_positions=0, lanes_override=0)
+    cap = 157 + 1200 + 2
+    talker = Talker(stack, max_lanes=args.lanes, capacity=cap)
+    # warm-up: capture the graphs of every width this shard will use on a short copy
+    talker.run([type(s)(s.index, s.prompt_len, min(s.frames, 2), 0) for s in queue[: args.lanes]])
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    st = talker.run(queue, refill=args.refill)
+    t = torch.tensor([st.seconds, st.frames, st.lane_steps], device=device, dtype=torch.float64)
+    if world > 1:
+        tmax = t.clone()
+        dist.all_reduce(tmax[:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(t[1:], op=dist.ReduceOp.SUM)
+        t[0] = tmax[0]
+    secs, frames, lane_steps = float(t[0]), int(t[1]), int(t[2])
+    if rank == 0:
+        line = {"metric": "codec frames/sec (lane sweep, whole box)", "value": round(frames / secs, 2),
+                "unit": "frames/s", "n_gpus": world, "higher_is_better": True, "scaling": "weak",
+                "dtype": "f16", "data": "synthetic",
+                "config": {"workload": "config[3]: talker lane sweep, segments log-U[40,1200] frames, "
+                                       "prompt 157, longest-first groups, tail shedding"
+                                       + (" + interior refill" if args.refill else ""),
+                           "lanes": args.lanes, "segments": n_segments, "refill": bool(args.refill)},
+                "frames": frames, "seconds": round(secs, 4), "useful_lane_step_fraction":
+                    round(frames / max(1, lane_steps), 4), "rtf": round(secs / (frames / 12.5), 5)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
 
 
 def run_kernel_case(args):
@@ -474,6 +527,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--workload", default="step", choices=["step", "sweep"],
+                    help="step: the config[2] decode step (headline); sweep: config[3]")
+    ap.add_argument("--lanes", type=int, default=48)
+    ap.add_argument("--segments", type=int, default=96, help="segments per GPU (sweep)")
+    ap.add_argument("--refill", action="store_true")
     ap.add_argument("--kernel", choices=["gemm", "attn", "conv"],
                     help="run a small standalone case of one kernel (for ncu captures)")
     args = ap.parse_args()
@@ -483,6 +541,8 @@ def main():
         return run_reference(args)
     if args.kernel:
         return run_kernel_case(args)
+    if args.workload == "sweep":
+        return run_sweep(args)
     return run_b200(args)
 
 

@@ -59,7 +59,8 @@ struct tts_stack {
   float* q = nullptr;         // [max_lanes][heads][head_dim]
   __half* attn = nullptr;     // [max_lanes][heads * head_dim]
   __half* act = nullptr;      // [max_lanes][ffn]
-  float* x_next = nullptr;    // [max_lanes][dim]
+  float* x_next = nullptr;    // [max_lanes][dim] (own buffer)
+  float* feedback = nullptr;  // caller's buffer replacing x_next, or null
   unsigned long long* keys = nullptr;  // [max_lanes][codebooks]
 };
 
@@ -541,6 +542,12 @@ tts_status tts_stack_set_head(tts_stack* s, const float* final_norm, const void*
   return TTS_OK;
 }
 
+tts_status tts_stack_set_feedback(tts_stack* s, float* x_next) {
+  if (!s) return fail(TTS_ERR_INVALID_ARG, "stack_set_feedback: stack is NULL");
+  s->feedback = x_next;
+  return TTS_OK;
+}
+
 tts_status tts_stack_destroy(tts_stack* s) {
   if (!s) return TTS_OK;
   DeviceGuard g(s->ctx->device);
@@ -583,7 +590,8 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
       return rc;                              \
   } while (0)
 
-  const float* src = x ? x : s->x_next;
+  float* next = s->feedback ? s->feedback : s->x_next;
+  const float* src = x ? x : next;
   if ((rc = cuda_status(cudaMemcpyAsync(s->h, src, size_t(B) * D * 4, cudaMemcpyDeviceToDevice, cs),
                         "decode_step")) != TTS_OK)
     return rc;
@@ -692,7 +700,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     hd.vocab = gm.vocab;
     TTS_TRY(launch_gemm(hd, c->gemm, cs, c->device), "proj");
     TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, s->embed, D, codes,
-                                 s->embed ? s->x_next : nullptr, nullptr, true, cs),
+                                 s->embed ? next : nullptr, nullptr, true, cs),
             "keys_to_codes");
   }
   TTS_TRY(launch_advance_positions(st->positions, B, true, cs), "advance_positions");

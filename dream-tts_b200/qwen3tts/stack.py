@@ -177,6 +177,11 @@ class Stack:
             L.call("tts_stack_set_layer", h, i, C.byref(w))
         L.call("tts_stack_set_head", h, ptr(self.final_norm), ptr(self.heads), ptr(self.embed))
 
+    def set_feedback(self, x_next: torch.Tensor | None) -> None:
+        """Use `x_next` ([lanes, dim] f32, caller-owned) as the step's feedback input buffer."""
+        self._feedback = x_next
+        L.call("tts_stack_set_feedback", self.handle, ptr(x_next))
+
     def weight_bytes(self) -> int:
         n = 0
         for lt in self.layers:

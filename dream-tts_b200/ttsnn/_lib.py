@@ -76,6 +76,7 @@ SIGNATURES = {
     "tts_stack_create": [P, C.POINTER(StackGeometry), C.POINTER(P)],
     "tts_stack_set_layer": [P, I, C.POINTER(LayerWeights)],
     "tts_stack_set_head": [P, P, P, P],
+    "tts_stack_set_feedback": [P, P],
     "tts_stack_destroy": [P],
     "tts_stack_decode_step": [P, C.POINTER(DecodeState), P, P, P, P, P],
     "tts_stack_graph_capture": [P, C.POINTER(DecodeState), P, P, P, P, P, C.POINTER(P)],

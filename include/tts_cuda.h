@@ -219,6 +219,11 @@ TTS_API tts_status tts_stack_set_layer(tts_stack* s, int layer, const tts_layer_
  * into the next step's input. */
 TTS_API tts_status tts_stack_set_head(tts_stack* s, const float* final_norm, const void* heads_f16,
                               const void* embed_f16);
+/* The buffer f32 [max_lanes][dim] the step writes the next input into (the sum of the picked
+ * codes' embedding rows) and reads when x is NULL. Caller-owned; NULL restores the stack's own
+ * buffer. Writing a lane's row restarts that lane from a new state (a lane slot reused by the
+ * next segment). */
+TTS_API tts_status tts_stack_set_feedback(tts_stack* s, float* x_next);
 TTS_API tts_status tts_stack_destroy(tts_stack* s);
 
 /* Decode-time cache state of one group of lanes, all layers: pages f16
