@@ -1,4 +1,4 @@
-"""Benchmark: qwen3tts talker decode on B200 — codec frames/s at 48 lanes.
+"""Benchmark: qwen3tts talker decode on B200 — codec frames/s at 48 lanes (benchmark config[2]).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -238,7 +238,7 @@ def bf16_peak():
 
 
 def build_codec_block(device, b=8, t=24000, c=512, seed=0):
-    """BASELINE config[1]: x [8, 512, 24000] f16 ~N(0,1) held channels-last [8, 24000, 512];
+    """Benchmark config[1]: x [8, 512, 24000] f16 ~N(0,1) held channels-last [8, 24000, 512];
     per dilation 1, 3, 9: x = x + conv_k7(snake(x)) with 'same' padding, alpha = exp(U(-1,1)),
     Snake's 1/alpha, weights ~N(0, 0.02), bias 0."""
     import torch
@@ -284,7 +284,7 @@ def time_codec_block(device, reps=5):
 
 
 def run_sweep(args):
-    """a document of segments with target lengths log-uniform in [40, 1200]
+    """Benchmark config[3]: a document of segments with target lengths log-uniform in [40, 1200]
     frames, grouped longest-first into runs of `--lanes` lanes, groups split over the ranks by
     LPT (no collective on the data path), each rank decoding its shard with tail shedding
     (`--refill` reuses finished lanes). frames/s = all frames / max over ranks of device time."""

@@ -282,7 +282,6 @@ bool conv_supported(const ConvRequest& r, std::string* why) {
   if (r.b < 1 || r.len < 1) return no("empty input");
   if (r.cin < kCB || r.cin % kCB) return no("cin must be a positive multiple of 64");
   if (r.cout < 32 || r.cout % 32) return no("cout must be a positive multiple of 32");
-  if (r.cout > 512 && r.cout % 512) return no("cout above 512 must be a multiple of 512");
   if (r.k < 1 || r.dil < 1) return no("k and dilation must be >= 1");
   if ((r.k - 1) * r.dil > 128) return no("(k - 1) * dilation must be <= 128");
   if (r.pad_left < 0 || r.pad_left > (r.k - 1) * r.dil)
@@ -310,7 +309,17 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
   a.k = r.k;
   a.dil = r.dil;
   a.pad_left = r.pad_left;
-  a.cout_cta = std::min(r.cout, 512);
+  // output channels per CTA: all of them up to 512, else the largest of 512/256/128/64/32
+  // that divides cout
+  a.cout_cta = r.cout;
+  if (r.cout > 512) {
+    a.cout_cta = 32;
+    for (int c : {512, 256, 128, 64})
+      if (r.cout % c == 0) {
+        a.cout_cta = c;
+        break;
+      }
+  }
   a.nh = a.cout_cta > 256 ? 2 : 1;
   a.nper = a.cout_cta / a.nh;
   a.R = (kRows + (r.k - 1) * r.dil + 7) / 8 * 8;

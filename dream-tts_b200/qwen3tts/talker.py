@@ -14,7 +14,7 @@ SHED_QUANTUM). Device-side differences, by design:
     decides lane completion from the segment targets without reading the device every step.
 
 Random-init weights never emit the end code, so a segment's end is its drawn target length
-(log-uniform in [40, 1200] frames), i.e. the end code is forced there.
+(the synthetic lane sweep: log-uniform in [40, 1200] frames), i.e. the end code is forced there.
 """
 from __future__ import annotations
 
@@ -37,7 +37,7 @@ class Segment:
 
 def synthetic_segments(n: int, seed: int = 0, lo: int = 40, hi: int = 1200,
                        prompt_len: int = 157) -> list[Segment]:
-    """BASELINE config[3]/[4]: target lengths log-uniform in [lo, hi] frames, one prompt width
+    """The synthetic sweep and document: target lengths log-uniform in [lo, hi] frames, one prompt width
     (157, the reference ICL width recorded in fixtures/qwen3tts/oracle.json)."""
     rng = np.random.default_rng(seed)
     f = np.exp(rng.uniform(math.log(lo), math.log(hi), n)).astype(int)

@@ -183,7 +183,7 @@ TTS_API tts_status tts_argmax(tts_ctx* ctx, const float* logits, int rows, int n
  *               (+ res[b, l, co]),   rows outside [0, len) read as zero,
  * s(x) = x + brecip * sin(alpha * x)^2 when alpha is given (SnakeBeta on load), else x.
  * x, res, y f16 channels-last; w f16 [cout][k][cin]; bias/alpha/brecip f32 (nullable).
- * cin % 64 == 0, cout % 128 == 0 and <= 512, k * dil <= 128. */
+ * cin % 64 == 0, cout % 32 == 0, (k - 1) * dil <= 128, 0 <= pad_left <= (k - 1) * dil. */
 TTS_API tts_status tts_conv1d_nlc(tts_ctx* ctx, const void* x_f16, int b, int len, int cin,
                           const void* w_f16, int cout, int k, int dilation, int pad_left,
                           const float* bias, const float* alpha, const float* brecip,

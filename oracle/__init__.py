@@ -209,7 +209,7 @@ class Layer:
 
 
 def synthetic_layer(rng: np.random.Generator, g: Geometry) -> Layer:
-    """Seeded random-init layer with the distributions BASELINE's configs name: projections
+    """Seeded random-init layer with the distributions the benchmark configs name: projections
     ~N(0, 0.02) as f16, norm weights near 1, 1/sqrt(head_dim) folded into the q norm."""
     dim, hd = g.dim, g.head_dim
     nq = (g.heads + 2 * g.n_kv) * hd

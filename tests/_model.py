@@ -1,6 +1,6 @@
 """Seeded synthetic talker weights and decode state shared by the oracle and GPU tests.
 
-random-init f16 projection weights ~N(0, 0.02), norm weights near 1,
+Benchmark config[2]: random-init f16 projection weights ~N(0, 0.02), norm weights near 1,
 KV caches prefilled ~N(0, 1), lane lengths per test. No checkpoint exists in this image.
 """
 from __future__ import annotations

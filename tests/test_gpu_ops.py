@@ -1,6 +1,6 @@
 """Per-operator parity on a B200: each C-ABI op against the CPU oracle on the same seeded
 inputs. Shapes follow the reference's own tests (cited per test). Tolerances are stated per
-test; BASELINE's bar for f16 ops is max relative error <= 2e-2."""
+test; the bar for f16 ops is max relative error <= 2e-2."""
 import numpy as np
 import pytest
 import torch

@@ -101,7 +101,7 @@ def test_step_graph_replay_matches_eager(tt, orc):
 
 
 def test_step_config2_48_lanes_28_layers(tt, orc):
-    """BASELINE config[2] geometry: 28 layers, 48 lanes, 16 heads x 2048; KV lengths drawn
+    """Benchmark config[2] geometry: 28 layers, 48 lanes, 16 heads x 2048; KV lengths drawn
     uniformly in [64, 320] (the oracle's contiguous caches bound the host memory of this test;
     the long-span path is covered above and in the attention tests)."""
     lengths = np.random.default_rng(7).integers(64, 321, 48)
