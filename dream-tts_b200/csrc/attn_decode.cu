@@ -1,4 +1,4 @@
-// Paged decode attention (GQA, head_dim 128, f16 KV pages, f32 math).
+// Paged decode attention on the tensor cores (GQA, head_dim 128, f16 KV pages, f32 results).
 //
 // The B200 form of tts-nn's `attn::decode_attention` (crates/tts-nn/src/attn.rs:22-73; its
 // CPU loops attn.rs:90-126 and 203-238, Metal `decode_attn_f16`): softmax(q . K^T) . V over
@@ -6,15 +6,25 @@
 // (the reference uses one span for the whole batch) let lanes of different lengths share a
 // step, which is what a paged cache is for.
 //
-// Work unit: one CTA per (chunk of 128 positions, kv head, lane). Both query heads of a kv head
-// are served from one read of each K/V row. The CTA first stages its chunk's K and V rows
-// (64 KB) into shared memory with bulk async copies completing on one mbarrier, so the whole
-// chunk is in flight at once and three CTAs per SM keep ~192 KB of reads outstanding. Then
-// eight half-warps each take 16 consecutive positions; each of their 16 lanes owns 8 of the 128
-// dims (one 16-byte shared load per row). Scores, the running max and the exp-rescaled sums
-// are kept per half-warp, combined across half-warps in shared memory, and, when a lane's span
-// needs several chunks, written as partials that the last CTA of that (lane, kv head) merges in
-// chunk order (deterministic).
+// Work: each (lane, kv head) pair's positions are cut into 128-position chunks; all chunks of
+// all pairs form one list (lane-major, then kv head, then chunk) that is split into equal
+// contiguous ranges, one per CTA, with one persistent CTA per SM. A CTA walks its range with
+// three kinds of warps tied together by mbarriers:
+//   * warp 4 (loader) stages each chunk's K and V tiles into three-deep rings with TMA
+//     (128-byte swizzle, one box per run of a page), reading the block table one chunk ahead;
+//   * warp 5 (MMA) issues S = K . Q^T (M = 128 positions, N = 16, K = 128 dims) and
+//     O^T = V^T . P^T (M = 128 dims, N = 16, K = 128 positions) on tcgen05, f32 accumulators
+//     double-buffered in TMEM, the scores of the next chunk ahead of the values of this one.
+//     The N = 16 columns hold each query head twice, as an f16 high part and a scaled f16 low
+//     part (q = hi + lo / 2048, likewise p), so the products keep f32-level accuracy;
+//   * warps 0-3 (softmax) take one position each for the scores and one output dim each for the
+//     values: running max, exp, P written back to shared memory for the MMA warp, and the
+//     running sum and output (folded in one chunk late, when that chunk's values are long done).
+// A pair wholly inside one CTA writes its output directly. A CTA's first and last segments may
+// hold only part of a pair: the softmax warps write a partial (o, max, sum) and hand it to warp
+// 6 (epilogue), which counts the pair's arrived chunks and, in the CTA that completes the pair,
+// merges the segments in chunk order, so results are deterministic and the softmax warps never
+// wait on a global fence or atomic.
 #include <cstdio>
 #include <mutex>
 
@@ -25,25 +35,31 @@ namespace tts {
 
 namespace {
 
-constexpr int kChunk = 128;  // positions per CTA
-constexpr int kHalfWarps = 8;
-constexpr int kPerHalf = kChunk / kHalfWarps;  // 16
-constexpr int kGroup = 8;                      // rows per inner iteration
-constexpr int kMaxPages = kChunk + 1;          // pages one chunk can touch (block_size 1)
-constexpr int kMaxChunks = 64;                 // 8192 positions
+constexpr int kChunk = 128;      // positions per chunk (the MMA's M for S)
+constexpr int kStages = 3;       // K and V ring depth
+constexpr int kSoftmax = 128;    // warps 0-3: one TMEM lane quarter each
+constexpr int kLoaderWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kEpiWarp = 6;
+constexpr int kThreads = 224;
+constexpr int kMaxChunks = 64;   // 8192 positions
+constexpr int kMaxLanes = 512;
+constexpr int kN = 16;           // MMA N: GQA high rows, GQA low rows, zero padding
+constexpr float kLo = 2048.f;    // scale of the low f16 parts
+constexpr uint32_t kBarSoftmax = 1;  // named barrier: softmax warps
+constexpr uint32_t kBarTmem = 2;     // named barrier: softmax + MMA warps (TMEM release)
 
 struct AttnArgs {
   const float* q;
-  const __half* k;
-  const __half* v;
   const int* bt;
   int max_blocks, bs, num_blocks;
   int max_span;
+  int box_rows;  // rows per TMA box: divides bs, or 128 when each lane has one page
   int* err;
   const int* spans;
   int span_add;
   int window;
-  int n_kv;
+  int lanes, n_kv;
   int max_chunks;
   float* part;  // [lanes][n_kv][max_chunks][GQA][130]: 128 o, m, l
   unsigned* counters;
@@ -51,292 +67,649 @@ struct AttnArgs {
   int out_f16;
 };
 
-// Dynamic shared memory of one CTA: the chunk's K and V rows (64 KB), the half-warp partials
-// and the merge scratch.
-struct AttnSmem {
-  __half k[kChunk][128];
-  __half v[kChunk][128];
-  float acc[kHalfWarps][2][128];
-  float m[kHalfWarps][2];
-  float l[kHalfWarps][2];
-  float cm[kMaxChunks][2];
-  float cl[kMaxChunks][2];
-  int page[kMaxPages];
-  uint64_t bar;
-  int last;
+// One K or V tile of a chunk: dims 0-63 / 64-127, each 128 rows x 128 B, 128-byte swizzle.
+struct __align__(1024) Tile {
+  uint8_t d[2][kChunk * 128];
 };
 
-TTS_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
+struct AttnSmem {
+  Tile kt[kStages];
+  Tile vt[kStages];
+  uint8_t qb[2][2][kN * 128];  // B of S per segment parity: q hi/lo rows, K-major, swizzled
+  uint8_t pb[2][2][kN * 128];  // B of O per item parity: p hi/lo rows over the positions
+  float red_max[2][4][8];
+  float red_sum[2][4][8];
+  uint64_t full_k[kStages], full_v[kStages], empty_k[kStages], empty_v[kStages];
+  uint64_t s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2], q_full[2];
+  uint64_t seg_done[2];  // partial segment k written (every softmax thread arrives)
+  struct {
+    int b, h, c_first, len;
+  } seg_info[2];
+  uint32_t inv_k[kStages];  // boxes of the tile whose page is outside the pool
+  uint32_t inv_v[kStages];
+  uint32_t tmem;
+  int last;
+  int span[kMaxLanes];
+  int cnt[kMaxLanes];         // chunk-list items of each lane (chunks x n_kv)
+  int prefix[kMaxLanes + 1];  // chunk-list offset of each lane
+};
+
+// Byte offset of element (row r, column e < 64) in a K-major tile of 128-byte rows written
+// with the 128-byte swizzle (16-byte chunk index XOR row mod 8).
+TTS_DEV uint32_t sw128(int r, int e) {
+  return uint32_t(r) * 128u + ((uint32_t((e >> 3) ^ (r & 7))) << 4) + uint32_t(e & 7) * 2u;
+}
+
+// Position range of one lane: [ws, span), chunks start at c0 (ws rounded down to 128).
+struct LaneRange {
+  int span, ws, c0, nch;
+};
+TTS_DEV LaneRange lane_range(int span, int window) {
+  LaneRange r;
+  r.span = span;
+  r.ws = (window > 0 && span > window) ? span - window : 0;
+  r.c0 = (r.ws / kChunk) * kChunk;
+  r.nch = (span - r.c0 + kChunk - 1) / kChunk;
+  return r;
+}
+
+// A place in a CTA's walk over the chunk list: lane, kv head, chunk, and a counter of the
+// (lane, kv head) segments started so far.
+struct Cursor {
+  int b, h, c, seg;
+  LaneRange lr;
+};
+TTS_DEV void cursor_next(Cursor& x, const int* span, const AttnArgs& a) {
+  if (++x.c == x.lr.nch) {
+    x.c = 0;
+    ++x.seg;
+    if (++x.h == a.n_kv) {
+      x.h = 0;
+      if (x.b + 1 < a.lanes) {
+        ++x.b;
+        x.lr = lane_range(span[x.b], a.window);
+      }
+    }
+  }
+}
+// Rows [vlo, vhi) of the cursor's chunk hold positions of the lane's range.
+TTS_DEV void chunk_rows(const Cursor& x, int& vlo, int& vhi) {
+  const int p0 = x.lr.c0 + x.c * kChunk;
+  vlo = max(x.lr.ws - p0, 0);
+  vhi = min(x.lr.span - p0, kChunk);
+}
+
+// Which CTA of `grid` owns item x of a list of `total` split as [total*i/grid, total*(i+1)/grid).
+TTS_DEV int owner_of(long long x, long long total, int grid) {
+  return int(((x + 1) * grid + total - 1) / total) - 1;
+}
+
+// Zeroes rows of a K or V tile: rows outside [vlo, vhi), and rows of boxes flagged in `inv`
+// (pages outside the pool). Thread `tid` of a group of `n` takes every n-th 16-byte piece.
+TTS_DEV void zero_rows(Tile& tile, int vlo, int vhi, uint32_t inv, int box, int tid, int n) {
+  const int r0 = (vlo / box) * box;
+  for (int u = tid; u < kChunk * 16; u += n) {
+    const int r = u >> 4;
+    const bool bad = r < vlo || r >= vhi || (inv && r >= r0 && ((inv >> ((r - r0) / box)) & 1u));
+    if (bad)
+      *reinterpret_cast<uint4*>(&tile.d[(u >> 3) & 1][r * 128 + (u & 7) * 16]) =
+          make_uint4(0, 0, 0, 0);
+  }
 }
 
 template <int GQA>
-__global__ void __launch_bounds__(128, 3) attn_decode_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_decode_kernel(const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
-  AttnSmem& S = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) &
-                                             ~uintptr_t(127));
-  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  AttnSmem& S = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   pdl_launch_dependents();
-  pdl_wait();
 
-  // Spans and page numbers are device data: clamp to what the grid, the block table and the
-  // pool cover, and flag anything outside instead of reading out of bounds.
-  int span = a.spans[b] + a.span_add;
-  const int lim = min(a.max_blocks * a.bs, a.max_span);
-  if (span < 1 || span > lim) {
-    if (threadIdx.x == 0 && c == 0 && a.err) atomicOr(a.err, 512);
-    span = max(1, min(span, lim));
-  }
-  const int ws = (a.window > 0 && span > a.window) ? span - a.window : 0;
-  const int nch = (span - ws + kChunk - 1) / kChunk;
-  if (c >= nch) return;
-  const int p0 = ws + c * kChunk;
-  const int p1 = min(p0 + kChunk, span);
-  const int pg0 = p0 / a.bs, npg = (p1 - 1) / a.bs - pg0 + 1;
-  const int t = threadIdx.x;
-
-  // ---- stage the chunk's K and V rows into shared memory with bulk copies (one barrier)
-  const int* bt = a.bt + (size_t)b * a.max_blocks;
-  for (int i = t; i < npg; i += 128) {
-    const int blk = bt[pg0 + i];
-    S.page[i] = (blk >= 0 && blk < a.num_blocks) ? blk : -1;
-  }
-  if (t == 0) {
-    mbar_init(&S.bar, 1);
+  if (warp == kLoaderWarp && lane == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&S.full_k[s], 1);
+      mbar_init(&S.full_v[s], 1);
+      mbar_init(&S.empty_k[s], 1);
+      mbar_init(&S.empty_v[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&S.s_full[i], 1);
+      mbar_init(&S.o_full[i], 1);
+      mbar_init(&S.s_empty[i], 4);  // one arrival per softmax warp
+      mbar_init(&S.p_full[i], 4);
+      mbar_init(&S.o_empty[i], 4);
+      mbar_init(&S.q_full[i], 4);
+      mbar_init(&S.seg_done[i], kSoftmax);
+    }
     fence_barrier_init();
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
   }
-  __syncthreads();  // barrier initialised, page table visible
-  if (t < 32) {
-    // warp 0, converged: one elected lane arms the barrier with the chunk's byte count, then
-    // each lane issues the copies of its pages
-    uint32_t bytes = 0;
-    for (int i = t; i < npg; i += 32) {
-      const int r0 = max(p0, (pg0 + i) * a.bs), r1 = min(p1, (pg0 + i + 1) * a.bs);
-      if (S.page[i] >= 0) bytes += uint32_t(r1 - r0) * 512u;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
-    if (elect_one()) mbar_arrive_expect_tx(&S.bar, bytes);
-    __syncwarp();
-    for (int i = t; i < npg; i += 32) {
-      if (S.page[i] < 0) continue;
-      const int r0 = max(p0, (pg0 + i) * a.bs), r1 = min(p1, (pg0 + i + 1) * a.bs);
-      const size_t src = (((size_t)S.page[i] * a.n_kv + h) * a.bs + (r0 - (pg0 + i) * a.bs)) * 128;
-      bulk_g2s(&S.k[r0 - p0][0], a.k + src, uint32_t(r1 - r0) * 256u, &S.bar);
-      bulk_g2s(&S.v[r0 - p0][0], a.v + src, uint32_t(r1 - r0) * 256u, &S.bar);
-    }
-    __syncwarp();
+  if (warp == kMmaWarp) {
+    tmem_alloc(&S.tmem, 64);
+    tmem_relinquish();
+    tc_fence_before();
   }
-  // rows of pages outside the pool read as zero (and are reported)
-  for (int i = 0; i < npg; ++i) {
-    if (S.page[i] >= 0) continue;
-    const int r0 = max(p0, (pg0 + i) * a.bs), r1 = min(p1, (pg0 + i + 1) * a.bs);
-    if (t == 0 && a.err) atomicOr(a.err, 1024);
-    for (int e = t; e < (r1 - r0) * 16; e += 128) {
-      reinterpret_cast<uint4*>(&S.k[r0 - p0][0])[e] = make_uint4(0, 0, 0, 0);
-      reinterpret_cast<uint4*>(&S.v[r0 - p0][0])[e] = make_uint4(0, 0, 0, 0);
-    }
-  }
+  // zero the B tiles once: rows past 2 * GQA stay zero for the whole kernel
+  for (int i = t; i < int(sizeof(S.qb) + sizeof(S.pb)) / 16; i += kThreads)
+    reinterpret_cast<uint4*>(&S.qb[0][0][0])[i] = make_uint4(0, 0, 0, 0);
 
-  const int lane = t & 31, warp = t >> 5;
-  const int hw = warp * 2 + (lane >> 4);
-  const int j = lane & 15;
-  const int heads = a.n_kv * GQA;
-  float qv[GQA][8];
-#pragma unroll
-  for (int g = 0; g < GQA; ++g) {
-    const float4* qp =
-        reinterpret_cast<const float4*>(a.q + ((size_t)b * heads + h * GQA + g) * 128 + 8 * j);
-    const float4 x0 = qp[0], x1 = qp[1];
-    qv[g][0] = x0.x; qv[g][1] = x0.y; qv[g][2] = x0.z; qv[g][3] = x0.w;
-    qv[g][4] = x1.x; qv[g][5] = x1.y; qv[g][6] = x1.z; qv[g][7] = x1.w;
-  }
-  float m[GQA], l[GQA], acc[GQA][8];
-#pragma unroll
-  for (int g = 0; g < GQA; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.f;
-#pragma unroll
-    for (int d = 0; d < 8; ++d) acc[g][d] = 0.f;
-  }
-  __syncthreads();  // zero-filled rows visible
-  if (!mbar_wait(&S.bar, 0) && t == 0 && a.err) atomicOr(a.err, 2048);
-
-  const int rows = p1 - p0;
-  const int q0 = hw * kPerHalf;
-  const int q1 = min(q0 + kPerHalf, rows);
-  // The trip count is the same for both half-warps of a warp (their shuffles use the full
-  // mask); rows past a half-warp's own range are masked instead.
-  for (int it = 0; it < kPerHalf; it += kGroup) {
-    const int pg = q0 + it;
-    if (__all_sync(0xffffffffu, pg >= q1)) break;
-    float kf[kGroup][8], vf[kGroup][8];
-#pragma unroll
-    for (int u = 0; u < kGroup; ++u) {
-      // rows past this half-warp's range hold stale shared memory (possibly NaN patterns):
-      // read zeros instead, so a masked row contributes exactly nothing
-      const bool valid = pg + u < q1;
-      const int p = valid ? pg + u : 0;
-      uint4 ku = *reinterpret_cast<const uint4*>(&S.k[p][8 * j]);
-      uint4 vu = *reinterpret_cast<const uint4*>(&S.v[p][8 * j]);
-      if (!valid) ku = vu = make_uint4(0, 0, 0, 0);
-      const __half2* kh = reinterpret_cast<const __half2*>(&ku);
-      const __half2* vh = reinterpret_cast<const __half2*>(&vu);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 kk = __half22float2(kh[i]);
-        const float2 vv = __half22float2(vh[i]);
-        kf[u][2 * i] = kk.x;
-        kf[u][2 * i + 1] = kk.y;
-        vf[u][2 * i] = vv.x;
-        vf[u][2 * i + 1] = vv.y;
-      }
+  pdl_wait();
+  // ---- spans and the chunk-list offsets of every lane
+  for (int b = t; b < a.lanes; b += kThreads) {
+    int span = a.spans[b] + a.span_add;
+    const int lim = min(a.max_blocks * a.bs, a.max_span);
+    if (span < 1 || span > lim) {
+      if (a.err && blockIdx.x == 0) atomicOr(a.err, kFlagSpanRange);
+      span = max(1, min(span, lim));
     }
-#pragma unroll
-    for (int g = 0; g < GQA; ++g) {
-      float s[kGroup];
-#pragma unroll
-      for (int u = 0; u < kGroup; ++u) {
-        float tt = 0.f;
-#pragma unroll
-        for (int d = 0; d < 8; ++d) tt += qv[g][d] * kf[u][d];
-        tt += __shfl_xor_sync(0xffffffffu, tt, 8);
-        tt += __shfl_xor_sync(0xffffffffu, tt, 4);
-        tt += __shfl_xor_sync(0xffffffffu, tt, 2);
-        tt += __shfl_xor_sync(0xffffffffu, tt, 1);
-        s[u] = (pg + u < q1) ? tt : -INFINITY;
-      }
-      float mx = s[0];
-#pragma unroll
-      for (int u = 1; u < kGroup; ++u) mx = fmaxf(mx, s[u]);
-      const float mn = fmaxf(m[g], mx);
-      if (mn != -INFINITY) {
-        const float corr = expf(m[g] - mn);
-        l[g] *= corr;
-#pragma unroll
-        for (int d = 0; d < 8; ++d) acc[g][d] *= corr;
-#pragma unroll
-        for (int u = 0; u < kGroup; ++u) {
-          const float p = expf(s[u] - mn);
-          l[g] += p;
-#pragma unroll
-          for (int d = 0; d < 8; ++d) acc[g][d] += p * vf[u][d];
-        }
-        m[g] = mn;
-      }
-    }
-  }
-
-  // ---- combine the eight half-warps
-#pragma unroll
-  for (int g = 0; g < GQA; ++g) {
-#pragma unroll
-    for (int d = 0; d < 8; ++d) S.acc[hw][g][8 * j + d] = acc[g][d];
-    if (j == 0) {
-      S.m[hw][g] = m[g];
-      S.l[hw][g] = l[g];
-    }
+    S.span[b] = span;
+    S.cnt[b] = lane_range(span, a.window).nch * a.n_kv;
   }
   __syncthreads();
-
-  constexpr int kDims = GQA;  // (g, d) outputs per thread
-  const size_t base = (((size_t)b * a.n_kv + h) * a.max_chunks + c) * GQA;
-  float o[kDims], M[kDims], L[kDims];
-  int gg[kDims], dd[kDims];
+  if (warp == 0) {
+    // exclusive scan of the per-lane counts: each lane of warp 0 takes a run of lanes
+    const int per = (a.lanes + 31) / 32;
+    const int b0 = min(lane * per, a.lanes), b1 = min(b0 + per, a.lanes);
+    int sum = 0;
+    for (int b = b0; b < b1; ++b) sum += S.cnt[b];
+    int incl = sum;
 #pragma unroll
-  for (int e = 0; e < kDims; ++e) {
-    const int idx = t + e * 128;
-    const int g = idx / 128, d = idx % 128;
-    gg[e] = g;
-    dd[e] = d;
-    float mm = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kHalfWarps; ++w) mm = fmaxf(mm, S.m[w][g]);
-    float ll = 0.f, oo = 0.f;
-#pragma unroll
-    for (int w = 0; w < kHalfWarps; ++w) {
-      if (S.m[w][g] == -INFINITY) continue;
-      const float f = expf(S.m[w][g] - mm);
-      ll += S.l[w][g] * f;
-      oo += S.acc[w][g][d] * f;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
     }
-    o[e] = oo;
-    M[e] = mm;
-    L[e] = ll;
+    int run = incl - sum;
+    for (int b = b0; b < b1; ++b) {
+      S.prefix[b] = run;
+      run += S.cnt[b];
+    }
+    if (lane == 31) S.prefix[a.lanes] = incl;
+  }
+  __syncthreads();
+  tc_fence_after();
+
+  const long long total = S.prefix[a.lanes];
+  const long long lo = total * blockIdx.x / gridDim.x;
+  const long long hi = total * (blockIdx.x + 1) / gridDim.x;
+  const long long n = hi - lo;  // items of this CTA
+  const uint32_t tmem = S.tmem;
+
+  // the first item: lane b with prefix[b] <= lo < prefix[b + 1]
+  Cursor first{};
+  {
+    int l = 0, r = a.lanes - 1;
+    while (l < r) {
+      const int m = (l + r + 1) >> 1;
+      if (S.prefix[m] <= lo) l = m; else r = m - 1;
+    }
+    first.b = n > 0 ? l : 0;
+    first.lr = lane_range(S.span[first.b], a.window);
+    const long long rel = n > 0 ? lo - S.prefix[first.b] : 0;
+    first.h = int(rel / first.lr.nch);
+    first.c = int(rel % first.lr.nch);
+    first.seg = 0;
   }
 
-  const size_t out_base = (size_t)b * heads * 128 + (size_t)h * GQA * 128;
-  if (nch == 1) {
+  if (warp == kLoaderWarp) {
+    // ================= loader: K of item k, then V of item k - 1 (the scores run one item
+    // ahead of the values). Lane i handles box i of a tile: its block-table read and its two
+    // TMA copies (dims 0-63 and 64-127).
+    const uint64_t pol = l2_policy_evict_first();
+    const int box = a.box_rows;
+    const uint32_t box_bytes = uint32_t(box) * 128u;
+    struct Boxes {
+      int r0, nbox, pos, blk, row;
+      bool valid;
+      uint32_t vmask, bmask;
+    };
+    auto lookup = [&](const Cursor& x) {
+      Boxes q{};
+      int vlo, vhi;
+      chunk_rows(x, vlo, vhi);
+      q.r0 = (vlo / box) * box;
+      q.nbox = (vhi - q.r0 + box - 1) / box;  // 1..16 (box >= 8)
+      q.blk = -1;
+      if (lane < q.nbox) {
+        q.pos = x.lr.c0 + x.c * kChunk + q.r0 + lane * box;
+        const int pg = q.pos / a.bs;
+        if (pg < a.max_blocks) q.blk = a.bt[(size_t)x.b * a.max_blocks + pg];
+      }
+      return q;
+    };
+    auto finish = [&](Boxes& q, int h) {
+      q.valid = lane < q.nbox && q.blk >= 0 && q.blk < a.num_blocks;
+      q.row = q.valid ? (q.blk * a.n_kv + h) * a.bs + q.pos % a.bs : 0;
+      q.vmask = __ballot_sync(0xffffffffu, q.valid);
+      q.bmask = (1u << q.nbox) - 1u;
+    };
+    auto issue = [&](const Boxes& q, const CUtensorMap* tm, Tile& dst, uint64_t* full,
+                     uint32_t* inv) {
+      if (elect_one()) {
+        *inv = q.bmask & ~q.vmask;
+        if ((q.bmask & ~q.vmask) && a.err) atomicOr(a.err, kFlagPageRange);
+        mbar_arrive_expect_tx(full, uint32_t(__popc(q.vmask)) * box_bytes * 2u);
+      }
+      __syncwarp();
+      if (q.valid) {
+        const int r = q.r0 + lane * box;
+        tma_load_2d_hint(&dst.d[0][r * 128], tm, full, 0, q.row, pol);
+        tma_load_2d_hint(&dst.d[1][r * 128], tm, full, 64, q.row, pol);
+      }
+      __syncwarp();
+    };
+    Cursor x = first;
+    Boxes next = n > 0 ? lookup(x) : Boxes{}, prev{};
+    bool ok = true;
+    long long nk = 0, nv = 0;  // tiles issued
+    for (long long k = 0; k <= n && ok; ++k) {
+      Boxes cur{};
+      if (k < n) {
+        const int s = int(k % kStages);
+        if (k >= kStages) ok = mbar_wait(&S.empty_k[s], uint32_t((k / kStages) - 1) & 1);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        cur = next;
+        finish(cur, x.h);
+        issue(cur, &tmK, S.kt[s], &S.full_k[s], &S.inv_k[s]);
+        ++nk;
+        cursor_next(x, S.span, a);
+        if (k + 1 < n) next = lookup(x);  // read ahead: used next round
+      }
+      if (k >= 1) {
+        const long long kv = k - 1;
+        const int s = int(kv % kStages);
+        if (kv >= kStages) ok = mbar_wait(&S.empty_v[s], uint32_t((kv / kStages) - 1) & 1);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        issue(prev, &tmV, S.vt[s], &S.full_v[s], &S.inv_v[s]);
+        ++nv;
+      }
+      prev = cur;
+    }
+    if (!ok && a.err && lane == 0) atomicOr(a.err, kFlagAttnWait);
+    // Leave no copy in flight: wait (bounded) for the last tiles issued to land.
+    for (long long j = max(0ll, nk - kStages); j < nk; ++j)
+      mbar_wait(&S.full_k[j % kStages], uint32_t(j / kStages) & 1);
+    for (long long j = max(0ll, nv - kStages); j < nv; ++j)
+      mbar_wait(&S.full_v[j % kStages], uint32_t(j / kStages) & 1);
+    return;
+  }
+
+  const uint32_t idesc_s = idesc_f16_f32(128, kN);
+  const uint32_t idesc_o = idesc_f16_f32(128, kN) | (1u << 15);  // A (V^T) MN-major
+
+  if (warp == kMmaWarp) {
+    // ================= MMA warp: S(j) then O(j - 1), each when its inputs are in place
+    bool ok = true;
+    long long ns = 0, no = 0;  // MMA groups issued
+    auto do_o = [&](long long i) {
+      const int s = int(i % kStages);
+      ok = mbar_wait(&S.p_full[i & 1], uint32_t(i >> 1) & 1) && ok;
+      ok = mbar_wait(&S.full_v[s], uint32_t(i / kStages) & 1) && ok;
+      if (i >= 2) ok = mbar_wait(&S.o_empty[i & 1], uint32_t((i >> 1) - 1) & 1) && ok;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) return;
+      if (S.inv_v[s]) {  // rows of pages outside the pool read as zero
+        zero_rows(S.vt[s], 0, kChunk, S.inv_v[s], a.box_rows, lane, 32);
+        fence_proxy_async();
+        __syncwarp();
+      }
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t vb = smem_u32(&S.vt[s].d[0][0]);
+        const uint32_t pb[2] = {smem_u32(&S.pb[i & 1][0][0]), smem_u32(&S.pb[i & 1][1][0])};
 #pragma unroll
-    for (int e = 0; e < kDims; ++e) {
-      const float r = o[e] / L[e];
-      const size_t oi = out_base + gg[e] * 128 + dd[e];
-      if (a.out_f16)
-        static_cast<__half*>(a.out)[oi] = __float2half_rn(r);
-      else
-        static_cast<float*>(a.out)[oi] = r;
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16(tmem + 32 + (i & 1) * 16, smem_desc(vb + kk * 2048, kChunk * 128, 1024, 2),
+                   desc_k_sw128(pb[kk >> 2] + (kk & 3) * 32), idesc_o, kk > 0);
+        umma_commit(&S.o_full[i & 1]);
+        umma_commit(&S.empty_v[s]);
+      }
+      __syncwarp();
+      ++no;
+    };
+    Cursor x = first;
+    for (long long j = 0; j < n && ok; ++j) {
+      const int s = int(j % kStages);
+      if (j == 0 || x.c == 0) ok = mbar_wait(&S.q_full[x.seg & 1], uint32_t(x.seg >> 1) & 1) && ok;
+      ok = mbar_wait(&S.full_k[s], uint32_t(j / kStages) & 1) && ok;
+      if (j >= 2) ok = mbar_wait(&S.s_empty[j & 1], uint32_t((j >> 1) - 1) & 1) && ok;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const uint32_t inv = S.inv_k[s];
+      if (inv) {
+        // rows of pages outside the pool read as zero
+        zero_rows(S.kt[s], 0, kChunk, inv, a.box_rows, lane, 32);
+        fence_proxy_async();
+        __syncwarp();
+      }
+      tc_fence_after();
+      if (elect_one()) {
+        const uint32_t kb[2] = {smem_u32(&S.kt[s].d[0][0]), smem_u32(&S.kt[s].d[1][0])};
+        const uint32_t qb[2] = {smem_u32(&S.qb[x.seg & 1][0][0]), smem_u32(&S.qb[x.seg & 1][1][0])};
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_f16(tmem + (j & 1) * 16, desc_k_sw128(kb[kk >> 2] + (kk & 3) * 32),
+                   desc_k_sw128(qb[kk >> 2] + (kk & 3) * 32), idesc_s, kk > 0);
+        umma_commit(&S.s_full[j & 1]);
+        umma_commit(&S.empty_k[s]);
+      }
+      __syncwarp();
+      ++ns;
+      if (j >= 1) do_o(j - 1);
+      cursor_next(x, S.span, a);
+    }
+    if (ok && n > 0) do_o(n - 1);
+    if (!ok && a.err && lane == 0) atomicOr(a.err, kFlagAttnWait);
+    // the softmax warps have consumed every result on the normal path; after a timeout, wait
+    // (bounded) for what was issued before TMEM is released
+    if (!ok) {
+      if (ns > 0) mbar_wait(&S.s_full[(ns - 1) & 1], uint32_t((ns - 1) >> 1) & 1, 100000000ull);
+      if (no > 0) mbar_wait(&S.o_full[(no - 1) & 1], uint32_t((no - 1) >> 1) & 1, 100000000ull);
+    }
+    tc_fence_before();
+    bar_and(kBarTmem, kSoftmax + 32, true);
+    tc_fence_after();
+    tmem_dealloc(tmem, 64);
+    return;
+  }
+
+  if (warp == kEpiWarp) {
+    // ================= epilogue warp: arrival counts and merges of split pairs. Only the
+    // first and the last segment of a CTA's range can hold part of a pair.
+    int expect = 0;
+    if (n > 0) {
+      Cursor x = first;
+      for (long long j = 1; j < n; ++j) cursor_next(x, S.span, a);
+      const bool first_part = first.c != 0;
+      const bool last_part = x.c + 1 != x.lr.nch;
+      expect = (x.seg == 0) ? ((first_part || last_part) ? 1 : 0)
+                            : int(first_part) + int(last_part);
+    }
+    const int heads = a.n_kv * GQA;
+    for (int k = 0; k < expect; ++k) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&S.seg_done[k], 0))) {
+        if (a.err && lane == 0) atomicOr(a.err, kFlagAttnWait);
+        break;
+      }
+      const int b = S.seg_info[k].b, h = S.seg_info[k].h;
+      const int nch = lane_range(S.span[b], a.window).nch;
+      unsigned last = 0;
+      if (lane == 0) {
+        __threadfence();  // release: the softmax warps' partial writes (ordered by the barrier)
+        const unsigned len = unsigned(S.seg_info[k].len);
+        const unsigned prev = atomicAdd(&a.counters[b * a.n_kv + h], len);
+        last = (prev + len == unsigned(nch)) ? 1u : 0u;
+        if (last) __threadfence();  // acquire: the other segments' partials
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      // merge the pair's segments in chunk order; lane l takes dims 4l .. 4l + 3
+      const size_t pbase = ((size_t)b * a.n_kv + h) * a.max_chunks;
+      const long long base = S.prefix[b] + (long long)h * nch;
+      float mm[GQA], ll[GQA], oo[GQA][4];
+#pragma unroll
+      for (int g = 0; g < GQA; ++g) {
+        mm[g] = -INFINITY;
+        ll[g] = 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) oo[g][u] = 0.f;
+      }
+      for (int cc = 0; cc < nch; ++cc) {
+        const bool st = cc == 0 || owner_of(base + cc, total, gridDim.x) !=
+                                       owner_of(base + cc - 1, total, gridDim.x);
+        if (!st) continue;
+#pragma unroll
+        for (int g = 0; g < GQA; ++g) {
+          const float* pp = a.part + ((pbase + cc) * GQA + g) * 130;
+          const float cm = __ldcg(pp + 128), cl = __ldcg(pp + 129);
+          // slots are 130 floats (8-byte aligned): four scalar loads
+          const float4 ov = make_float4(__ldcg(pp + lane * 4), __ldcg(pp + lane * 4 + 1),
+                                        __ldcg(pp + lane * 4 + 2), __ldcg(pp + lane * 4 + 3));
+          const float mn = fmaxf(mm[g], cm);
+          const float f0 = (mm[g] == -INFINITY) ? 0.f : expf(mm[g] - mn);
+          const float f1 = expf(cm - mn);
+          ll[g] = ll[g] * f0 + cl * f1;
+          oo[g][0] = oo[g][0] * f0 + ov.x * f1;
+          oo[g][1] = oo[g][1] * f0 + ov.y * f1;
+          oo[g][2] = oo[g][2] * f0 + ov.z * f1;
+          oo[g][3] = oo[g][3] * f0 + ov.w * f1;
+          mm[g] = mn;
+        }
+      }
+      const size_t out_base = (size_t)b * heads * 128 + (size_t)h * GQA * 128;
+#pragma unroll
+      for (int g = 0; g < GQA; ++g) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float r = oo[g][u] / ll[g];
+          const size_t oi = out_base + g * 128 + lane * 4 + u;
+          if (a.out_f16)
+            static_cast<__half*>(a.out)[oi] = __float2half_rn(r);
+          else
+            static_cast<float*>(a.out)[oi] = r;
+        }
+      }
+      if (lane == 0) a.counters[b * a.n_kv + h] = 0u;
     }
     return;
   }
 
-  // ---- several chunks: write this chunk's partial; the last CTA to arrive merges them in
-  // chunk order (deterministic)
+  // ================= softmax warps 0-3 (thread t: TMEM lane t = chunk row t = output dim t)
+  const int heads = a.n_kv * GQA;
+  const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
+  bool ok = true;
+
+  // q of a pair, loaded a segment ahead into registers, written as f16 hi/lo rows of the S
+  // operand of its segment's buffer
+  float qn[GQA];
+  auto load_q = [&](const Cursor& x) {
 #pragma unroll
-  for (int e = 0; e < kDims; ++e) {
-    float* pp = a.part + (base + gg[e]) * 130;
-    pp[dd[e]] = o[e];
-    if (dd[e] == 0) {
-      pp[128] = M[e];
-      pp[129] = L[e];
+    for (int g = 0; g < GQA; ++g) qn[g] = a.q[((size_t)x.b * heads + x.h * GQA + g) * 128 + t];
+  };
+  auto store_q = [&](int seg) {
+#pragma unroll
+    for (int g = 0; g < GQA; ++g) {
+      const __half hi16 = __float2half_rn(qn[g]);
+      const __half lo16 = __float2half_rn((qn[g] - __half2float(hi16)) * kLo);
+      *reinterpret_cast<__half*>(&S.qb[seg & 1][t >> 6][sw128(g, t & 63)]) = hi16;
+      *reinterpret_cast<__half*>(&S.qb[seg & 1][t >> 6][sw128(GQA + g, t & 63)]) = lo16;
+    }
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.q_full[seg & 1]);
+  };
+  // the first item of the segment after the one `x` is in (x itself if none follows)
+  auto next_segment = [&](Cursor x, long long& at) -> Cursor {
+    const int left = x.lr.nch - x.c;  // items of x's segment from x on
+    at += left;
+    x.c = x.lr.nch - 1;
+    cursor_next(x, S.span, a);
+    return x;
+  };
+
+  Cursor cur = first;
+  // q of segments 0 and 1 now; registers then hold segment 2's
+  long long pos1 = 0, pos2 = 0;
+  Cursor seg1 = cur, seg2 = cur;
+  if (n > 0) {
+    load_q(cur);
+    store_q(0);
+    seg1 = next_segment(cur, pos1);
+    if (pos1 < n) {
+      load_q(seg1);
+      store_q(1);
+      pos2 = pos1;
+      seg2 = next_segment(seg1, pos2);
+      if (pos2 < n) load_q(seg2);
     }
   }
-  __threadfence();
-  __syncthreads();
-  if (t == 0) {
-    const unsigned prev = atomicAdd(&a.counters[b * a.n_kv + h], 1u);
-    S.last = (prev == unsigned(nch - 1));
+
+  float m_run[GQA], l_run[GQA], acc[GQA], corr[GQA];
+#pragma unroll
+  for (int g = 0; g < GQA; ++g) {
+    m_run[g] = -INFINITY;
+    l_run[g] = 0.f;
+    acc[g] = 0.f;
+    corr[g] = 0.f;
   }
-  __syncthreads();
-  if (!S.last) return;
-  __threadfence();
-  const size_t pb = ((size_t)b * a.n_kv + h) * a.max_chunks * GQA;
-  for (int i = t; i < nch * GQA; i += 128) {
-    const float* pp = a.part + (pb + i) * 130;
-    S.cm[i / GQA][i % GQA] = __ldcg(pp + 128);
-    S.cl[i / GQA][i % GQA] = __ldcg(pp + 129);
-  }
-  __syncthreads();
+  int n_partial = 0;  // partial segments handed to the epilogue warp (at most 2)
+  // The item before this one: its sum and values are folded in one item late (when its PV is
+  // long done), and when it ended a segment that segment is written out then.
+  bool pend = false;
+  struct {
+    int b, h, c_first, c_last, nch;
+    bool ends;
+  } prev{};
+  int c_first = cur.c;
+
+  // folds the previous item's sum and O into the running state
+  auto fold_prev = [&](long long i) {
+    ok = mbar_wait(&S.o_full[i & 1], uint32_t(i >> 1) & 1) && ok;
+    tc_fence_after();
+    float ov[16];
+    tmem_ld16(lane_base + 32 + (i & 1) * 16, ov);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.o_empty[i & 1]);
 #pragma unroll
-  for (int e = 0; e < kDims; ++e) {
-    const int g = gg[e], d = dd[e];
-    float mm = -INFINITY;
-    for (int cc = 0; cc < nch; ++cc) mm = fmaxf(mm, S.cm[cc][g]);
-    float ll = 0.f, oo = 0.f;
-    for (int c0 = 0; c0 < nch; c0 += 4) {
-      float ov[4];
+    for (int g = 0; g < GQA; ++g) {
+      l_run[g] = l_run[g] * corr[g] + ((S.red_sum[i & 1][0][g] + S.red_sum[i & 1][1][g]) +
+                                       (S.red_sum[i & 1][2][g] + S.red_sum[i & 1][3][g]));
+      acc[g] = acc[g] * corr[g] + (ov[g] + ov[GQA + g] * (1.f / kLo));
+    }
+  };
+  // writes a finished segment: the output of a whole pair, or a partial for the epilogue warp
+  auto finish_segment = [&]() {
+    const size_t out_base = (size_t)prev.b * heads * 128 + (size_t)prev.h * GQA * 128;
+    if (prev.c_first == 0 && prev.c_last + 1 == prev.nch) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
-        ov[u] = (c0 + u < nch) ? __ldcg(a.part + (pb + (size_t)(c0 + u) * GQA + g) * 130 + d) : 0.f;
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (c0 + u >= nch) break;
-        const float f = expf(S.cm[c0 + u][g] - mm);
-        ll += S.cl[c0 + u][g] * f;
-        oo += ov[u] * f;
+      for (int g = 0; g < GQA; ++g) {
+        const float r = acc[g] / l_run[g];
+        const size_t oi = out_base + g * 128 + t;
+        if (a.out_f16)
+          static_cast<__half*>(a.out)[oi] = __float2half_rn(r);
+        else
+          static_cast<float*>(a.out)[oi] = r;
       }
+    } else if (n_partial < 2) {
+      const size_t pbase = ((size_t)prev.b * a.n_kv + prev.h) * a.max_chunks;
+#pragma unroll
+      for (int g = 0; g < GQA; ++g) {
+        float* pp = a.part + ((pbase + prev.c_first) * GQA + g) * 130;
+        pp[t] = acc[g];
+        if (t == 0) {
+          pp[128] = m_run[g];
+          pp[129] = l_run[g];
+        }
+      }
+      if (t == 0) {
+        S.seg_info[n_partial].b = prev.b;
+        S.seg_info[n_partial].h = prev.h;
+        S.seg_info[n_partial].c_first = prev.c_first;
+        S.seg_info[n_partial].len = prev.c_last - prev.c_first + 1;
+      }
+      mbar_arrive(&S.seg_done[n_partial]);
+      ++n_partial;
     }
-    const float r = oo / ll;
-    const size_t oi = out_base + g * 128 + d;
-    if (a.out_f16)
-      static_cast<__half*>(a.out)[oi] = __float2half_rn(r);
-    else
-      static_cast<float*>(a.out)[oi] = r;
+#pragma unroll
+    for (int g = 0; g < GQA; ++g) {
+      m_run[g] = -INFINITY;
+      l_run[g] = 0.f;
+      acc[g] = 0.f;
+    }
+  };
+
+  for (long long j = 0; j < n; ++j) {
+    const int s = int(j % kStages);
+    // first item of a segment after the first: the segment after next gets its q now (its
+    // buffer was last read by scores that are complete)
+    if (j > 0 && cur.c == 0 && pos2 < n) {
+      store_q(cur.seg + 1);
+      Cursor nx = seg2;
+      long long at = pos2;
+      seg2 = next_segment(nx, at);
+      pos2 = at;
+      if (pos2 < n) load_q(seg2);
+    }
+    // ---- scores of item j (thread t = row t)
+    int vlo, vhi;
+    chunk_rows(cur, vlo, vhi);
+    ok = mbar_wait(&S.s_full[j & 1], uint32_t(j >> 1) & 1) && ok;
+    tc_fence_after();
+    float sv[16];
+    tmem_ld16(lane_base + (j & 1) * 16, sv);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.s_empty[j & 1]);
+    const bool valid = t >= vlo && t < vhi;
+    float sc[GQA];
+#pragma unroll
+    for (int g = 0; g < GQA; ++g) {
+      sc[g] = valid ? sv[g] + sv[GQA + g] * (1.f / kLo) : -INFINITY;
+      const float wm = warp_max(sc[g]);
+      if (lane == 0) S.red_max[j & 1][warp][g] = wm;
+    }
+    if (!bar_and(kBarSoftmax, kSoftmax, ok)) {  // also makes item j - 1's sums visible
+      ok = false;
+      break;
+    }
+    // ---- the previous item, and the segment it ended
+    if (pend) {
+      fold_prev(j - 1);
+      if (prev.ends) finish_segment();
+    }
+    // ---- softmax of item j; P as f16 hi/lo rows of the O operand
+#pragma unroll
+    for (int g = 0; g < GQA; ++g) {
+      const float cmax = fmaxf(fmaxf(S.red_max[j & 1][0][g], S.red_max[j & 1][1][g]),
+                               fmaxf(S.red_max[j & 1][2][g], S.red_max[j & 1][3][g]));
+      const float mn = fmaxf(m_run[g], cmax);
+      corr[g] = (m_run[g] == -INFINITY) ? 0.f : expf(m_run[g] - mn);
+      const float p = valid ? expf(sc[g] - mn) : 0.f;
+      m_run[g] = mn;
+      const __half phi = __float2half_rn(p);
+      const __half plo = __float2half_rn((p - __half2float(phi)) * kLo);
+      *reinterpret_cast<__half*>(&S.pb[j & 1][t >> 6][sw128(g, t & 63)]) = phi;
+      *reinterpret_cast<__half*>(&S.pb[j & 1][t >> 6][sw128(GQA + g, t & 63)]) = plo;
+      const float ws = warp_sum(p);
+      if (lane == 0) S.red_sum[j & 1][warp][g] = ws;
+    }
+    // V rows outside [vlo, vhi) must read as zero before the MMA (rows of missing pages are
+    // cleared by the MMA warp)
+    if (vlo > 0 || vhi < kChunk) {
+      ok = mbar_wait(&S.full_v[s], uint32_t(j / kStages) & 1) && ok;
+      zero_rows(S.vt[s], vlo, vhi, 0u, a.box_rows, t, kSoftmax);
+    }
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.p_full[j & 1]);
+
+    pend = true;
+    prev.b = cur.b;
+    prev.h = cur.h;
+    prev.c_first = c_first;
+    prev.c_last = cur.c;
+    prev.nch = cur.lr.nch;
+    prev.ends = (cur.c + 1 == cur.lr.nch) || (j + 1 == n);
+    if (prev.ends) c_first = 0;  // the next item starts a pair
+    cursor_next(cur, S.span, a);
   }
-  if (t == 0) a.counters[b * a.n_kv + h] = 0u;
+  // the last item: its sums need every warp's partial sum, then its segment is written
+  if (ok && pend) {
+    if (bar_and(kBarSoftmax, kSoftmax, ok)) {
+      fold_prev(n - 1);
+      finish_segment();
+    } else {
+      ok = false;
+    }
+  }
+  if (!ok && a.err && t == 0) atomicOr(a.err, kFlagAttnWait);
+  tc_fence_before();
+  bar_and(kBarTmem, kSoftmax + 32, true);
 }
 
 }  // namespace
@@ -356,12 +729,16 @@ size_t attn_part_bytes(int lanes, int n_kv, int gqa, int max_span) {
 }
 
 cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream_t st) {
-  if (r.gqa != 1 && r.gqa != 2) {
-    set_error("decode_attention: gqa must be 1 or 2");
+  if (r.gqa != 1 && r.gqa != 2 && r.gqa != 4 && r.gqa != 8) {
+    set_error("decode_attention: gqa must be 1, 2, 4 or 8");
     return cudaErrorInvalidValue;
   }
   if (r.lanes < 1 || r.n_kv < 1 || r.max_span < 1 || r.block_size < 1) {
     set_error("decode_attention: empty shape");
+    return cudaErrorInvalidValue;
+  }
+  if (r.lanes > kMaxLanes) {
+    set_error("decode_attention: at most 512 lanes per call");
     return cudaErrorInvalidValue;
   }
   const int chunks = (r.max_span + kChunk - 1) / kChunk;
@@ -369,24 +746,44 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
     set_error("decode_attention: max_span exceeds 8192");
     return cudaErrorInvalidValue;
   }
+  // TMA boxes copy runs of whole rows; a run never crosses a page, so the box height divides
+  // the page size (or the lane's single page holds every position).
+  int box = 0;
+  if (r.max_blocks == 1) {
+    box = kChunk;
+  } else {
+    if (r.block_size % 8) {
+      set_error("decode_attention: block_size must be a multiple of 8 (or one page per lane)");
+      return cudaErrorInvalidValue;
+    }
+    box = 8;
+    while (box < kChunk && r.block_size % (box * 2) == 0) box *= 2;
+  }
   if (attn_part_bytes(r.lanes, r.n_kv, r.gqa, r.max_span) > w.part_bytes ||
       r.lanes * r.n_kv > w.n_counters) {
     set_error("decode_attention: workspace too small");
     return cudaErrorInvalidValue;
   }
+  const uint64_t rows = uint64_t(r.num_blocks) * r.n_kv * r.block_size;
+  CUtensorMap tmK, tmV;
+  if (!make_tmap_2d_f16(&tmK, r.k_pool, 128, rows, 256, 64, uint32_t(box), true) ||
+      !make_tmap_2d_f16(&tmV, r.v_pool, 128, rows, 256, 64, uint32_t(box), true)) {
+    set_error("decode_attention: cuTensorMapEncodeTiled failed (pool pointer must be 16-byte aligned)");
+    return cudaErrorInvalidValue;
+  }
   AttnArgs a{};
   a.q = r.q;
-  a.k = r.k_pool;
-  a.v = r.v_pool;
   a.bt = r.block_table;
   a.max_blocks = r.max_blocks;
   a.bs = r.block_size;
   a.num_blocks = r.num_blocks;
   a.max_span = r.max_span;
+  a.box_rows = box;
   a.err = r.err;
   a.spans = r.spans;
   a.span_add = r.span_add;
   a.window = r.window;
+  a.lanes = r.lanes;
   a.n_kv = r.n_kv;
   a.max_chunks = chunks;
   a.part = w.part;
@@ -394,22 +791,26 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
   a.out = r.out;
   a.out_f16 = r.out_f16 ? 1 : 0;
 
-  cudaLaunchConfig_t cfg{};
-  const size_t smem = sizeof(AttnSmem) + 128;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const size_t smem = sizeof(AttnSmem) + 1024;
   {
     static std::mutex mu;
     static bool done[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(mu);
     if (dev >= 0 && dev < 64 && !done[dev]) {
       cudaFuncSetAttribute(attn_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
       cudaFuncSetAttribute(attn_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      cudaFuncSetAttribute(attn_decode_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      cudaFuncSetAttribute(attn_decode_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
       done[dev] = true;
     }
   }
-  cfg.gridDim = dim3(chunks, r.n_kv, r.lanes);
-  cfg.blockDim = dim3(128, 1, 1);
+  const long long items = (long long)r.lanes * r.n_kv * chunks;
+  const int grid = int(std::min<long long>(num_sms(dev), items));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -417,8 +818,12 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
   attr[0].val.programmaticStreamSerializationAllowed = r.pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (r.gqa == 2) return cudaLaunchKernelEx(&cfg, attn_decode_kernel<2>, a);
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel<1>, a);
+  switch (r.gqa) {
+    case 1: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<1>, tmK, tmV, a);
+    case 2: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<2>, tmK, tmV, a);
+    case 4: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<4>, tmK, tmV, a);
+    default: return cudaLaunchKernelEx(&cfg, attn_decode_kernel<8>, tmK, tmV, a);
+  }
 }
 
 size_t attn_static_part_limit() { return kStaticPartBytes; }

@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int cb = 0; cb < ncb; ++cb) {
       const int s = cb % kAStages;
       if (!mbar_wait(&full_a[s], (cb / kAStages) & 1)) {
-        if (tt == 0) atomicOr(a.err, 256);
+        if (tt == 0) atomicOr(a.err, 4096);
       }
       if (a.alpha) {
         uint8_t* halo = a_base + s * a_bytes;
@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---------------- epilogue (warps 2..5: TMEM lane quadrant = warp % 4)
   if (warp >= 2 && warp <= 5) {
-    if (!mbar_wait(done, 0) && lane == 0) atomicOr(a.err, 512);
+    if (!mbar_wait(done, 0) && lane == 0) atomicOr(a.err, 8192);
     tc_fence_after();
     const int quad = warp & 3;
     const int l = l0 + quad * 32 + lane;

@@ -20,7 +20,7 @@ __device__ __forceinline__ void qkrope_row(const QkRopeArgs& q, int head, int j,
   // (j, head) is the same for the whole warp, so the early return is warp-uniform.
   const int pos = q.positions[j];
   if (pos < 0 || pos >= q.rope_len || pos >= q.max_blocks * q.block_size) {
-    if (lane == 0 && q.err) atomicOr(q.err, 256);
+    if (lane == 0 && q.err) atomicOr(q.err, kFlagRopeRange);
     return;
   }
   int blk = 0;
@@ -28,7 +28,7 @@ __device__ __forceinline__ void qkrope_row(const QkRopeArgs& q, int head, int j,
   if (head >= q.heads) {
     blk = q.block_table[(size_t)j * q.max_blocks + pos / q.block_size];
     if (blk < 0 || blk >= q.num_blocks) {
-      if (lane == 0 && q.err) atomicOr(q.err, 256);
+      if (lane == 0 && q.err) atomicOr(q.err, kFlagRopeRange);
       return;
     }
   }

@@ -213,8 +213,15 @@ tts_status tts_ctx_check(tts_ctx* c, void* stream) {
     const int code = c->err_host[0];
     cudaMemsetAsync(c->gemm.err, 0, sizeof(int), S(stream));
     cudaStreamSynchronize(S(stream));
-    return fail(TTS_ERR_TIMEOUT, "device wait gave up (code " + std::to_string(code) +
-                                     "): results of the affected launches are not valid");
+    if (code & kFlagWaitMask)
+      return fail(TTS_ERR_TIMEOUT, "device wait gave up (code " + std::to_string(code) +
+                                       "): results of the affected launches are not valid");
+    std::string what;
+    if (code & kFlagRopeRange) what += " a position outside the RoPE table, block table or pool;";
+    if (code & kFlagSpanRange) what += " an attention span outside 1..max_span or the block table;";
+    if (code & kFlagPageRange) what += " a block-table page outside the pool;";
+    return fail(TTS_ERR_INVALID_ARG, "device data out of range (code " + std::to_string(code) +
+                                         "):" + what + " those rows were skipped or read as zero");
   }
   return TTS_OK;
 }
@@ -374,8 +381,8 @@ tts_status tts_decode_attention(tts_ctx* c, const float* q, int lanes, int gqa,
   std::string why;
   if (!c || !q || !spans || !out) return fail(TTS_ERR_INVALID_ARG, "decode_attention: NULL argument");
   if (!kv_ok(kv, &why)) return fail(TTS_ERR_INVALID_ARG, "decode_attention: " + why);
-  if (gqa != 1 && gqa != 2)
-    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "decode_attention: gqa must be 1 or 2");
+  if (gqa != 1 && gqa != 2 && gqa != 4 && gqa != 8)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "decode_attention: gqa must be 1, 2, 4 or 8");
   if (lanes < 1 || lanes > c->max_lanes || max_span < 1 || max_span > 8192)
     return fail(TTS_ERR_UNSUPPORTED_SHAPE,
                 "decode_attention: lanes must be in 1..max_lanes and max_span in 1..8192");
@@ -409,8 +416,8 @@ tts_status tts_decode_attention_static(const float* q, int lanes, int gqa,
   if (!q || !spans || !out)
     return fail(TTS_ERR_INVALID_ARG, "decode_attention_static: NULL argument");
   if (!kv_ok(kv, &why)) return fail(TTS_ERR_INVALID_ARG, "decode_attention_static: " + why);
-  if (gqa != 1 && gqa != 2)
-    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "decode_attention_static: gqa must be 1 or 2");
+  if (gqa != 1 && gqa != 2 && gqa != 4 && gqa != 8)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "decode_attention_static: gqa must be 1, 2, 4 or 8");
   if (lanes < 1 || max_span < 1 || max_span > 8192)
     return fail(TTS_ERR_UNSUPPORTED_SHAPE,
                 "decode_attention_static: lanes must be >= 1 and max_span in 1..8192");

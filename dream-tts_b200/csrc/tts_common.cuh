@@ -30,6 +30,22 @@ TTS_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
 TTS_DEV void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// Generic-proxy shared-memory writes made visible to the async proxy (tcgen05.mma operands).
+TTS_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Named barrier over `n` threads (whole warps) that also ANDs a predicate across them, so a
+// group of warps takes one uniform branch after a bounded wait.
+TTS_DEV bool bar_and(uint32_t id, uint32_t n, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(p)), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
 TTS_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

@@ -14,6 +14,18 @@ namespace tts {
 void set_error(const std::string& msg);
 const char* last_error();
 
+// ------------------------------------------------------------------ device error flags
+// Kernels OR these into the context's device flag word; tts_ctx_check reads and clears it.
+// Waits that gave up (results of that launch are not valid):
+constexpr int kFlagGemmWait = 1 | 2 | 4;
+constexpr int kFlagConvWait = 16 | 32 | 64 | 128 | 4096 | 8192;
+constexpr int kFlagAttnWait = 2048;
+constexpr int kFlagWaitMask = kFlagGemmWait | kFlagConvWait | kFlagAttnWait;
+// Device data outside what the launch covers (the rows involved are skipped or read as zero):
+constexpr int kFlagRopeRange = 256;   // position outside the RoPE table, block table or pool
+constexpr int kFlagSpanRange = 512;   // attention span outside 1..min(max_span, table)
+constexpr int kFlagPageRange = 1024;  // attention page outside the pool
+
 // ------------------------------------------------------------------ device properties
 int num_sms(int device);
 
@@ -37,7 +49,7 @@ struct QkRopeArgs {
   int block_size = 0;
   int num_blocks = 0;        // pages in the pool; out-of-range table entries are skipped
   int rope_len = 0;          // rows of cos_t/sin_t; positions outside are skipped
-  int* err = nullptr;        // set (bit 8) when a table entry or position is out of range
+  int* err = nullptr;        // kFlagRopeRange when a table entry or position is out of range
   __half* k_pool = nullptr;  // this layer's K pages [num_blocks][n_kv][block_size][128]
   __half* v_pool = nullptr;
   float* q_out = nullptr;  // [lanes][heads][128]

@@ -57,8 +57,10 @@ TTS_API const char* tts_last_error(void);
  * in crates/qwen3tts/src/engine.rs:529-533. */
 TTS_API tts_status tts_ctx_create(int device, int max_lanes, tts_ctx** out);
 TTS_API tts_status tts_ctx_destroy(tts_ctx* ctx);
-/* Synchronises `stream` and reports TTS_ERR_TIMEOUT if any kernel's bounded wait gave up
- * since the last check (then clears the flag). */
+/* Synchronises `stream` and reports what the kernels flagged since the last check (then clears
+ * it): TTS_ERR_TIMEOUT if a bounded device-side wait gave up (those results are not valid),
+ * else TTS_ERR_INVALID_ARG if device data (positions, spans, block-table pages) was out of
+ * range (those rows were skipped or read as zero). */
 TTS_API tts_status tts_ctx_check(tts_ctx* ctx, void* stream);
 
 /* ---------------------------------------------------------------- projections
@@ -145,7 +147,9 @@ TTS_API tts_status tts_qk_rope_append(tts_ctx* ctx, const float* qkv, int lanes,
 /* attn::decode_attention: crates/tts-nn/src/attn.rs:22-73. q f32 [lanes][n_kv * gqa][128]
  * with the scale folded in; lane i attends positions [wstart_i, spans[i]) where
  * wstart_i = max(0, spans[i] - window) (window 0 = none). max_span bounds every spans[i].
- * out [lanes][n_kv * gqa * 128], f16 or f32. gqa in {1, 2}. */
+ * out [lanes][n_kv * gqa * 128], f16 or f32. gqa in {1, 2, 4, 8}; lanes <= 512; block_size
+ * a multiple of 8 unless max_blocks == 1 (each lane one contiguous page); pool pointers
+ * 16-byte aligned. Pages outside [0, num_blocks) read as zero and are reported. */
 TTS_API tts_status tts_decode_attention(tts_ctx* ctx, const float* q, int lanes, int gqa,
                                 const tts_kv_cache* kv, const int* spans, int max_span,
                                 int window, void* out, int out_f16, void* stream);

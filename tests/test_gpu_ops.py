@@ -169,3 +169,83 @@ def test_swiglu_snake_argmax(tt, orc):
     mask[2150] = 0
     assert np.array_equal(tt.topk.argmax(dev_f32(big), torch.from_numpy(mask).cuda()).cpu().numpy(),
                           orc.argmax(big, mask).astype(np.int32))
+
+
+def _paged(rng, kb, vb, bs, spare=5):
+    """Contiguous `[lanes, n_kv, cap, 128]` f16 bits -> shuffled pages + block table."""
+    lanes, n_kv, cap, _ = kb.shape
+    per = cap // bs
+    nb = lanes * per + spare
+    table = rng.permutation(nb)[:lanes * per].reshape(lanes, per).astype(np.int32)
+
+    def pages(c):
+        p = c.reshape(lanes, n_kv, per, bs, 128).transpose(0, 2, 1, 3, 4).reshape(-1, n_kv, bs, 128)
+        host = np.zeros((nb, n_kv, bs, 128), np.uint16)
+        host[table.reshape(-1)] = p
+        return dev_f16(host)
+    return pages(kb), pages(vb), table, nb
+
+
+@pytest.mark.parametrize("bs,n_kv,gqa,window", [(8, 8, 2, 0), (16, 4, 4, 0), (64, 2, 8, 0),
+                                                (128, 8, 1, 0), (32, 8, 2, 300), (16, 8, 2, 129)])
+def test_decode_attention_paged_geometries(tt, orc, bs, n_kv, gqa, window):
+    """Page sizes 8..128 (one TMA box per page run), gqa 1..8, sliding windows whose start
+    falls mid-chunk; per-lane spans cross chunk and page edges."""
+    from ttsnn import _lib as L
+    rng = np.random.default_rng(bs * 10 + gqa + window)
+    lanes, cap = 20, 1152
+    spans = np.concatenate([[1, 7, 8, 127, 128, 129, 640, 1152],
+                            rng.integers(1, cap + 1, lanes - 8)]).astype(np.int32)
+    q = rng.standard_normal((lanes, n_kv * gqa, 128), dtype=np.float32) * 0.1
+    kb = orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
+    vb = orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
+    kp, vp, table, nb = _paged(rng, kb, vb, bs)
+    tdev = torch.from_numpy(table).cuda()
+    kv = L.KvCache(kp.data_ptr(), vp.data_ptr(), tdev.data_ptr(), cap // bs, bs, nb, n_kv, 128)
+    got = tt.attn.decode_attention_paged(dev_f32(q), kv, torch.from_numpy(spans).cuda(), cap,
+                                         window=window, out_f16=False)
+    wstart = np.where((window > 0) & (spans > window), spans - window, 0).astype(np.int32)
+    want = orc.decode_attention(q.reshape(lanes, n_kv, gqa, 128), kb, vb, spans, wstart)
+    assert rel(np_(got), want.reshape(lanes, -1)) < 1e-5
+    tt.check()
+
+
+def test_decode_attention_pages_outside_pool(tt, orc):
+    """Block-table entries outside [0, num_blocks) read as zero rows and are reported as
+    out-of-range device data (not as a timeout); the other lanes are unaffected."""
+    from ttsnn import _lib as L
+    rng = np.random.default_rng(77)
+    lanes, n_kv, gqa, cap, bs = 6, 8, 2, 512, 32
+    spans = np.array([512, 300, 64, 511, 129, 33], np.int32)
+    q = rng.standard_normal((lanes, n_kv * gqa, 128), dtype=np.float32) * 0.1
+    kb = orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
+    vb = orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
+    kp, vp, table, nb = _paged(rng, kb, vb, bs)
+    bad = [(0, 3, -1), (1, 0, nb), (3, 15, nb + 7)]  # (lane, page, entry)
+    kz, vz = kb.copy(), vb.copy()
+    for lane, page, entry in bad:
+        table[lane, page] = entry
+        kz[lane, :, page * bs:(page + 1) * bs] = 0
+        vz[lane, :, page * bs:(page + 1) * bs] = 0
+    tdev = torch.from_numpy(table).cuda()
+    kv = L.KvCache(kp.data_ptr(), vp.data_ptr(), tdev.data_ptr(), cap // bs, bs, nb, n_kv, 128)
+    got = tt.attn.decode_attention_paged(dev_f32(q), kv, torch.from_numpy(spans).cuda(), cap,
+                                         out_f16=False)
+    with pytest.raises(tt.TtsError) as e:
+        tt.check()
+    assert e.value.status == 1  # TTS_ERR_INVALID_ARG: bad device data, not a timeout
+    assert "out of range" in str(e.value)
+    want = orc.decode_attention(q.reshape(lanes, n_kv, gqa, 128), kz, vz, spans, 0)
+    assert rel(np_(got), want.reshape(lanes, -1)) < 1e-5
+    tt.check()  # the flag was cleared by the previous check
+
+
+def test_decode_attention_rejects_unaligned_pages(tt):
+    from ttsnn import _lib as L
+    kp = torch.zeros(4, 8, 12, 128, dtype=torch.float16, device="cuda")
+    table = torch.zeros(2, 2, dtype=torch.int32, device="cuda")
+    kv = L.KvCache(kp.data_ptr(), kp.data_ptr(), table.data_ptr(), 2, 12, 4, 8, 128)
+    q = torch.zeros(2, 16, 128, device="cuda")
+    with pytest.raises(tt.TtsError) as e:
+        tt.attn.decode_attention_paged(q, kv, torch.full((2,), 20, dtype=torch.int32, device="cuda"), 24)
+    assert "multiple of 8" in str(e.value)
