@@ -245,6 +245,48 @@ TTS_DEV void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Four 32x32b.x16 loads (e.g. the same columns of four accumulators) behind one wait, so their
+// latencies overlap: v[i][c] = column c of address a_i.
+TTS_DEV void tmem_ld16x4(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, float (*v)[16]) {
+  uint32_t r[4][16];
+#define TTS_LD16(I, A)                                                                        \
+  asm volatile(                                                                               \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32"                                                \
+      " {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"                      \
+      : "=r"(r[I][0]), "=r"(r[I][1]), "=r"(r[I][2]), "=r"(r[I][3]), "=r"(r[I][4]),            \
+        "=r"(r[I][5]), "=r"(r[I][6]), "=r"(r[I][7]), "=r"(r[I][8]), "=r"(r[I][9]),            \
+        "=r"(r[I][10]), "=r"(r[I][11]), "=r"(r[I][12]), "=r"(r[I][13]), "=r"(r[I][14]),       \
+        "=r"(r[I][15])                                                                        \
+      : "r"(A))
+  TTS_LD16(0, a0);
+  TTS_LD16(1, a1);
+  TTS_LD16(2, a2);
+  TTS_LD16(3, a3);
+#undef TTS_LD16
+  // the wait names every destination register, so no use of them moves above it
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0][0]), "+r"(r[0][1]), "+r"(r[0][2]), "+r"(r[0][3]), "+r"(r[0][4]),
+                 "+r"(r[0][5]), "+r"(r[0][6]), "+r"(r[0][7]), "+r"(r[0][8]), "+r"(r[0][9]),
+                 "+r"(r[0][10]), "+r"(r[0][11]), "+r"(r[0][12]), "+r"(r[0][13]),
+                 "+r"(r[0][14]), "+r"(r[0][15]), "+r"(r[1][0]), "+r"(r[1][1]), "+r"(r[1][2]),
+                 "+r"(r[1][3]), "+r"(r[1][4]), "+r"(r[1][5]), "+r"(r[1][6]), "+r"(r[1][7]),
+                 "+r"(r[1][8]), "+r"(r[1][9]), "+r"(r[1][10]), "+r"(r[1][11]),
+                 "+r"(r[1][12]), "+r"(r[1][13]), "+r"(r[1][14]), "+r"(r[1][15]),
+                 "+r"(r[2][0]), "+r"(r[2][1]), "+r"(r[2][2]), "+r"(r[2][3]), "+r"(r[2][4]),
+                 "+r"(r[2][5]), "+r"(r[2][6]), "+r"(r[2][7]), "+r"(r[2][8]), "+r"(r[2][9]),
+                 "+r"(r[2][10]), "+r"(r[2][11]), "+r"(r[2][12]), "+r"(r[2][13]),
+                 "+r"(r[2][14]), "+r"(r[2][15]), "+r"(r[3][0]), "+r"(r[3][1]), "+r"(r[3][2]),
+                 "+r"(r[3][3]), "+r"(r[3][4]), "+r"(r[3][5]), "+r"(r[3][6]), "+r"(r[3][7]),
+                 "+r"(r[3][8]), "+r"(r[3][9]), "+r"(r[3][10]), "+r"(r[3][11]),
+                 "+r"(r[3][12]), "+r"(r[3][13]), "+r"(r[3][14]), "+r"(r[3][15])
+               :
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int c = 0; c < 16; ++c) v[i][c] = __uint_as_float(r[i][c]);
+}
+
 // ------------------------------------------------------------------ numerics
 // Monotone map of a float onto u32 so that an unsigned max picks the larger float.
 TTS_DEV uint32_t float_order_key(float f) {
