@@ -19,8 +19,10 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "ttsnn", "libtts_cuda.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["runtime.cu", "gemm_decode.cu", "attn_decode.cu", "ops_small.cu", "conv_nlc.cu"]
-HEADERS = ["tts_common.cuh", "tts_internal.h", "qkrope_row.cuh"]
+SOURCES = ["runtime.cu", "gemm_decode.cu", "attn_decode.cu", "chain.cu", "ops_small.cu",
+           "conv_nlc.cu"]
+HEADERS = ["tts_common.cuh", "tts_internal.h", "qkrope_row.cuh", "gemm_epilogue.cuh",
+           "l2_prefetch.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -63,7 +65,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
         subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = OUT + ".tmp"
-    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp, *objs]
+    # --no-undefined: a symbol missing from the objects fails the build, not the first load
+    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xlinker",
+           "--no-undefined", "-o", tmp, *objs]
     subprocess.run(cmd, check=True)
     os.replace(tmp, OUT)
     return OUT

@@ -30,6 +30,7 @@
 
 #include "tts_common.cuh"
 #include "tts_internal.h"
+#include "l2_prefetch.cuh"
 
 namespace tts {
 
@@ -65,6 +66,7 @@ struct AttnArgs {
   unsigned* counters;
   void* out;
   int out_f16;
+  L2Prefetch pf;  // the next GEMM's first weight blocks
 };
 
 // One K or V tile of a chunk: dims 0-63 / 64-127, each 128 rows x 128 B, 128-byte swizzle.
@@ -329,6 +331,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       prev = cur;
     }
+    // the cache is all requested: start on the output projection's weights
+    if (elect_one()) issue_l2_prefetch(a.pf, blockIdx.x, gridDim.x);
+    __syncwarp();
     if (!ok && a.err && lane == 0) atomicOr(a.err, kFlagAttnWait);
     // Leave no copy in flight: wait (bounded) for the last tiles issued to land.
     for (long long j = max(0ll, nk - kStages); j < nk; ++j)
@@ -790,6 +795,7 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
   a.counters = w.counters;
   a.out = r.out;
   a.out_f16 = r.out_f16 ? 1 : 0;
+  a.pf = r.next;
 
   int dev = 0;
   cudaGetDevice(&dev);

@@ -25,7 +25,8 @@
 
 #include "tts_common.cuh"
 #include "tts_internal.h"
-#include "qkrope_row.cuh"
+#include "gemm_epilogue.cuh"
+#include "l2_prefetch.cuh"
 
 namespace tts {
 
@@ -52,87 +53,9 @@ struct GemmArgs {
   unsigned long long* keys;
   int vocab;
   int codebooks;
+  L2Prefetch pf;  // the next GEMM's first weight blocks
 };
 
-// x * sigmoid(x) with the fast exponential and division intrinsics: the result is rounded to
-// f16, far coarser than their few-ulp error, and the IEEE division's branchy slow path kept the
-// rows of the epilogue from overlapping (measured ~3x slower per row).
-__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
-
-// One token row of one 128-row tile: lane owns rows 4*lane .. 4*lane + 3.
-__device__ __forceinline__ void epilogue_row(const GemmArgs& a, int tile, int j, int lane,
-                                             float4 acc) {
-  const int f0 = tile * kTileM + 4 * lane;
-  switch (a.epi) {
-    case EPI_F32: {
-      float* y = static_cast<float*>(a.y) + (size_t)j * a.ldy + f0;
-      *reinterpret_cast<float4*>(y) = acc;
-      break;
-    }
-    case EPI_F16: {
-      __half2* y = reinterpret_cast<__half2*>(static_cast<__half*>(a.y) + (size_t)j * a.ldy + f0);
-      y[0] = __floats2half2_rn(acc.x, acc.y);
-      y[1] = __floats2half2_rn(acc.z, acc.w);
-      break;
-    }
-    case EPI_RESIDUAL: {
-      float4* y = reinterpret_cast<float4*>(static_cast<float*>(a.y) + (size_t)j * a.ldy + f0);
-      float4 r = *y;
-      r.x += acc.x;
-      r.y += acc.y;
-      r.z += acc.z;
-      r.w += acc.w;
-      *y = r;
-      break;
-    }
-    case EPI_SWIGLU: {
-      // rows 0..63 of the tile are gate features, 64..127 the matching up features.
-      float4 p;
-      p.x = __shfl_xor_sync(0xffffffffu, acc.x, 16);
-      p.y = __shfl_xor_sync(0xffffffffu, acc.y, 16);
-      p.z = __shfl_xor_sync(0xffffffffu, acc.z, 16);
-      p.w = __shfl_xor_sync(0xffffffffu, acc.w, 16);
-      if (lane < 16) {
-        const int f = tile * (kTileM / 2) + 4 * lane;
-        __half2* y = reinterpret_cast<__half2*>(static_cast<__half*>(a.y) + (size_t)j * a.ldy + f);
-        y[0] = __floats2half2_rn(silu(acc.x) * p.x, silu(acc.y) * p.y);
-        y[1] = __floats2half2_rn(silu(acc.z) * p.z, silu(acc.w) * p.w);
-      }
-      break;
-    }
-    case EPI_QKROPE: {
-      // 128 rows = one head: q heads, then k heads, then v heads
-      float v[4] = {acc.x, acc.y, acc.z, acc.w};
-      qkrope_row(a.qk, tile, j, lane, v);
-      break;
-    }
-    case EPI_ARGMAX: {
-      if (a.y) {
-        float* y = static_cast<float*>(a.y) + (size_t)j * a.ldy + f0;
-        *reinterpret_cast<float4*>(y) = acc;
-      }
-      const int cb = (tile * kTileM) / a.vocab;
-      const int id0 = f0 - cb * a.vocab;
-      float v[4] = {acc.x, acc.y, acc.z, acc.w};
-      unsigned long long best = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        unsigned long long key =
-            (static_cast<unsigned long long>(float_order_key(v[i])) << 32) | unsigned(id0 + i);
-        best = key > best ? key : best;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-        best = other > best ? other : best;
-      }
-      if (lane == 0) atomicMax(a.keys + (size_t)j * a.codebooks + cb, best);
-      break;
-    }
-    default:
-      break;
-  }
-}
 
 constexpr int kThreads = 256;  // 8 warps: 0..3 producers, 4..7 MMA issuers + epilogue
 
@@ -232,6 +155,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
       }
+      // this pipeline's weights are all requested: start on the next GEMM's
+      if (pp == 0 && elect_one())
+        issue_l2_prefetch(a.pf, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+      __syncwarp();
     }
   } else {
     const int pp = warp - 4;
@@ -520,6 +447,23 @@ bool gemm_supported(int m, int k, int n, int epi, std::string* why) {
   return true;
 }
 
+L2Prefetch gemm_prefetch_plan(const void* w_packed, int m, int k, int n, int device,
+                              size_t budget) {
+  L2Prefetch pf;
+  if (!w_packed || !gemm_supported(m, k, n, EPI_F32, nullptr)) return pf;
+  const Plan p = plan_gemm(m, k, n, device, 0);
+  pf.w = static_cast<const __half*>(w_packed);
+  pf.tiles = n / kTileM;
+  pf.kb_total = k / kBlockK;
+  pf.splits = p.splits;
+  const size_t heads = size_t(pf.tiles) * pf.splits * kWBytes;  // one block per range
+  const int per_range = pf.kb_total / pf.splits;
+  pf.depth = int(std::max<size_t>(1, budget / heads));
+  // no deeper than what the next GEMM's pipelines request at once, nor its range
+  pf.depth = std::min(pf.depth, std::min(per_range, p.pipes * p.stages));
+  return pf;
+}
+
 cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t st, int device) {
   std::string why;
   if (!gemm_supported(r.m, r.k, r.n, r.epi, &why)) {
@@ -564,6 +508,7 @@ cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t
   a.keys = r.argmax_keys;
   a.vocab = r.vocab;
   a.codebooks = r.vocab > 0 ? r.n / r.vocab : 0;
+  a.pf = r.next;
 
   {
     // The opt-in shared-memory limit is a per-device function attribute.

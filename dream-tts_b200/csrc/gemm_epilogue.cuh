@@ -1,0 +1,150 @@
+// Epilogue of one token row of a 128-row weight tile, shared by the decode GEMM and the layer
+// chain: lane l holds rows 4l .. 4l + 3 of the tile for token row j.
+#pragma once
+#include "qkrope_row.cuh"
+#include "tts_common.cuh"
+#include "tts_internal.h"
+
+namespace tts {
+
+constexpr int kTileRows = 128;
+
+// x * sigmoid(x) with the fast exponential and division intrinsics: the result is rounded to
+// f16, far coarser than their few-ulp error, and the IEEE division's branchy slow path kept the
+// rows of the epilogue from overlapping (measured ~3x slower per row).
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// One token row of one 128-row tile: lane owns rows 4*lane .. 4*lane + 3.
+template <typename A>
+__device__ __forceinline__ void epilogue_row(const A& a, int tile, int j, int lane,
+                                             float4 acc) {
+  const int f0 = tile * kTileRows + 4 * lane;
+  switch (a.epi) {
+    case EPI_F32: {
+      float* y = static_cast<float*>(a.y) + (size_t)j * a.ldy + f0;
+      *reinterpret_cast<float4*>(y) = acc;
+      break;
+    }
+    case EPI_F16: {
+      __half2* y = reinterpret_cast<__half2*>(static_cast<__half*>(a.y) + (size_t)j * a.ldy + f0);
+      y[0] = __floats2half2_rn(acc.x, acc.y);
+      y[1] = __floats2half2_rn(acc.z, acc.w);
+      break;
+    }
+    case EPI_RESIDUAL: {
+      // an L2 read: within the layer chain other CTAs wrote this row earlier in the kernel
+      float4* y = reinterpret_cast<float4*>(static_cast<float*>(a.y) + (size_t)j * a.ldy + f0);
+      float4 r = __ldcg(y);
+      r.x += acc.x;
+      r.y += acc.y;
+      r.z += acc.z;
+      r.w += acc.w;
+      *y = r;
+      break;
+    }
+    case EPI_SWIGLU: {
+      // rows 0..63 of the tile are gate features, 64..127 the matching up features.
+      float4 p;
+      p.x = __shfl_xor_sync(0xffffffffu, acc.x, 16);
+      p.y = __shfl_xor_sync(0xffffffffu, acc.y, 16);
+      p.z = __shfl_xor_sync(0xffffffffu, acc.z, 16);
+      p.w = __shfl_xor_sync(0xffffffffu, acc.w, 16);
+      if (lane < 16) {
+        const int f = tile * (kTileRows / 2) + 4 * lane;
+        __half2* y = reinterpret_cast<__half2*>(static_cast<__half*>(a.y) + (size_t)j * a.ldy + f);
+        y[0] = __floats2half2_rn(silu(acc.x) * p.x, silu(acc.y) * p.y);
+        y[1] = __floats2half2_rn(silu(acc.z) * p.z, silu(acc.w) * p.w);
+      }
+      break;
+    }
+    case EPI_QKROPE: {
+      // 128 rows = one head: q heads, then k heads, then v heads
+      float v[4] = {acc.x, acc.y, acc.z, acc.w};
+      qkrope_row(a.qk, tile, j, lane, v);
+      break;
+    }
+    case EPI_ARGMAX: {
+      if (a.y) {
+        float* y = static_cast<float*>(a.y) + (size_t)j * a.ldy + f0;
+        *reinterpret_cast<float4*>(y) = acc;
+      }
+      const int cb = (tile * kTileRows) / a.vocab;
+      const int id0 = f0 - cb * a.vocab;
+      float v[4] = {acc.x, acc.y, acc.z, acc.w};
+      unsigned long long best = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        unsigned long long key =
+            (static_cast<unsigned long long>(float_order_key(v[i])) << 32) | unsigned(id0 + i);
+        best = key > best ? key : best;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+      }
+      if (lane == 0) atomicMax(a.keys + (size_t)j * a.codebooks + cb, best);
+      break;
+    }
+    default:
+      break;
+  }
+}
+
+// Token rows j0, j0 + step, ... (below m) of one tile, read from a [m][128] f32 tile in shared
+// memory, four rows at a time: a batch's global loads (residual rows, RoPE tables) are issued
+// before its first store.
+template <typename A>
+__device__ __forceinline__ void epilogue_rows(const A& a, int tile, int j0, int step, int m,
+                                              int lane, const float* red) {
+  for (int jb = j0; jb < m; jb += 4 * step) {
+    int j[4];
+    float4 acc[4];
+    int n = 0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      j[u] = jb + u * step;
+      acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j[u] < m) {
+        acc[u] = *reinterpret_cast<const float4*>(red + j[u] * kTileRows + 4 * lane);
+        n = u + 1;
+      }
+    }
+    if (a.epi == EPI_RESIDUAL) {
+      float4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        r[u] = u < n ? __ldcg(reinterpret_cast<const float4*>(static_cast<float*>(a.y) +
+                                                              (size_t)j[u] * a.ldy + tile * kTileRows +
+                                                              4 * lane))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (u >= n) break;
+        float4 o = r[u];
+        o.x += acc[u].x;
+        o.y += acc[u].y;
+        o.z += acc[u].z;
+        o.w += acc[u].w;
+        *reinterpret_cast<float4*>(static_cast<float*>(a.y) + (size_t)j[u] * a.ldy +
+                                   tile * kTileRows + 4 * lane) = o;
+      }
+    } else if (a.epi == EPI_QKROPE) {
+      float v[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        v[u][0] = acc[u].x;
+        v[u][1] = acc[u].y;
+        v[u][2] = acc[u].z;
+        v[u][3] = acc[u].w;
+      }
+      qkrope_rows4(a.qk, tile, j, n, lane, v);
+    } else {
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (u < n) epilogue_row(a, tile, j[u], lane, acc[u]);
+    }
+  }
+}
+
+}  // namespace tts

@@ -62,6 +62,9 @@ struct tts_stack {
   float* x_next = nullptr;    // [max_lanes][dim] (own buffer)
   float* feedback = nullptr;  // caller's buffer replacing x_next, or null
   unsigned long long* keys = nullptr;  // [max_lanes][codebooks]
+  // layer chain (steps of up to 128 lanes): phase counters and partial tiles
+  ChainWorkspace chain;
+  int chain_lanes = 0;  // lanes the partial buffer is sized for (0: no chain)
 };
 
 struct tts_graph {
@@ -521,6 +524,24 @@ tts_status tts_stack_create(tts_ctx* c, const tts_stack_geometry* geo, tts_stack
   if (e == cudaSuccess) e = dmalloc(&s->keys, size_t(L) * std::max(1, gm.codebooks) * 8);
   if (e == cudaSuccess) e = cudaMemset(s->keys, 0, size_t(L) * std::max(1, gm.codebooks) * 8);
   if (e == cudaSuccess) e = cudaMemset(s->x_next, 0, size_t(L) * gm.dim * 4);
+  // the layer chain serves steps of up to kMaxChainLanes lanes
+  s->chain_lanes = std::min(L, kMaxChainLanes);
+  {
+    const int nqkv = (gm.heads + 2 * gm.n_kv) * 128;
+    int tiles = std::max(std::max(nqkv, gm.dim), 2 * gm.ffn) / 128;
+    if (gm.codebooks > 0) tiles = std::max(tiles, gm.codebooks * gm.vocab / 128);
+    s->chain.max_tiles = tiles;
+    s->chain.part_bytes = chain_part_bytes(s->chain_lanes, num_sms(c->device));
+    s->chain.err = c->gemm.err;
+    const size_t cnt_bytes = size_t(2) * kMaxChainPhases * tiles * sizeof(unsigned);
+    if (e == cudaSuccess) e = dmalloc(&s->chain.part, s->chain.part_bytes);
+    if (e == cudaSuccess) e = dmalloc(&s->chain.done, kMaxChainPhases * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = dmalloc(&s->chain.exit_cnt, sizeof(unsigned));
+    if (e == cudaSuccess) e = dmalloc(&s->chain.tile_cnt, cnt_bytes);
+    if (e == cudaSuccess) e = cudaMemset(s->chain.done, 0, kMaxChainPhases * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemset(s->chain.exit_cnt, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(s->chain.tile_cnt, 0, cnt_bytes);
+  }
   if (e != cudaSuccess) {
     tts_stack_destroy(s);
     return cuda_status(e, "stack_create");
@@ -567,6 +588,10 @@ tts_status tts_stack_destroy(tts_stack* s) {
   cudaFree(s->act);
   cudaFree(s->x_next);
   cudaFree(s->keys);
+  cudaFree(s->chain.part);
+  cudaFree(s->chain.done);
+  cudaFree(s->chain.exit_cnt);
+  cudaFree(s->chain.tile_cnt);
   delete s;
   return TTS_OK;
 }
@@ -603,13 +628,21 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
                         "decode_step")) != TTS_OK)
     return rc;
 
-  for (int l = 0; l < gm.layers; ++l) {
+  // each projection (and the attention) prefetches the head of the next projection's weights
+  // into L2 once its own stream is out (separate-kernel path)
+  // (TTS_L2_PREFETCH_MB overrides the budget for A/B measurement; 0 turns it off)
+  const char* pf_env = getenv("TTS_L2_PREFETCH_MB");
+  const size_t pf_budget = size_t(pf_env && *pf_env ? atoi(pf_env) : 12) << 20;
+  auto pf = [&](const void* w, int k, int n) {
+    return pf_budget ? gemm_prefetch_plan(w, B, k, n, c->device, pf_budget) : L2Prefetch{};
+  };
+  auto pages = [&](int l, bool v) {
+    return (v ? static_cast<__half*>(st->v_pages) : static_cast<__half*>(st->k_pages)) +
+           layer_pages * l;
+  };
+  // the step's projections (qwen3.rs:339-463), as requests for either path
+  auto req_qkv = [&](int l) {
     const tts_layer_weights& w = s->layers[l];
-    __half* kp = static_cast<__half*>(st->k_pages) + layer_pages * l;
-    __half* vp = static_cast<__half*>(st->v_pages) + layer_pages * l;
-    // attention block (qwen3.rs:339-451)
-    TTS_TRY(launch_rms_norm(s->h, w.attn_norm, B, D, gm.eps, nullptr, s->xn, nullptr, 0, true, cs),
-            "rms_norm");
     GemmRequest r;
     r.w = static_cast<const __half*>(w.wqkv);
     r.packed = true;
@@ -628,17 +661,69 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     r.qk.num_blocks = st->num_blocks;
     r.qk.rope_len = gm.rope_len;
     r.qk.err = c->gemm.err;
-    r.qk.k_pool = kp;
-    r.qk.v_pool = vp;
+    r.qk.k_pool = pages(l, false);
+    r.qk.v_pool = pages(l, true);
     r.qk.q_out = s->q;
     r.qk.heads = gm.heads;
     r.qk.n_kv = gm.n_kv;
     r.qk.eps = gm.eps;
-    TTS_TRY(launch_gemm(r, c->gemm, cs, c->device), "proj");
+    return r;
+  };
+  auto req_o = [&](int l) {
+    GemmRequest o;
+    o.w = static_cast<const __half*>(s->layers[l].wo);
+    o.packed = true;
+    o.x = s->attn;
+    o.m = B;
+    o.k = qw;
+    o.n = D;
+    o.epi = EPI_RESIDUAL;
+    o.y = s->h;
+    return o;
+  };
+  auto req_gu = [&](int l) {
+    GemmRequest gu;
+    gu.w = static_cast<const __half*>(s->layers[l].w_gate_up);
+    gu.packed = true;
+    gu.x = s->xn;
+    gu.m = B;
+    gu.k = D;
+    gu.n = 2 * gm.ffn;
+    gu.epi = EPI_SWIGLU;
+    gu.y = s->act;
+    return gu;
+  };
+  auto req_dn = [&](int l) {
+    GemmRequest dn;
+    dn.w = static_cast<const __half*>(s->layers[l].w_down);
+    dn.packed = true;
+    dn.x = s->act;
+    dn.m = B;
+    dn.k = gm.ffn;
+    dn.n = D;
+    dn.epi = EPI_RESIDUAL;
+    dn.y = s->h;
+    return dn;
+  };
+  auto req_heads = [&]() {
+    GemmRequest hd;
+    hd.w = s->heads;
+    hd.packed = true;
+    hd.x = s->xn;
+    hd.m = B;
+    hd.k = D;
+    hd.n = gm.codebooks * gm.vocab;
+    hd.epi = EPI_ARGMAX;
+    hd.y = logits;
+    hd.argmax_keys = s->keys;
+    hd.vocab = gm.vocab;
+    return hd;
+  };
+  auto req_attn = [&](int l) {
     AttnRequest ar;
     ar.q = s->q;
-    ar.k_pool = kp;
-    ar.v_pool = vp;
+    ar.k_pool = pages(l, false);
+    ar.v_pool = pages(l, true);
     ar.block_table = st->block_table;
     ar.max_blocks = st->max_blocks;
     ar.block_size = st->block_size;
@@ -653,62 +738,103 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     ar.gqa = gm.heads / gm.n_kv;
     ar.out = s->attn;
     ar.out_f16 = true;
-    TTS_TRY(launch_attn(ar, c->attn, cs), "decode_attention");
-    GemmRequest o;
-    o.w = static_cast<const __half*>(w.wo);
-    o.packed = true;
-    o.x = s->attn;
-    o.m = B;
-    o.k = qw;
-    o.n = D;
-    o.epi = EPI_RESIDUAL;
-    o.y = s->h;
-    TTS_TRY(launch_gemm(o, c->gemm, cs, c->device), "proj");
-    // feed-forward block (qwen3.rs:453-463)
-    TTS_TRY(launch_rms_norm(s->h, w.ffn_norm, B, D, gm.eps, nullptr, s->xn, nullptr, 0, true, cs),
-            "rms_norm");
-    GemmRequest gu;
-    gu.w = static_cast<const __half*>(w.w_gate_up);
-    gu.packed = true;
-    gu.x = s->xn;
-    gu.m = B;
-    gu.k = D;
-    gu.n = 2 * gm.ffn;
-    gu.epi = EPI_SWIGLU;
-    gu.y = s->act;
-    TTS_TRY(launch_gemm(gu, c->gemm, cs, c->device), "proj");
-    GemmRequest dn;
-    dn.w = static_cast<const __half*>(w.w_down);
-    dn.packed = true;
-    dn.x = s->act;
-    dn.m = B;
-    dn.k = gm.ffn;
-    dn.n = D;
-    dn.epi = EPI_RESIDUAL;
-    dn.y = s->h;
-    TTS_TRY(launch_gemm(dn, c->gemm, cs, c->device), "proj");
-  }
-  // final norm (qwen3.rs:466), heads + greedy pick, next input
+    return ar;
+  };
   const int nkeys = s->heads ? B * gm.codebooks : 0;
-  TTS_TRY(launch_rms_norm(s->h, s->final_norm, B, D, gm.eps, h_out, s->xn, s->heads ? s->keys : nullptr,
-                          nkeys, true, cs),
-          "rms_norm");
-  if (s->heads) {
-    GemmRequest hd;
-    hd.w = s->heads;
-    hd.packed = true;
-    hd.x = s->xn;
-    hd.m = B;
-    hd.k = D;
-    hd.n = gm.codebooks * gm.vocab;
-    hd.epi = EPI_ARGMAX;
-    hd.y = logits;
-    hd.argmax_keys = s->keys;
-    hd.vocab = gm.vocab;
-    TTS_TRY(launch_gemm(hd, c->gemm, cs, c->device), "proj");
-    TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, s->embed, D, codes,
-                                 s->embed ? next : nullptr, nullptr, true, cs),
-            "keys_to_codes");
+
+  // Opt-in (TTS_CHAIN=1): the layer chain runs everything between two attentions as one
+  // persistent kernel, per layer the attention, then [O, norm, gate/up, down, next norm, next
+  // QKV] (or the final norm and the heads after the last layer). Measured on B200 at 48 lanes
+  // it is slower than the separate kernels (its cross-CTA reductions and phase barriers cost
+  // more per projection than a kernel boundary under programmatic dependent launch), so the
+  // separate kernels are the default.
+  const char* chain_env = getenv("TTS_CHAIN");
+  const bool use_chain = B <= s->chain_lanes && chain_env && *chain_env == '1';
+  if (use_chain) {
+    auto gemm_ph = [](const GemmRequest& g) {
+      ChainPhaseRequest p;
+      p.kind = CHAIN_GEMM;
+      p.gemm = g;
+      return p;
+    };
+    auto norm_ph = [&](const float* wn, float* y32, unsigned long long* zk, int nk) {
+      ChainPhaseRequest p;
+      p.kind = CHAIN_NORM;
+      p.norm_src = s->h;
+      p.norm_w = wn;
+      p.norm_dst16 = s->xn;
+      p.norm_dst32 = y32;
+      p.zero_keys = zk;
+      p.n_keys = nk;
+      return p;
+    };
+    ChainRequest k0;
+    k0.m = B;
+    k0.dim = D;
+    k0.eps = gm.eps;
+    k0.nph = 2;
+    k0.ph[0] = norm_ph(s->layers[0].attn_norm, nullptr, nullptr, 0);
+    k0.ph[1] = gemm_ph(req_qkv(0));
+    TTS_TRY(launch_chain(k0, s->chain, cs, c->device), "layer_chain");
+    for (int l = 0; l < gm.layers; ++l) {
+      TTS_TRY(launch_attn(req_attn(l), c->attn, cs), "decode_attention");
+      ChainRequest kr;
+      kr.m = B;
+      kr.dim = D;
+      kr.eps = gm.eps;
+      kr.ph[kr.nph++] = gemm_ph(req_o(l));
+      kr.ph[kr.nph++] = norm_ph(s->layers[l].ffn_norm, nullptr, nullptr, 0);
+      kr.ph[kr.nph++] = gemm_ph(req_gu(l));
+      kr.ph[kr.nph++] = gemm_ph(req_dn(l));
+      if (l + 1 < gm.layers) {
+        kr.ph[kr.nph++] = norm_ph(s->layers[l + 1].attn_norm, nullptr, nullptr, 0);
+        kr.ph[kr.nph++] = gemm_ph(req_qkv(l + 1));
+      } else {
+        kr.ph[kr.nph++] = norm_ph(s->final_norm, h_out, s->heads ? s->keys : nullptr, nkeys);
+        if (s->heads) kr.ph[kr.nph++] = gemm_ph(req_heads());
+      }
+      TTS_TRY(launch_chain(kr, s->chain, cs, c->device), "layer_chain");
+    }
+    if (s->heads)
+      TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, s->embed, D, codes,
+                                   s->embed ? next : nullptr, nullptr, true, cs),
+              "keys_to_codes");
+  } else {
+    for (int l = 0; l < gm.layers; ++l) {
+      const tts_layer_weights& w = s->layers[l];
+      // attention block (qwen3.rs:339-451)
+      TTS_TRY(launch_rms_norm(s->h, w.attn_norm, B, D, gm.eps, nullptr, s->xn, nullptr, 0, true, cs),
+              "rms_norm");
+      TTS_TRY(launch_gemm(req_qkv(l), c->gemm, cs, c->device), "proj");
+      AttnRequest ar = req_attn(l);
+      ar.next = pf(w.wo, qw, D);
+      TTS_TRY(launch_attn(ar, c->attn, cs), "decode_attention");
+      GemmRequest o = req_o(l);
+      o.next = pf(w.w_gate_up, D, 2 * gm.ffn);
+      TTS_TRY(launch_gemm(o, c->gemm, cs, c->device), "proj");
+      // feed-forward block (qwen3.rs:453-463)
+      TTS_TRY(launch_rms_norm(s->h, w.ffn_norm, B, D, gm.eps, nullptr, s->xn, nullptr, 0, true, cs),
+              "rms_norm");
+      GemmRequest gu = req_gu(l);
+      gu.next = pf(w.w_down, gm.ffn, D);
+      TTS_TRY(launch_gemm(gu, c->gemm, cs, c->device), "proj");
+      GemmRequest dn = req_dn(l);
+      if (l + 1 < gm.layers)
+        dn.next = pf(s->layers[l + 1].wqkv, D, nqkv);
+      else if (s->heads)
+        dn.next = pf(s->heads, D, gm.codebooks * gm.vocab);
+      TTS_TRY(launch_gemm(dn, c->gemm, cs, c->device), "proj");
+    }
+    // final norm (qwen3.rs:466), heads + greedy pick, next input
+    TTS_TRY(launch_rms_norm(s->h, s->final_norm, B, D, gm.eps, h_out, s->xn,
+                            s->heads ? s->keys : nullptr, nkeys, true, cs),
+            "rms_norm");
+    if (s->heads) {
+      TTS_TRY(launch_gemm(req_heads(), c->gemm, cs, c->device), "proj");
+      TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, s->embed, D, codes,
+                                   s->embed ? next : nullptr, nullptr, true, cs),
+              "keys_to_codes");
+    }
   }
   TTS_TRY(launch_advance_positions(st->positions, B, true, cs), "advance_positions");
 #undef TTS_TRY

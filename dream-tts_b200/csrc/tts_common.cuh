@@ -32,6 +32,8 @@ TTS_DEV void mbar_arrive(uint64_t* bar) {
 }
 // Generic-proxy shared-memory writes made visible to the async proxy (tcgen05.mma operands).
 TTS_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// The same for global memory: generic stores that a TMA load (async proxy) reads later.
+TTS_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 // Named barrier over `n` threads (whole warps) that also ANDs a predicate across them, so a
 // group of warps takes one uniform branch after a bounded wait.
 TTS_DEV bool bar_and(uint32_t id, uint32_t n, bool p) {
@@ -122,6 +124,14 @@ TTS_DEV void tma_load_4d(void* smem_dst, const void* desc, uint64_t* bar, int c0
       "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
       "r"(c3)
       : "memory");
+}
+// Prefetch `bytes` (a multiple of 16, from a 16-byte aligned address) into L2; no completion
+// to wait for.
+TTS_DEV void l2_prefetch_bulk(const void* src, uint32_t bytes, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(src)),
+               "r"(bytes), "l"(policy)
+               : "memory");
 }
 // L2 eviction-priority policies for streamed (read once) and reused operands.
 TTS_DEV uint64_t l2_policy_evict_first() {

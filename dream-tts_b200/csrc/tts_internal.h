@@ -20,7 +20,8 @@ const char* last_error();
 constexpr int kFlagGemmWait = 1 | 2 | 4;
 constexpr int kFlagConvWait = 16 | 32 | 64 | 128 | 4096 | 8192;
 constexpr int kFlagAttnWait = 2048;
-constexpr int kFlagWaitMask = kFlagGemmWait | kFlagConvWait | kFlagAttnWait;
+constexpr int kFlagChainWait = 16384;
+constexpr int kFlagWaitMask = kFlagGemmWait | kFlagConvWait | kFlagAttnWait | kFlagChainWait;
 // Device data outside what the launch covers (the rows involved are skipped or read as zero):
 constexpr int kFlagRopeRange = 256;   // position outside the RoPE table, block table or pool
 constexpr int kFlagSpanRange = 512;   // attention span outside 1..min(max_span, table)
@@ -58,6 +59,18 @@ struct QkRopeArgs {
   float eps = 1e-6f;
 };
 
+// The next projection's packed weights, for an L2 prefetch issued at the end of a kernel's own
+// weight or cache stream (when HBM would otherwise idle through that kernel's epilogue and the
+// next kernel's start): the first `depth` 128x64 tiles of every (128-row tile, split-K range)
+// of the next GEMM, i.e. the blocks its CTAs load first.
+struct L2Prefetch {
+  const __half* w = nullptr;  // packed [tiles][kb_total][128][64]
+  int tiles = 0, kb_total = 0, splits = 1, depth = 0;
+};
+// The prefetch plan for a packed weight [n][k] read by a GEMM of m lanes, about `budget` bytes.
+L2Prefetch gemm_prefetch_plan(const void* w_packed, int m, int k, int n, int device,
+                              size_t budget);
+
 struct GemmRequest {
   // [n][k] (out-major, K contiguous), or packed: [n/128][k/64][128][64], each 128 x 64 tile
   // one contiguous 16 KB block (tts_weight_pack)
@@ -73,6 +86,7 @@ struct GemmRequest {
   int vocab = 0;
   bool pdl = true;
   int force_splits = 0;  // 0 = automatic
+  L2Prefetch next;       // optional: the next GEMM's first weight blocks
 };
 
 struct Workspace {
@@ -81,6 +95,43 @@ struct Workspace {
 
 bool gemm_supported(int m, int k, int n, int epi, std::string* why);
 cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t st, int device);
+
+// ------------------------------------------------------------------ layer chain
+// A run of projections and RMS norms as one persistent kernel (chain.cu).
+constexpr int kMaxChainPhases = 6;
+constexpr int kMaxChainLanes = 128;
+enum ChainKind : int { CHAIN_GEMM = 0, CHAIN_NORM = 1 };
+struct ChainPhaseRequest {
+  int kind = CHAIN_GEMM;
+  GemmRequest gemm;  // CHAIN_GEMM: packed weights, x [m][k] f16, epilogue as for launch_gemm
+  // CHAIN_NORM: dst16[r] (and dst32[r] when set) = src[r] / rms(src[r]) * w; zeroes keys
+  const float* norm_src = nullptr;
+  const float* norm_w = nullptr;
+  __half* norm_dst16 = nullptr;
+  float* norm_dst32 = nullptr;
+  unsigned long long* zero_keys = nullptr;
+  int n_keys = 0;
+};
+struct ChainRequest {
+  int m = 0, dim = 0;  // lanes; row width of the norm phases
+  float eps = 1e-6f;
+  int nph = 0;
+  ChainPhaseRequest ph[kMaxChainPhases];
+  bool pdl = true;
+};
+struct ChainWorkspace {
+  unsigned long long* done = nullptr;  // [kMaxChainPhases], zero between launches
+  unsigned* exit_cnt = nullptr;        // zero between launches
+  unsigned* tile_cnt = nullptr;        // [2][kMaxChainPhases][max_tiles], zero between launches
+  int max_tiles = 0;
+  float* part = nullptr;
+  size_t part_bytes = 0;
+  int* err = nullptr;
+};
+bool chain_supported(int m, std::string* why);
+size_t chain_part_bytes(int m, int grid);
+cudaError_t launch_chain(const ChainRequest& r, const ChainWorkspace& w, cudaStream_t st,
+                         int device);
 
 // ------------------------------------------------------------------ decode attention
 struct AttnRequest {
@@ -100,6 +151,7 @@ struct AttnRequest {
   void* out = nullptr;  // [lanes][n_kv*gqa*128]
   bool out_f16 = true;
   bool pdl = true;
+  L2Prefetch next;  // optional: the next GEMM's first weight blocks
 };
 struct AttnWorkspace {
   float* part = nullptr;
