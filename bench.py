@@ -33,6 +33,8 @@ METRIC = "codec frames/sec (48-lane decode, whole box)"
 UNIT = "frames/s"
 LANES, LAYERS, DIM, HEADS, N_KV, HD, FFN, CB, VOCAB = 48, 28, 2048, 16, 8, 128, 6144, 16, 2048
 BLOCK = 32
+# DRAM bytes (read + write) of one gate/up launch at 48 lanes, from its ncu capture
+GATEUP_NCU_TRAFFIC = 50_606_336 + 6_912
 KV_LO, KV_HI = 64, 1024
 WORKLOAD = ("config[2]: full talker decode step, 28 layers, hidden 2048, 16q/8kv heads x 128, "
             "SwiGLU 6144, f16 weights N(0,0.02), 16 codebook heads x 2048, greedy; 48 lanes, "
@@ -491,7 +493,9 @@ def run_b200(args):
             "roofline": {"bound": "hbm", "kernel": "gemm_decode (gate/up, SwiGLU epilogue)",
                          "achieved": round(gemm_bytes / gemm_s / 1e9, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(gemm_bytes / gemm_s / 1e9 / hbm, 4),
-                         "traffic": None, "peak_source": peak_kind,
+                         "traffic": GATEUP_NCU_TRAFFIC,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one cold launch (profiles/gemm_decode_gateup_config2.md)",
+                         "peak_source": peak_kind,
                          "algorithmic_bytes_per_launch": gemm_bytes,
                          "launch_us": round(gemm_s * 1e6, 2)},
             "roofline_step": {"bound": "hbm", "achieved": round(step_bytes / step_s / 1e9, 1),
