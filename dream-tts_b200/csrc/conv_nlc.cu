@@ -3,8 +3,11 @@
 //
 // The B200 form of tts-nn's fused `nlc_conv_f32` (crates/tts-nn/src/nlcconv.rs:15-198 and
 // crates/tts-nn/src/nlc.rs:40-132): the tap gather happens inside the GEMM, so no im2col matrix
-// exists. GEMM view: M = output positions (128 per CTA), N = output channels (<= 512 per CTA,
-// the whole TMEM as 128 x 512 f32), K = taps x input channels.
+// exists. GEMM view: M = output positions, N = output channels, K = taps x input channels.
+// A CTA computes MS (1 or 2) sub-tiles of 128 positions against the same weight tiles: with
+// N <= 256 per CTA the two accumulators fill the 512 TMEM columns and every weight tile read
+// from L2 feeds twice the MMAs (the weight stream, not the tensor core, limited the single
+// sub-tile form: measured 35% tensor-pipe activity at 1 sub-tile x N = 512).
 //
 // For each 64-channel block, one TMA load brings a "halo" of R = 128 + (k-1)*dil input rows
 // into shared memory in the no-swizzle K-major core-matrix layout: slab g (8 channels) holds
@@ -15,9 +18,9 @@
 // len are zero-filled by TMA, and snake(0) = 0, so padding matches the reference's
 // pad-then-activate order.
 //
-// Warp roles (224 threads): warp 0 lane 0 issues the weight tiles (B ring), warp 1 lane 0 the
-// MMAs, warps 2..5 issue the halos (A ring), apply the snake and run the epilogue, warp 6 is
-// spare. Every wait is bounded; a wait that gives up sets an error flag the host reads.
+// Warp roles (224 threads): warp 0 issues the weight tiles (B ring), warp 1 the MMAs (each
+// from one elected lane of the converged warp), warps 2..5 issue the halos (A ring, one halo
+// per sub-tile), apply the snake and run the epilogue, warp 6 is spare. Every wait is bounded; a wait that gives up sets an error flag the host reads.
 #include <algorithm>
 #include <mutex>
 
@@ -28,17 +31,18 @@ namespace tts {
 
 namespace {
 
-constexpr int kRows = 128;      // output positions per CTA
+constexpr int kRows = 128;      // output positions per sub-tile (the MMA's M)
 constexpr int kCB = 64;         // input channels per halo
-constexpr int kAStages = 3;     // halo ring
-constexpr int kBStages = 2;     // weight-tile ring
 constexpr int kThreads = 224;
 
 struct ConvArgs {
   int b, len, cin, cout, k, dil, pad_left;
   int cout_cta;  // output channels per CTA (<= 512)
-  int nh, nper;  // MMAs per K step and N of each
+  int nh, nper;  // MMAs per K step and sub-tile, and N of each
+  int ms;        // 128-position sub-tiles per CTA (1 or 2), one accumulator each
+  int acc_stride;  // TMEM columns between the sub-tiles' accumulators
   int R;         // halo rows (multiple of 8)
+  int as, bs;    // halo and weight ring depths
   int tmem_cols;
   const float* bias;
   const float* alpha;
@@ -48,13 +52,17 @@ struct ConvArgs {
   int* err;
 };
 
+// SnakeBeta on 8 f16 channels in place. The fast hardware sine is used: its absolute error
+// (about 2^-21 near the origin, growing slowly with the argument) stays far below the f16
+// rounding of the result, while the accurate sinf's range reduction made the snake, applied to
+// every halo element, cost as much as the MMAs it feeds.
 __device__ __forceinline__ void snake8(uint4& u, const float* alpha, const float* brecip) {
   __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     float2 f = __half22float2(h[q]);
-    const float s0 = sinf(__ldg(alpha + 2 * q) * f.x);
-    const float s1 = sinf(__ldg(alpha + 2 * q + 1) * f.y);
+    const float s0 = __sinf(__ldg(alpha + 2 * q) * f.x);
+    const float s1 = __sinf(__ldg(alpha + 2 * q + 1) * f.y);
     f.x = f.x + __ldg(brecip + 2 * q) * (s0 * s0);
     f.y = f.y + __ldg(brecip + 2 * q + 1) * (s1 * s1);
     h[q] = __floats2half2_rn(f.x, f.y);
@@ -67,11 +75,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  const int l0 = blockIdx.x * kRows;
+  const int kAStages = a.as, kBStages = a.bs;
+  const int l0 = blockIdx.x * kRows * a.ms;
   const int bb = blockIdx.y;
   const int co0 = blockIdx.z * a.cout_cta;
   const int ncb = a.cin / kCB;
-  const uint32_t a_bytes = uint32_t(a.R) * kCB * 2;        // 8 slabs x R rows x 16 B
+  const uint32_t halo_bytes = uint32_t(a.R) * kCB * 2;     // 8 slabs x R rows x 16 B
+  const uint32_t a_bytes = halo_bytes * uint32_t(a.ms);     // one halo per sub-tile
   const uint32_t b_bytes = uint32_t(a.cout_cta) * kCB * 2;  // cout_cta rows x 128 B
   uint8_t* a_base = smem;
   uint8_t* b_base = smem + kAStages * a_bytes;
@@ -156,10 +166,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t hb = smem_u32(b_base + sb * b_bytes);
 #pragma unroll
           for (int kk = 0; kk < kCB / 16; ++kk) {
-            const uint64_t ad = desc_k_interleave(ha + 2 * kk * slab + t * a.dil * 16, slab);
             for (int h = 0; h < a.nh; ++h) {
               const uint64_t bd = desc_k_sw128(hb + h * a.nper * 128 + kk * 32);
-              umma_f16(tmem + h * a.nper, ad, bd, idesc, (i | kk) != 0);
+              for (int j = 0; j < a.ms; ++j) {
+                const uint64_t ad =
+                    desc_k_interleave(ha + j * halo_bytes + 2 * kk * slab + t * a.dil * 16, slab);
+                umma_f16(tmem + j * a.acc_stride + h * a.nper, ad, bd, idesc, (i | kk) != 0);
+              }
             }
           }
           umma_commit(&empty_b[sb]);
@@ -184,7 +197,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (elect_one()) {
         mbar_arrive_expect_tx(&full_a[s], a_bytes);
-        tma_load_4d(a_base + s * a_bytes, &tmX, &full_a[s], 0, l0 - a.pad_left, cb * (kCB / 8), bb);
+        for (int j = 0; j < a.ms; ++j)
+          tma_load_4d(a_base + s * a_bytes + j * halo_bytes, &tmX, &full_a[s], 0,
+                      l0 + j * kRows - a.pad_left, cb * (kCB / 8), bb);
       }
       __syncwarp();
     };
@@ -196,12 +211,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tt == 0) atomicOr(a.err, 4096);
       }
       if (a.alpha) {
-        uint8_t* halo = a_base + s * a_bytes;
-        const int chunks = 8 * a.R;
-        for (int c = tt; c < chunks; c += 128) {
-          const int g = c / a.R;
+        uint8_t* halos = a_base + s * a_bytes;
+        const int chunks = 8 * a.R;  // per halo
+        for (int c = tt; c < chunks * a.ms; c += 128) {
+          const int g = (c % chunks) / a.R;
           const int ch = cb * kCB + g * 8;
-          uint4* p = reinterpret_cast<uint4*>(halo) + c;
+          uint4* p = reinterpret_cast<uint4*>(halos) + c;
           uint4 u = *p;
           snake8(u, a.alpha + ch, a.brecip + ch);
           *p = u;
@@ -219,23 +234,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!mbar_wait(done, 0) && lane == 0) atomicOr(a.err, 8192);
     tc_fence_after();
     const int quad = warp & 3;
-    const int l = l0 + quad * 32 + lane;
-    const bool live = l < a.len;
-    const size_t row = ((size_t)bb * a.len + (live ? l : 0)) * a.cout + co0;
-    for (int c0 = 0; c0 < a.cout_cta; c0 += 16) {
-      float v[16];
-      tmem_ld16(tmem + (uint32_t(quad * 32) << 16) + c0, v);
-      if (!live) continue;
+    // 64 columns per TMEM wait; the residual of the next 64 columns is read while this batch
+    // is finished, so the row's residual loads overlap instead of adding up
+    auto finish16 = [&](float* v, const uint4* rr, int c0, size_t row, bool live) {
+      if (!live) return;
       if (a.bias) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] += __ldg(a.bias + co0 + c0 + i);
       }
       if (a.res) {
-        const uint4* rp = reinterpret_cast<const uint4*>(a.res + row + c0);
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
-          uint4 u = rp[hh];
-          const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+          const __half2* h2 = reinterpret_cast<const __half2*>(&rr[hh]);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const float2 f = __half22float2(h2[q]);
@@ -251,6 +261,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint4* yp = reinterpret_cast<uint4*>(a.y + row + c0);
       yp[0] = o[0];
       yp[1] = o[1];
+    };
+    const int c64 = a.cout_cta / 64 * 64;  // columns done 64 at a time
+    for (int j = 0; j < a.ms; ++j) {
+      const int l = l0 + j * kRows + quad * 32 + lane;
+      const bool live = l < a.len;
+      const size_t row = ((size_t)bb * a.len + (live ? l : 0)) * a.cout + co0;
+      const uint32_t acc = tmem + (uint32_t(quad * 32) << 16) + uint32_t(j * a.acc_stride);
+      const uint4* rp = reinterpret_cast<const uint4*>(a.res + row);  // 8 channels per uint4
+      const bool rd = a.res && live;
+      uint4 rnext[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        rnext[q] = (rd && q * 8 < c64) ? rp[q] : make_uint4(0, 0, 0, 0);
+      for (int c0 = 0; c0 < c64; c0 += 64) {
+        uint4 rcur[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) rcur[q] = rnext[q];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          rnext[q] = (rd && c0 + 64 + q * 8 < c64) ? rp[(c0 + 64) / 8 + q] : make_uint4(0, 0, 0, 0);
+        float v[4][16];
+        tmem_ld16x4(acc + c0, acc + c0 + 16, acc + c0 + 32, acc + c0 + 48, v);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) finish16(v[i], rcur + 2 * i, c0 + 16 * i, row, live);
+      }
+      for (int c0 = c64; c0 < a.cout_cta; c0 += 16) {
+        float v[16];
+        tmem_ld16(acc + c0, v);
+        uint4 rr[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+        if (rd) {
+          rr[0] = rp[c0 / 8];
+          rr[1] = rp[c0 / 8 + 1];
+        }
+        finish16(v, rr, c0, row, live);
+      }
     }
   }
   tc_fence_before();
@@ -309,12 +354,18 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
   a.k = r.k;
   a.dil = r.dil;
   a.pad_left = r.pad_left;
-  // output channels per CTA: all of them up to 512, else the largest of 512/256/128/64/32
-  // that divides cout
-  a.cout_cta = r.cout;
-  if (r.cout > 512) {
+  // Output channels per CTA: all of them up to 256, else 256 when it divides cout, else all
+  // up to 512 (two MMAs of N = cout/2), else the largest of 128/64/32 that divides cout. With
+  // N <= 256 a CTA takes two 128-position sub-tiles (when the input is that long).
+  if (r.cout <= 256)
+    a.cout_cta = r.cout;
+  else if (r.cout % 256 == 0)
+    a.cout_cta = 256;
+  else if (r.cout <= 512)
+    a.cout_cta = r.cout;
+  else {
     a.cout_cta = 32;
-    for (int c : {512, 256, 128, 64})
+    for (int c : {128, 64})
       if (r.cout % c == 0) {
         a.cout_cta = c;
         break;
@@ -322,9 +373,31 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
   }
   a.nh = a.cout_cta > 256 ? 2 : 1;
   a.nper = a.cout_cta / a.nh;
+  a.ms = (a.cout_cta <= 256 && r.len > kRows) ? 2 : 1;
+  {
+    // TTS_CONV_SUBTILES=1 forces one sub-tile per CTA (A/B measurement)
+    const char* v = getenv("TTS_CONV_SUBTILES");
+    if (v && *v == '1') a.ms = 1;
+  }
+  a.acc_stride = 32;
+  while (a.acc_stride < a.cout_cta) a.acc_stride *= 2;
+  a.tmem_cols = a.acc_stride * a.ms;
   a.R = (kRows + (r.k - 1) * r.dil + 7) / 8 * 8;
-  a.tmem_cols = 32;
-  while (a.tmem_cols < a.cout_cta) a.tmem_cols *= 2;
+  // ring depths: the weight tiles are the steady stream (one per tap), halos one per 64 input
+  // channels; fill what fits in 224 KB, at least two of each
+  {
+    const size_t halo = size_t(a.ms) * a.R * kCB * 2, wt = size_t(a.cout_cta) * kCB * 2;
+    const size_t budget = 224 * 1024;
+    a.as = 2;
+    a.bs = int(std::min<size_t>(4, (budget - 2 * halo) / wt));
+    if (a.bs < 2) a.bs = 2;
+    if (a.bs >= 4 && 3 * halo + 4 * wt <= budget) a.as = 3;
+    // TTS_CONV_AS / TTS_CONV_BS override the ring depths (A/B measurement)
+    const char* va = getenv("TTS_CONV_AS");
+    const char* vb = getenv("TTS_CONV_BS");
+    if (va && *va) a.as = std::max(2, std::min(4, atoi(va)));
+    if (vb && *vb) a.bs = std::max(2, std::min(6, atoi(vb)));
+  }
   a.bias = r.bias;
   a.alpha = r.alpha;
   a.brecip = r.brecip;
@@ -352,7 +425,7 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     set_error("conv1d: weight tensor map rejected");
     return cudaErrorInvalidValue;
   }
-  const size_t smem = size_t(kAStages) * a.R * kCB * 2 + size_t(kBStages) * a.cout_cta * kCB * 2 +
+  const size_t smem = size_t(a.as) * a.ms * a.R * kCB * 2 + size_t(a.bs) * a.cout_cta * kCB * 2 +
                       1024 + 256;
   {
     // The opt-in shared-memory limit is a per-device function attribute.
@@ -371,7 +444,7 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     return cudaErrorInvalidValue;
   }
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3((r.len + kRows - 1) / kRows, r.b, r.cout / a.cout_cta);
+  cfg.gridDim = dim3((r.len + kRows * a.ms - 1) / (kRows * a.ms), r.b, r.cout / a.cout_cta);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
