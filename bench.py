@@ -336,6 +336,92 @@ def run_sweep(args):
     return 0
 
 
+def run_document(args):
+    """Benchmark config[4] (bounded sample): a synthetic document of `--segments` segments per
+    GPU (2000 in the config) with target lengths log-uniform in [40, 1200] frames, decoded by
+    the talker at `--lanes` lanes with tail shedding and interior refill, then turned into 24 kHz
+    audio by the codec decoder stack (x2 x2 pre-upsample, x8 x5 x4 x3 transposed convs 1024 ->
+    64, three snake residual blocks after each, random-init) over each segment's chunk windows
+    (300 frames + 25 left context + 8 frames of lookahead for the 'same'-padded blocks), all
+    windows of a rank decoded in batches. The codec's RVQ dequantiser and pre-transformer are
+    not on this path: seeded random latents stand in for its input. Segments are split over the
+    ranks by LPT, no collective on the data path. frames/s = all frames / max over ranks of
+    (talker + codec device time); rtf = that time / audio seconds (12.5 frames per second)."""
+    import torch
+    import torch.distributed as dist
+    from qwen3tts.codec import SAMPLES_PER_FRAME, WaveStack, chunk_plan, gather_windows
+    from qwen3tts.talker import Talker, plan_groups, shard_groups, synthetic_segments
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    n_segments = args.segments * world
+    segs = synthetic_segments(n_segments, seed=0)
+    groups = plan_groups(segs, args.lanes)
+    mine = shard_groups(groups, world)[rank]
+    queue = [s for g in mine for s in g]
+    stack, _, _, _ = build_device_talker(device, seed=0, extra_positions=0, lanes_override=0)
+    talker = Talker(stack, max_lanes=args.lanes, capacity=157 + 1200 + 2)
+    talker.run([type(s)(s.index, s.prompt_len, min(s.frames, 2), 0) for s in queue[: args.lanes]])
+
+    # codec windows of every segment of this shard, one uniform span
+    right = 8
+    span = 300 + 25 + right
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    wins = []
+    for sg in queue:
+        lat = torch.randn(sg.frames, 1024, generator=gen, device=device).half()
+        for w in chunk_plan(sg.frames, right=right):
+            idx = torch.arange(w.lo, w.lo + span, device=device).clamp(max=w.hi - 1)
+            wins.append(lat.index_select(0, idx))
+    codec = WaveStack(device, seed=7)
+    batch = 16
+    xs = [torch.stack(wins[i:i + batch]) for i in range(0, len(wins), batch)]
+    codec(xs[0][:1])  # warm-up
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    st = talker.run(queue, refill=True)
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    samples = 0
+    for xb in xs:
+        samples += codec(xb).numel()
+    e1.record()
+    torch.cuda.synchronize()
+    codec_s = e0.elapsed_time(e1) * 1e-3
+    flops = codec.flops_per_frame() * len(wins) * span
+    t = torch.tensor([st.seconds + codec_s, st.seconds, codec_s, st.frames, flops, samples],
+                     device=device, dtype=torch.float64)
+    if world > 1:
+        tmax = t[:3].clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tsum = t[3:].clone()
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        t = torch.cat([tmax, tsum])
+    secs, tk_s, cd_s, frames, flops, samples = [float(v) for v in t]
+    if rank == 0:
+        line = {"metric": "codec frames/sec (end-to-end document, whole box)",
+                "value": round(frames / secs, 2), "unit": "frames/s", "n_gpus": world,
+                "higher_is_better": True, "scaling": "weak", "dtype": "f16",
+                "data": "synthetic (random-init weights; random latents in place of the RVQ front)",
+                "config": {"workload": "config[4] sample: talker (lane scheduler, shedding, refill) "
+                                       "+ codec stack at 24 kHz over chunk windows",
+                           "segments": n_segments, "lanes": args.lanes, "window_frames": span,
+                           "codec_batch_windows": batch},
+                "frames": int(frames), "audio_seconds": round(frames / 12.5, 2),
+                "seconds": round(secs, 4), "talker_seconds": round(tk_s, 4),
+                "codec_seconds": round(cd_s, 4), "rtf": round(secs / (frames / 12.5), 6),
+                "codec_tflops": round(flops / max(cd_s, 1e-9) / 1e12, 1),
+                "samples": int(samples)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_kernel_case(args):
     """Small standalone cases of one kernel, for ncu captures (a few launches, < 1 GB)."""
     import torch
@@ -531,10 +617,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", default="step", choices=["step", "sweep"],
-                    help="step: the config[2] decode step (headline); sweep: config[3]")
+    ap.add_argument("--workload", default="step", choices=["step", "sweep", "document"],
+                    help="step: the config[2] decode step (headline); sweep: config[3]; "
+                         "document: a bounded config[4] sample (talker + codec)")
     ap.add_argument("--lanes", type=int, default=48)
-    ap.add_argument("--segments", type=int, default=96, help="segments per GPU (sweep)")
+    ap.add_argument("--segments", type=int, default=96, help="segments per GPU (sweep, document)")
     ap.add_argument("--refill", action="store_true")
     ap.add_argument("--kernel", choices=["gemm", "attn", "conv"],
                     help="run a small standalone case of one kernel (for ncu captures)")
@@ -547,6 +634,8 @@ def main():
         return run_kernel_case(args)
     if args.workload == "sweep":
         return run_sweep(args)
+    if args.workload == "document":
+        return run_document(args)
     return run_b200(args)
 
 
