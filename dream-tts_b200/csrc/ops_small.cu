@@ -171,7 +171,8 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* logits, int n,
 // crates/qwen3tts/src/talker.rs:1019-1023, 528-550). Resets the keys for the next step.
 __global__ void __launch_bounds__(256) keys_to_codes_kernel(const unsigned long long* keys,
                                                             int codebooks, int vocab,
-                                                            const __half* embed, int dim,
+                                                            const __half* embed,
+                                                            const float* embed32, int dim,
                                                             uint32_t* codes, float* x_next,
                                                             unsigned long long* keys_reset) {
   __shared__ int sc[64];
@@ -191,6 +192,19 @@ __global__ void __launch_bounds__(256) keys_to_codes_kernel(const unsigned long 
         const __half2 e = *reinterpret_cast<const __half2*>(
             embed + (((size_t)q * vocab + sc[q]) * dim + d));
         const float2 f = __half22float2(e);
+        s0 += f.x;
+        s1 += f.y;
+      }
+      x_next[(size_t)row * dim + d] = s0;
+      x_next[(size_t)row * dim + d + 1] = s1;
+    }
+  } else if (embed32 && x_next) {
+    // f32 tables (the predictor's resized rows, summed in codebook order)
+    for (int d = threadIdx.x * 2; d < dim; d += blockDim.x * 2) {
+      float s0 = 0.f, s1 = 0.f;
+      for (int q = 0; q < codebooks; ++q) {
+        const float2 f = *reinterpret_cast<const float2*>(
+            embed32 + (((size_t)q * vocab + sc[q]) * dim + d));
         s0 += f.x;
         s1 += f.y;
       }
@@ -270,15 +284,16 @@ cudaError_t launch_argmax(const float* logits, int rows, int n, const uint8_t* b
 }
 
 cudaError_t launch_keys_to_codes(const unsigned long long* keys, int rows, int codebooks,
-                                 int vocab, const __half* embed, int dim, uint32_t* codes,
-                                 float* x_next, unsigned long long* keys_reset, bool pdl,
-                                 cudaStream_t st) {
-  if (codebooks > 64 || codebooks < 1 || (embed && dim % 2)) {
+                                 int vocab, const __half* embed, const float* embed32, int dim,
+                                 uint32_t* codes, float* x_next, unsigned long long* keys_reset,
+                                 bool pdl, cudaStream_t st) {
+  if (codebooks > 64 || codebooks < 1 || ((embed || embed32) && dim % 2)) {
     set_error("keys_to_codes: 1..64 codebooks, even dim");
     return cudaErrorInvalidValue;
   }
-  void* args[] = {(void*)&keys, (void*)&codebooks, (void*)&vocab, (void*)&embed,
-                  (void*)&dim,  (void*)&codes,     (void*)&x_next, (void*)&keys_reset};
+  void* args[] = {(void*)&keys, (void*)&codebooks, (void*)&vocab,  (void*)&embed,
+                  (void*)&embed32, (void*)&dim,    (void*)&codes, (void*)&x_next,
+                  (void*)&keys_reset};
   return launch_ex(reinterpret_cast<void (*)(void*)>(keys_to_codes_kernel), dim3(rows),
                    dim3(256), st, pdl, args);
 }

@@ -67,6 +67,21 @@ struct tts_stack {
   int chain_lanes = 0;  // lanes the partial buffer is sized for (0: no chain)
 };
 
+// The depth predictor: its stack, weights, the doubled resize weight and per-frame scratch
+// for up to max_lanes lanes (the prefill runs 2 * max_lanes rows).
+constexpr int kPredictorMaxBlocks = 64;
+struct tts_predictor {
+  tts_stack* s = nullptr;
+  tts_predictor_weights w{};
+  int max_lanes = 0;
+  __half* resize2 = nullptr;     // packed [dim][2 embed_dim]: [W | W]
+  __half* x16 = nullptr;         // [2 max_lanes][2 embed_dim]: [hi | lo]
+  float* x0 = nullptr;           // [2 max_lanes][dim]
+  int* table2 = nullptr;         // [2 max_lanes][kPredictorMaxBlocks]
+  int* pos2 = nullptr;           // [2 max_lanes]
+  unsigned* step_codes = nullptr;  // [steps][2 max_lanes]
+};
+
 struct tts_graph {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
@@ -596,9 +611,21 @@ tts_status tts_stack_destroy(tts_stack* s) {
   return TTS_OK;
 }
 
+// The heads a step uses in place of the stack's own (the depth predictor's per-step head and
+// its f32 resized table as the next input).
+struct HeadSel {
+  const __half* heads = nullptr;
+  const float* embed32 = nullptr;
+};
+
 static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const float* x,
-                            float* h_out, float* logits, unsigned int* codes, cudaStream_t cs) {
+                            float* h_out, float* logits, unsigned int* codes, cudaStream_t cs,
+                            const HeadSel* hsel = nullptr) {
   const tts_stack_geometry& gm = s->geo;
+  const __half* heads = hsel ? hsel->heads : s->heads;
+  const __half* embed16 = hsel ? nullptr : s->embed;
+  const float* embed32 = hsel ? hsel->embed32 : nullptr;
+  const bool feed = embed16 || embed32;
   tts_ctx* c = s->ctx;
   if (!st || !st->positions || !st->block_table || !st->k_pages || !st->v_pages)
     return fail(TTS_ERR_INVALID_ARG, "decode_step: state pointers are NULL");
@@ -610,7 +637,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
   for (int l = 0; l < gm.layers; ++l)
     if (!s->layers[l].wqkv) return fail(TTS_ERR_INVALID_ARG, "decode_step: layer weights not set");
   if (!s->final_norm) return fail(TTS_ERR_INVALID_ARG, "decode_step: final norm not set");
-  if ((logits || codes) && !s->heads)
+  if ((logits || codes) && !heads)
     return fail(TTS_ERR_INVALID_ARG, "decode_step: logits/codes need codebook heads");
 
   const int D = gm.dim, qw = gm.heads * gm.head_dim, nqkv = (gm.heads + 2 * gm.n_kv) * 128;
@@ -707,7 +734,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
   };
   auto req_heads = [&]() {
     GemmRequest hd;
-    hd.w = s->heads;
+    hd.w = heads;
     hd.packed = true;
     hd.x = s->xn;
     hd.m = B;
@@ -740,7 +767,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     ar.out_f16 = true;
     return ar;
   };
-  const int nkeys = s->heads ? B * gm.codebooks : 0;
+  const int nkeys = heads ? B * gm.codebooks : 0;
 
   // Opt-in (TTS_CHAIN=1): the layer chain runs everything between two attentions as one
   // persistent kernel, per layer the attention, then [O, norm, gate/up, down, next norm, next
@@ -790,14 +817,14 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
         kr.ph[kr.nph++] = norm_ph(s->layers[l + 1].attn_norm, nullptr, nullptr, 0);
         kr.ph[kr.nph++] = gemm_ph(req_qkv(l + 1));
       } else {
-        kr.ph[kr.nph++] = norm_ph(s->final_norm, h_out, s->heads ? s->keys : nullptr, nkeys);
-        if (s->heads) kr.ph[kr.nph++] = gemm_ph(req_heads());
+        kr.ph[kr.nph++] = norm_ph(s->final_norm, h_out, heads ? s->keys : nullptr, nkeys);
+        if (heads) kr.ph[kr.nph++] = gemm_ph(req_heads());
       }
       TTS_TRY(launch_chain(kr, s->chain, cs, c->device), "layer_chain");
     }
-    if (s->heads)
-      TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, s->embed, D, codes,
-                                   s->embed ? next : nullptr, nullptr, true, cs),
+    if (heads)
+      TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, embed16, embed32, D, codes,
+                                   feed ? next : nullptr, nullptr, true, cs),
               "keys_to_codes");
   } else {
     for (int l = 0; l < gm.layers; ++l) {
@@ -821,18 +848,18 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
       GemmRequest dn = req_dn(l);
       if (l + 1 < gm.layers)
         dn.next = pf(s->layers[l + 1].wqkv, D, nqkv);
-      else if (s->heads)
-        dn.next = pf(s->heads, D, gm.codebooks * gm.vocab);
+      else if (heads)
+        dn.next = pf(heads, D, gm.codebooks * gm.vocab);
       TTS_TRY(launch_gemm(dn, c->gemm, cs, c->device), "proj");
     }
     // final norm (qwen3.rs:466), heads + greedy pick, next input
     TTS_TRY(launch_rms_norm(s->h, s->final_norm, B, D, gm.eps, h_out, s->xn,
-                            s->heads ? s->keys : nullptr, nkeys, true, cs),
+                            heads ? s->keys : nullptr, nkeys, true, cs),
             "rms_norm");
-    if (s->heads) {
+    if (heads) {
       TTS_TRY(launch_gemm(req_heads(), c->gemm, cs, c->device), "proj");
-      TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, s->embed, D, codes,
-                                   s->embed ? next : nullptr, nullptr, true, cs),
+      TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, embed16, embed32, D, codes,
+                                   feed ? next : nullptr, nullptr, true, cs),
               "keys_to_codes");
     }
   }
@@ -841,24 +868,13 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
   return TTS_OK;
 }
 
-tts_status tts_stack_decode_step(tts_stack* s, const tts_decode_state* st, const float* x,
-                                 float* h_out, float* logits, unsigned int* codes, void* stream) {
-  if (!s) return fail(TTS_ERR_INVALID_ARG, "decode_step: stack is NULL");
-  DeviceGuard g(s->ctx->device);
-  return step_impl(s, st, x, h_out, logits, codes, S(stream));
-}
-
-tts_status tts_stack_graph_capture(tts_stack* s, const tts_decode_state* st, const float* x,
-                                   float* h_out, float* logits, unsigned int* codes, void* stream,
-                                   tts_graph** out) {
-  if (!s || !out) return fail(TTS_ERR_INVALID_ARG, "graph_capture: NULL argument");
-  if (!stream) return fail(TTS_ERR_INVALID_ARG, "graph_capture: needs a non-legacy stream");
-  DeviceGuard g(s->ctx->device);
-  cudaStream_t cs = S(stream);
+extern "C++" {
+template <class Fn>
+static tts_status capture_graph(cudaStream_t cs, tts_graph** out, Fn&& body) {
   const long long before = g_launches;
   cudaError_t e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
   if (e != cudaSuccess) return cuda_status(e, "graph_capture");
-  tts_status rc = step_impl(s, st, x, h_out, logits, codes, cs);
+  tts_status rc = body(cs);
   cudaGraph_t graph = nullptr;
   e = cudaStreamEndCapture(cs, &graph);
   const long long kernels = g_launches - before;
@@ -879,6 +895,25 @@ tts_status tts_stack_graph_capture(tts_stack* s, const tts_decode_state* st, con
   *out = gr;
   return TTS_OK;
 }
+}  // extern "C++"
+
+tts_status tts_stack_decode_step(tts_stack* s, const tts_decode_state* st, const float* x,
+                                 float* h_out, float* logits, unsigned int* codes, void* stream) {
+  if (!s) return fail(TTS_ERR_INVALID_ARG, "decode_step: stack is NULL");
+  DeviceGuard g(s->ctx->device);
+  return step_impl(s, st, x, h_out, logits, codes, S(stream));
+}
+
+tts_status tts_stack_graph_capture(tts_stack* s, const tts_decode_state* st, const float* x,
+                                   float* h_out, float* logits, unsigned int* codes, void* stream,
+                                   tts_graph** out) {
+  if (!s || !out) return fail(TTS_ERR_INVALID_ARG, "graph_capture: NULL argument");
+  if (!stream) return fail(TTS_ERR_INVALID_ARG, "graph_capture: needs a non-legacy stream");
+  DeviceGuard g(s->ctx->device);
+  return capture_graph(S(stream), out, [&](cudaStream_t cs) {
+    return step_impl(s, st, x, h_out, logits, codes, cs);
+  });
+}
 
 tts_status tts_graph_launch(tts_graph* g, void* stream) {
   if (!g) return fail(TTS_ERR_INVALID_ARG, "graph_launch: NULL graph");
@@ -893,6 +928,162 @@ tts_status tts_graph_destroy(tts_graph* g) {
   if (g->graph) cudaGraphDestroy(g->graph);
   delete g;
   return TTS_OK;
+}
+
+// ---------------------------------------------------------------- depth predictor
+
+tts_status tts_predictor_create(tts_stack* s, const tts_predictor_weights* w,
+                                tts_predictor** out) {
+  if (!s || !w || !out) return fail(TTS_ERR_INVALID_ARG, "predictor_create: NULL argument");
+  const tts_stack_geometry& gm = s->geo;
+  if (!w->resize || !w->heads || !w->resized || !w->tables)
+    return fail(TTS_ERR_INVALID_ARG, "predictor_create: resize, heads, resized and tables are required");
+  if (gm.codebooks != 1 || gm.vocab < 128)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE,
+                "predictor_create: the stack needs codebooks = 1 (one head per depth step)");
+  if (w->steps < 1 || w->steps > 64 || w->embed_dim < 64 || w->embed_dim % 64)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "predictor_create: 1..64 steps, embed_dim % 64 == 0");
+  if (gm.rope_len < w->steps + 1)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "predictor_create: rope_len must cover steps + 1");
+  if (!aligned16(w->resize) || !aligned16(w->heads) || !aligned16(w->resized) ||
+      !aligned16(w->tables))
+    return fail(TTS_ERR_INVALID_ARG, "predictor_create: weights must be 16-byte aligned");
+  tts_ctx* c = s->ctx;
+  DeviceGuard g(c->device);
+  auto* p = new tts_predictor();
+  p->s = s;
+  p->w = *w;
+  p->max_lanes = c->max_lanes / 2;
+  const int D = gm.dim, E = w->embed_dim, R = 2 * p->max_lanes;
+  if (p->max_lanes < 1) {
+    delete p;
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "predictor_create: the context needs max_lanes >= 2");
+  }
+  cudaError_t e = dmalloc(&p->resize2, size_t(D) * 2 * E * 2);
+  __half* plain2 = nullptr;
+  if (e == cudaSuccess) e = dmalloc(&plain2, size_t(D) * 2 * E * 2);
+  // [W | W] along k, then packed for the GEMM
+  if (e == cudaSuccess)
+    e = cudaMemcpy2D(plain2, size_t(2) * E * 2, w->resize, size_t(E) * 2, size_t(E) * 2, D,
+                     cudaMemcpyDeviceToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy2D(plain2 + E, size_t(2) * E * 2, w->resize, size_t(E) * 2, size_t(E) * 2, D,
+                     cudaMemcpyDeviceToDevice);
+  if (e == cudaSuccess) {
+    pack_weight_kernel<<<1184, 256>>>(plain2, D, 2 * E, p->resize2);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(plain2);
+  if (e == cudaSuccess) e = dmalloc(&p->x16, size_t(R) * 2 * E * 2);
+  if (e == cudaSuccess) e = dmalloc(&p->x0, size_t(R) * D * 4);
+  if (e == cudaSuccess) e = dmalloc(&p->table2, size_t(R) * kPredictorMaxBlocks * 4);
+  if (e == cudaSuccess) e = dmalloc(&p->pos2, size_t(R) * 4);
+  if (e == cudaSuccess) e = dmalloc(&p->step_codes, size_t(w->steps) * R * 4);
+  if (e == cudaSuccess) e = cudaMemset(p->step_codes, 0, size_t(w->steps) * R * 4);
+  if (e != cudaSuccess) {
+    tts_predictor_destroy(p);
+    return cuda_status(e, "predictor_create");
+  }
+  *out = p;
+  return TTS_OK;
+}
+
+tts_status tts_predictor_destroy(tts_predictor* p) {
+  if (!p) return TTS_OK;
+  DeviceGuard g(p->s->ctx->device);
+  cudaFree(p->resize2);
+  cudaFree(p->x16);
+  cudaFree(p->x0);
+  cudaFree(p->table2);
+  cudaFree(p->pos2);
+  cudaFree(p->step_codes);
+  delete p;
+  return TTS_OK;
+}
+
+// Predictor::frame_batch with greedy picks (talker.rs:407-468) and gather_sum (:528-550).
+static tts_status frame_impl(tts_predictor* p, const tts_decode_state* st, const float* hidden,
+                             const float* code0, unsigned int* codes, float* sum,
+                             cudaStream_t cs) {
+  tts_stack* s = p->s;
+  const tts_stack_geometry& gm = s->geo;
+  const tts_predictor_weights& w = p->w;
+  if (!st || !st->positions || !st->block_table || !st->k_pages || !st->v_pages)
+    return fail(TTS_ERR_INVALID_ARG, "predictor_frame: state pointers are NULL");
+  if (!hidden || !code0 || !codes || !sum)
+    return fail(TTS_ERR_INVALID_ARG, "predictor_frame: hidden, code0_embed, codes and sum are required");
+  const int B = st->lanes;
+  if (B < 1 || B > p->max_lanes)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "predictor_frame: lanes must be in 1..max_lanes / 2");
+  if (st->max_blocks < 1 || st->max_blocks > kPredictorMaxBlocks ||
+      long(st->max_blocks) * st->block_size < w.steps + 1 || st->max_span < w.steps + 1)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE,
+                "predictor_frame: pages for steps + 1 positions (max_blocks <= 64), "
+                "max_span >= steps + 1");
+  if (!aligned16(hidden) || !aligned16(code0) || !aligned16(sum))
+    return fail(TTS_ERR_INVALID_ARG, "predictor_frame: hidden, code0_embed, sum 16-byte aligned");
+  const int D = gm.dim, E = w.embed_dim, V = gm.vocab, stride = 2 * p->max_lanes;
+  tts_status rc;
+#define TTS_TRY(expr, op)                     \
+  do {                                        \
+    if ((rc = counted((expr), op)) != TTS_OK) \
+      return rc;                              \
+  } while (0)
+  TTS_TRY(launch_predictor_prefill(hidden, code0, B, E, p->x16, w.resize_bias, D, p->x0,
+                                   st->block_table, st->max_blocks, p->table2, p->pos2,
+                                   st->positions, cs),
+          "predictor_prefill");
+  GemmRequest rz;
+  rz.w = p->resize2;
+  rz.packed = true;
+  rz.x = p->x16;
+  rz.m = 2 * B;
+  rz.k = 2 * E;
+  rz.n = D;
+  rz.epi = EPI_RESIDUAL;
+  rz.y = p->x0;
+  TTS_TRY(launch_gemm(rz, s->ctx->gemm, cs, s->ctx->device), "proj");
+  tts_decode_state pre = *st;
+  pre.lanes = 2 * B;
+  pre.positions = p->pos2;
+  pre.block_table = p->table2;
+  pre.max_span = 2;
+  for (int i = 0; i < w.steps; ++i) {
+    HeadSel hs;
+    hs.heads = static_cast<const __half*>(w.heads) + size_t(i) * V * D;
+    // the last pick feeds nothing (talker.rs:455: no stack step after the last head)
+    hs.embed32 = i + 1 < w.steps ? w.resized + size_t(i) * V * D : nullptr;
+    rc = step_impl(s, i == 0 ? &pre : st, i == 0 ? p->x0 : nullptr, nullptr, nullptr,
+                   p->step_codes + size_t(i) * stride, cs, &hs);
+    if (rc != TTS_OK) return rc;
+  }
+  TTS_TRY(launch_predictor_finish(p->step_codes, stride, B, w.steps,
+                                  static_cast<const __half*>(w.tables), V, E, code0, codes, sum,
+                                  cs),
+          "predictor_finish");
+#undef TTS_TRY
+  return TTS_OK;
+}
+
+tts_status tts_predictor_frame(tts_predictor* p, const tts_decode_state* st, const float* hidden,
+                               const float* code0_embed, unsigned int* codes, float* sum,
+                               void* stream) {
+  if (!p) return fail(TTS_ERR_INVALID_ARG, "predictor_frame: predictor is NULL");
+  DeviceGuard g(p->s->ctx->device);
+  return frame_impl(p, st, hidden, code0_embed, codes, sum, S(stream));
+}
+
+tts_status tts_predictor_graph_capture(tts_predictor* p, const tts_decode_state* st,
+                                       const float* hidden, const float* code0_embed,
+                                       unsigned int* codes, float* sum, void* stream,
+                                       tts_graph** out) {
+  if (!p || !out) return fail(TTS_ERR_INVALID_ARG, "graph_capture: NULL argument");
+  if (!stream) return fail(TTS_ERR_INVALID_ARG, "graph_capture: needs a non-legacy stream");
+  DeviceGuard g(p->s->ctx->device);
+  return capture_graph(S(stream), out, [&](cudaStream_t cs) {
+    return frame_impl(p, st, hidden, code0_embed, codes, sum, cs);
+  });
 }
 
 }  // extern "C"

@@ -179,9 +179,20 @@ cudaError_t launch_snake(const void* x, bool x_f16, const float* alpha, const fl
 cudaError_t launch_argmax(const float* logits, int rows, int n, const uint8_t* banned,
                           uint32_t* out, cudaStream_t st);
 cudaError_t launch_keys_to_codes(const unsigned long long* keys, int rows, int codebooks,
-                                 int vocab, const __half* embed, int dim, uint32_t* codes,
-                                 float* x_next, unsigned long long* keys_reset, bool pdl,
-                                 cudaStream_t st);
+                                 int vocab, const __half* embed, const float* embed32, int dim,
+                                 uint32_t* codes, float* x_next, unsigned long long* keys_reset,
+                                 bool pdl, cudaStream_t st);
+// The depth predictor's frame ends (predictor.cu): the prefill rows (f32 inputs split into
+// f16 hi | lo halves, the projection's bias rows, the paired-lane block table and positions)
+// and the codes transpose with the embedding sum at talker width.
+cudaError_t launch_predictor_prefill(const float* hidden, const float* code0, int lanes,
+                                     int embed_dim, __half* x16, const float* bias, int dim,
+                                     float* x0, const int* table, int max_blocks, int* table2,
+                                     int* pos2, int* positions, cudaStream_t st);
+cudaError_t launch_predictor_finish(const uint32_t* step_codes, int stride, int lanes, int steps,
+                                    const __half* tables, int vocab, int embed_dim,
+                                    const float* code0, uint32_t* codes, float* sum,
+                                    cudaStream_t st);
 cudaError_t launch_advance_positions(int* positions, int lanes, bool pdl, cudaStream_t st);
 cudaError_t launch_cast_f32_f16(const float* x, __half* y, long n, cudaStream_t st);
 

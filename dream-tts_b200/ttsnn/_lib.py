@@ -48,6 +48,12 @@ class DecodeState(C.Structure):
                 ("k_pages", C.c_void_p), ("v_pages", C.c_void_p), ("max_span", C.c_int)]
 
 
+class PredictorWeights(C.Structure):
+    _fields_ = [("resize", C.c_void_p), ("resize_bias", C.c_void_p), ("heads", C.c_void_p),
+                ("resized", C.c_void_p), ("tables", C.c_void_p), ("steps", C.c_int),
+                ("embed_dim", C.c_int)]
+
+
 P = C.c_void_p
 I = C.c_int
 L = C.c_long
@@ -82,6 +88,10 @@ SIGNATURES = {
     "tts_stack_graph_capture": [P, C.POINTER(DecodeState), P, P, P, P, P, C.POINTER(P)],
     "tts_graph_launch": [P, P],
     "tts_graph_destroy": [P],
+    "tts_predictor_create": [P, C.POINTER(PredictorWeights), C.POINTER(P)],
+    "tts_predictor_destroy": [P],
+    "tts_predictor_frame": [P, C.POINTER(DecodeState), P, P, P, P, P],
+    "tts_predictor_graph_capture": [P, C.POINTER(DecodeState), P, P, P, P, P, C.POINTER(P)],
 }
 _RESTYPE = {"tts_last_error": C.c_char_p, "tts_launch_count": C.c_longlong}
 

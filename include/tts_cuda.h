@@ -263,6 +263,47 @@ TTS_API tts_status tts_stack_graph_capture(tts_stack* s, const tts_decode_state*
 TTS_API tts_status tts_graph_launch(tts_graph* g, void* stream);
 TTS_API tts_status tts_graph_destroy(tts_graph* g);
 
+/* ---------------------------------------------------------------- depth predictor
+ * The code predictor (crates/qwen3tts/src/talker.rs:255-550): a decoder stack of its own
+ * (created with codebooks = 1 and vocab = the residual codebook size, heads left unset), the
+ * talker-to-predictor projection with bias, one head per residual codebook, the resized tables
+ * (tables[i] projected to the predictor's width, talker.rs:268-273, computed once at load in
+ * f32) and the tables at talker width for the embedding sum. */
+typedef struct tts_predictor_weights {
+  const void* resize;      /* f16 [dim][embed_dim] plain (small_to_mtp_projection.weight) */
+  const float* resize_bias; /* f32 [dim] (NULL = none) */
+  const void* heads;       /* f16 [steps * vocab][dim] packed by tts_weight_pack */
+  const float* resized;    /* f32 [steps][vocab][dim]: tables[i] @ resize^T + bias */
+  const void* tables;      /* f16 [steps][vocab][embed_dim] */
+  int steps;               /* residual codebooks (15) */
+  int embed_dim;           /* talker width (2048), multiple of 64 */
+} tts_predictor_weights;
+
+typedef struct tts_predictor tts_predictor;
+
+/* Binds a predictor to `stack` (which it drives; one predictor per stack). Allocates its scratch
+ * for up to max_lanes / 2 lanes of the stack's context and the doubled resize weight it uses for
+ * an f32-exact projection of f32 inputs. Weights are referenced, not copied. */
+TTS_API tts_status tts_predictor_create(tts_stack* stack, const tts_predictor_weights* w,
+                                        tts_predictor** out);
+TTS_API tts_status tts_predictor_destroy(tts_predictor* p);
+
+/* One frame for st->lanes lanes with greedy picks (Predictor::frame_batch, talker.rs:407-468,
+ * and gather_sum, talker.rs:528-550): prefill [hidden, code0_embed] through the projection and
+ * the stack (both positions in one pass), then per residual codebook i the head, the pick and,
+ * before the next pick, the stack on resized[i][code]. st: the predictor's own KV pages, room for
+ * steps + 1 positions per lane (positions are reset by the call; max_span >= steps + 1).
+ * hidden, code0_embed f32 [lanes][embed_dim]; codes u32 [lanes][steps]; sum f32
+ * [lanes][embed_dim] = code0_embed + the picked codes' table rows. */
+TTS_API tts_status tts_predictor_frame(tts_predictor* p, const tts_decode_state* st,
+                                       const float* hidden, const float* code0_embed,
+                                       unsigned int* codes, float* sum, void* stream);
+/* The same frame captured into one CUDA graph (non-legacy stream); pointers baked in. */
+TTS_API tts_status tts_predictor_graph_capture(tts_predictor* p, const tts_decode_state* st,
+                                               const float* hidden, const float* code0_embed,
+                                               unsigned int* codes, float* sum, void* stream,
+                                               tts_graph** out);
+
 /* Kernel launches made by the calling thread through this library since the last call
  * (observability: the bench reports it). */
 TTS_API long long tts_launch_count(int reset);

@@ -279,3 +279,99 @@ def snake_residual_block(x: np.ndarray, convs, dilations=(1, 3, 9), same: bool =
         pad = (k - 1) * d // 2 if same else (k - 1) * d
         x = conv1d_nlc(x, w, bias, d, pad, snake=(alpha, brecip), res=x)
     return x
+
+
+# ---------------------------------------------------------------- depth predictor
+@dataclass
+class PredictorWeights:
+    """The code predictor's own weights besides its stack (talker.rs:255-330): the talker-to-
+    predictor projection (small_to_mtp_projection, with bias), one head per residual codebook,
+    the residual codebooks' tables at talker width, and `resized` = each table through the
+    projection, precomputed at load (talker.rs:268-273, 315-323)."""
+    resize: np.ndarray       # f16 bits [dim, embed_dim]
+    resize_bias: np.ndarray  # f32 [dim]
+    heads: np.ndarray        # f16 bits [steps * vocab, dim]
+    tables: np.ndarray       # f16 bits [steps, vocab, embed_dim]
+    resized: np.ndarray      # f32 [steps, vocab, dim]
+
+    @property
+    def steps(self) -> int:
+        return self.tables.shape[0]
+
+
+def linear(x: np.ndarray, w_bits: np.ndarray, bias: np.ndarray | None) -> np.ndarray:
+    """`Linear::forward` in f32 (an f32 weight, f32 inputs, plus bias), computed in f64 and
+    rounded once to f32."""
+    y = np.asarray(x, np.float64) @ f16_value(w_bits).astype(np.float64).T
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)
+    return y.astype(np.float32)
+
+
+def resize_tables(tables_bits: np.ndarray, resize_bits: np.ndarray, bias) -> np.ndarray:
+    """talker.rs:315-323: `resized[i] = host.forward(tables[i])`, f32, bias folded in."""
+    return np.stack([linear(f16_value(t), resize_bits, bias) for t in tables_bits])
+
+
+def synthetic_predictor(rng: np.random.Generator, g: Geometry, steps: int,
+                        embed_dim: int) -> PredictorWeights:
+    """Seeded random-init predictor weights: projections and tables ~N(0, 0.02) as f16, bias
+    ~N(0, 0.02)."""
+    def w(*shape):
+        return f16_bits(rng.standard_normal(shape, dtype=np.float32) * 0.02)
+
+    resize = w(g.dim, embed_dim)
+    bias = (rng.standard_normal(g.dim, dtype=np.float32) * 0.02).astype(np.float32)
+    heads = w(steps * g.vocab, g.dim)
+    tables = w(steps, g.vocab, embed_dim)
+    return PredictorWeights(resize, bias, heads, tables, resize_tables(tables, resize, bias))
+
+
+def predictor_frame(hidden: np.ndarray, code0_embed: np.ndarray, layers: list[Layer],
+                    final_norm: np.ndarray, pw: PredictorWeights, g: Geometry,
+                    forced: np.ndarray | None = None, tie_tol: float = 0.0):
+    """Predictor::frame_batch with greedy picks (talker.rs:407-468) and gather_sum (:528-550).
+
+    hidden, code0_embed f32 [b, embed_dim]. The two-position prefill (talker.rs:416-420) is run
+    as decode steps at positions 0 and 1, which the causal mask makes the same computation. Each
+    depth step: head i on the last hidden, the greedy pick, then (before the last) the stack on
+    resized[i][code]. Returns (codes u32 [b, steps], sum f32 [b, embed_dim], ties, mismatches).
+
+    `forced` (u32 [b, steps], e.g. the device's picks) is followed wherever its logit is within
+    `tie_tol` of the maximum: a near-tie resolved the other way by a different but equally valid
+    accumulation order, which the chain then continues from. Picks outside that band count in
+    `mismatches` and the oracle keeps its own."""
+    b = hidden.shape[0]
+    steps = pw.steps
+    cap = steps + 2
+    cos, sin = rope_table(cap, g.head_dim, g.rope_base)
+    kc = [np.zeros((b, g.n_kv, cap, g.head_dim), np.uint16) for _ in layers]
+    vc = [np.zeros((b, g.n_kv, cap, g.head_dim), np.uint16) for _ in layers]
+    x0 = linear(hidden, pw.resize, pw.resize_bias)
+    x1 = linear(code0_embed, pw.resize, pw.resize_bias)
+    decode_step(x0, layers, final_norm, kc, vc, np.zeros(b, np.int32), cos, sin, g)
+    h = decode_step(x1, layers, final_norm, kc, vc, np.ones(b, np.int32), cos, sin, g)
+    codes = np.zeros((b, steps), np.uint32)
+    ties = mismatches = 0
+    for i in range(steps):
+        logits = proj(h, pw.heads[i * g.vocab:(i + 1) * g.vocab])
+        pick = argmax(logits)
+        if forced is not None:
+            for lane in range(b):
+                f = int(forced[lane, i])
+                if f == int(pick[lane]):
+                    continue
+                if 0 <= f < g.vocab and logits[lane, f] >= logits[lane, pick[lane]] - tie_tol:
+                    pick[lane] = f
+                    ties += 1
+                else:
+                    mismatches += 1
+        codes[:, i] = pick
+        if i + 1 < steps:
+            x = pw.resized[i][pick.astype(np.int64)]
+            h = decode_step(x, layers, final_norm, kc, vc, np.full(b, 2 + i, np.int32), cos, sin, g)
+    rows = [f16_value(pw.tables[i][codes[:, i].astype(np.int64)]) for i in range(steps)]
+    acc = np.zeros_like(rows[0])
+    for r in rows:
+        acc = acc + r
+    return codes, np.asarray(code0_embed, np.float32) + acc, ties, mismatches

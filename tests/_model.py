@@ -101,3 +101,36 @@ def gather_pages(kv_pool_layer, table, lanes, n_kv, length, block_size):
     out = pool[table.reshape(-1)].reshape(lanes, per_lane, n_kv, block_size, 128)
     out = out.transpose(0, 2, 1, 3, 4).reshape(lanes, n_kv, per_lane * block_size, 128)
     return out[:, :, :length]
+
+
+# ---------------------------------------------------------------- depth predictor
+def make_predictor(orc, lanes, dim, layers, heads, n_kv, ffn, vocab, steps, embed_dim, seed):
+    """Seeded predictor weights and one frame's inputs: the talker's normed hidden ~N(0, 1) and
+    its code-0 embedding (an f16 table row ~N(0, 0.02))."""
+    rng = np.random.default_rng(seed)
+    g = orc.Geometry(dim=dim, layers=layers, heads=heads, n_kv=n_kv, ffn=ffn, codebooks=1,
+                     vocab=vocab)
+    Ls = [make_layer(orc, rng, g) for _ in range(layers)]
+    final = rng.uniform(0.8, 1.2, dim).astype(np.float32)
+    pw = orc.synthetic_predictor(rng, g, steps, embed_dim)
+    hidden = rng.standard_normal((lanes, embed_dim), dtype=np.float32)
+    code0 = orc.f16_value(orc.f16_bits(rng.standard_normal((lanes, embed_dim), dtype=np.float32)
+                                       * 0.02))
+    return g, Ls, final, pw, hidden, code0
+
+
+def device_predictor(orc, g, layers, final, pw):
+    """The predictor on the device: its stack (codebooks 1, heads supplied per depth step) and
+    weights, with the oracle's f32 resized tables."""
+    from qwen3tts import Geometry, LayerTensors, Predictor, Stack
+    import ttsnn
+    geo = Geometry(dim=g.dim, layers=g.layers, heads=g.heads, n_kv=g.n_kv, head_dim=g.head_dim,
+                   ffn=g.ffn, eps=g.eps, rope_base=g.rope_base, rope_len=64, codebooks=1,
+                   vocab=g.vocab)
+    lts = [LayerTensors.from_plain(dev_f32(L.attn_norm), dev_f32(L.ffn_norm), dev_f16(L.wqkv),
+                                   dev_f32(L.qk_norms), dev_f16(L.wo),
+                                   ttsnn.interleave_gate_up(dev_f16(L.gate), dev_f16(L.up)),
+                                   dev_f16(L.down)) for L in layers]
+    stack = Stack(geo, lts, dev_f32(final))
+    return Predictor(stack, dev_f16(pw.resize), dev_f32(pw.resize_bias), dev_f16(pw.heads),
+                     dev_f16(pw.tables), dev_f32(pw.resized))

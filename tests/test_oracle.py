@@ -215,3 +215,90 @@ def torch_decode_step(orc, x, layers, final, kc, vc, pos, cos, sin, g):
         up = f16(xn) @ W(L.up).T
         h = h + f16(F.silu(gate) * up) @ W(L.down).T
     return F.rms_norm(h, (g.dim,), T(final), g.eps).numpy()
+
+
+def torch_stack_sequence(orc, X, layers, final, g):
+    """Stack::forward over a whole sequence (prefill form, causal mask) in float64 PyTorch:
+    X [b, t, dim] -> final-normed hidden [b, t, dim]. K/V are rounded to f16 as the cache
+    stores them, projection inputs to f16 as Proj::Half takes them."""
+    T = lambda a: torch.from_numpy(np.asarray(a)).double()
+    W = lambda bits: T(orc.f16_value(bits))
+    f16 = lambda t: t.float().half().double()
+    b, t, _ = X.shape
+    cos, sin = orc.rope_table(t, 128, g.rope_base)
+    c = T(cos)[None, :, None]
+    s = T(sin)[None, :, None]
+    gqa = g.heads // g.n_kv
+    h = X.clone()
+    mask = torch.ones(t, t, dtype=torch.bool).tril()
+    for L in layers:
+        xn = F.rms_norm(h, (g.dim,), T(L.attn_norm), g.eps)
+        qkv = (f16(xn) @ W(L.wqkv).T).reshape(b, t, -1, 128)
+        q = rotate_half_rope(F.rms_norm(qkv[:, :, :g.heads], (128,), T(L.qk_norms[0]), g.eps), c, s)
+        k = f16(rotate_half_rope(F.rms_norm(qkv[:, :, g.heads:g.heads + g.n_kv], (128,),
+                                            T(L.qk_norms[1]), g.eps), c, s))
+        v = f16(qkv[:, :, g.heads + g.n_kv:])
+        k = k.repeat_interleave(gqa, 2).transpose(1, 2)
+        v = v.repeat_interleave(gqa, 2).transpose(1, 2)
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k, v, attn_mask=mask, scale=1.0)
+        h = h + f16(o.transpose(1, 2).reshape(b, t, -1)) @ W(L.wo).T
+        xn = F.rms_norm(h, (g.dim,), T(L.ffn_norm), g.eps)
+        h = h + f16(F.silu(f16(xn) @ W(L.gate).T) * (f16(xn) @ W(L.up).T)) @ W(L.down).T
+    return F.rms_norm(h, (g.dim,), T(final), g.eps)
+
+
+def test_predictor_frame_vs_torch_full_sequence(orc):
+    """The oracle's depth predictor (KV-cached decode steps, the two-position prefill as two
+    steps) against a float64 PyTorch form that re-runs the whole causal sequence for every pick
+    (talker.rs:407-468) and gathers the frame's sum as gather_sum does (talker.rs:528-550)."""
+    g = orc.Geometry(dim=256, layers=2, heads=4, n_kv=2, ffn=512, codebooks=1, vocab=256)
+    rng = np.random.default_rng(21)
+    layers = [orc.synthetic_layer(rng, g) for _ in range(2)]
+    final = rng.uniform(0.8, 1.2, g.dim).astype(np.float32)
+    pw = orc.synthetic_predictor(rng, g, steps=5, embed_dim=384)
+    b = 3
+    hidden = rng.standard_normal((b, 384), dtype=np.float32)
+    code0 = orc.f16_value(orc.f16_bits(rng.standard_normal((b, 384), dtype=np.float32) * 0.02))
+    codes, total, ties, mism = orc.predictor_frame(hidden, code0, layers, final, pw, g)
+
+    T = lambda a: torch.from_numpy(np.asarray(a)).double()
+    Wr = T(orc.f16_value(pw.resize))
+    seq = torch.stack([T(hidden), T(code0)], 1) @ Wr.T + T(pw.resize_bias)
+    want = np.zeros((b, pw.steps), np.int64)
+    for i in range(pw.steps):
+        h = torch_stack_sequence(orc, seq, layers, final, g)[:, -1]
+        logits = h.float().half().double() @ T(orc.f16_value(pw.heads[i * g.vocab:(i + 1) * g.vocab])).T
+        want[:, i] = logits.argmax(-1).numpy()
+        # the device-side f32 resized rows are the reference's Linear outputs, bias folded in
+        rows = T(orc.f16_value(pw.tables[i]))[want[:, i]] @ Wr.T + T(pw.resize_bias)
+        seq = torch.cat([seq, rows[:, None]], 1)
+    assert np.array_equal(codes.astype(np.int64), want)
+    gathered = sum(orc.f16_value(pw.tables[i][want[:, i]]).astype(np.float64)
+                   for i in range(pw.steps))
+    assert rel(total, code0 + gathered) < 1e-6
+    # resized is the projection of each table row, bias included (talker.rs:268-273)
+    r = orc.resize_tables(pw.tables[:1], pw.resize, pw.resize_bias)[0]
+    assert rel(r[7], (T(orc.f16_value(pw.tables[0][7])) @ Wr.T + T(pw.resize_bias)).numpy()) < 1e-6
+
+
+def test_predictor_forced_ties(orc):
+    """Following forced picks inside the tie band keeps the chain on them; picks outside it
+    are counted as mismatches and not followed."""
+    g = orc.Geometry(dim=256, layers=1, heads=4, n_kv=2, ffn=512, codebooks=1, vocab=128)
+    rng = np.random.default_rng(3)
+    layers = [orc.synthetic_layer(rng, g)]
+    final = rng.uniform(0.8, 1.2, g.dim).astype(np.float32)
+    pw = orc.synthetic_predictor(rng, g, steps=3, embed_dim=256)
+    hidden = rng.standard_normal((2, 256), dtype=np.float32)
+    code0 = np.zeros((2, 256), np.float32)
+    codes, _, _, _ = orc.predictor_frame(hidden, code0, layers, final, pw, g)
+    same, _, ties, mism = orc.predictor_frame(hidden, code0, layers, final, pw, g, forced=codes)
+    assert np.array_equal(same, codes) and ties == 0 and mism == 0
+    wrong = codes.copy()
+    wrong[0, 0] = (codes[0, 0] + 1) % g.vocab
+    got, _, ties, mism = orc.predictor_frame(hidden, code0, layers, final, pw, g, forced=wrong,
+                                             tie_tol=0.0)
+    assert mism >= 1 and got[0, 0] == codes[0, 0]
+    got, _, ties, mism = orc.predictor_frame(hidden, code0, layers, final, pw, g, forced=wrong,
+                                             tie_tol=1e9)
+    assert got[0, 0] == wrong[0, 0] and ties >= 1
