@@ -422,6 +422,188 @@ def run_document(args):
     return 0
 
 
+def build_device_predictor(device, seed=0):
+    """The depth predictor at the reference's shape (crates/qwen3tts/src/cfg.rs): a 5-layer
+    stack at dim 1024 (16/8 heads x 128, SwiGLU 3072), 15 heads [2048, 1024], the 2048 -> 1024
+    projection with bias, 15 tables [2048, 2048]; f16 weights ~N(0, 0.02), random init."""
+    import torch
+    import ttsnn
+    from qwen3tts import PREDICTOR_GEOMETRY as g, LayerTensors, Predictor, Stack
+    gen = torch.Generator(device=device).manual_seed(seed)
+
+    def w(*shape):
+        return (torch.randn(*shape, generator=gen, device=device) * 0.02).half()
+
+    def norm(n):
+        return torch.rand(n, generator=gen, device=device) * 0.4 + 0.8
+
+    nqkv = (g.heads + 2 * g.n_kv) * g.head_dim
+    layers = [LayerTensors.from_plain(norm(g.dim), norm(g.dim), w(nqkv, g.dim),
+                                      torch.stack([norm(128) / 128 ** 0.5, norm(128)]),
+                                      w(g.dim, g.heads * g.head_dim),
+                                      ttsnn.interleave_gate_up(w(g.ffn, g.dim), w(g.ffn, g.dim)),
+                                      w(g.dim, g.ffn)) for _ in range(g.layers)]
+    stack = Stack(g, layers, norm(g.dim))
+    return Predictor(stack, w(g.dim, 2048), (torch.randn(g.dim, generator=gen, device=device) * 0.02),
+                     w(15 * g.vocab, g.dim), w(15, g.vocab, 2048))
+
+
+class PredictorCpuSample:
+    """The oracle's predictor frame (all 15 depth steps) for `lanes` lanes at the reference's
+    shape; seconds per frame of those lanes."""
+
+    def __init__(self, lanes=2, threads=None, seed=0):
+        import oracle as orc
+        self.orc = orc
+        if threads:
+            orc.set_threads(threads)
+        rng = np.random.default_rng(seed)
+        self.g = orc.Geometry(dim=1024, layers=5, heads=16, n_kv=8, ffn=3072, codebooks=1,
+                              vocab=2048)
+        self.layers = [orc.synthetic_layer(rng, self.g) for _ in range(5)]
+        self.final = np.ones(1024, np.float32)
+        w = lambda *sh: orc.f16_bits(rng.standard_normal(sh, dtype=np.float32) * 0.02)
+        resize, heads, tables = w(1024, 2048), w(15 * 2048, 1024), w(15, 2048, 2048)
+        bias = np.zeros(1024, np.float32)
+        resized = (orc.f16_value(tables) @ orc.f16_value(resize).T).astype(np.float32)
+        self.pw = orc.PredictorWeights(resize, bias, heads, tables, resized)
+        self.lanes = lanes
+        self.hidden = rng.standard_normal((lanes, 2048), dtype=np.float32)
+        self.code0 = orc.f16_value(w(lanes, 2048))
+        self.sample = (f"one predictor frame (prefill + 15 depth steps + embedding sum) for "
+                       f"{lanes} lanes at the reference's shape")
+
+    def threads(self):
+        return self.orc.threads()
+
+    def time(self):
+        t0 = time.perf_counter()
+        self.orc.predictor_frame(self.hidden, self.code0, self.layers, self.final, self.pw, self.g)
+        return time.perf_counter() - t0
+
+
+def run_predictor(args):
+    """The depth predictor (crates/qwen3tts/src/talker.rs:255-550) at `--lanes` lanes per GPU.
+    One step = one frame for every lane: the two-position prefill, 15 greedy depth steps, the
+    embedding sum at talker width, as one captured graph; frames/s = lanes x frames per second.
+    Roofline: HBM, the frame's weight stream (the 5-layer stack once per depth step, one head per
+    step, the doubled projection) over the frame time. Weak scaling: each rank its own lanes."""
+    import torch
+    import torch.distributed as dist
+    import ttsnn
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
+    lanes, steps, warmup = args.lanes, args.steps, args.warmup
+    p = build_device_predictor(device, seed=rank)
+    kv = p.new_state(lanes)
+    h_host = torch.randn(lanes, 2048).pin_memory()
+    c_host = (torch.randn(lanes, 2048) * 0.02).half().float().pin_memory()
+    codes_host = torch.empty(lanes, 15, dtype=torch.int32).pin_memory()
+    sum_host = torch.empty(lanes, 2048).pin_memory()
+    h = h_host.to(device)
+    c0 = c_host.to(device)
+    codes = torch.empty(lanes, 15, dtype=torch.int32, device=device)
+    total = torch.empty(lanes, 2048, device=device)
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        graph = p.capture(kv, h, c0, codes, total)
+        for _ in range(warmup):
+            graph.replay()
+    stream.synchronize()
+    ttsnn.check(local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local, os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
+                    if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/clocks_rank{rank}.csv")
+    ttsnn.launch_count(reset=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    stream.synchronize()
+    launches = ttsnn.launch_count()
+    clk = clocks.stop()
+    barrier()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ttsnn.check(local)
+    # end to end through the public API: the talker's hidden and code-0 embedding in from
+    # pinned host memory, the codes and the next-input sum back, every frame
+    barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e2.record(stream)
+        for _ in range(steps):
+            h.copy_(h_host, non_blocking=True)
+            c0.copy_(c_host, non_blocking=True)
+            graph.replay()
+            codes_host.copy_(codes, non_blocking=True)
+            sum_host.copy_(total, non_blocking=True)
+            stream.synchronize()
+        e3.record(stream)
+    stream.synchronize()
+    t2 = torch.tensor([e2.elapsed_time(e3)], device=device)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t2.item())
+    ttsnn.check(local)
+    hbm, peak_kind = peaks()
+    frame_s = ms / steps * 1e-3
+    wbytes = p.weight_bytes()
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            cs = PredictorCpuSample(threads=os.cpu_count())
+            cs.time()
+            cpu_t = statistics.median([cs.time() for _ in range(3)])
+            cpu = {"value": round(cs.lanes / cpu_t, 3), "unit": UNIT, "cores": cs.threads(),
+                   "kind": "port", "sample": cs.sample}
+        line = {
+            "metric": "codec frames/sec (depth predictor, whole box)",
+            "value": round(world * lanes * steps / (ms * 1e-3), 2), "unit": UNIT,
+            "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (random-init weights)",
+            "config": {"workload": "depth predictor frame (talker.rs:407-550): 5 layers dim 1024, "
+                                   "16q/8kv heads x 128, SwiGLU 3072, 15 heads x 2048 greedy, "
+                                   "resize 2048->1024 + bias, tables 15 x [2048, 2048]",
+                       "lanes_per_gpu": lanes, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2: each frame streams 2.4 GB of weights"},
+            "roofline": {"bound": "hbm", "kernel": "whole frame (weight stream)",
+                         "achieved": round(wbytes / frame_s / 1e9, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(wbytes / frame_s / 1e9 / hbm, 4),
+                         "traffic": None, "peak_source": peak_kind,
+                         "algorithmic_bytes_per_frame": int(wbytes)},
+            "e2e": {"value": round(world * lanes * steps / (e2e_ms * 1e-3), 2), "unit": UNIT,
+                    "h2d_bytes_per_step": lanes * 2048 * 4 * 2,
+                    "d2h_bytes_per_step": lanes * (15 * 4 + 2048 * 4)},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_kernel_case(args):
     """Small standalone cases of one kernel, for ncu captures (a few launches, < 1 GB)."""
     import torch
@@ -617,9 +799,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", default="step", choices=["step", "sweep", "document"],
+    ap.add_argument("--workload", default="step",
+                    choices=["step", "sweep", "document", "predictor"],
                     help="step: the config[2] decode step (headline); sweep: config[3]; "
-                         "document: a bounded config[4] sample (talker + codec)")
+                         "document: a bounded config[4] sample (talker + codec); predictor: "
+                         "the depth predictor's frame")
     ap.add_argument("--lanes", type=int, default=48)
     ap.add_argument("--segments", type=int, default=96, help="segments per GPU (sweep, document)")
     ap.add_argument("--refill", action="store_true")
@@ -636,6 +820,8 @@ def main():
         return run_sweep(args)
     if args.workload == "document":
         return run_document(args)
+    if args.workload == "predictor":
+        return run_predictor(args)
     return run_b200(args)
 
 

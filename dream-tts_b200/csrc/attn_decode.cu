@@ -746,6 +746,7 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
     set_error("decode_attention: at most 512 lanes per call");
     return cudaErrorInvalidValue;
   }
+  if (r.max_span <= kShortSpanMax) return launch_attn_short(r, st);
   const int chunks = (r.max_span + kChunk - 1) / kChunk;
   if (chunks > kMaxChunks) {
     set_error("decode_attention: max_span exceeds 8192");

@@ -174,11 +174,14 @@ __global__ void __launch_bounds__(256) keys_to_codes_kernel(const unsigned long 
                                                             const __half* embed,
                                                             const float* embed32, int dim,
                                                             uint32_t* codes, float* x_next,
-                                                            unsigned long long* keys_reset) {
+                                                            unsigned long long* keys_reset,
+                                                            int* positions) {
   __shared__ int sc[64];
   pdl_launch_dependents();
   pdl_wait();
   const int row = blockIdx.x;
+  // the step's last reader of the positions has finished: advance this lane's
+  if (positions && threadIdx.x == 0) positions[row] += 1;
   if (threadIdx.x < codebooks) {
     const unsigned c = unsigned(keys[(size_t)row * codebooks + threadIdx.x] & 0xffffffffu);
     sc[threadIdx.x] = int(c < unsigned(vocab) ? c : 0);
@@ -286,14 +289,14 @@ cudaError_t launch_argmax(const float* logits, int rows, int n, const uint8_t* b
 cudaError_t launch_keys_to_codes(const unsigned long long* keys, int rows, int codebooks,
                                  int vocab, const __half* embed, const float* embed32, int dim,
                                  uint32_t* codes, float* x_next, unsigned long long* keys_reset,
-                                 bool pdl, cudaStream_t st) {
+                                 int* positions, bool pdl, cudaStream_t st) {
   if (codebooks > 64 || codebooks < 1 || ((embed || embed32) && dim % 2)) {
     set_error("keys_to_codes: 1..64 codebooks, even dim");
     return cudaErrorInvalidValue;
   }
   void* args[] = {(void*)&keys, (void*)&codebooks, (void*)&vocab,  (void*)&embed,
                   (void*)&embed32, (void*)&dim,    (void*)&codes, (void*)&x_next,
-                  (void*)&keys_reset};
+                  (void*)&keys_reset, (void*)&positions};
   return launch_ex(reinterpret_cast<void (*)(void*)>(keys_to_codes_kernel), dim3(rows),
                    dim3(256), st, pdl, args);
 }

@@ -76,7 +76,6 @@ struct tts_predictor {
   int max_lanes = 0;
   __half* resize2 = nullptr;     // packed [dim][2 embed_dim]: [W | W]
   __half* x16 = nullptr;         // [2 max_lanes][2 embed_dim]: [hi | lo]
-  float* x0 = nullptr;           // [2 max_lanes][dim]
   int* table2 = nullptr;         // [2 max_lanes][kPredictorMaxBlocks]
   int* pos2 = nullptr;           // [2 max_lanes]
   unsigned* step_codes = nullptr;  // [steps][2 max_lanes]
@@ -612,10 +611,14 @@ tts_status tts_stack_destroy(tts_stack* s) {
 }
 
 // The heads a step uses in place of the stack's own (the depth predictor's per-step head and
-// its f32 resized table as the next input).
+// its f32 resized table as the next input), and where its input and feedback live: with
+// `in_h` the input is already in the residual stream buffer (no copy), with `feed_h` the next
+// input is written there (the buffer is dead once the final norm has read it).
 struct HeadSel {
   const __half* heads = nullptr;
   const float* embed32 = nullptr;
+  bool in_h = false;
+  bool feed_h = false;
 };
 
 static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const float* x,
@@ -649,9 +652,10 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
       return rc;                              \
   } while (0)
 
-  float* next = s->feedback ? s->feedback : s->x_next;
+  float* next = hsel && hsel->feed_h ? s->h : (s->feedback ? s->feedback : s->x_next);
   const float* src = x ? x : next;
-  if ((rc = cuda_status(cudaMemcpyAsync(s->h, src, size_t(B) * D * 4, cudaMemcpyDeviceToDevice, cs),
+  if (!(hsel && hsel->in_h) &&
+      (rc = cuda_status(cudaMemcpyAsync(s->h, src, size_t(B) * D * 4, cudaMemcpyDeviceToDevice, cs),
                         "decode_step")) != TTS_OK)
     return rc;
 
@@ -824,7 +828,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     }
     if (heads)
       TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, embed16, embed32, D, codes,
-                                   feed ? next : nullptr, nullptr, true, cs),
+                                   feed ? next : nullptr, nullptr, st->positions, true, cs),
               "keys_to_codes");
   } else {
     for (int l = 0; l < gm.layers; ++l) {
@@ -859,11 +863,12 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     if (heads) {
       TTS_TRY(launch_gemm(req_heads(), c->gemm, cs, c->device), "proj");
       TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, embed16, embed32, D, codes,
-                                   feed ? next : nullptr, nullptr, true, cs),
+                                   feed ? next : nullptr, nullptr, st->positions, true, cs),
               "keys_to_codes");
     }
   }
-  TTS_TRY(launch_advance_positions(st->positions, B, true, cs), "advance_positions");
+  // with heads, the code gather advanced the positions
+  if (!heads) TTS_TRY(launch_advance_positions(st->positions, B, true, cs), "advance_positions");
 #undef TTS_TRY
   return TTS_OK;
 }
@@ -976,7 +981,6 @@ tts_status tts_predictor_create(tts_stack* s, const tts_predictor_weights* w,
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   cudaFree(plain2);
   if (e == cudaSuccess) e = dmalloc(&p->x16, size_t(R) * 2 * E * 2);
-  if (e == cudaSuccess) e = dmalloc(&p->x0, size_t(R) * D * 4);
   if (e == cudaSuccess) e = dmalloc(&p->table2, size_t(R) * kPredictorMaxBlocks * 4);
   if (e == cudaSuccess) e = dmalloc(&p->pos2, size_t(R) * 4);
   if (e == cudaSuccess) e = dmalloc(&p->step_codes, size_t(w->steps) * R * 4);
@@ -994,7 +998,6 @@ tts_status tts_predictor_destroy(tts_predictor* p) {
   DeviceGuard g(p->s->ctx->device);
   cudaFree(p->resize2);
   cudaFree(p->x16);
-  cudaFree(p->x0);
   cudaFree(p->table2);
   cudaFree(p->pos2);
   cudaFree(p->step_codes);
@@ -1030,7 +1033,7 @@ static tts_status frame_impl(tts_predictor* p, const tts_decode_state* st, const
     if ((rc = counted((expr), op)) != TTS_OK) \
       return rc;                              \
   } while (0)
-  TTS_TRY(launch_predictor_prefill(hidden, code0, B, E, p->x16, w.resize_bias, D, p->x0,
+  TTS_TRY(launch_predictor_prefill(hidden, code0, B, E, p->x16, w.resize_bias, D, s->h,
                                    st->block_table, st->max_blocks, p->table2, p->pos2,
                                    st->positions, cs),
           "predictor_prefill");
@@ -1042,7 +1045,7 @@ static tts_status frame_impl(tts_predictor* p, const tts_decode_state* st, const
   rz.k = 2 * E;
   rz.n = D;
   rz.epi = EPI_RESIDUAL;
-  rz.y = p->x0;
+  rz.y = s->h;  // the stack's residual stream: the first depth step starts from it
   TTS_TRY(launch_gemm(rz, s->ctx->gemm, cs, s->ctx->device), "proj");
   tts_decode_state pre = *st;
   pre.lanes = 2 * B;
@@ -1054,7 +1057,9 @@ static tts_status frame_impl(tts_predictor* p, const tts_decode_state* st, const
     hs.heads = static_cast<const __half*>(w.heads) + size_t(i) * V * D;
     // the last pick feeds nothing (talker.rs:455: no stack step after the last head)
     hs.embed32 = i + 1 < w.steps ? w.resized + size_t(i) * V * D : nullptr;
-    rc = step_impl(s, i == 0 ? &pre : st, i == 0 ? p->x0 : nullptr, nullptr, nullptr,
+    hs.in_h = true;
+    hs.feed_h = true;
+    rc = step_impl(s, i == 0 ? &pre : st, nullptr, nullptr, nullptr,
                    p->step_codes + size_t(i) * stride, cs, &hs);
     if (rc != TTS_OK) return rc;
   }

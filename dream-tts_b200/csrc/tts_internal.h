@@ -159,6 +159,10 @@ struct AttnWorkspace {
   unsigned* counters = nullptr;
   int n_counters = 0;
 };
+// Spans up to kShortSpanMax take the CUDA-core kernel (attn_short.cu): at a few dozen positions
+// the tensor-core kernel's fixed cost dominates.
+constexpr int kShortSpanMax = 64;
+cudaError_t launch_attn_short(const AttnRequest& r, cudaStream_t st);
 size_t attn_part_bytes(int lanes, int n_kv, int gqa, int max_span);
 cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream_t st);
 // The same attention with its scratch in a fixed device array (no allocation anywhere).
@@ -181,7 +185,7 @@ cudaError_t launch_argmax(const float* logits, int rows, int n, const uint8_t* b
 cudaError_t launch_keys_to_codes(const unsigned long long* keys, int rows, int codebooks,
                                  int vocab, const __half* embed, const float* embed32, int dim,
                                  uint32_t* codes, float* x_next, unsigned long long* keys_reset,
-                                 bool pdl, cudaStream_t st);
+                                 int* positions, bool pdl, cudaStream_t st);
 // The depth predictor's frame ends (predictor.cu): the prefill rows (f32 inputs split into
 // f16 hi | lo halves, the projection's bias rows, the paired-lane block table and positions)
 // and the codes transpose with the embedding sum at talker width.

@@ -247,5 +247,41 @@ def test_decode_attention_rejects_unaligned_pages(tt):
     kv = L.KvCache(kp.data_ptr(), kp.data_ptr(), table.data_ptr(), 2, 12, 4, 8, 128)
     q = torch.zeros(2, 16, 128, device="cuda")
     with pytest.raises(tt.TtsError) as e:
-        tt.attn.decode_attention_paged(q, kv, torch.full((2,), 20, dtype=torch.int32, device="cuda"), 24)
+        tt.attn.decode_attention_paged(q, kv, torch.full((2,), 20, dtype=torch.int32, device="cuda"), 100)
     assert "multiple of 8" in str(e.value)
+
+
+@pytest.mark.parametrize("bs,n_kv,gqa,window", [(12, 8, 2, 0), (16, 8, 1, 0), (8, 4, 4, 0),
+                                                (5, 2, 8, 0), (16, 8, 2, 9), (64, 8, 2, 0)])
+def test_decode_attention_short_spans(tt, orc, bs, n_kv, gqa, window):
+    """max_span <= 64 takes the CUDA-core kernel: any page size (the tensor-core kernel's
+    multiple-of-8 rule does not apply), gqa 1..8, windows, per-lane spans 1..64, and one page
+    outside the pool read as zeros and reported."""
+    from ttsnn import _lib as L
+    rng = np.random.default_rng(bs * 100 + gqa * 10 + window)
+    lanes, cap = 14, -(-64 // bs) * bs
+    spans = np.concatenate([[1, 2, 16, 17, 63, 64], rng.integers(1, 65, lanes - 6)]).astype(np.int32)
+    q = rng.standard_normal((lanes, n_kv * gqa, 128), dtype=np.float32) * 0.1
+    kb = orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
+    vb = orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
+    kp, vp, table, nb = _paged(rng, kb, vb, bs)
+    kz, vz = kb.copy(), vb.copy()
+    last = (int(spans[4]) - 1) // bs  # lane 4 (span 63): its last page is outside the pool
+    table[4, last] = nb + 3
+    kz[4, :, last * bs:(last + 1) * bs] = 0
+    vz[4, :, last * bs:(last + 1) * bs] = 0
+    tdev = torch.from_numpy(table).cuda()
+    kv = L.KvCache(kp.data_ptr(), vp.data_ptr(), tdev.data_ptr(), cap // bs, bs, nb, n_kv, 128)
+    got = tt.attn.decode_attention_paged(dev_f32(q), kv, torch.from_numpy(spans).cuda(), 64,
+                                         window=window, out_f16=False)
+    with pytest.raises(tt.TtsError) as e:
+        tt.check()
+    assert e.value.status == 1
+    wstart = np.where((window > 0) & (spans > window), spans - window, 0).astype(np.int32)
+    want = orc.decode_attention(q.reshape(lanes, n_kv, gqa, 128), kz, vz, spans, wstart)
+    assert rel(np_(got), want.reshape(lanes, -1)) < 1e-5
+    got16 = tt.attn.decode_attention_paged(dev_f32(q), kv, torch.from_numpy(spans).cuda(), 64,
+                                           window=window, out_f16=True)
+    assert rel(np_(got16.float()), want.reshape(lanes, -1)) < 2e-3
+    with pytest.raises(tt.TtsError):
+        tt.check()
