@@ -634,6 +634,19 @@ def run_kernel_case(args):
                        kv.num_blocks, N_KV, HD)
         for _ in range(4):
             ttsnn.attn.decode_attention_paged(q, st, kv.positions, per * BLOCK)
+    elif args.kernel == "attn_short":
+        # the depth predictor's attention: 48 lanes x 8 kv heads, spans 1..16, 16-position pages
+        from qwen3tts import PREDICTOR_GEOMETRY, PagedKv
+        kv = PagedKv(PREDICTOR_GEOMETRY, LANES, LANES, 16, 1, device)
+        for i in range(LANES):
+            kv.admit(i, 16, 1 + i % 16)
+        kv.k.normal_()
+        kv.v.normal_()
+        q = torch.randn(LANES, HEADS, HD, device=device) * 0.1
+        st = L.KvCache(kv.k.data_ptr(), kv.v.data_ptr(), kv.table.data_ptr(), 1, 16,
+                       kv.num_blocks, N_KV, HD)
+        for _ in range(4):
+            ttsnn.attn.decode_attention_paged(q, st, kv.positions, 16)
     elif args.kernel == "conv":
         x, convs = build_codec_block(device)
         bufs = [torch.empty_like(x), torch.empty_like(x)]
@@ -807,7 +820,7 @@ def main():
     ap.add_argument("--lanes", type=int, default=48)
     ap.add_argument("--segments", type=int, default=96, help="segments per GPU (sweep, document)")
     ap.add_argument("--refill", action="store_true")
-    ap.add_argument("--kernel", choices=["gemm", "attn", "conv"],
+    ap.add_argument("--kernel", choices=["gemm", "attn", "attn_short", "conv"],
                     help="run a small standalone case of one kernel (for ncu captures)")
     args = ap.parse_args()
     if args.warmup < 3:

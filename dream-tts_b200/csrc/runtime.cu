@@ -62,6 +62,10 @@ struct tts_stack {
   float* x_next = nullptr;    // [max_lanes][dim] (own buffer)
   float* feedback = nullptr;  // caller's buffer replacing x_next, or null
   unsigned long long* keys = nullptr;  // [max_lanes][codebooks]
+  // bytes of the next projection's weights each kernel prefetches into L2 (0: none). 12 MB
+  // measured best for the talker; the depth predictor's stack runs without (its kernels are
+  // latency-bound, and the prefetch measured 6% slower per frame at 48 lanes).
+  size_t pf_budget = size_t(12) << 20;
   // layer chain (steps of up to 128 lanes): phase counters and partial tiles
   ChainWorkspace chain;
   int chain_lanes = 0;  // lanes the partial buffer is sized for (0: no chain)
@@ -663,7 +667,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
   // into L2 once its own stream is out (separate-kernel path)
   // (TTS_L2_PREFETCH_MB overrides the budget for A/B measurement; 0 turns it off)
   const char* pf_env = getenv("TTS_L2_PREFETCH_MB");
-  const size_t pf_budget = size_t(pf_env && *pf_env ? atoi(pf_env) : 12) << 20;
+  const size_t pf_budget = pf_env && *pf_env ? size_t(atoi(pf_env)) << 20 : s->pf_budget;
   auto pf = [&](const void* w, int k, int n) {
     return pf_budget ? gemm_prefetch_plan(w, B, k, n, c->device, pf_budget) : L2Prefetch{};
   };
@@ -957,6 +961,7 @@ tts_status tts_predictor_create(tts_stack* s, const tts_predictor_weights* w,
   DeviceGuard g(c->device);
   auto* p = new tts_predictor();
   p->s = s;
+  s->pf_budget = 0;
   p->w = *w;
   p->max_lanes = c->max_lanes / 2;
   const int D = gm.dim, E = w->embed_dim, R = 2 * p->max_lanes;
