@@ -165,7 +165,8 @@ class Clocks:
                 "samples": len(rows)}
 
 
-def build_device_talker(device, seed=0, extra_positions=256, lanes_override=None):
+def build_device_talker(device, seed=0, extra_positions=256, lanes_override=None, codebooks=CB,
+                        vocab=VOCAB):
     import torch
     import ttsnn
     from qwen3tts import Geometry, LayerTensors, PagedKv, Stack
@@ -175,7 +176,8 @@ def build_device_talker(device, seed=0, extra_positions=256, lanes_override=None
         return (torch.randn(n, k, generator=gen, device=device) * 0.02).half()
 
     geo = Geometry(dim=DIM, layers=LAYERS, heads=HEADS, n_kv=N_KV, head_dim=HD, ffn=FFN,
-                   rope_len=max(KV_HI + extra_positions + 64, 1600), codebooks=CB, vocab=VOCAB)
+                   rope_len=max(KV_HI + extra_positions + 64, 1600), codebooks=codebooks,
+                   vocab=vocab)
     ones = torch.ones(DIM, device=device)
     qk = torch.stack([torch.full((HD,), 1.0 / HD ** 0.5, device=device), torch.ones(HD, device=device)])
     layers = []
@@ -184,8 +186,8 @@ def build_device_talker(device, seed=0, extra_positions=256, lanes_override=None
                                               w(DIM, HEADS * HD),
                                               ttsnn.interleave_gate_up(w(FFN, DIM), w(FFN, DIM)),
                                               w(DIM, FFN)))
-    heads = w(CB * VOCAB, DIM)
-    embed = (torch.randn(CB, VOCAB, DIM, generator=gen, device=device) * 0.02).half()
+    heads = w(codebooks * vocab, DIM)
+    embed = (torch.randn(codebooks, vocab, DIM, generator=gen, device=device) * 0.02).half()
     stack = Stack(geo, layers, ones, heads, embed)
     if lanes_override == 0:
         return stack, None, None, None
@@ -604,6 +606,146 @@ def run_predictor(args):
     return 0
 
 
+def run_frames(args):
+    """The reference's talker loop, greedy (talker.rs:903-1073), at 48 lanes per GPU: one step =
+    one frame for every lane = the 28-layer talker step with its codec head (3072 ids) under the
+    pick rule (banned top 1024 except eos, eos after 2 frames, repetition penalty 1.05), code 0's
+    codec_embed row, the depth predictor's 15 residual codes and the next input (their sum plus
+    the lane's text row), as one captured graph. KV lengths U[64, 1024] as config[2]. frames/s =
+    lanes x frames per second; e2e adds each frame's text rows in (pinned host -> device) and
+    its 16 codes out. Weak scaling: each rank its own lanes."""
+    import torch
+    import torch.distributed as dist
+    import ttsnn
+    from qwen3tts import FrameLoop, reference_pick
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
+    steps, warmup = args.steps, args.warmup
+    extra = steps + warmup + 8
+    stack, _, _, _ = build_device_talker(device, seed=rank, extra_positions=extra,
+                                         lanes_override=0, codebooks=1, vocab=3072)
+    pred = build_device_predictor(device, seed=100 + rank)
+    lengths = kv_lengths(rank)
+    cap = KV_HI + extra + 8
+    text_len = 64
+    gen = torch.Generator(device=device).manual_seed(200 + rank)
+    text = torch.randn(LANES, text_len, DIM, generator=gen, device=device) * 0.1
+    pad = torch.randn(DIM, generator=gen, device=device) * 0.1
+    loop = FrameLoop(stack, pred, LANES, cap, reference_pick(lanes=LANES, device=device), text,
+                     pad, block_size=BLOCK)
+    for i in range(LANES):
+        loop.admit(i, int(lengths[i]) + 1, extra, torch.randn(DIM, generator=gen, device=device))
+    for li in range(LAYERS):
+        loop.kv.k[li].normal_(generator=gen)
+        loop.kv.v[li].normal_(generator=gen)
+    stream = torch.cuda.Stream(device)
+    text_host = (torch.randn(LANES, DIM) * 0.1).pin_memory()
+    codes_host = torch.empty(LANES, 16, dtype=torch.int32).pin_memory()
+    with torch.cuda.stream(stream):
+        graph = loop.graph(LANES)
+        for _ in range(warmup):
+            graph.replay()
+    stream.synchronize()
+    ttsnn.check(local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local, os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
+                    if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/clocks_rank{rank}.csv")
+    ttsnn.launch_count(reset=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    stream.synchronize()
+    launches = ttsnn.launch_count()
+    clk = clocks.stop()
+    barrier()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    ttsnn.check(local)
+    # end to end: each frame's text rows in from pinned host memory, its 16 codes out
+    barrier()
+    torch.cuda.synchronize()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e2.record(stream)
+        for i in range(steps):
+            f = (warmup + steps + i) % text_len
+            loop.text.rows[:, f].copy_(text_host, non_blocking=True)
+            graph.replay()
+            codes_host[:, 0].copy_(loop.code0[:LANES], non_blocking=True)
+            codes_host[:, 1:].copy_(loop.codes[:LANES], non_blocking=True)
+            stream.synchronize()
+        e3.record(stream)
+    stream.synchronize()
+    t2 = torch.tensor([e2.elapsed_time(e3)], device=device)
+    if world > 1:
+        dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t2.item())
+    ttsnn.check(local)
+    hbm, peak_kind = peaks()
+    frame_s = ms / steps * 1e-3
+    mean_len = float(lengths.mean()) + warmup + steps / 2.0 + 1
+    kv_bytes = LAYERS * N_KV * HD * 2 * 2 * LANES * mean_len
+    fbytes = stack.weight_bytes() + kv_bytes + pred.weight_bytes()
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            ts = CpuSample(threads=os.cpu_count())
+            ps = PredictorCpuSample(threads=os.cpu_count())
+            ts.time()
+            ps.time()
+            t_talker = statistics.median([ts.time() for _ in range(3)])
+            t_pred = statistics.median([ps.time() for _ in range(3)]) * LANES / ps.lanes
+            cpu = {"value": round(LANES / (t_talker + t_pred), 3), "unit": UNIT,
+                   "cores": ts.threads(), "kind": "port",
+                   "sample": ts.sample + "; plus " + ps.sample + ", scaled to 48 lanes"}
+        line = {
+            "metric": "codec frames/sec (reference talker loop: talker + depth predictor, whole box)",
+            "value": round(world * LANES * steps / (ms * 1e-3), 2), "unit": UNIT,
+            "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": round(ms / steps, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (random-init weights)",
+            "config": {"workload": "talker.rs:903-1073 greedy: 28-layer talker (config[2] shape) "
+                                   "with codec head 3072 + pick rule, depth predictor (5 x 1024, "
+                                   "15 heads), text rows; 48 lanes, KV lengths U[64,1024]",
+                       "lanes_per_gpu": LANES, "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2: each frame streams 5.3 GB of weights "
+                             "and ~3 GB of KV"},
+            "roofline": {"bound": "hbm", "kernel": "whole frame (weights + KV)",
+                         "achieved": round(fbytes / frame_s / 1e9, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(fbytes / frame_s / 1e9 / hbm, 4),
+                         "traffic": None, "peak_source": peak_kind,
+                         "algorithmic_bytes_per_frame": int(fbytes)},
+            "e2e": {"value": round(world * LANES * steps / (e2e_ms * 1e-3), 2), "unit": UNIT,
+                    "h2d_bytes_per_step": LANES * DIM * 4, "d2h_bytes_per_step": LANES * 16 * 4},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    del graph
+    loop.graphs.clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_kernel_case(args):
     """Small standalone cases of one kernel, for ncu captures (a few launches, < 1 GB)."""
     import torch
@@ -813,10 +955,11 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--workload", default="step",
-                    choices=["step", "sweep", "document", "predictor"],
+                    choices=["step", "sweep", "document", "predictor", "frames"],
                     help="step: the config[2] decode step (headline); sweep: config[3]; "
                          "document: a bounded config[4] sample (talker + codec); predictor: "
-                         "the depth predictor's frame")
+                         "the depth predictor's frame; frames: the reference's talker loop "
+                         "(talker + predictor)")
     ap.add_argument("--lanes", type=int, default=48)
     ap.add_argument("--segments", type=int, default=96, help="segments per GPU (sweep, document)")
     ap.add_argument("--refill", action="store_true")
@@ -835,6 +978,8 @@ def main():
         return run_document(args)
     if args.workload == "predictor":
         return run_predictor(args)
+    if args.workload == "frames":
+        return run_frames(args)
     return run_b200(args)
 
 

@@ -50,6 +50,7 @@ struct Phase {
   QkRopeArgs qk;
   unsigned long long* keys;
   int vocab, codebooks;
+  PickRule pick;
   // NORM: y16[r] = src[r] / rms(src[r]) * w, optionally y32 too; zeroes keys[0, n_keys)
   const float* src;
   const float* w;
@@ -574,6 +575,7 @@ cudaError_t launch_chain(const ChainRequest& r, const ChainWorkspace& w, cudaStr
       ph.keys = g.argmax_keys;
       ph.vocab = g.vocab;
       ph.codebooks = g.vocab > 0 ? g.n / g.vocab : 0;
+      ph.pick = g.pick;
       if (!make_tmap_2d_f16(&maps.w[p], g.w, kBlockK, uint64_t(ph.tiles) * ph.kb_total * kTileM,
                             kBlockK * 2, kBlockK, kTileM, true) ||
           !make_tmap_2d_f16(&maps.x[p], g.x, g.k, g.m, uint64_t(g.k) * 2, kBlockK, a.ng, true)) {

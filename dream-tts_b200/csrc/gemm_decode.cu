@@ -53,6 +53,7 @@ struct GemmArgs {
   unsigned long long* keys;
   int vocab;
   int codebooks;
+  PickRule pick;  // EPI_ARGMAX: the talker's pick rule (words == 0: none)
   L2Prefetch pf;  // the next GEMM's first weight blocks
 };
 
@@ -508,6 +509,7 @@ cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t
   a.keys = r.argmax_keys;
   a.vocab = r.vocab;
   a.codebooks = r.vocab > 0 ? r.n / r.vocab : 0;
+  a.pick = r.pick;
   a.pf = r.next;
 
   {

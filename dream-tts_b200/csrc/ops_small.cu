@@ -175,13 +175,21 @@ __global__ void __launch_bounds__(256) keys_to_codes_kernel(const unsigned long 
                                                             const float* embed32, int dim,
                                                             uint32_t* codes, float* x_next,
                                                             unsigned long long* keys_reset,
-                                                            int* positions) {
+                                                            int* positions, PickRule pick) {
   __shared__ int sc[64];
   pdl_launch_dependents();
   pdl_wait();
   const int row = blockIdx.x;
   // the step's last reader of the positions has finished: advance this lane's
   if (positions && threadIdx.x == 0) positions[row] += 1;
+  // the pick rule's history (one codebook): the pick joins the row's seen ids unless it is eos
+  // (talker.rs:990-996), and the row has one more frame
+  if (pick.words && threadIdx.x == 0) {
+    const unsigned c = unsigned(keys[row] & 0xffffffffu);
+    if (pick.seen && int(c) != pick.eos && c < unsigned(pick.words * 32))
+      pick.seen[(size_t)row * pick.words + (c >> 5)] |= 1u << (c & 31);
+    if (pick.frames) pick.frames[row] += 1;
+  }
   if (threadIdx.x < codebooks) {
     const unsigned c = unsigned(keys[(size_t)row * codebooks + threadIdx.x] & 0xffffffffu);
     sc[threadIdx.x] = int(c < unsigned(vocab) ? c : 0);
@@ -289,14 +297,20 @@ cudaError_t launch_argmax(const float* logits, int rows, int n, const uint8_t* b
 cudaError_t launch_keys_to_codes(const unsigned long long* keys, int rows, int codebooks,
                                  int vocab, const __half* embed, const float* embed32, int dim,
                                  uint32_t* codes, float* x_next, unsigned long long* keys_reset,
-                                 int* positions, bool pdl, cudaStream_t st) {
+                                 int* positions, const PickRule* pick, bool pdl,
+                                 cudaStream_t st) {
+  PickRule pr = pick ? *pick : PickRule{};
+  if (pr.words && codebooks != 1) {
+    set_error("keys_to_codes: a pick rule takes one codebook");
+    return cudaErrorInvalidValue;
+  }
   if (codebooks > 64 || codebooks < 1 || ((embed || embed32) && dim % 2)) {
     set_error("keys_to_codes: 1..64 codebooks, even dim");
     return cudaErrorInvalidValue;
   }
   void* args[] = {(void*)&keys, (void*)&codebooks, (void*)&vocab,  (void*)&embed,
                   (void*)&embed32, (void*)&dim,    (void*)&codes, (void*)&x_next,
-                  (void*)&keys_reset, (void*)&positions};
+                  (void*)&keys_reset, (void*)&positions, (void*)&pr};
   return launch_ex(reinterpret_cast<void (*)(void*)>(keys_to_codes_kernel), dim3(rows),
                    dim3(256), st, pdl, args);
 }

@@ -64,13 +64,21 @@ __global__ void __launch_bounds__(256) predictor_prefill_kernel(
 // Frame end (talker.rs:466-467, 528-550): the per-step codes transposed to [lane][step], and
 // sum = code0_embed + sum over steps of tables[step][code] at talker width, the table rows summed
 // in f32 in step order first, as gather_sum's sum_keepdim, then added to code0_embed.
+// With a text feed the lane's text row (its trailing text while rows remain, then the pad
+// row) is added last, as the talker adds it to the predictor's sum (talker.rs:1043-1050).
 __global__ void __launch_bounds__(256) predictor_finish_kernel(
     const uint32_t* step_codes, int stride, int steps, const __half* tables, int vocab,
-    int embed_dim, const float* code0, uint32_t* codes, float* sum) {
+    int embed_dim, const float* code0, uint32_t* codes, float* sum, TextFeed text) {
   __shared__ int sc[64];
   pdl_launch_dependents();
   pdl_wait();
   const int lane = blockIdx.x;
+  const float* trow = nullptr;
+  if (text.pad) {
+    const int t = text.frames ? text.frames[lane] - 1 : 0;
+    trow = t >= 0 && t < text.len ? text.rows + ((size_t)lane * text.len + t) * embed_dim
+                                  : text.pad;
+  }
   if (threadIdx.x < steps) {
     const uint32_t c = step_codes[(size_t)threadIdx.x * stride + lane];
     codes[(size_t)lane * steps + threadIdx.x] = c;
@@ -86,8 +94,15 @@ __global__ void __launch_bounds__(256) predictor_finish_kernel(
       s1 += f.y;
     }
     const float2 c0 = *reinterpret_cast<const float2*>(code0 + (size_t)lane * embed_dim + e);
-    sum[(size_t)lane * embed_dim + e] = c0.x + s0;
-    sum[(size_t)lane * embed_dim + e + 1] = c0.y + s1;
+    float2 r = make_float2(c0.x + s0, c0.y + s1);
+    if (trow) {
+      const float2 tx = *reinterpret_cast<const float2*>(trow + e);
+      r.x += tx.x;
+      r.y += tx.y;
+    }
+    // in place over code0 is allowed: this thread read the element it overwrites
+    sum[(size_t)lane * embed_dim + e] = r.x;
+    sum[(size_t)lane * embed_dim + e + 1] = r.y;
   }
 }
 
@@ -112,14 +127,15 @@ cudaError_t launch_predictor_prefill(const float* hidden, const float* code0, in
 cudaError_t launch_predictor_finish(const uint32_t* step_codes, int stride, int lanes, int steps,
                                     const __half* tables, int vocab, int embed_dim,
                                     const float* code0, uint32_t* codes, float* sum,
-                                    cudaStream_t st) {
+                                    const TextFeed& text, cudaStream_t st) {
   if (lanes < 1 || steps < 1 || steps > 64 || embed_dim % 2) {
     set_error("predictor_finish: lanes >= 1, 1..64 steps, even embed_dim");
     return cudaErrorInvalidValue;
   }
+  TextFeed tf = text;
   void* args[] = {(void*)&step_codes, (void*)&stride, (void*)&steps, (void*)&tables,
                   (void*)&vocab,      (void*)&embed_dim, (void*)&code0, (void*)&codes,
-                  (void*)&sum};
+                  (void*)&sum,        (void*)&tf};
   return launch_pdl(reinterpret_cast<void (*)(void*)>(predictor_finish_kernel), dim3(lanes),
                     dim3(256), st, args);
 }

@@ -61,6 +61,7 @@ struct tts_stack {
   __half* act = nullptr;      // [max_lanes][ffn]
   float* x_next = nullptr;    // [max_lanes][dim] (own buffer)
   float* feedback = nullptr;  // caller's buffer replacing x_next, or null
+  PickRule pick;              // the codec head's greedy pick rule (words == 0: plain argmax)
   unsigned long long* keys = nullptr;  // [max_lanes][codebooks]
   // bytes of the next projection's weights each kernel prefetches into L2 (0: none). 12 MB
   // measured best for the talker; the depth predictor's stack runs without (its kernels are
@@ -588,6 +589,32 @@ tts_status tts_stack_set_head(tts_stack* s, const float* final_norm, const void*
   return TTS_OK;
 }
 
+tts_status tts_stack_set_pick(tts_stack* s, const tts_pick_rule* rule) {
+  if (!s) return fail(TTS_ERR_INVALID_ARG, "stack_set_pick: stack is NULL");
+  if (!rule) {
+    s->pick = PickRule{};
+    return TTS_OK;
+  }
+  if (s->geo.codebooks != 1 || s->geo.vocab % 32)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "stack_set_pick: needs one codebook head");
+  if (!(rule->penalty > 0.f) || rule->min_new < 0 || rule->eos >= s->geo.vocab)
+    return fail(TTS_ERR_INVALID_ARG, "stack_set_pick: penalty > 0, min_new >= 0, eos < vocab");
+  if ((rule->min_new > 0 && rule->eos >= 0 && !rule->frames) ||
+      (rule->penalty != 1.f && !rule->seen))
+    return fail(TTS_ERR_INVALID_ARG,
+                "stack_set_pick: min_new needs frames, a penalty needs the seen bits");
+  PickRule p;
+  p.ban = rule->ban;
+  p.seen = rule->seen;
+  p.frames = rule->frames;
+  p.penalty = rule->penalty;
+  p.eos = rule->eos;
+  p.min_new = rule->min_new;
+  p.words = s->geo.vocab / 32;
+  s->pick = p;
+  return TTS_OK;
+}
+
 tts_status tts_stack_set_feedback(tts_stack* s, float* x_next) {
   if (!s) return fail(TTS_ERR_INVALID_ARG, "stack_set_feedback: stack is NULL");
   s->feedback = x_next;
@@ -752,6 +779,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     hd.y = logits;
     hd.argmax_keys = s->keys;
     hd.vocab = gm.vocab;
+    if (!hsel) hd.pick = s->pick;
     return hd;
   };
   auto req_attn = [&](int l) {
@@ -832,7 +860,8 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     }
     if (heads)
       TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, embed16, embed32, D, codes,
-                                   feed ? next : nullptr, nullptr, st->positions, true, cs),
+                                   feed ? next : nullptr, nullptr, st->positions,
+                                   hsel ? nullptr : &s->pick, true, cs),
               "keys_to_codes");
   } else {
     for (int l = 0; l < gm.layers; ++l) {
@@ -867,7 +896,8 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     if (heads) {
       TTS_TRY(launch_gemm(req_heads(), c->gemm, cs, c->device), "proj");
       TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, embed16, embed32, D, codes,
-                                   feed ? next : nullptr, nullptr, st->positions, true, cs),
+                                   feed ? next : nullptr, nullptr, st->positions,
+                                   hsel ? nullptr : &s->pick, true, cs),
               "keys_to_codes");
     }
   }
@@ -1011,9 +1041,22 @@ tts_status tts_predictor_destroy(tts_predictor* p) {
 }
 
 // Predictor::frame_batch with greedy picks (talker.rs:407-468) and gather_sum (:528-550).
+static bool text_feed(const tts_text_feed* t, int embed_dim, TextFeed* out) {
+  *out = TextFeed{};
+  if (!t) return true;
+  if (!t->pad || (t->len > 0 && !t->rows) || t->len < 0 || (t->len > 0 && !t->frames))
+    return false;
+  out->rows = t->rows;
+  out->len = t->len;
+  out->pad = t->pad;
+  out->frames = t->frames;
+  (void)embed_dim;
+  return true;
+}
+
 static tts_status frame_impl(tts_predictor* p, const tts_decode_state* st, const float* hidden,
-                             const float* code0, unsigned int* codes, float* sum,
-                             cudaStream_t cs) {
+                             const float* code0, const tts_text_feed* text, unsigned int* codes,
+                             float* sum, cudaStream_t cs) {
   tts_stack* s = p->s;
   const tts_stack_geometry& gm = s->geo;
   const tts_predictor_weights& w = p->w;
@@ -1031,6 +1074,10 @@ static tts_status frame_impl(tts_predictor* p, const tts_decode_state* st, const
                 "max_span >= steps + 1");
   if (!aligned16(hidden) || !aligned16(code0) || !aligned16(sum))
     return fail(TTS_ERR_INVALID_ARG, "predictor_frame: hidden, code0_embed, sum 16-byte aligned");
+  TextFeed tf;
+  if (!text_feed(text, w.embed_dim, &tf))
+    return fail(TTS_ERR_INVALID_ARG,
+                "predictor_frame: a text feed needs pad, and rows and frames when len > 0");
   const int D = gm.dim, E = w.embed_dim, V = gm.vocab, stride = 2 * p->max_lanes;
   tts_status rc;
 #define TTS_TRY(expr, op)                     \
@@ -1070,29 +1117,76 @@ static tts_status frame_impl(tts_predictor* p, const tts_decode_state* st, const
   }
   TTS_TRY(launch_predictor_finish(p->step_codes, stride, B, w.steps,
                                   static_cast<const __half*>(w.tables), V, E, code0, codes, sum,
-                                  cs),
+                                  tf, cs),
           "predictor_finish");
 #undef TTS_TRY
   return TTS_OK;
 }
 
 tts_status tts_predictor_frame(tts_predictor* p, const tts_decode_state* st, const float* hidden,
-                               const float* code0_embed, unsigned int* codes, float* sum,
-                               void* stream) {
+                               const float* code0_embed, const tts_text_feed* text,
+                               unsigned int* codes, float* sum, void* stream) {
   if (!p) return fail(TTS_ERR_INVALID_ARG, "predictor_frame: predictor is NULL");
   DeviceGuard g(p->s->ctx->device);
-  return frame_impl(p, st, hidden, code0_embed, codes, sum, S(stream));
+  return frame_impl(p, st, hidden, code0_embed, text, codes, sum, S(stream));
 }
 
 tts_status tts_predictor_graph_capture(tts_predictor* p, const tts_decode_state* st,
                                        const float* hidden, const float* code0_embed,
-                                       unsigned int* codes, float* sum, void* stream,
-                                       tts_graph** out) {
+                                       const tts_text_feed* text, unsigned int* codes,
+                                       float* sum, void* stream, tts_graph** out) {
   if (!p || !out) return fail(TTS_ERR_INVALID_ARG, "graph_capture: NULL argument");
   if (!stream) return fail(TTS_ERR_INVALID_ARG, "graph_capture: needs a non-legacy stream");
   DeviceGuard g(p->s->ctx->device);
   return capture_graph(S(stream), out, [&](cudaStream_t cs) {
-    return frame_impl(p, st, hidden, code0_embed, codes, sum, cs);
+    return frame_impl(p, st, hidden, code0_embed, text, codes, sum, cs);
+  });
+}
+
+// ---------------------------------------------------------------- the talker's frame
+
+// Talker::generate_batch's loop body with greedy picks (talker.rs:953-1057): the talker step
+// (head, pick rule, code 0's codec_embed row into the feedback buffer), then the predictor on
+// the step's hidden state and that row; the predictor's sum plus the text row replaces the row
+// in the feedback buffer, the next step's input.
+static tts_status talker_frame_impl(tts_stack* t, const tts_decode_state* tst, tts_predictor* p,
+                                    const tts_decode_state* pst, const tts_text_feed* text,
+                                    float* hidden, unsigned int* code0, unsigned int* codes,
+                                    cudaStream_t cs) {
+  if (!t || !tst || !p || !pst || !hidden || !code0 || !codes)
+    return fail(TTS_ERR_INVALID_ARG, "talker_frame: NULL argument");
+  if (t->geo.codebooks != 1 || !t->heads || !t->embed || !t->feedback)
+    return fail(TTS_ERR_INVALID_ARG,
+                "talker_frame: the talker needs one codebook head, its embedding table and a "
+                "feedback buffer");
+  if (t->geo.dim != p->w.embed_dim)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "talker_frame: talker dim != predictor embed_dim");
+  if (pst->lanes != tst->lanes)
+    return fail(TTS_ERR_INVALID_ARG, "talker_frame: talker and predictor lane counts differ");
+  tts_status rc = step_impl(t, tst, nullptr, hidden, nullptr, code0, cs);
+  if (rc != TTS_OK) return rc;
+  return frame_impl(p, pst, hidden, t->feedback, text, codes, t->feedback, cs);
+}
+
+tts_status tts_talker_frame(tts_stack* talker, const tts_decode_state* talker_st,
+                            tts_predictor* p, const tts_decode_state* pred_st,
+                            const tts_text_feed* text, float* hidden, unsigned int* code0,
+                            unsigned int* codes, void* stream) {
+  if (!talker) return fail(TTS_ERR_INVALID_ARG, "talker_frame: talker is NULL");
+  DeviceGuard g(talker->ctx->device);
+  return talker_frame_impl(talker, talker_st, p, pred_st, text, hidden, code0, codes, S(stream));
+}
+
+tts_status tts_talker_frame_capture(tts_stack* talker, const tts_decode_state* talker_st,
+                                    tts_predictor* p, const tts_decode_state* pred_st,
+                                    const tts_text_feed* text, float* hidden,
+                                    unsigned int* code0, unsigned int* codes, void* stream,
+                                    tts_graph** out) {
+  if (!talker || !out) return fail(TTS_ERR_INVALID_ARG, "graph_capture: NULL argument");
+  if (!stream) return fail(TTS_ERR_INVALID_ARG, "graph_capture: needs a non-legacy stream");
+  DeviceGuard g(talker->ctx->device);
+  return capture_graph(S(stream), out, [&](cudaStream_t cs) {
+    return talker_frame_impl(talker, talker_st, p, pred_st, text, hidden, code0, codes, cs);
   });
 }
 

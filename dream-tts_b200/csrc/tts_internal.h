@@ -71,6 +71,20 @@ struct L2Prefetch {
 L2Prefetch gemm_prefetch_plan(const void* w_packed, int m, int k, int n, int device,
                               size_t budget);
 
+// The talker's greedy pick rule (crates/qwen3tts/src/talker.rs:154-189, 940, 971-981), applied
+// to the codec head's logits before the argmax: ids with their bit set in `ban` are excluded,
+// `eos` too while frames[row] < min_new, and ids with their bit set in the row's `seen` are
+// divided (if positive) or multiplied (if negative) by `penalty`. The code gather then marks
+// the pick in `seen` (unless it is eos) and counts the row's frame.
+struct PickRule {
+  const uint32_t* ban = nullptr;  // [words]
+  uint32_t* seen = nullptr;       // [rows][words]
+  int* frames = nullptr;          // [rows]
+  float penalty = 1.f;
+  int eos = -1, min_new = 0;
+  int words = 0;                  // vocab / 32
+};
+
 struct GemmRequest {
   // [n][k] (out-major, K contiguous), or packed: [n/128][k/64][128][64], each 128 x 64 tile
   // one contiguous 16 KB block (tts_weight_pack)
@@ -84,6 +98,7 @@ struct GemmRequest {
   QkRopeArgs qk;
   unsigned long long* argmax_keys = nullptr;  // [m][codebooks]
   int vocab = 0;
+  PickRule pick;  // EPI_ARGMAX with one codebook: the talker's pick rule (empty: plain argmax)
   bool pdl = true;
   int force_splits = 0;  // 0 = automatic
   L2Prefetch next;       // optional: the next GEMM's first weight blocks
@@ -185,7 +200,8 @@ cudaError_t launch_argmax(const float* logits, int rows, int n, const uint8_t* b
 cudaError_t launch_keys_to_codes(const unsigned long long* keys, int rows, int codebooks,
                                  int vocab, const __half* embed, const float* embed32, int dim,
                                  uint32_t* codes, float* x_next, unsigned long long* keys_reset,
-                                 int* positions, bool pdl, cudaStream_t st);
+                                 int* positions, const PickRule* pick, bool pdl,
+                                 cudaStream_t st);
 // The depth predictor's frame ends (predictor.cu): the prefill rows (f32 inputs split into
 // f16 hi | lo halves, the projection's bias rows, the paired-lane block table and positions)
 // and the codes transpose with the embedding sum at talker width.
@@ -193,10 +209,16 @@ cudaError_t launch_predictor_prefill(const float* hidden, const float* code0, in
                                      int embed_dim, __half* x16, const float* bias, int dim,
                                      float* x0, const int* table, int max_blocks, int* table2,
                                      int* pos2, int* positions, cudaStream_t st);
+struct TextFeed {
+  const float* rows = nullptr;  // [lanes][len][embed_dim]
+  int len = 0;
+  const float* pad = nullptr;   // [embed_dim]; null: no text added
+  const int* frames = nullptr;  // [lanes]: row frames - 1
+};
 cudaError_t launch_predictor_finish(const uint32_t* step_codes, int stride, int lanes, int steps,
                                     const __half* tables, int vocab, int embed_dim,
                                     const float* code0, uint32_t* codes, float* sum,
-                                    cudaStream_t st);
+                                    const TextFeed& text, cudaStream_t st);
 cudaError_t launch_advance_positions(int* positions, int lanes, bool pdl, cudaStream_t st);
 cudaError_t launch_cast_f32_f16(const float* x, __half* y, long n, cudaStream_t st);
 

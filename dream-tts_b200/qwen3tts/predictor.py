@@ -42,6 +42,23 @@ def resize_tables(tables: torch.Tensor, resize: torch.Tensor,
     return out.to(torch.float32).contiguous()
 
 
+class TextFeed:
+    """Each lane's trailing text embeddings f32 [lanes, len, dim] and the pad row f32 [dim]
+    (talker.rs:933-937, 1043-1048); `frames` int32 [lanes] on the device counts each lane's
+    frames (the pick rule's counter): a frame adds row frames - 1, or the pad row past the end."""
+
+    def __init__(self, rows: torch.Tensor, pad: torch.Tensor, frames: torch.Tensor):
+        self.rows = rows.to(torch.float32).contiguous()
+        self.pad = pad.to(torch.float32).contiguous()
+        self.frames = frames
+        self.c = L.TextFeed(self.rows.data_ptr(), self.rows.shape[1], self.pad.data_ptr(),
+                            frames.data_ptr())
+
+
+def _feed(text: "TextFeed | None"):
+    return None if text is None else C.byref(text.c)
+
+
 class Predictor:
     """`Predictor` of talker.rs:255-330 over a `Stack` created with codebooks = 1 and vocab =
     the residual codebook size (its heads unset: the predictor supplies one per depth step)."""
@@ -81,9 +98,11 @@ class Predictor:
         return kv
 
     def frame(self, kv: PagedKv, hidden: torch.Tensor, code0_embed: torch.Tensor,
-              codes: torch.Tensor | None = None, total: torch.Tensor | None = None):
+              codes: torch.Tensor | None = None, total: torch.Tensor | None = None,
+              text: "TextFeed | None" = None):
         """One frame for kv.lanes lanes: hidden, code0_embed f32 [lanes, embed_dim] -> codes
-        int32 [lanes, steps] and the talker's next-input sum f32 [lanes, embed_dim]."""
+        int32 [lanes, steps] and the talker's next-input sum f32 [lanes, embed_dim] (plus each
+        lane's text row when `text` is given)."""
         n = hidden.shape[0]
         if codes is None:
             codes = torch.empty(n, self.steps, dtype=torch.int32, device=hidden.device)
@@ -91,17 +110,17 @@ class Predictor:
             total = torch.empty(n, self.embed_dim, dtype=torch.float32, device=hidden.device)
         st = kv.state(n, self.steps + 1)
         L.call("tts_predictor_frame", self.handle, C.byref(st), ptr(hidden), ptr(code0_embed),
-               ptr(codes), ptr(total), stream())
+               _feed(text), ptr(codes), ptr(total), stream())
         return codes, total
 
     def capture(self, kv: PagedKv, hidden: torch.Tensor, code0_embed: torch.Tensor,
-                codes: torch.Tensor, total: torch.Tensor) -> Graph:
+                codes: torch.Tensor, total: torch.Tensor, text: "TextFeed | None" = None) -> Graph:
         """The frame as one CUDA graph on the current (non-default) stream."""
         st = kv.state(hidden.shape[0], self.steps + 1)
         g = C.c_void_p()
         L.call("tts_predictor_graph_capture", self.handle, C.byref(st), ptr(hidden),
-               ptr(code0_embed), ptr(codes), ptr(total), stream(), C.byref(g))
-        return Graph(g, [kv, hidden, code0_embed, codes, total])
+               ptr(code0_embed), _feed(text), ptr(codes), ptr(total), stream(), C.byref(g))
+        return Graph(g, [kv, hidden, code0_embed, codes, total, text])
 
     def weight_bytes(self) -> int:
         """Bytes a frame streams from HBM for weights: the stack and one head per depth step

@@ -132,6 +132,34 @@ class PagedKv:
                              self.k.data_ptr(), self.v.data_ptr(), ms)
 
 
+class PickState:
+    """The talker's greedy pick rule on the device (talker.rs:154-189, 940, 971-981): `banned`
+    ids never picked, `eos` banned while a lane has fewer than `min_new` frames, and logits of
+    ids a lane has emitted divided (positive) or multiplied (negative) by `penalty`. The seen
+    bits int32 [lanes, vocab / 32] and frame counts int32 [lanes] live on the device and are
+    updated by every step; `reset(lane)` clears a lane slot for a new segment."""
+
+    def __init__(self, vocab: int, lanes: int, banned, eos: int = -1, min_new: int = 0,
+                 penalty: float = 1.0, device: torch.device | str = "cuda"):
+        import numpy as np
+        if vocab % 32:
+            raise ValueError("vocab must be a multiple of 32")
+        words = vocab // 32
+        bits = np.zeros(words, np.uint32)
+        for i in banned:
+            bits[int(i) >> 5] |= np.uint32(1 << (int(i) & 31))
+        self.vocab, self.eos, self.min_new, self.penalty = vocab, eos, min_new, penalty
+        self.ban = torch.from_numpy(bits.view(np.int32)).to(device)
+        self.seen = torch.zeros(lanes, words, dtype=torch.int32, device=device)
+        self.frames = torch.zeros(lanes, dtype=torch.int32, device=device)
+        self.c = L.PickRule(self.ban.data_ptr(), self.seen.data_ptr(), self.frames.data_ptr(),
+                            float(penalty), int(eos), int(min_new))
+
+    def reset(self, lane: int) -> None:
+        self.seen[lane].zero_()
+        self.frames[lane] = 0
+
+
 class Graph:
     """A captured decode step, replayed with `replay()` (one tts_graph_launch)."""
 
@@ -176,6 +204,11 @@ class Stack:
                                lt.w_gate_up.data_ptr(), lt.w_down.data_ptr())
             L.call("tts_stack_set_layer", h, i, C.byref(w))
         L.call("tts_stack_set_head", h, ptr(self.final_norm), ptr(self.heads), ptr(self.embed))
+
+    def set_pick(self, pick: "PickState | None") -> None:
+        """Use the talker's pick rule for the codec head (one codebook); None: plain argmax."""
+        self._pick = pick
+        L.call("tts_stack_set_pick", self.handle, None if pick is None else C.byref(pick.c))
 
     def set_feedback(self, x_next: torch.Tensor | None) -> None:
         """Use `x_next` ([lanes, dim] f32, caller-owned) as the step's feedback input buffer."""

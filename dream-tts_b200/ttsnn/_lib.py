@@ -54,6 +54,16 @@ class PredictorWeights(C.Structure):
                 ("embed_dim", C.c_int)]
 
 
+class PickRule(C.Structure):
+    _fields_ = [("ban", C.c_void_p), ("seen", C.c_void_p), ("frames", C.c_void_p),
+                ("penalty", C.c_float), ("eos", C.c_int), ("min_new", C.c_int)]
+
+
+class TextFeed(C.Structure):
+    _fields_ = [("rows", C.c_void_p), ("len", C.c_int), ("pad", C.c_void_p),
+                ("frames", C.c_void_p)]
+
+
 P = C.c_void_p
 I = C.c_int
 L = C.c_long
@@ -90,8 +100,14 @@ SIGNATURES = {
     "tts_graph_destroy": [P],
     "tts_predictor_create": [P, C.POINTER(PredictorWeights), C.POINTER(P)],
     "tts_predictor_destroy": [P],
-    "tts_predictor_frame": [P, C.POINTER(DecodeState), P, P, P, P, P],
-    "tts_predictor_graph_capture": [P, C.POINTER(DecodeState), P, P, P, P, P, C.POINTER(P)],
+    "tts_predictor_frame": [P, C.POINTER(DecodeState), P, P, C.POINTER(TextFeed), P, P, P],
+    "tts_predictor_graph_capture": [P, C.POINTER(DecodeState), P, P, C.POINTER(TextFeed), P, P,
+                                    P, C.POINTER(P)],
+    "tts_stack_set_pick": [P, C.POINTER(PickRule)],
+    "tts_talker_frame": [P, C.POINTER(DecodeState), P, C.POINTER(DecodeState),
+                         C.POINTER(TextFeed), P, P, P, P],
+    "tts_talker_frame_capture": [P, C.POINTER(DecodeState), P, C.POINTER(DecodeState),
+                                 C.POINTER(TextFeed), P, P, P, P, C.POINTER(P)],
 }
 _RESTYPE = {"tts_last_error": C.c_char_p, "tts_launch_count": C.c_longlong}
 

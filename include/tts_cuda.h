@@ -228,6 +228,23 @@ TTS_API tts_status tts_stack_set_head(tts_stack* s, const float* final_norm, con
  * buffer. Writing a lane's row restarts that lane from a new state (a lane slot reused by the
  * next segment). */
 TTS_API tts_status tts_stack_set_feedback(tts_stack* s, float* x_next);
+
+/* The talker's greedy pick over its codec head (crates/qwen3tts/src/talker.rs:154-189, 940,
+ * 971-981), for a stack with one codebook head: ids whose bit is set in `ban` are never picked,
+ * nor `eos` while the lane's frames < min_new; ids set in the lane's `seen` bits have their
+ * logit divided (if positive) or multiplied (if negative) by `penalty` first. Each step marks
+ * its pick in `seen` (unless it is eos) and adds one to the lane's `frames`. All device
+ * memory, caller-owned; a lane slot reused for a new segment is cleared by the caller. NULL
+ * restores the plain argmax. */
+typedef struct tts_pick_rule {
+  const unsigned int* ban; /* [vocab / 32] bits, or NULL */
+  unsigned int* seen;      /* [max_lanes][vocab / 32] bits, or NULL (needs penalty == 1) */
+  int* frames;             /* [max_lanes], or NULL (needs min_new == 0 or eos < 0) */
+  float penalty;           /* repetition penalty, 1 = none */
+  int eos;                 /* the end id (-1: none) */
+  int min_new;             /* frames before eos may be picked */
+} tts_pick_rule;
+TTS_API tts_status tts_stack_set_pick(tts_stack* s, const tts_pick_rule* rule);
 TTS_API tts_status tts_stack_destroy(tts_stack* s);
 
 /* Decode-time cache state of one group of lanes, all layers: pages f16
@@ -294,15 +311,41 @@ TTS_API tts_status tts_predictor_destroy(tts_predictor* p);
  * before the next pick, the stack on resized[i][code]. st: the predictor's own KV pages, room for
  * steps + 1 positions per lane (positions are reset by the call; max_span >= steps + 1).
  * hidden, code0_embed f32 [lanes][embed_dim]; codes u32 [lanes][steps]; sum f32
- * [lanes][embed_dim] = code0_embed + the picked codes' table rows. */
+ * [lanes][embed_dim] = code0_embed + the picked codes' table rows (+ the lane's text row, when
+ * `text` is given: the talker's next input, talker.rs:1043-1050). sum may be code0_embed. */
+typedef struct tts_text_feed {
+  const float* rows;  /* f32 [lanes][len][embed_dim]: each lane's trailing text embeddings */
+  int len;            /* rows per lane */
+  const float* pad;   /* f32 [embed_dim]: the tts_pad embedding, once a lane's rows run out */
+  const int* frames;  /* device [lanes]: frames picked so far, this one included; the lane
+                       * adds row frames - 1 (the pick rule's counter) */
+} tts_text_feed;
 TTS_API tts_status tts_predictor_frame(tts_predictor* p, const tts_decode_state* st,
                                        const float* hidden, const float* code0_embed,
-                                       unsigned int* codes, float* sum, void* stream);
+                                       const tts_text_feed* text, unsigned int* codes,
+                                       float* sum, void* stream);
 /* The same frame captured into one CUDA graph (non-legacy stream); pointers baked in. */
 TTS_API tts_status tts_predictor_graph_capture(tts_predictor* p, const tts_decode_state* st,
                                                const float* hidden, const float* code0_embed,
-                                               unsigned int* codes, float* sum, void* stream,
-                                               tts_graph** out);
+                                               const tts_text_feed* text, unsigned int* codes,
+                                               float* sum, void* stream, tts_graph** out);
+
+/* One reference-faithful talker frame for st->lanes lanes (talker.rs:953-1057, greedy): the
+ * talker stack's decode step from its feedback input with the codec head and its pick rule
+ * (code 0, its codec_embed row as the feedback), then the predictor's frame on the step's
+ * hidden state and that row, whose sum plus the lane's text row becomes the next feedback
+ * input. `talker` needs one codebook head, an embedding table and a caller-owned feedback
+ * buffer (tts_stack_set_feedback); hidden f32 [max_lanes][talker dim] scratch; code0 u32
+ * [lanes]; codes u32 [lanes][steps] the residual codes. */
+TTS_API tts_status tts_talker_frame(tts_stack* talker, const tts_decode_state* talker_st,
+                                    tts_predictor* p, const tts_decode_state* pred_st,
+                                    const tts_text_feed* text, float* hidden,
+                                    unsigned int* code0, unsigned int* codes, void* stream);
+TTS_API tts_status tts_talker_frame_capture(tts_stack* talker, const tts_decode_state* talker_st,
+                                            tts_predictor* p, const tts_decode_state* pred_st,
+                                            const tts_text_feed* text, float* hidden,
+                                            unsigned int* code0, unsigned int* codes,
+                                            void* stream, tts_graph** out);
 
 /* Kernel launches made by the calling thread through this library since the last call
  * (observability: the bench reports it). */

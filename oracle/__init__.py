@@ -375,3 +375,82 @@ def predictor_frame(hidden: np.ndarray, code0_embed: np.ndarray, layers: list[La
     for r in rows:
         acc = acc + r
     return codes, np.asarray(code0_embed, np.float32) + acc, ties, mismatches
+
+
+# ---------------------------------------------------------------- the talker's frame
+def talker_pick(logits: np.ndarray, banned, seen: list[set], frames: np.ndarray, eos: int,
+                min_new: int, penalty: float, forced: np.ndarray | None = None,
+                tie_tol: float = 0.0):
+    """sample_with_u with greedy on (crates/qwen3tts/src/talker.rs:154-189) for each row: banned
+    ids (and eos while the row has fewer than `min_new` frames, :971-981) to -inf, then each
+    seen id's finite logit divided (positive) or multiplied (negative) by `penalty`, then the
+    last of equal maxima. `forced` picks within `tie_tol` of the row's maximum are followed
+    (near-ties resolved the other way by a different accumulation order). Returns
+    (picks, ties, mismatches)."""
+    b, n = logits.shape
+    picks = np.zeros(b, np.uint32)
+    ties = mismatches = 0
+    for r in range(b):
+        l = logits[r].astype(np.float32).copy()
+        for i in banned:
+            l[i] = -np.inf
+        if frames[r] < min_new and 0 <= eos < n:
+            l[eos] = -np.inf
+        if penalty != 1.0:
+            for i in seen[r]:
+                if np.isfinite(l[i]):
+                    l[i] = np.float32(l[i] / np.float32(penalty)) if l[i] > 0 else np.float32(l[i] * np.float32(penalty))
+        best = int(np.flatnonzero(l == l.max())[-1])
+        if forced is not None and int(forced[r]) != best:
+            f = int(forced[r])
+            if 0 <= f < n and np.isfinite(l[f]) and l[f] >= l[best] - tie_tol:
+                best = f
+                ties += 1
+            else:
+                mismatches += 1
+        picks[r] = best
+    return picks, ties, mismatches
+
+
+@dataclass
+class TalkerState:
+    """One group's talker-side state: per-layer caches [b, n_kv, cap, hd] f16 bits, positions,
+    the pick rule's seen ids and frame counts, and the next input rows."""
+    kc: list
+    vc: list
+    pos: np.ndarray
+    seen: list
+    frames: np.ndarray
+    x: np.ndarray
+
+
+def talker_frame(st: TalkerState, layers: list[Layer], final_norm: np.ndarray, g: Geometry,
+                 codec_head: np.ndarray, codec_embed: np.ndarray, banned, eos: int,
+                 min_new: int, penalty: float, p_layers: list[Layer], p_final: np.ndarray,
+                 pw: PredictorWeights, pg: Geometry, text_rows: np.ndarray, pad: np.ndarray,
+                 forced0=None, forced=None, tie_tol: float = 0.0):
+    """One iteration of Talker::generate_batch with greedy picks (talker.rs:953-1057), started
+    from the step that feeds the talker stack: Stack::forward on `st.x` at each lane's
+    position, codec head, pick, code 0's codec_embed row, the predictor's frame on the hidden
+    state and that row, then the sum plus the lane's text row (trailing row frames - 1, else the
+    pad row) as the next input. Updates `st`; returns (code0, codes, ties, mismatches)."""
+    cap = st.kc[0].shape[2]
+    cos, sin = rope_table(cap + 1, g.head_dim, g.rope_base)
+    h = decode_step(st.x, layers, final_norm, st.kc, st.vc, st.pos, cos, sin, g)
+    st.pos = st.pos + 1
+    logits = proj(h, codec_head)
+    code0, t0, m0 = talker_pick(logits, banned, st.seen, st.frames, eos, min_new, penalty,
+                                forced0, tie_tol)
+    for r, c in enumerate(code0):
+        if int(c) != eos:
+            st.seen[r].add(int(c))
+    st.frames = st.frames + 1
+    code0_embed = f16_value(codec_embed[code0.astype(np.int64)])
+    codes, total, t1, m1 = predictor_frame(h, code0_embed, p_layers, p_final, pw, pg, forced,
+                                           tie_tol)
+    length = text_rows.shape[1]
+    for r in range(total.shape[0]):
+        t = int(st.frames[r]) - 1
+        total[r] = total[r] + (text_rows[r, t] if 0 <= t < length else pad)
+    st.x = total
+    return code0, codes, t0 + t1, m0 + m1

@@ -1,0 +1,129 @@
+"""Talker::generate_batch's loop body, greedy (crates/qwen3tts/src/talker.rs:903-1073), on a
+B200 against the CPU oracle's composition: per frame the talker step with its codec head under
+the pick rule (banned top ids except eos, eos held back for the first frames, repetition
+penalty), code 0's codec_embed row, the depth predictor's residual codes and the next input
+(their embedding sum plus the lane's text row). Several frames in a row, so the pick rule's
+history (seen ids, frame counts) and the text rows are exercised. Bar: every pick equal to the
+oracle's except near-ties (followed by the oracle), and the next input equal for equal picks."""
+import numpy as np
+import pytest
+import torch
+
+from _model import dev_f16, dev_f32, device_predictor, device_stack, make_predictor, make_talker
+
+pytestmark = pytest.mark.gpu
+
+LANES, CAP, BS = 5, 64, 32
+VOCAB, EOS, MIN_NEW, PENALTY = 384, 300, 2, 1.05
+BANNED = [i for i in range(256, 384) if i != EOS]
+
+
+def rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def build(orc, seed):
+    lengths = np.array([3, 9, 20, 31, 40], np.int32)  # cached positions before the first step
+    g, Ls, final, kc, vc, pos, x = make_talker(orc, LANES, 2, 256, 4, 2, 512, CAP, seed,
+                                               codebooks=1, vocab=VOCAB, lengths=lengths)
+    rng = np.random.default_rng(seed + 1)
+    head = rng.standard_normal((VOCAB, g.dim), dtype=np.float32) * 0.02
+    # near-equal rows so the penalty decides between them, eos competitive once allowed, a
+    # banned row that would win if it were not banned
+    head[10] *= 4.0
+    head[11] = head[10] * 1.02
+    head[EOS] = head[10] * 1.04
+    head[290] = head[10] * 2.0
+    head = orc.f16_bits(head)
+    embed = orc.f16_bits(rng.standard_normal((VOCAB, g.dim), dtype=np.float32) * 0.02)
+    for L_ in (kc, vc):
+        for a in L_:
+            for b in range(LANES):
+                a[b, :, lengths[b]:] = 0
+    pg, pLs, pfinal, pw, _, _ = make_predictor(orc, LANES, 256, 1, 4, 2, 512, 128, 3, g.dim,
+                                               seed + 2)
+    text = rng.standard_normal((LANES, 3, g.dim), dtype=np.float32) * 0.1
+    pad = rng.standard_normal(g.dim, dtype=np.float32) * 0.1
+    return dict(g=g, Ls=Ls, final=final, kc=kc, vc=vc, lengths=lengths, x=x, head=head,
+                embed=embed, pg=pg, pLs=pLs, pfinal=pfinal, pw=pw, text=text, pad=pad)
+
+
+def device_loop(orc, m):
+    from qwen3tts import FrameLoop, PickState
+    g = m["g"]
+    talker = device_stack(orc, g, m["Ls"], m["final"], m["head"], m["embed"][None])
+    pred = device_predictor(orc, m["pg"], m["pLs"], m["pfinal"], m["pw"])
+    pick = PickState(VOCAB, LANES, BANNED, EOS, MIN_NEW, PENALTY)
+    loop = FrameLoop(talker, pred, LANES, CAP, pick, dev_f32(m["text"]), dev_f32(m["pad"]),
+                     block_size=BS)
+    for b in range(LANES):
+        loop.admit(b, int(m["lengths"][b]) + 1, CAP - int(m["lengths"][b]) - 2,
+                   dev_f32(m["x"][b]))
+    # the prompt's K/V: the oracle's caches scattered into the lanes' pages
+    table = loop.kv.table.cpu().numpy()
+    for li in range(g.layers):
+        for src, pool in ((m["kc"][li], loop.kv.k), (m["vc"][li], loop.kv.v)):
+            for b in range(LANES):
+                for p in range(CAP // BS):
+                    pool[li][int(table[b, p])] = dev_f16(
+                        np.ascontiguousarray(src[b, :, p * BS:(p + 1) * BS]))
+    torch.cuda.synchronize()
+    return loop, talker, pred
+
+
+def oracle_state(orc, m):
+    return orc.TalkerState(kc=[a.copy() for a in m["kc"]], vc=[a.copy() for a in m["vc"]],
+                           pos=m["lengths"].copy(), seen=[set() for _ in range(LANES)],
+                           frames=np.zeros(LANES, np.int64), x=m["x"].copy())
+
+
+def test_frame_loop_matches_oracle(tt, orc):
+    m = build(orc, 41)
+    loop, talker, pred = device_loop(orc, m)
+    st = oracle_state(orc, m)
+    ties = 0
+    picked = set()
+    for f in range(6):
+        loop.frame(LANES)
+        torch.cuda.synchronize()
+        tt.check()
+        c0 = loop.code0.cpu().numpy().astype(np.uint32)
+        codes = loop.codes.cpu().numpy().astype(np.uint32)
+        want0, want, t, mism = orc.talker_frame(
+            st, m["Ls"], m["final"], m["g"], m["head"], m["embed"], BANNED, EOS, MIN_NEW,
+            PENALTY, m["pLs"], m["pfinal"], m["pw"], m["pg"], m["text"], m["pad"],
+            forced0=c0, forced=codes, tie_tol=2e-3)
+        assert mism == 0, (f, c0, want0, codes, want)
+        ties += t
+        assert np.array_equal(want0, c0) and np.array_equal(want, codes)
+        assert not any(int(c) in BANNED for c in c0)
+        if f < MIN_NEW:
+            assert EOS not in c0.tolist()
+        picked.update(c0.tolist())
+        assert rel(loop.feedback.cpu().numpy(), st.x) < 1e-6
+        assert loop.pick.frames.cpu().tolist() == [f + 1] * LANES
+    assert ties <= 3
+    assert loop.kv.positions.cpu().numpy().tolist() == (m["lengths"] + 6).tolist()
+
+
+def test_frame_loop_graph_matches_eager(tt, orc):
+    m = build(orc, 42)
+    a, _, _ = device_loop(orc, m)
+    b, _, _ = device_loop(orc, m)
+    s = torch.cuda.Stream()
+    outs = []
+    for f in range(3):
+        a.frame(LANES)
+        outs.append((a.code0.clone(), a.codes.clone(), a.feedback.clone()))
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        g = b.graph(LANES)
+        for f in range(3):
+            g.replay()
+            s.synchronize()
+            c0, codes, fb = outs[f]
+            assert torch.equal(b.code0, c0) and torch.equal(b.codes, codes)
+            assert torch.equal(b.feedback, fb)
+    tt.check()

@@ -302,3 +302,23 @@ def test_predictor_forced_ties(orc):
     got, _, ties, mism = orc.predictor_frame(hidden, code0, layers, final, pw, g, forced=wrong,
                                              tie_tol=1e9)
     assert got[0, 0] == wrong[0, 0] and ties >= 1
+
+
+def test_talker_pick_rule(orc):
+    """sample_with_u greedy (talker.rs:154-189): banned ids never win, eos waits for min_new
+    frames, the penalty divides positive and multiplies negative logits of seen ids, and the
+    last of equal maxima wins."""
+    logits = np.array([[1.0, 3.0, 2.9, 5.0, 4.0],
+                       [1.0, 3.0, 2.9, 5.0, 4.0],
+                       [-1.0, -2.0, -1.02, -9.0, -9.0],
+                       [2.0, 2.0, 1.0, 0.0, 2.0]], np.float32)
+    banned = [3]
+    seen = [set(), {4}, {0}, set()]
+    frames = np.array([0, 5, 5, 5])
+    picks, _, _ = orc.talker_pick(logits, banned, seen, frames, eos=4, min_new=2, penalty=1.05)
+    # row 0: 3 banned, eos (4) too young -> 1; row 1: eos old enough but seen: 4/1.05 = 3.81 > 3
+    # -> 4; row 2: -1 * 1.05 = -1.05 < -1.02 -> 2; row 3: tie of 2.0 at ids 0, 1, 4 -> 4
+    assert picks.tolist() == [1, 4, 2, 4]
+    forced = np.array([2, 4, 2, 0], np.uint32)
+    p2, ties, mism = orc.talker_pick(logits, banned, seen, frames, 4, 2, 1.05, forced, 0.2)
+    assert p2.tolist() == [2, 4, 2, 0] and ties == 2 and mism == 0
