@@ -84,6 +84,11 @@ struct tts_predictor {
   int* table2 = nullptr;         // [2 max_lanes][kPredictorMaxBlocks]
   int* pos2 = nullptr;           // [2 max_lanes]
   unsigned* step_codes = nullptr;  // [steps][2 max_lanes]
+  // top-k sampling of the depth picks (draws [steps][draw_stride]); null draws: greedy
+  const float* draws = nullptr;
+  int draw_stride = 0, top_k = 0;
+  float temperature = 1.f;
+  float* logits = nullptr;  // [2 max_lanes][vocab]
 };
 
 struct tts_graph {
@@ -503,6 +508,19 @@ tts_status tts_conv1d_nlc(tts_ctx* c, const void* x, int b, int len, int cin, co
   return counted(launch_conv(r, S(stream), c->device, c->gemm.err), "conv1d");
 }
 
+tts_status tts_topk_sample(tts_ctx* c, const float* logits, int rows, int n, const float* draws,
+                           int k, float temperature, unsigned int* out, void* stream) {
+  if (!c || !logits || !draws || !out) return fail(TTS_ERR_INVALID_ARG, "topk_sample: NULL argument");
+  if (rows < 1) return fail(TTS_ERR_INVALID_ARG, "topk_sample: rows must be >= 1");
+  if (k < 1 || k > kTopkMaxK || k > n || n > kTopkMaxN)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "topk_sample: k=" + std::to_string(k) + " n=" +
+                                               std::to_string(n) + " outside the kernel's limits");
+  DeviceGuard g(c->device);
+  return counted(launch_topk_sample(logits, rows, n, n, draws, rows, k, temperature, out, 1,
+                                    nullptr, nullptr, 0, nullptr, false, S(stream)),
+                 "topk_sample");
+}
+
 // ---------------------------------------------------------------- stack
 
 tts_status tts_stack_create(tts_ctx* c, const tts_stack_geometry* geo, tts_stack** out) {
@@ -650,6 +668,12 @@ struct HeadSel {
   const float* embed32 = nullptr;
   bool in_h = false;
   bool feed_h = false;
+  // top-k sampling in place of the greedy pick: the heads write `logits` [rows][vocab] and
+  // row r draws draws[r % draw_rows]
+  const float* draws = nullptr;
+  int draw_rows = 0, top_k = 0;
+  float temperature = 1.f;
+  float* logits = nullptr;
 };
 
 static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const float* x,
@@ -780,6 +804,11 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     hd.argmax_keys = s->keys;
     hd.vocab = gm.vocab;
     if (!hsel) hd.pick = s->pick;
+    if (hsel && hsel->draws) {
+      hd.epi = EPI_F32;
+      hd.y = hsel->logits;
+      hd.argmax_keys = nullptr;
+    }
     return hd;
   };
   auto req_attn = [&](int l) {
@@ -812,7 +841,8 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
   // more per projection than a kernel boundary under programmatic dependent launch), so the
   // separate kernels are the default.
   const char* chain_env = getenv("TTS_CHAIN");
-  const bool use_chain = B <= s->chain_lanes && chain_env && *chain_env == '1';
+  const bool use_chain = B <= s->chain_lanes && chain_env && *chain_env == '1' &&
+                         !(hsel && hsel->draws);
   if (use_chain) {
     auto gemm_ph = [](const GemmRequest& g) {
       ChainPhaseRequest p;
@@ -895,10 +925,16 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
             "rms_norm");
     if (heads) {
       TTS_TRY(launch_gemm(req_heads(), c->gemm, cs, c->device), "proj");
-      TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, embed16, embed32, D, codes,
-                                   feed ? next : nullptr, nullptr, st->positions,
-                                   hsel ? nullptr : &s->pick, true, cs),
-              "keys_to_codes");
+      if (hsel && hsel->draws)
+        TTS_TRY(launch_topk_sample(hsel->logits, B, gm.vocab, gm.vocab, hsel->draws,
+                                   hsel->draw_rows, hsel->top_k, hsel->temperature, codes, 1,
+                                   embed32, feed ? next : nullptr, D, st->positions, true, cs),
+                "topk_sample");
+      else
+        TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, embed16, embed32, D,
+                                     codes, feed ? next : nullptr, nullptr, st->positions,
+                                     hsel ? nullptr : &s->pick, true, cs),
+                "keys_to_codes");
     }
   }
   // with heads, the code gather advanced the positions
@@ -1019,12 +1055,31 @@ tts_status tts_predictor_create(tts_stack* s, const tts_predictor_weights* w,
   if (e == cudaSuccess) e = dmalloc(&p->table2, size_t(R) * kPredictorMaxBlocks * 4);
   if (e == cudaSuccess) e = dmalloc(&p->pos2, size_t(R) * 4);
   if (e == cudaSuccess) e = dmalloc(&p->step_codes, size_t(w->steps) * R * 4);
+  if (e == cudaSuccess) e = dmalloc(&p->logits, size_t(R) * gm.vocab * 4);
   if (e == cudaSuccess) e = cudaMemset(p->step_codes, 0, size_t(w->steps) * R * 4);
   if (e != cudaSuccess) {
     tts_predictor_destroy(p);
     return cuda_status(e, "predictor_create");
   }
   *out = p;
+  return TTS_OK;
+}
+
+tts_status tts_predictor_set_sampling(tts_predictor* p, const float* draws, int stride,
+                                      int top_k, float temperature) {
+  if (!p) return fail(TTS_ERR_INVALID_ARG, "predictor_set_sampling: predictor is NULL");
+  if (!draws) {
+    p->draws = nullptr;
+    return TTS_OK;
+  }
+  if (stride < 1 || top_k < 1 || top_k > kTopkMaxK || top_k > p->s->geo.vocab ||
+      p->s->geo.vocab > kTopkMaxN)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE,
+                "predictor_set_sampling: stride >= 1, 1 <= top_k <= 64, vocab <= 4096");
+  p->draws = draws;
+  p->draw_stride = stride;
+  p->top_k = top_k;
+  p->temperature = temperature > 0.f ? temperature : 1.f;
   return TTS_OK;
 }
 
@@ -1036,6 +1091,7 @@ tts_status tts_predictor_destroy(tts_predictor* p) {
   cudaFree(p->table2);
   cudaFree(p->pos2);
   cudaFree(p->step_codes);
+  cudaFree(p->logits);
   delete p;
   return TTS_OK;
 }
@@ -1111,6 +1167,15 @@ static tts_status frame_impl(tts_predictor* p, const tts_decode_state* st, const
     hs.embed32 = i + 1 < w.steps ? w.resized + size_t(i) * V * D : nullptr;
     hs.in_h = true;
     hs.feed_h = true;
+    if (p->draws) {
+      if (B > p->draw_stride)
+        return fail(TTS_ERR_UNSUPPORTED_SHAPE, "predictor_frame: more lanes than the draws hold");
+      hs.draws = p->draws + size_t(i) * p->draw_stride;
+      hs.draw_rows = B;
+      hs.top_k = p->top_k;
+      hs.temperature = p->temperature;
+      hs.logits = p->logits;
+    }
     rc = step_impl(s, i == 0 ? &pre : st, nullptr, nullptr, nullptr,
                    p->step_codes + size_t(i) * stride, cs, &hs);
     if (rc != TTS_OK) return rc;

@@ -220,6 +220,15 @@ cudaError_t launch_predictor_finish(const uint32_t* step_codes, int stride, int 
                                     const float* code0, uint32_t* codes, float* sum,
                                     const TextFeed& text, cudaStream_t st);
 cudaError_t launch_advance_positions(int* positions, int lanes, bool pdl, cudaStream_t st);
+// Top-k sampling (topk_sample.cu): rows of logits (row stride ldl), a draw per row (row r
+// takes draws[r % draw_rows]), codes[r * code_stride]; optionally the pick's f32 embedding row
+// into x_next and the row's position advanced (a decode step's code gather).
+constexpr int kTopkMaxN = 4096;
+constexpr int kTopkMaxK = 64;
+cudaError_t launch_topk_sample(const float* logits, int rows, int n, int ldl, const float* draws,
+                               int draw_rows, int k, float temperature, uint32_t* codes,
+                               int code_stride, const float* embed32, float* x_next, int dim,
+                               int* positions, bool pdl, cudaStream_t st);
 cudaError_t launch_cast_f32_f16(const float* x, __half* y, long n, cudaStream_t st);
 
 // ------------------------------------------------------------------ codec conv

@@ -87,6 +87,21 @@ class Predictor:
         L.call("tts_predictor_create", stack.handle, C.byref(w), C.byref(h))
         self.handle = h
 
+    def set_sampling(self, draws: torch.Tensor | None, top_k: int = 50,
+                     temperature: float = 0.9) -> None:
+        """Top-k sampling of the depth picks with draws f32 [steps, lanes] (refilled by the
+        caller before each frame; step-major as the reference draws them), or greedy (None).
+        The defaults are the reference's sub-talker settings (cfg.rs: top_k 50, temperature
+        0.9, top_p 1)."""
+        self._draws = draws
+        if draws is None:
+            L.call("tts_predictor_set_sampling", self.handle, None, 0, 0, 0.0)
+            return
+        if draws.dtype != torch.float32 or not draws.is_contiguous() or draws.shape[0] != self.steps:
+            raise ValueError("draws must be contiguous f32 [steps, lanes]")
+        L.call("tts_predictor_set_sampling", self.handle, ptr(draws), draws.shape[1], int(top_k),
+               float(temperature))
+
     def new_state(self, lanes: int, block_size: int = 16) -> PagedKv:
         """KV pages for `lanes` lanes of one frame: steps + 1 positions each, one page per lane
         (the reference's `new_state(b)` with capacity CODE_GROUPS + 2, talker.rs:291-298)."""

@@ -1,5 +1,5 @@
-"""Device-side code picking (crates/tts-nn/src/topk.rs; greedy path of
-crates/qwen3tts/src/talker.rs:154-189)."""
+"""Device-side code picking: greedy (crates/qwen3tts/src/talker.rs:154-189) and top-k sampling
+with caller-supplied draws (crates/tts-nn/src/topk.rs)."""
 from __future__ import annotations
 
 import torch
@@ -20,4 +20,22 @@ def argmax(logits: torch.Tensor, banned: torch.Tensor | None = None) -> torch.Te
         if b.numel() != n:
             raise ValueError("argmax: banned mask must cover every id")
     L.call("tts_argmax", ctx_of(x), ptr(x), rows, n, ptr(b), ptr(out), stream())
+    return out
+
+
+MAX_N = 4096
+MAX_K = 64
+
+
+def sample(logits: torch.Tensor, draws: torch.Tensor, k: int, temperature: float) -> torch.Tensor:
+    """One index per row of `logits` `[rows, n]` drawn from its top `k` at `temperature` with
+    `draws[row]` in `[0, 1)` (crates/tts-nn/src/topk.rs:98-107): no nucleus cut, no penalty."""
+    x = logits.to(torch.float32).contiguous()
+    rows, n = x.shape
+    d = draws.to(torch.float32).contiguous()
+    if d.numel() != rows:
+        raise L.TtsError(1, f"topk_sample: {d.numel()} draws for {rows} rows")
+    out = torch.empty(rows, dtype=torch.int32, device=x.device)
+    L.call("tts_topk_sample", ctx_of(x), ptr(x), rows, n, ptr(d), int(k), float(temperature),
+           ptr(out), stream())
     return out

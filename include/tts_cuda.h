@@ -193,6 +193,14 @@ TTS_API tts_status tts_conv1d_nlc(tts_ctx* ctx, const void* x_f16, int b, int le
                           const float* bias, const float* alpha, const float* brecip,
                           const void* res_f16, void* y_f16, void* stream);
 
+/* Top-k sampling per row (crates/tts-nn/src/topk.rs:98-107): logits f32 [rows][n], draws f32
+ * [rows] in [0, 1); out u32 [rows] = the row's pick among its k best (ties by lowest index) at
+ * `temperature` (<= 0 means 1), walked with the draw as the reference's host sampler does at
+ * top_p = 1. Limits as the reference's: 1 <= k <= min(n, 64), n <= 4096. */
+TTS_API tts_status tts_topk_sample(tts_ctx* ctx, const float* logits, int rows, int n,
+                                   const float* draws, int k, float temperature,
+                                   unsigned int* out, void* stream);
+
 /* ---------------------------------------------------------------- decoder stack
  * The qwen3 decoder stack (crates/qwen3tts/src/qwen3.rs:15-467): geometry, per-layer weights
  * (caller-owned device memory, referenced not copied) and the decode step at t == 1. */
@@ -304,6 +312,14 @@ typedef struct tts_predictor tts_predictor;
 TTS_API tts_status tts_predictor_create(tts_stack* stack, const tts_predictor_weights* w,
                                         tts_predictor** out);
 TTS_API tts_status tts_predictor_destroy(tts_predictor* p);
+
+/* Samples the depth picks on the device (Predictor::depth_on_device, talker.rs:478-515;
+ * tts_topk_sample's rule) instead of the greedy pick: draws f32 [steps][stride] in [0, 1), the
+ * frame's lane i at step j taking draws[j * stride + i] (the reference's step-major order over
+ * lanes); the caller refills it before each frame. NULL draws restores greedy. Pointers are
+ * baked into captured graphs. */
+TTS_API tts_status tts_predictor_set_sampling(tts_predictor* p, const float* draws, int stride,
+                                              int top_k, float temperature);
 
 /* One frame for st->lanes lanes with greedy picks (Predictor::frame_batch, talker.rs:407-468,
  * and gather_sum, talker.rs:528-550): prefill [hidden, code0_embed] through the projection and

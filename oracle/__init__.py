@@ -327,9 +327,25 @@ def synthetic_predictor(rng: np.random.Generator, g: Geometry, steps: int,
     return PredictorWeights(resize, bias, heads, tables, resize_tables(tables, resize, bias))
 
 
+def topk_interval(logits: np.ndarray, k: int, temperature: float, pick: int):
+    """Where `pick` sits in the host sampler's walk over one row: (lo, hi) of the scaled draw
+    u * renorm that selects it, or None when it is not among the k best."""
+    t = np.float32(temperature if temperature > 0 else 1.0)
+    l = np.asarray(logits, np.float32)
+    order = sorted(range(l.shape[0]), key=lambda i: (-float(l[i]), i))[:k]
+    if pick not in order:
+        return None
+    p = np.exp((l[order].astype(np.float64) - float(l[order[0]])) / float(t))
+    c = np.concatenate([[0.0], np.cumsum(p / p.sum())])
+    j = order.index(pick)
+    return c[j], c[j + 1]
+
+
 def predictor_frame(hidden: np.ndarray, code0_embed: np.ndarray, layers: list[Layer],
                     final_norm: np.ndarray, pw: PredictorWeights, g: Geometry,
-                    forced: np.ndarray | None = None, tie_tol: float = 0.0):
+                    forced: np.ndarray | None = None, tie_tol: float = 0.0,
+                    draws: np.ndarray | None = None, top_k: int = 50,
+                    temperature: float = 0.9, logit_tol: float = 0.0):
     """Predictor::frame_batch with greedy picks (talker.rs:407-468) and gather_sum (:528-550).
 
     hidden, code0_embed f32 [b, embed_dim]. The two-position prefill (talker.rs:416-420) is run
@@ -340,7 +356,13 @@ def predictor_frame(hidden: np.ndarray, code0_embed: np.ndarray, layers: list[La
     `forced` (u32 [b, steps], e.g. the device's picks) is followed wherever its logit is within
     `tie_tol` of the maximum: a near-tie resolved the other way by a different but equally valid
     accumulation order, which the chain then continues from. Picks outside that band count in
-    `mismatches` and the oracle keeps its own."""
+    `mismatches` and the oracle keeps its own.
+
+    With `draws` (f32 [steps, b]) the picks are the host sampler's top-k draws instead
+    (depth_on_device, talker.rs:478-515); a forced pick is then followed when the scaled draw
+    lies within `tie_tol` of its interval of the walk, or when its logit is within `logit_tol`
+    of the oracle pick's (two near-equal candidates whose order in the walk, and so whose
+    intervals, another accumulation order swaps)."""
     b = hidden.shape[0]
     steps = pw.steps
     cap = steps + 2
@@ -355,13 +377,23 @@ def predictor_frame(hidden: np.ndarray, code0_embed: np.ndarray, layers: list[La
     ties = mismatches = 0
     for i in range(steps):
         logits = proj(h, pw.heads[i * g.vocab:(i + 1) * g.vocab])
-        pick = argmax(logits)
+        pick = argmax(logits) if draws is None else topk_sample(logits, draws[i], top_k,
+                                                                 temperature)
         if forced is not None:
             for lane in range(b):
                 f = int(forced[lane, i])
                 if f == int(pick[lane]):
                     continue
-                if 0 <= f < g.vocab and logits[lane, f] >= logits[lane, pick[lane]] - tie_tol:
+                if draws is None:
+                    near = 0 <= f < g.vocab and logits[lane, f] >= logits[lane, pick[lane]] - tie_tol
+                else:
+                    iv = topk_interval(logits[lane], top_k, temperature, f)
+                    u = float(draws[i][lane])
+                    o = int(pick[lane])
+                    near = iv is not None and (iv[0] - tie_tol <= u <= iv[1] + tie_tol or
+                                               abs(float(logits[lane, f] - logits[lane, o]))
+                                               <= logit_tol)
+                if near:
                     pick[lane] = f
                     ties += 1
                 else:
@@ -454,3 +486,34 @@ def talker_frame(st: TalkerState, layers: list[Layer], final_norm: np.ndarray, g
         total[r] = total[r] + (text_rows[r, t] if 0 <= t < length else pad)
     st.x = total
     return code0, codes, t0 + t1, m0 + m1
+
+
+# ---------------------------------------------------------------- top-k sampling
+def topk_sample(logits: np.ndarray, draws: np.ndarray, k: int, temperature: float) -> np.ndarray:
+    """The host sampler at top_p = 1 and no penalty (crates/qwen3tts/src/talker.rs:189-236,
+    the form crates/tts-nn/src/topk.rs:122-142 tests the device kernel against): the k best ids
+    (value descending, index ascending on ties), p_j = exp((l_j - max) / t) in f32 normalised
+    by their sequential sum, u = draw * (sum of the normalised p), walked down in order."""
+    t = np.float32(temperature if temperature > 0 else 1.0)
+    out = np.zeros(logits.shape[0], np.uint32)
+    for r in range(logits.shape[0]):
+        l = np.asarray(logits[r], np.float32)
+        order = sorted(range(l.shape[0]), key=lambda i: (-float(l[i]), i))[:k]
+        mx = l[order[0]]
+        p = [np.float32(np.exp(np.float32((l[i] - mx) / t))) for i in order]
+        total = np.float32(0)
+        for q in p:
+            total = np.float32(total + q)
+        p = [np.float32(q / total) for q in p]
+        renorm = np.float32(0)
+        for q in p:
+            renorm = np.float32(renorm + q)
+        u = np.float32(np.float32(draws[r]) * renorm)
+        pick = order[k - 1]
+        for j, q in enumerate(p):
+            u = np.float32(u - q)
+            if u <= 0:
+                pick = order[j]
+                break
+        out[r] = pick
+    return out

@@ -285,3 +285,30 @@ def test_decode_attention_short_spans(tt, orc, bs, n_kv, gqa, window):
     assert rel(np_(got16.float()), want.reshape(lanes, -1)) < 2e-3
     with pytest.raises(tt.TtsError):
         tt.check()
+
+
+@pytest.mark.parametrize("rows,n,k,temp", [(64, 2048, 50, 0.9), (32, 3072, 64, 1.3),
+                                           (16, 4096, 1, 0.9), (40, 100, 7, 0.0)])
+def test_topk_sample(tt, orc, rows, n, k, temp):
+    """tts_topk_sample against the host sampler's restatement on the same logits and draws:
+    equal picks, ties (logits quantised to a few levels) broken by the lower index."""
+    rng = np.random.default_rng(n + k)
+    logits = rng.standard_normal((rows, n)).astype(np.float32) * 2
+    logits[: rows // 2] = np.round(logits[: rows // 2] * 2) / 2  # many exact ties
+    draws = rng.random(rows).astype(np.float32)
+    draws[0] = 0.0
+    draws[1] = 0.99999
+    got = tt.topk.sample(dev_f32(logits), dev_f32(draws), k, temp)
+    want = orc.topk_sample(logits, draws, k, temp)
+    assert np.array_equal(np_(got).astype(np.uint32), want)
+    tt.check()
+
+
+def test_topk_sample_limits(tt):
+    x = torch.zeros(2, 5000, device="cuda")
+    d = torch.zeros(2, device="cuda")
+    with pytest.raises(tt.TtsError) as e:
+        tt.topk.sample(x, d, 10, 1.0)
+    assert e.value.status == 2
+    with pytest.raises(tt.TtsError):
+        tt.topk.sample(x[:, :100], d, 65, 1.0)

@@ -132,3 +132,38 @@ def test_predictor_paged_and_rejects_bad_shapes(tt, orc):
     with pytest.raises(_lib.TtsError) as e:
         p.frame(kv, many, many)
     assert e.value.status == 2
+
+
+def test_predictor_top_k_sampling(tt, orc):
+    """depth_on_device (talker.rs:478-515): the 15 picks drawn from each head's top 50 at
+    temperature 0.9 with the caller's draws [steps, lanes]; against the oracle's host sampler
+    on the same draws. The oracle follows a differing pick when the draw lies within 1e-4 of
+    its interval's edge or when its logit is within 2e-3 of the oracle pick's (two near-equal
+    candidates swapped in the walk's order); at most 5% of the picks."""
+    lanes = 8
+    g, Ls, final, pw, hidden, code0 = make_predictor(orc, lanes, 1024, 5, 16, 8, 3072, 2048, 15,
+                                                     2048, seed=36)
+    p = device_predictor(orc, g, Ls, final, pw)
+    kv = p.new_state(lanes)
+    draws = np.random.default_rng(37).random((15, lanes)).astype(np.float32)
+    d = dev_f32(draws)
+    p.set_sampling(d, 50, 0.9)
+    codes, total = p.frame(kv, dev_f32(hidden), dev_f32(code0))
+    torch.cuda.synchronize()
+    tt.check()
+    got = codes.cpu().numpy().astype(np.uint32)
+    want, want_sum, ties, mism = orc.predictor_frame(hidden, code0, Ls, final, pw, g, forced=got,
+                                                     tie_tol=1e-4, draws=draws, top_k=50,
+                                                     temperature=0.9, logit_tol=2e-3)
+    assert mism == 0, (got, want)
+    assert ties <= 6
+    assert rel(total.cpu().numpy(), want_sum) < 1e-6
+    greedy, _ = orc.predictor_frame(hidden, code0, Ls, final, pw, g)[:2]
+    assert not np.array_equal(got, greedy)  # sampling, not the argmax
+    # back to greedy
+    p.set_sampling(None)
+    codes2, _ = p.frame(kv, dev_f32(hidden), dev_f32(code0))
+    torch.cuda.synchronize()
+    g2 = codes2.cpu().numpy().astype(np.uint32)
+    _, _, _, mism2 = orc.predictor_frame(hidden, code0, Ls, final, pw, g, forced=g2, tie_tol=2e-3)
+    assert mism2 == 0

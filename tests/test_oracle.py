@@ -322,3 +322,22 @@ def test_talker_pick_rule(orc):
     forced = np.array([2, 4, 2, 0], np.uint32)
     p2, ties, mism = orc.talker_pick(logits, banned, seen, frames, 4, 2, 1.05, forced, 0.2)
     assert p2.tolist() == [2, 4, 2, 0] and ties == 2 and mism == 0
+
+
+def test_topk_sample_walk(orc):
+    """The host sampler's walk: draw 0 takes the best id, a draw near 1 the k-th, ties by the
+    lower index; the empirical frequencies follow the tempered softmax over the top k."""
+    l = np.array([[0.0, 2.0, 1.0, 2.0, -1.0]], np.float32)
+    assert orc.topk_sample(l, np.array([0.0]), 3, 1.0).tolist() == [1]
+    assert orc.topk_sample(l, np.array([0.9999]), 3, 1.0).tolist() == [2]
+    assert orc.topk_sample(l, np.array([0.45]), 3, 1.0).tolist() == [3]  # second of the tie
+    rng = np.random.default_rng(0)
+    row = rng.standard_normal(64).astype(np.float32)
+    draws = rng.random(4000).astype(np.float32)
+    picks = orc.topk_sample(np.repeat(row[None], 4000, 0), draws, 8, 0.9)
+    top = np.argsort(-row, kind="stable")[:8]
+    p = np.exp((row[top] - row[top].max()) / 0.9)
+    p /= p.sum()
+    freq = np.array([(picks == i).mean() for i in top])
+    assert set(np.unique(picks)) <= set(top.tolist())
+    assert np.abs(freq - p).max() < 0.03
