@@ -441,7 +441,8 @@ bool gemm_supported(int m, int k, int n, int epi, std::string* why) {
     if (why) *why = s;
     return false;
   };
-  if (m < 1 || m > 512) return no("lanes (m) must be in 1..512");
+  // the split-K partial tile [m][128] f32 lives in shared memory: 448 rows fit in 227 KB
+  if (m < 1 || m > kMaxGemmRows) return no("lanes (m) must be in 1..448");
   if (k < kBlockK || k % kBlockK) return no("k must be a positive multiple of 64");
   if (n < kTileM || n % kTileM) return no("n must be a positive multiple of 128");
   if (epi < EPI_F32 || epi > EPI_ARGMAX) return no("unknown epilogue");

@@ -235,6 +235,27 @@ __global__ void advance_positions_kernel(int* positions, int lanes) {
   if (i < lanes) positions[i] += 1;
 }
 
+// Prefill rows as decode rows: row r is (lane, offset) map[r]; it gets the lane's block-table
+// row and the position the lane's offset-th new row takes.
+__global__ void prefill_rows_kernel(const int* map, int rows, const int* table, int max_blocks,
+                                    const int* positions, int* table2, int* pos2) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  const int lane = map[2 * r], off = map[2 * r + 1];
+  for (int j = threadIdx.x; j < max_blocks; j += blockDim.x)
+    table2[(size_t)r * max_blocks + j] = table[(size_t)lane * max_blocks + j];
+  if (threadIdx.x == 0) pos2[r] = positions[lane] + off;
+}
+
+__global__ void advance_by_kernel(int* positions, const int* lens, int lanes) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < lanes) positions[i] += lens[i];
+}
+
 __global__ void cast_kernel(const float* x, __half* y, long n) {
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
        i += (long)gridDim.x * blockDim.x)
@@ -319,6 +340,20 @@ cudaError_t launch_advance_positions(int* positions, int lanes, bool pdl, cudaSt
   void* args[] = {(void*)&positions, (void*)&lanes};
   return launch_ex(reinterpret_cast<void (*)(void*)>(advance_positions_kernel),
                    dim3((lanes + 127) / 128), dim3(128), st, pdl, args);
+}
+
+cudaError_t launch_prefill_rows(const int* map, int rows, const int* table, int max_blocks,
+                                const int* positions, int* table2, int* pos2, cudaStream_t st) {
+  void* args[] = {(void*)&map,       (void*)&rows,      (void*)&table, (void*)&max_blocks,
+                  (void*)&positions, (void*)&table2,    (void*)&pos2};
+  return launch_ex(reinterpret_cast<void (*)(void*)>(prefill_rows_kernel), dim3(rows), dim3(64),
+                   st, true, args);
+}
+
+cudaError_t launch_advance_by(int* positions, const int* lens, int lanes, cudaStream_t st) {
+  void* args[] = {(void*)&positions, (void*)&lens, (void*)&lanes};
+  return launch_ex(reinterpret_cast<void (*)(void*)>(advance_by_kernel),
+                   dim3((lanes + 127) / 128), dim3(128), st, true, args);
 }
 
 cudaError_t launch_cast_f32_f16(const float* x, __half* y, long n, cudaStream_t st) {

@@ -62,6 +62,13 @@ struct tts_stack {
   float* x_next = nullptr;    // [max_lanes][dim] (own buffer)
   float* feedback = nullptr;  // caller's buffer replacing x_next, or null
   PickRule pick;              // the codec head's greedy pick rule (words == 0: plain argmax)
+  // prefill scratch, grown on demand by tts_stack_prefill: per-row (lane, offset) pairs and
+  // lane lengths; per-row block-table rows and positions for one chunk of rows
+  int* pre_map = nullptr;
+  size_t pre_map_ints = 0;
+  int* pre_table = nullptr;
+  size_t pre_table_ints = 0;
+  int* pre_pos = nullptr;
   unsigned long long* keys = nullptr;  // [max_lanes][codebooks]
   // bytes of the next projection's weights each kernel prefetches into L2 (0: none). 12 MB
   // measured best for the talker; the depth predictor's stack runs without (its kernels are
@@ -187,8 +194,8 @@ long long tts_launch_count(int reset) {
 
 tts_status tts_ctx_create(int device, int max_lanes, tts_ctx** out) {
   if (!out) return fail(TTS_ERR_INVALID_ARG, "ctx_create: out is NULL");
-  if (max_lanes < 1 || max_lanes > 512)
-    return fail(TTS_ERR_INVALID_ARG, "ctx_create: max_lanes must be in 1..512");
+  if (max_lanes < 1 || max_lanes > kMaxGemmRows)
+    return fail(TTS_ERR_INVALID_ARG, "ctx_create: max_lanes must be in 1..448");
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
     return fail(TTS_ERR_CUDA, "ctx_create: no such CUDA device");
@@ -655,6 +662,9 @@ tts_status tts_stack_destroy(tts_stack* s) {
   cudaFree(s->chain.done);
   cudaFree(s->chain.exit_cnt);
   cudaFree(s->chain.tile_cnt);
+  cudaFree(s->pre_map);
+  cudaFree(s->pre_table);
+  cudaFree(s->pre_pos);
   delete s;
   return TTS_OK;
 }
@@ -971,6 +981,84 @@ static tts_status capture_graph(cudaStream_t cs, tts_graph** out, Fn&& body) {
   return TTS_OK;
 }
 }  // extern "C++"
+
+// Stack::forward at t > 1 (qwen3.rs:294-467 with a multi-position input): every new row of
+// every lane runs as a decode row of its own (its lane's pages, its own position), in chunks of
+// up to max_lanes rows; the QKV epilogue writes a chunk's K/V before its attention reads them, so
+// each row sees the lane's earlier rows, as the causal mask does.
+static tts_status prefill_impl(tts_stack* s, const tts_decode_state* st, const int* lens,
+                               const float* x, float* h_out, cudaStream_t cs) {
+  tts_ctx* c = s->ctx;
+  if (!st || !lens || !x || !st->positions || !st->block_table)
+    return fail(TTS_ERR_INVALID_ARG, "stack_prefill: NULL argument");
+  const int lanes = st->lanes;
+  if (lanes < 1 || st->max_blocks < 1)
+    return fail(TTS_ERR_INVALID_ARG, "stack_prefill: lanes and max_blocks must be >= 1");
+  std::vector<int> host;
+  long rows = 0;
+  for (int i = 0; i < lanes; ++i) {
+    if (lens[i] < 0) return fail(TTS_ERR_INVALID_ARG, "stack_prefill: negative length");
+    rows += lens[i];
+  }
+  if (rows < 1) return TTS_OK;
+  if (rows > (1L << 24)) return fail(TTS_ERR_UNSUPPORTED_SHAPE, "stack_prefill: too many rows");
+  host.reserve(size_t(2 * rows + lanes));
+  for (int i = 0; i < lanes; ++i)
+    for (int t = 0; t < lens[i]; ++t) {
+      host.push_back(i);
+      host.push_back(t);
+    }
+  for (int i = 0; i < lanes; ++i) host.push_back(lens[i]);
+  const int chunk = c->max_lanes;
+  const size_t table_ints = size_t(chunk) * st->max_blocks;
+  cudaError_t e = cudaSuccess;
+  if (host.size() > s->pre_map_ints) {
+    cudaFree(s->pre_map);
+    s->pre_map = nullptr;
+    s->pre_map_ints = 0;
+    e = dmalloc(&s->pre_map, host.size() * 4);
+    if (e == cudaSuccess) s->pre_map_ints = host.size();
+  }
+  if (e == cudaSuccess && table_ints > s->pre_table_ints) {
+    cudaFree(s->pre_table);
+    cudaFree(s->pre_pos);
+    s->pre_table = nullptr;
+    s->pre_pos = nullptr;
+    s->pre_table_ints = 0;
+    e = dmalloc(&s->pre_table, table_ints * 4);
+    if (e == cudaSuccess) e = dmalloc(&s->pre_pos, size_t(chunk) * 4);
+    if (e == cudaSuccess) s->pre_table_ints = table_ints;
+  }
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(s->pre_map, host.data(), host.size() * 4, cudaMemcpyHostToDevice, cs);
+  if (e != cudaSuccess) return cuda_status(e, "stack_prefill");
+  const int D = s->geo.dim;
+  tts_status rc;
+  for (long r0 = 0; r0 < rows; r0 += chunk) {
+    const int n = int(std::min<long>(chunk, rows - r0));
+    if ((rc = counted(launch_prefill_rows(s->pre_map + 2 * r0, n, st->block_table, st->max_blocks,
+                                          st->positions, s->pre_table, s->pre_pos, cs),
+                      "stack_prefill")) != TTS_OK)
+      return rc;
+    tts_decode_state rowst = *st;
+    rowst.lanes = n;
+    rowst.positions = s->pre_pos;
+    rowst.block_table = s->pre_table;
+    HeadSel none;  // no heads: the prompt's rows pick nothing
+    rc = step_impl(s, &rowst, x + size_t(r0) * D, h_out ? h_out + size_t(r0) * D : nullptr,
+                   nullptr, nullptr, cs, &none);
+    if (rc != TTS_OK) return rc;
+  }
+  return counted(launch_advance_by(st->positions, s->pre_map + 2 * rows, lanes, cs),
+                 "stack_prefill");
+}
+
+tts_status tts_stack_prefill(tts_stack* s, const tts_decode_state* st, const int* lens,
+                             const float* x, float* h_out, void* stream) {
+  if (!s) return fail(TTS_ERR_INVALID_ARG, "stack_prefill: stack is NULL");
+  DeviceGuard g(s->ctx->device);
+  return prefill_impl(s, st, lens, x, h_out, S(stream));
+}
 
 tts_status tts_stack_decode_step(tts_stack* s, const tts_decode_state* st, const float* x,
                                  float* h_out, float* logits, unsigned int* codes, void* stream) {

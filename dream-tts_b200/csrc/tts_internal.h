@@ -108,6 +108,7 @@ struct Workspace {
   int* err = nullptr;  // device error flags (bounded waits that gave up, out-of-range rows)
 };
 
+constexpr int kMaxGemmRows = 448;
 bool gemm_supported(int m, int k, int n, int epi, std::string* why);
 cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t st, int device);
 
@@ -230,6 +231,11 @@ cudaError_t launch_topk_sample(const float* logits, int rows, int n, int ldl, co
                                int code_stride, const float* embed32, float* x_next, int dim,
                                int* positions, bool pdl, cudaStream_t st);
 cudaError_t launch_cast_f32_f16(const float* x, __half* y, long n, cudaStream_t st);
+// Prefill as decode rows (map[r] = (lane, offset)): per-row block-table copies and positions;
+// then each lane's position advanced by its row count.
+cudaError_t launch_prefill_rows(const int* map, int rows, const int* table, int max_blocks,
+                                const int* positions, int* table2, int* pos2, cudaStream_t st);
+cudaError_t launch_advance_by(int* positions, const int* lens, int lanes, cudaStream_t st);
 
 // ------------------------------------------------------------------ codec conv
 struct ConvRequest {

@@ -100,26 +100,63 @@ class PagedKv:
         self.positions = torch.zeros(lanes, dtype=torch.int32, device=device)
         self._free = list(range(num_blocks - 1, -1, -1))
         self._owned: dict[int, list[int]] = {}
+        self._refs: dict[int, int] = {}  # lanes holding each page (shared prefixes)
+
+    def _take(self, n: int) -> list[int]:
+        if n > len(self._free):
+            raise MemoryError("KV pool exhausted")
+        pages = [self._free.pop() for _ in range(n)]
+        for p in pages:
+            self._refs[p] = 1
+        return pages
+
+    def _set_row(self, lane: int, pages: list[int], length: int) -> None:
+        self._owned[lane] = pages
+        row = torch.zeros(self.max_blocks, dtype=torch.int32)
+        row[:len(pages)] = torch.tensor(pages, dtype=torch.int32)
+        self.table[lane].copy_(row)
+        self.positions[lane] = length
 
     def admit(self, lane: int, capacity: int, length: int = 0) -> list[int]:
         """Give `lane` pages for `capacity` positions; it holds `length` of them already."""
         need = -(-capacity // self.block_size)
         if need > self.max_blocks:
             raise ValueError(f"lane needs {need} pages, the table holds {self.max_blocks}")
-        if need > len(self._free):
-            raise MemoryError("KV pool exhausted")
         self.release(lane)
-        pages = [self._free.pop() for _ in range(need)]
-        self._owned[lane] = pages
-        row = torch.zeros(self.max_blocks, dtype=torch.int32)
-        row[:need] = torch.tensor(pages, dtype=torch.int32)
-        self.table[lane].copy_(row)
-        self.positions[lane] = length
+        pages = self._take(need)
+        self._set_row(lane, pages, length)
         return pages
+
+    def share_prefix(self, src: int, lane: int, length: int, capacity: int) -> list[int]:
+        """Admit `lane` with the first `length` cached positions of lane `src` (the shared
+        prompt prefix every lane of a group starts from, which the reference broadcast-copies
+        into each lane, crates/qwen3tts/src/qwen3.rs:261-284): its full pages are shared
+        through the block table, only a partly filled last page is copied, and fresh pages
+        cover the rest of `capacity`. `src` must hold at least `length` positions."""
+        bs = self.block_size
+        need = -(-capacity // bs)
+        if need > self.max_blocks or length > capacity:
+            raise ValueError("share_prefix: capacity exceeds the block table or the prefix")
+        full, part = divmod(length, bs)
+        src_pages = self._owned[src]
+        self.release(lane)
+        shared = src_pages[:full]
+        for p in shared:
+            self._refs[p] += 1
+        own = self._take(need - full)
+        if part:
+            # the partly filled page: a copy, since this lane writes its own rows after it
+            self.k[:, own[0]].copy_(self.k[:, src_pages[full]])
+            self.v[:, own[0]].copy_(self.v[:, src_pages[full]])
+        self._set_row(lane, shared + own, length)
+        return shared + own
 
     def release(self, lane: int) -> None:
         for p in self._owned.pop(lane, []):
-            self._free.append(p)
+            self._refs[p] -= 1
+            if self._refs[p] == 0:
+                del self._refs[p]
+                self._free.append(p)
 
     def free_pages(self) -> int:
         return len(self._free)
@@ -223,6 +260,17 @@ class Stack:
         if self.heads is not None:
             n += self.heads.numel() * 2
         return n
+
+    def prefill(self, kv: PagedKv, lens, x: torch.Tensor, h_out: torch.Tensor | None = None,
+                max_span: int | None = None) -> None:
+        """Stack::forward at t > 1: lane i (of the first len(lens)) appends lens[i] rows of `x`
+        (f32 [sum(lens), dim], lane after lane) at its next positions, causal over its cached
+        and new rows; `h_out` (f32 [sum(lens), dim]) gets every row's final-normed hidden."""
+        import numpy as np
+        arr = np.ascontiguousarray(np.asarray(lens, dtype=np.int32))
+        st = kv.state(len(arr), max_span)
+        L.call("tts_stack_prefill", self.handle, C.byref(st),
+               arr.ctypes.data_as(C.c_void_p), ptr(x), ptr(h_out), stream())
 
     def decode_step(self, kv: PagedKv, x: torch.Tensor | None = None, lanes: int | None = None,
                     h_out: torch.Tensor | None = None, logits: torch.Tensor | None = None,

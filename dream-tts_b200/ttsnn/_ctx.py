@@ -7,12 +7,12 @@ import torch
 
 from . import _lib as L
 
-MAX_LANES = 512
+MAX_LANES = 448
 _ctx: dict[int, C.c_void_p] = {}
 
 
 def ctx(device: int | None = None) -> C.c_void_p:
-    """The library context of `device` (created on first use, with scratch for 512 lanes)."""
+    """The library context of `device` (created on first use, with scratch for 448 lanes)."""
     dev = torch.cuda.current_device() if device is None else int(device)
     if dev not in _ctx:
         p = C.c_void_p()

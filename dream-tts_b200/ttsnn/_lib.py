@@ -106,6 +106,7 @@ SIGNATURES = {
     "tts_stack_set_pick": [P, C.POINTER(PickRule)],
     "tts_topk_sample": [P, P, I, I, P, I, F, P, P],
     "tts_predictor_set_sampling": [P, P, I, I, F],
+    "tts_stack_prefill": [P, C.POINTER(DecodeState), P, P, P, P],
     "tts_talker_frame": [P, C.POINTER(DecodeState), P, C.POINTER(DecodeState),
                          C.POINTER(TextFeed), P, P, P, P],
     "tts_talker_frame_capture": [P, C.POINTER(DecodeState), P, C.POINTER(DecodeState),

@@ -53,7 +53,7 @@ TTS_API int tts_abi_version(void);
 TTS_API const char* tts_last_error(void);
 
 /* One context per device (and per host thread driving it). Allocates the split-K and
- * attention scratch for up to `max_lanes` rows. Replaces the candle Device the reference opens
+ * attention scratch for up to `max_lanes` rows (1..448). Replaces the candle Device the reference opens
  * in crates/qwen3tts/src/engine.rs:529-533. */
 TTS_API tts_status tts_ctx_create(int device, int max_lanes, tts_ctx** out);
 TTS_API tts_status tts_ctx_destroy(tts_ctx* ctx);
@@ -67,7 +67,7 @@ TTS_API tts_status tts_ctx_check(tts_ctx* ctx, void* stream);
  * Proj::forward for Proj::Half: crates/tts-nn/src/lib.rs:510-533, via skinny::matmul
  * (crates/tts-nn/src/skinny.rs:155-165) and matmul_2d (lib.rs:438-459).
  * y = x[m, k] (f16) . w[n, k]^T (f16, the checkpoint's [out, in] layout), f32 accumulate.
- * m in 1..512, k % 64 == 0, n % 128 == 0. `epilogue`:
+ * m in 1..448, k % 64 == 0, n % 128 == 0. `epilogue`:
  *   TTS_EPI_F32          y f32 [m][ldy]
  *   TTS_EPI_F16          y f16 [m][ldy]
  *   TTS_EPI_RESIDUAL_F32 y f32 [m][ldy] += x.w^T   (qwen3.rs:451 and :463, h += proj)
@@ -147,7 +147,7 @@ TTS_API tts_status tts_qk_rope_append(tts_ctx* ctx, const float* qkv, int lanes,
 /* attn::decode_attention: crates/tts-nn/src/attn.rs:22-73. q f32 [lanes][n_kv * gqa][128]
  * with the scale folded in; lane i attends positions [wstart_i, spans[i]) where
  * wstart_i = max(0, spans[i] - window) (window 0 = none). max_span bounds every spans[i].
- * out [lanes][n_kv * gqa * 128], f16 or f32. gqa in {1, 2, 4, 8}; lanes <= 512; block_size
+ * out [lanes][n_kv * gqa * 128], f16 or f32. gqa in {1, 2, 4, 8}; lanes <= max_lanes; block_size
  * a multiple of 8 unless max_blocks == 1 (each lane one contiguous page); pool pointers
  * 16-byte aligned. Pages outside [0, num_blocks) read as zero and are reported. */
 TTS_API tts_status tts_decode_attention(tts_ctx* ctx, const float* q, int lanes, int gqa,
@@ -279,6 +279,16 @@ typedef struct tts_decode_state {
  * codes u32 [lanes][codebooks]. */
 TTS_API tts_status tts_stack_decode_step(tts_stack* s, const tts_decode_state* st, const float* x,
                                  float* h_out, float* logits, unsigned int* codes, void* stream);
+
+/* Stack::forward at t > 1, the prompt's prefill (qwen3.rs:294-467; talker.rs:903-931): lane i
+ * appends lens[i] (host array) rows at positions positions[i] .. + lens[i] - 1, causal over the
+ * lane's cached and new rows, K/V written into its pages; positions advance by lens[i].
+ * x f32 [sum of lens][dim], the lanes' rows one lane after another; h_out (NULL = none) f32
+ * [sum of lens][dim] every row's final-normed hidden. st->max_span must cover every lane's new
+ * end. Not for stream capture: it uploads the row plan and may grow the stack's prefill scratch
+ * (the one allocation a stack makes after creation). */
+TTS_API tts_status tts_stack_prefill(tts_stack* s, const tts_decode_state* st, const int* lens,
+                                     const float* x, float* h_out, void* stream);
 
 /* The same step captured once into a CUDA graph (stream must not be the legacy stream) and
  * replayed with tts_graph_launch. Pointers are baked in at capture. */
