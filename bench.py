@@ -746,6 +746,67 @@ def run_frames(args):
     return 0
 
 
+def run_prefill(args):
+    """Prompt prefill (Stack::forward at t > 1, qwen3.rs:294-467) at config[2]'s talker shape:
+    48 lanes x 157 prompt positions (the reference's ICL width) through the 28 layers, as
+    chunks of 448 decode rows sharing each lane's pages. value = prompt tokens per second over
+    the whole call (its row plan upload included). Roofline: tensor (2 x tokens x 1.41 G
+    weights FLOP, the attention's share is < 1 %)."""
+    import torch
+    import ttsnn
+    from qwen3tts import PagedKv
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    prompt = 157
+    stack, _, _, _ = build_device_talker(device, seed=rank, extra_positions=0, lanes_override=0)
+    cap = prompt + 3
+    per = -(-cap // BLOCK)
+    kv = PagedKv(stack.geo, LANES, LANES * per, BLOCK, per, device)
+    gen = torch.Generator(device=device).manual_seed(rank)
+    x = torch.randn(LANES * prompt, DIM, generator=gen, device=device)
+    lens = [prompt] * LANES
+
+    def run():
+        for i in range(LANES):
+            kv.positions[i] = 0
+        stack.prefill(kv, lens, x, max_span=cap)
+
+    for i in range(LANES):
+        kv.admit(i, cap, 0)
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    ttsnn.check(local)
+    ttsnn.launch_count(reset=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    launches = ttsnn.launch_count()
+    ttsnn.check(local)
+    s_per = e0.elapsed_time(e1) * 1e-3 / args.steps
+    tokens = LANES * prompt
+    flops = 2.0 * tokens * (stack.weight_bytes() - 16 * VOCAB * DIM * 2) / 2
+    tpeak, tkind = bf16_peak()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "prompt tokens/sec (prefill, one GPU)", "value": round(tokens / s_per, 1),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(s_per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (random-init weights)",
+            "config": {"workload": "prefill of 48 lanes x 157 positions through the config[2] "
+                                   "talker (28 layers), chunks of 448 rows", "tokens": tokens},
+            "roofline": {"bound": "tensor", "achieved": round(flops / s_per / 1e12, 1),
+                         "peak": tpeak, "unit": "TFLOP/s",
+                         "frac": round(flops / s_per / 1e12 / tpeak, 4), "traffic": None,
+                         "peak_source": tkind + " dense bf16"},
+            "gpu_launches": int(launches)}), flush=True)
+    return 0
+
+
 def run_kernel_case(args):
     """Small standalone cases of one kernel, for ncu captures (a few launches, < 1 GB)."""
     import torch
@@ -955,7 +1016,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--workload", default="step",
-                    choices=["step", "sweep", "document", "predictor", "frames"],
+                    choices=["step", "sweep", "document", "predictor", "frames", "prefill"],
                     help="step: the config[2] decode step (headline); sweep: config[3]; "
                          "document: a bounded config[4] sample (talker + codec); predictor: "
                          "the depth predictor's frame; frames: the reference's talker loop "
@@ -980,6 +1041,8 @@ def main():
         return run_predictor(args)
     if args.workload == "frames":
         return run_frames(args)
+    if args.workload == "prefill":
+        return run_prefill(args)
     return run_b200(args)
 
 
