@@ -20,7 +20,7 @@ OUT = os.path.join(HERE, "ttsnn", "libtts_cuda.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 SOURCES = ["runtime.cu", "gemm_decode.cu", "attn_decode.cu", "chain.cu", "ops_small.cu",
-           "predictor.cu", "attn_short.cu", "topk_sample.cu",
+           "predictor.cu", "attn_short.cu", "topk_sample.cu", "safetensors.cpp",
            "conv_nlc.cu"]
 HEADERS = ["tts_common.cuh", "tts_internal.h", "qkrope_row.cuh", "gemm_epilogue.cuh",
            "l2_prefetch.cuh"]
@@ -59,7 +59,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(objdir, exist_ok=True)
     objs = []
     for s in SOURCES:
-        obj = os.path.join(objdir, s.replace(".cu", ".o"))
+        obj = os.path.join(objdir, os.path.splitext(s)[0] + ".o")
         cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-c", os.path.join(CSRC, s), "-o", obj]
         if verbose:
             print(" ".join(cmd))

@@ -64,6 +64,11 @@ class TextFeed(C.Structure):
                 ("frames", C.c_void_p)]
 
 
+class TensorView(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("dtype", C.c_int), ("ndim", C.c_int),
+                ("shape", C.c_longlong * 8), ("data", C.c_void_p), ("nbytes", C.c_size_t)]
+
+
 P = C.c_void_p
 I = C.c_int
 L = C.c_long
@@ -107,12 +112,18 @@ SIGNATURES = {
     "tts_topk_sample": [P, P, I, I, P, I, F, P, P],
     "tts_predictor_set_sampling": [P, P, I, I, F],
     "tts_stack_prefill": [P, C.POINTER(DecodeState), P, P, P, P],
+    "tts_safetensors_open": [C.c_char_p, C.POINTER(P)],
+    "tts_safetensors_count": [P],
+    "tts_safetensors_at": [P, I, C.POINTER(TensorView)],
+    "tts_safetensors_find": [P, C.c_char_p, C.POINTER(TensorView)],
+    "tts_safetensors_close": [P],
     "tts_talker_frame": [P, C.POINTER(DecodeState), P, C.POINTER(DecodeState),
                          C.POINTER(TextFeed), P, P, P, P],
     "tts_talker_frame_capture": [P, C.POINTER(DecodeState), P, C.POINTER(DecodeState),
                                  C.POINTER(TextFeed), P, P, P, P, C.POINTER(P)],
 }
-_RESTYPE = {"tts_last_error": C.c_char_p, "tts_launch_count": C.c_longlong}
+_RESTYPE = {"tts_last_error": C.c_char_p, "tts_launch_count": C.c_longlong,
+            "tts_safetensors_count": C.c_int}
 
 _lib = None
 

@@ -373,6 +373,32 @@ TTS_API tts_status tts_talker_frame_capture(tts_stack* talker, const tts_decode_
                                             unsigned int* code0, unsigned int* codes,
                                             void* stream, tts_graph** out);
 
+/* ---------------------------------------------------------------- checkpoint files
+ * Memory-mapped safetensors (the reference's Weights over candle's MmapedSafetensors,
+ * crates/tts-nn/src/lib.rs:153-373): the header parsed at open, every tensor a view into the
+ * mapping (host memory, on-disk dtype). Casts, transposes and folds are the caller's load-time
+ * work. Errors name the file and the broken entry; a missing name is "missing tensor <name>". */
+typedef struct tts_safetensors tts_safetensors;
+typedef enum tts_dtype {
+  TTS_DT_F32 = 0, TTS_DT_F16 = 1, TTS_DT_BF16 = 2, TTS_DT_I32 = 3, TTS_DT_I64 = 4,
+  TTS_DT_U8 = 5, TTS_DT_F64 = 6, TTS_DT_I8 = 7, TTS_DT_I16 = 8, TTS_DT_BOOL = 9,
+  TTS_DT_OTHER = 99
+} tts_dtype;
+typedef struct tts_tensor_view {
+  const char* name;     /* valid while the file is open */
+  int dtype;            /* tts_dtype */
+  int ndim;
+  long long shape[8];
+  const void* data;     /* host, read-only */
+  size_t nbytes;
+} tts_tensor_view;
+TTS_API tts_status tts_safetensors_open(const char* path, tts_safetensors** out);
+TTS_API int tts_safetensors_count(const tts_safetensors* f);
+TTS_API tts_status tts_safetensors_at(const tts_safetensors* f, int i, tts_tensor_view* out);
+TTS_API tts_status tts_safetensors_find(const tts_safetensors* f, const char* name,
+                                        tts_tensor_view* out);
+TTS_API tts_status tts_safetensors_close(tts_safetensors* f);
+
 /* Kernel launches made by the calling thread through this library since the last call
  * (observability: the bench reports it). */
 TTS_API long long tts_launch_count(int reset);
