@@ -553,17 +553,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  float m_run[GQA], l_run[GQA], acc[GQA], corr[GQA];
+  // Running state of the current segment (max, sum, output dim t per q head), and the state of
+  // a segment that ended at the previous item, set aside until that item is folded in.
+  float m_run[GQA], l_run[GQA], acc[GQA];
+  float m_fin[GQA], l_fin[GQA], acc_fin[GQA];
+  float corr_pend[GQA];  // the pending item's rescale (previous max -> its max)
 #pragma unroll
   for (int g = 0; g < GQA; ++g) {
     m_run[g] = -INFINITY;
     l_run[g] = 0.f;
     acc[g] = 0.f;
-    corr[g] = 0.f;
+    m_fin[g] = -INFINITY;
+    l_fin[g] = 0.f;
+    acc_fin[g] = 0.f;
+    corr_pend[g] = 0.f;
   }
   int n_partial = 0;  // partial segments handed to the epilogue warp (at most 2)
-  // The item before this one: its sum and values are folded in one item late (when its PV is
-  // long done), and when it ended a segment that segment is written out then.
+  // The item before this one: its sum and values are folded in one item late, after this
+  // item's P is out (so its PV has run meanwhile and the chain scores -> P never waits on it);
+  // when it ended a segment, that segment is written out then.
   bool pend = false;
   struct {
     int b, h, c_first, c_last, nch;
@@ -571,8 +579,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } prev{};
   int c_first = cur.c;
 
-  // folds the previous item's sum and O into the running state
-  auto fold_prev = [&](long long i) {
+  // folds item i's sum and O into a state (l, acc) at the previous item's scale
+  auto fold = [&](long long i, float* l, float* o_acc) {
     ok = mbar_wait(&S.o_full[i & 1], uint32_t(i >> 1) & 1) && ok;
     tc_fence_after();
     float ov[16];
@@ -582,18 +590,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) mbar_arrive(&S.o_empty[i & 1]);
 #pragma unroll
     for (int g = 0; g < GQA; ++g) {
-      l_run[g] = l_run[g] * corr[g] + ((S.red_sum[i & 1][0][g] + S.red_sum[i & 1][1][g]) +
-                                       (S.red_sum[i & 1][2][g] + S.red_sum[i & 1][3][g]));
-      acc[g] = acc[g] * corr[g] + (ov[g] + ov[GQA + g] * (1.f / kLo));
+      l[g] = l[g] * corr_pend[g] + ((S.red_sum[i & 1][0][g] + S.red_sum[i & 1][1][g]) +
+                                    (S.red_sum[i & 1][2][g] + S.red_sum[i & 1][3][g]));
+      o_acc[g] = o_acc[g] * corr_pend[g] + (ov[g] + ov[GQA + g] * (1.f / kLo));
     }
   };
-  // writes a finished segment: the output of a whole pair, or a partial for the epilogue warp
-  auto finish_segment = [&]() {
+  // writes a finished segment (max m, sum l, output o_acc): the output of a whole pair, or a
+  // partial for the epilogue warp
+  auto finish_segment = [&](const float* m, const float* l, const float* o_acc) {
     const size_t out_base = (size_t)prev.b * heads * 128 + (size_t)prev.h * GQA * 128;
     if (prev.c_first == 0 && prev.c_last + 1 == prev.nch) {
 #pragma unroll
       for (int g = 0; g < GQA; ++g) {
-        const float r = acc[g] / l_run[g];
+        const float r = o_acc[g] / l[g];
         const size_t oi = out_base + g * 128 + t;
         if (a.out_f16)
           static_cast<__half*>(a.out)[oi] = __float2half_rn(r);
@@ -605,10 +614,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int g = 0; g < GQA; ++g) {
         float* pp = a.part + ((pbase + prev.c_first) * GQA + g) * 130;
-        pp[t] = acc[g];
+        pp[t] = o_acc[g];
         if (t == 0) {
-          pp[128] = m_run[g];
-          pp[129] = l_run[g];
+          pp[128] = m[g];
+          pp[129] = l[g];
         }
       }
       if (t == 0) {
@@ -619,12 +628,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mbar_arrive(&S.seg_done[n_partial]);
       ++n_partial;
-    }
-#pragma unroll
-    for (int g = 0; g < GQA; ++g) {
-      m_run[g] = -INFINITY;
-      l_run[g] = 0.f;
-      acc[g] = 0.f;
     }
   };
 
@@ -639,6 +642,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       seg2 = next_segment(nx, at);
       pos2 = at;
       if (pos2 < n) load_q(seg2);
+    }
+    // a segment ended at the previous item: set its state aside until that item is folded,
+    // and start this segment fresh
+    const bool fin = pend && prev.ends;
+    if (fin) {
+#pragma unroll
+      for (int g = 0; g < GQA; ++g) {
+        m_fin[g] = m_run[g];
+        l_fin[g] = l_run[g];
+        acc_fin[g] = acc[g];
+        m_run[g] = -INFINITY;
+        l_run[g] = 0.f;
+        acc[g] = 0.f;
+      }
     }
     // ---- scores of item j (thread t = row t)
     int vlo, vhi;
@@ -662,18 +679,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = false;
       break;
     }
-    // ---- the previous item, and the segment it ended
-    if (pend) {
-      fold_prev(j - 1);
-      if (prev.ends) finish_segment();
-    }
     // ---- softmax of item j; P as f16 hi/lo rows of the O operand
+    float corr_new[GQA];
 #pragma unroll
     for (int g = 0; g < GQA; ++g) {
       const float cmax = fmaxf(fmaxf(S.red_max[j & 1][0][g], S.red_max[j & 1][1][g]),
                                fmaxf(S.red_max[j & 1][2][g], S.red_max[j & 1][3][g]));
       const float mn = fmaxf(m_run[g], cmax);
-      corr[g] = (m_run[g] == -INFINITY) ? 0.f : expf(m_run[g] - mn);
+      corr_new[g] = (m_run[g] == -INFINITY) ? 0.f : expf(m_run[g] - mn);
       const float p = valid ? expf(sc[g] - mn) : 0.f;
       m_run[g] = mn;
       const __half phi = __float2half_rn(p);
@@ -692,6 +705,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) mbar_arrive(&S.p_full[j & 1]);
+    // ---- the previous item, now that this item's P is out, and the segment it ended
+    if (pend) {
+      if (fin) {
+        fold(j - 1, l_fin, acc_fin);
+        finish_segment(m_fin, l_fin, acc_fin);
+      } else {
+        fold(j - 1, l_run, acc);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < GQA; ++g) corr_pend[g] = corr_new[g];
 
     pend = true;
     prev.b = cur.b;
@@ -706,8 +730,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the last item: its sums need every warp's partial sum, then its segment is written
   if (ok && pend) {
     if (bar_and(kBarSoftmax, kSoftmax, ok)) {
-      fold_prev(n - 1);
-      finish_segment();
+      fold(n - 1, l_run, acc);
+      finish_segment(m_run, l_run, acc);
     } else {
       ok = false;
     }

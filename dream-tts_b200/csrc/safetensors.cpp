@@ -14,7 +14,7 @@
 #include <unordered_map>
 #include <vector>
 
-#include "../../include/tts_cuda.h"
+#include "tts_cuda.h"
 
 namespace tts {
 void set_error(const std::string& msg);
