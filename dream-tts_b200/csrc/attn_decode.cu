@@ -42,13 +42,15 @@ constexpr int kSoftmax = 128;    // warps 0-3: one TMEM lane quarter each
 constexpr int kLoaderWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr int kEpiWarp = 6;
-constexpr int kThreads = 224;
+constexpr int kPvWarp = 7;     // issues the O MMAs, beside the score MMAs of kMmaWarp
+constexpr int kThreads = 256;
 constexpr int kMaxChunks = 64;   // 8192 positions
 constexpr int kMaxLanes = 512;
 constexpr int kN = 16;           // MMA N: GQA high rows, GQA low rows, zero padding
 constexpr float kLo = 2048.f;    // scale of the low f16 parts
 constexpr uint32_t kBarSoftmax = 1;  // named barrier: softmax warps
-constexpr uint32_t kBarTmem = 2;     // named barrier: softmax + MMA warps (TMEM release)
+constexpr uint32_t kBarTmem = 2;     // named barrier: softmax + both MMA warps (TMEM release)
+constexpr int kTmemBarThreads = kSoftmax + 64;
 
 struct AttnArgs {
   const float* q;
@@ -346,36 +348,52 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t idesc_s = idesc_f16_f32(128, kN);
   const uint32_t idesc_o = idesc_f16_f32(128, kN) | (1u << 15);  // A (V^T) MN-major
 
-  if (warp == kMmaWarp) {
-    // ================= MMA warp: S(j) then O(j - 1), each when its inputs are in place
-    bool ok = true;
-    long long ns = 0, no = 0;  // MMA groups issued
-    auto do_o = [&](long long i) {
-      const int s = int(i % kStages);
-      ok = mbar_wait(&S.p_full[i & 1], uint32_t(i >> 1) & 1) && ok;
-      ok = mbar_wait(&S.full_v[s], uint32_t(i / kStages) & 1) && ok;
-      if (i >= 2) ok = mbar_wait(&S.o_empty[i & 1], uint32_t((i >> 1) - 1) & 1) && ok;
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) return;
-      if (S.inv_v[s]) {  // rows of pages outside the pool read as zero
-        zero_rows(S.vt[s], 0, kChunk, S.inv_v[s], a.box_rows, lane, 32);
-        fence_proxy_async();
-        __syncwarp();
-      }
-      tc_fence_after();
-      if (elect_one()) {
-        const uint32_t vb = smem_u32(&S.vt[s].d[0][0]);
-        const uint32_t pb[2] = {smem_u32(&S.pb[i & 1][0][0]), smem_u32(&S.pb[i & 1][1][0])};
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_f16(tmem + 32 + (i & 1) * 16, smem_desc(vb + kk * 2048, kChunk * 128, 1024, 2),
-                   desc_k_sw128(pb[kk >> 2] + (kk & 3) * 32), idesc_o, kk > 0);
-        umma_commit(&S.o_full[i & 1]);
-        umma_commit(&S.empty_v[s]);
-      }
+  // O(i) = V(i)^T . P(i)^T, issued by the O warp when P(i) and V(i) are in place
+  auto do_o = [&](long long i, bool& ok, long long& no) {
+    const int s = int(i % kStages);
+    ok = mbar_wait(&S.p_full[i & 1], uint32_t(i >> 1) & 1) && ok;
+    ok = mbar_wait(&S.full_v[s], uint32_t(i / kStages) & 1) && ok;
+    if (i >= 2) ok = mbar_wait(&S.o_empty[i & 1], uint32_t((i >> 1) - 1) & 1) && ok;
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) return;
+    if (S.inv_v[s]) {  // rows of pages outside the pool read as zero
+      zero_rows(S.vt[s], 0, kChunk, S.inv_v[s], a.box_rows, lane, 32);
+      fence_proxy_async();
       __syncwarp();
-      ++no;
-    };
+    }
+    tc_fence_after();
+    if (elect_one()) {
+      const uint32_t vb = smem_u32(&S.vt[s].d[0][0]);
+      const uint32_t pb[2] = {smem_u32(&S.pb[i & 1][0][0]), smem_u32(&S.pb[i & 1][1][0])};
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_f16(tmem + 32 + (i & 1) * 16, smem_desc(vb + kk * 2048, kChunk * 128, 1024, 2),
+                 desc_k_sw128(pb[kk >> 2] + (kk & 3) * 32), idesc_o, kk > 0);
+      umma_commit(&S.o_full[i & 1]);
+      umma_commit(&S.empty_v[s]);
+    }
+    __syncwarp();
+    ++no;
+  };
+
+  if (warp == kPvWarp) {
+    // ================= O warp: O(i) for every item, in order. Its MMAs and the score warp's
+    // run side by side (different TMEM columns and operands), so neither chain waits for the
+    // other's issue.
+    bool ok = true;
+    long long no = 0;
+    for (long long i = 0; i < n && ok; ++i) do_o(i, ok, no);
+    if (!ok && a.err && lane == 0) atomicOr(a.err, kFlagAttnWait);
+    if (!ok && no > 0) mbar_wait(&S.o_full[(no - 1) & 1], uint32_t((no - 1) >> 1) & 1, 100000000ull);
+    tc_fence_before();
+    bar_and(kBarTmem, kTmemBarThreads, true);
+    return;
+  }
+
+  if (warp == kMmaWarp) {
+    // ================= score warp: S(j) = K(j) . Q^T when K(j) and its segment's q are in place
+    bool ok = true;
+    long long ns = 0;  // MMA groups issued
     Cursor x = first;
     for (long long j = 0; j < n && ok; ++j) {
       const int s = int(j % kStages);
@@ -404,19 +422,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       ++ns;
-      if (j >= 1) do_o(j - 1);
       cursor_next(x, S.span, a);
     }
-    if (ok && n > 0) do_o(n - 1);
     if (!ok && a.err && lane == 0) atomicOr(a.err, kFlagAttnWait);
     // the softmax warps have consumed every result on the normal path; after a timeout, wait
     // (bounded) for what was issued before TMEM is released
-    if (!ok) {
-      if (ns > 0) mbar_wait(&S.s_full[(ns - 1) & 1], uint32_t((ns - 1) >> 1) & 1, 100000000ull);
-      if (no > 0) mbar_wait(&S.o_full[(no - 1) & 1], uint32_t((no - 1) >> 1) & 1, 100000000ull);
-    }
+    if (!ok && ns > 0)
+      mbar_wait(&S.s_full[(ns - 1) & 1], uint32_t((ns - 1) >> 1) & 1, 100000000ull);
     tc_fence_before();
-    bar_and(kBarTmem, kSoftmax + 32, true);
+    bar_and(kBarTmem, kTmemBarThreads, true);
     tc_fence_after();
     tmem_dealloc(tmem, 64);
     return;
@@ -738,7 +752,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (!ok && a.err && t == 0) atomicOr(a.err, kFlagAttnWait);
   tc_fence_before();
-  bar_and(kBarTmem, kSoftmax + 32, true);
+  bar_and(kBarTmem, kTmemBarThreads, true);
 }
 
 }  // namespace
