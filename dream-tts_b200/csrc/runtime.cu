@@ -528,6 +528,68 @@ tts_status tts_topk_sample(tts_ctx* c, const float* logits, int rows, int n, con
                  "topk_sample");
 }
 
+// ---------------------------------------------------------------- codec front
+
+tts_status tts_rvq_gather(tts_ctx* c, const unsigned int* codes, int T, int ncodes, int q0,
+                          int nq, const float* tables, int entries, int dim, float* out,
+                          void* stream) {
+  if (!c || !codes || !tables || !out) return fail(TTS_ERR_INVALID_ARG, "rvq_gather: NULL argument");
+  if (T < 1 || nq < 1 || q0 < 0 || q0 + nq > ncodes || entries < 1 || dim < 1)
+    return fail(TTS_ERR_INVALID_ARG, "rvq_gather: T, nq >= 1 and q0 + nq <= ncodes");
+  DeviceGuard g(c->device);
+  return counted(launch_rvq_gather(codes, ncodes, q0, nq, tables, entries, dim, out, T, S(stream)),
+                 "rvq_gather");
+}
+
+tts_status tts_rope_rows(tts_ctx* c, float* x, int T, int ld, int col0, int heads, int hd,
+                         const float* cos_t, const float* sin_t, int pos0, void* stream) {
+  if (!c || !x || !cos_t || !sin_t) return fail(TTS_ERR_INVALID_ARG, "rope_rows: NULL argument");
+  if (T < 1 || heads < 1 || hd < 2 || hd % 2 || col0 < 0 || col0 + heads * hd > ld || pos0 < 0)
+    return fail(TTS_ERR_INVALID_ARG, "rope_rows: even hd, heads fit in the row");
+  DeviceGuard g(c->device);
+  return counted(launch_rope_rows(x, T, ld, col0, heads, hd, cos_t, sin_t, pos0, S(stream)),
+                 "rope_rows");
+}
+
+tts_status tts_window_attention(tts_ctx* c, const float* qkv, int T, int heads, int hd,
+                                int window, float scale, void* out, int out_f16, void* stream) {
+  if (!c || !qkv || !out) return fail(TTS_ERR_INVALID_ARG, "window_attention: NULL argument");
+  if (T < 1 || heads < 1 || hd < 1 || hd > 128 || window < 0)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "window_attention: T, heads >= 1, hd in 1..128");
+  DeviceGuard g(c->device);
+  return counted(launch_window_attn(qkv, T, 3 * heads * hd, heads, hd, window, scale, out,
+                                    out_f16 != 0, S(stream)),
+                 "window_attention");
+}
+
+tts_status tts_layer_norm(tts_ctx* c, const float* x, const float* w, const float* b, int rows,
+                          int dim, float eps, void* y, int y_f16, void* stream) {
+  if (!c || !x || !w || !y) return fail(TTS_ERR_INVALID_ARG, "layer_norm: NULL argument");
+  if (rows < 1 || dim < 1) return fail(TTS_ERR_INVALID_ARG, "layer_norm: empty shape");
+  DeviceGuard g(c->device);
+  return counted(launch_layer_norm(x, w, b, rows, dim, eps, y, y_f16 != 0, S(stream)),
+                 "layer_norm");
+}
+
+tts_status tts_depthwise_conv(tts_ctx* c, const float* x, int b, int L, int C, const float* w,
+                              int k, const float* bias, float* y, void* stream) {
+  if (!c || !x || !w || !y) return fail(TTS_ERR_INVALID_ARG, "depthwise: NULL argument");
+  if (b < 1 || L < 1 || C < 1 || k < 1) return fail(TTS_ERR_INVALID_ARG, "depthwise: empty shape");
+  DeviceGuard g(c->device);
+  return counted(launch_depthwise(x, w, bias, b, L, C, k, y, S(stream)), "depthwise");
+}
+
+tts_status tts_bias_act(tts_ctx* c, const float* y, int rows, int n, const float* bias, int act,
+                        const float* scale, const float* res, void* out, int out_f16,
+                        void* stream) {
+  if (!c || !y || !out) return fail(TTS_ERR_INVALID_ARG, "bias_act: NULL argument");
+  if (rows < 1 || n < 1 || act < 0 || act > 1)
+    return fail(TTS_ERR_INVALID_ARG, "bias_act: empty shape or unknown activation");
+  DeviceGuard g(c->device);
+  return counted(launch_bias_act(y, rows, n, bias, act, scale, res, out, out_f16 != 0, S(stream)),
+                 "bias_act");
+}
+
 // ---------------------------------------------------------------- stack
 
 tts_status tts_stack_create(tts_ctx* c, const tts_stack_geometry* geo, tts_stack** out) {

@@ -221,6 +221,21 @@ cudaError_t launch_predictor_finish(const uint32_t* step_codes, int stride, int 
                                     const float* code0, uint32_t* codes, float* sum,
                                     const TextFeed& text, cudaStream_t st);
 cudaError_t launch_advance_positions(int* positions, int lanes, bool pdl, cudaStream_t st);
+// The codec front's row kernels (codec_front.cu).
+cudaError_t launch_rvq_gather(const uint32_t* codes, int ncodes, int q0, int nq,
+                              const float* tables, int entries, int dim, float* out, int T,
+                              cudaStream_t st);
+cudaError_t launch_rope_rows(float* x, int T, int ld, int col0, int heads, int hd,
+                             const float* cos_t, const float* sin_t, int pos0, cudaStream_t st);
+cudaError_t launch_window_attn(const float* qkv, int T, int ld, int heads, int hd, int window,
+                               float scale, void* out, bool out_f16, cudaStream_t st);
+cudaError_t launch_layer_norm(const float* x, const float* w, const float* b, int rows, int dim,
+                              float eps, void* y, bool y_f16, cudaStream_t st);
+cudaError_t launch_depthwise(const float* x, const float* w, const float* bias, int b, int L,
+                             int C, int k, float* y, cudaStream_t st);
+cudaError_t launch_bias_act(const float* y, int rows, int n, const float* bias, int act,
+                            const float* scale, const float* res, void* out, bool out_f16,
+                            cudaStream_t st);
 // Top-k sampling (topk_sample.cu): rows of logits (row stride ldl), a draw per row (row r
 // takes draws[r % draw_rows]), codes[r * code_stride]; optionally the pick's f32 embedding row
 // into x_next and the row's position advanced (a decode step's code gather).

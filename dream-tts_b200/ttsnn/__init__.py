@@ -126,3 +126,61 @@ def abs_and_rel(a: torch.Tensor, b: torch.Tensor) -> tuple[float, float]:
     d = (a - b).abs().max().item() if a.numel() else 0.0
     s = b.abs().max().item() if b.numel() else 0.0
     return d, (d / s if s > 0 else 0.0)
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, eps: float,
+               out_f16: bool = False) -> torch.Tensor:
+    """`layer_norm` (crates/tts-nn/src/lib.rs:1006-1035): mean, centred variance, affine."""
+    dim = x.shape[-1]
+    xf = x.to(torch.float32).contiguous()
+    w = weight.to(torch.float32).contiguous()
+    b = None if bias is None else bias.to(torch.float32).contiguous()
+    y = torch.empty(xf.shape, device=x.device, dtype=torch.float16 if out_f16 else torch.float32)
+    L.call("tts_layer_norm", ctx_of(xf), ptr(xf), ptr(w), ptr(b), xf.numel() // dim, dim,
+           float(eps), ptr(y), 1 if out_f16 else 0, stream())
+    return y
+
+
+def bias_act(y: torch.Tensor, bias: torch.Tensor | None = None, gelu: bool = False,
+             scale: torch.Tensor | None = None, res: torch.Tensor | None = None,
+             out_f16: bool = False) -> torch.Tensor:
+    """A projection's f32 result finished: act(y + bias) (GELU with the exact erf,
+    `gelu_exact` lib.rs:1129), times a per-channel `scale`, plus `res`."""
+    yf = y.to(torch.float32).contiguous()
+    n = yf.shape[-1]
+    rows = yf.numel() // n
+    out = torch.empty(yf.shape, device=y.device, dtype=torch.float16 if out_f16 else torch.float32)
+    f = lambda t: None if t is None else t.to(torch.float32).contiguous()
+    b, sc, r = f(bias), f(scale), f(res)
+    L.call("tts_bias_act", ctx_of(yf), ptr(yf), rows, n, ptr(b), 1 if gelu else 0, ptr(sc),
+           ptr(r), ptr(out), 1 if out_f16 else 0, stream())
+    return out
+
+
+def gelu_exact(x: torch.Tensor) -> torch.Tensor:
+    """`gelu_exact` (crates/tts-nn/src/lib.rs:1129): 0.5 x (1 + erf(x / sqrt 2)), f32."""
+    return bias_act(x, gelu=True)
+
+
+def rope_rows(x: torch.Tensor, col0: int, heads: int, head_dim: int, cos: torch.Tensor,
+              sin: torch.Tensor, pos0: int = 0) -> None:
+    """Half-split RoPE (candle_nn::rotary_emb::rope) in place on `heads` heads of `head_dim`
+    from column `col0` of the f32 rows of x; row t at position pos0 + t."""
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise ValueError("rope_rows: x must be contiguous f32 [T, ld]")
+    T, ld = x.shape
+    L.call("tts_rope_rows", ctx_of(x), ptr(x), T, ld, int(col0), int(heads), int(head_dim),
+           ptr(cos.contiguous()), ptr(sin.contiguous()), int(pos0), stream())
+
+
+def window_attention(qkv: torch.Tensor, heads: int, head_dim: int, window: int, scale: float,
+                     out_f16: bool = True) -> torch.Tensor:
+    """Causal self-attention over one sequence with a sliding window (the prefill branch of
+    Stack::forward with causal_window_mask, qwen3.rs:409-444): qkv f32 [T, 3 heads hd]."""
+    q = qkv.to(torch.float32).contiguous()
+    T = q.shape[0]
+    out = torch.empty(T, heads * head_dim, device=q.device,
+                      dtype=torch.float16 if out_f16 else torch.float32)
+    L.call("tts_window_attention", ctx_of(q), ptr(q), T, int(heads), int(head_dim), int(window),
+           float(scale), ptr(out), 1 if out_f16 else 0, stream())
+    return out

@@ -112,6 +112,12 @@ SIGNATURES = {
     "tts_topk_sample": [P, P, I, I, P, I, F, P, P],
     "tts_predictor_set_sampling": [P, P, I, I, F],
     "tts_stack_prefill": [P, C.POINTER(DecodeState), P, P, P, P],
+    "tts_rvq_gather": [P, P, I, I, I, I, P, I, I, P, P],
+    "tts_rope_rows": [P, P, I, I, I, I, I, P, P, I, P],
+    "tts_window_attention": [P, P, I, I, I, I, F, P, I, P],
+    "tts_layer_norm": [P, P, P, P, I, I, F, P, I, P],
+    "tts_depthwise_conv": [P, P, I, I, I, P, I, P, P, P],
+    "tts_bias_act": [P, P, I, I, P, I, P, P, P, I, P],
     "tts_safetensors_open": [C.c_char_p, C.POINTER(P)],
     "tts_safetensors_count": [P],
     "tts_safetensors_at": [P, I, C.POINTER(TensorView)],

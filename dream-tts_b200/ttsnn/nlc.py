@@ -85,3 +85,17 @@ def snake_conv_residual(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, di
         return None
     y = conv1d(x, device_weight(w), bias, dilation, (k - 1) * dilation, snake=snake, res=res)
     return y if x.dtype == torch.float16 else y.to(x.dtype)
+
+
+def depthwise(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """`nlc::depthwise` (crates/tts-nn/src/nlc.rs:232-256): causal per-channel conv over
+    [b, L, C] with torch's [C, 1, k] taps, f32."""
+    xf = x.to(torch.float32).contiguous()
+    b, L_, C_ = xf.shape
+    k = w.shape[-1]
+    taps = w.reshape(C_, k).to(torch.float32).contiguous()
+    bb = None if bias is None else bias.to(torch.float32).contiguous()
+    y = torch.empty_like(xf)
+    L.call("tts_depthwise_conv", ctx_of(xf), ptr(xf), b, L_, C_, ptr(taps), k, ptr(bb), ptr(y),
+           stream())
+    return y

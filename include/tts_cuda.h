@@ -373,6 +373,43 @@ TTS_API tts_status tts_talker_frame_capture(tts_stack* talker, const tts_decode_
                                             unsigned int* code0, unsigned int* codes,
                                             void* stream, tts_graph** out);
 
+/* ---------------------------------------------------------------- codec front
+ * The ops the codec decoder's front uses besides projections and convs (crates/qwen3tts/src/
+ * codec.rs:161-196, 261-317, 403-424). All f32 unless stated, rows contiguous.
+ *
+ * Rvq::decode's lookups (codec.rs:285-299): out f32 [T][dim] = sum over q in [q0, q0 + nq) of
+ * tables[q - q0][codes[t][q]], codes u32 [T][ncodes], tables f32 [nq][entries][dim]. */
+TTS_API tts_status tts_rvq_gather(tts_ctx* ctx, const unsigned int* codes, int T, int ncodes,
+                                  int q0, int nq, const float* tables, int entries, int dim,
+                                  float* out, void* stream);
+/* candle_nn::rotary_emb::rope (half-split) in place on `heads` heads of width hd from column
+ * col0 of x [T][ld]; row t at position pos0 + t of cos/sin [positions][hd / 2]. */
+TTS_API tts_status tts_rope_rows(tts_ctx* ctx, float* x, int T, int ld, int col0, int heads,
+                                 int hd, const float* cos_t, const float* sin_t, int pos0,
+                                 void* stream);
+/* Causal (optionally windowed) self-attention over one sequence, the prefill branch of
+ * Stack::forward with causal_window_mask (qwen3.rs:409-444, lib.rs:1210-1225): qkv f32
+ * [T][3 heads hd] (q | k | v, one kv head per q head), row t attends rows [t + 1 - window, t]
+ * (window 0: all earlier rows), scores * scale; out [T][heads hd] f16 or f32. hd <= 128. */
+TTS_API tts_status tts_window_attention(tts_ctx* ctx, const float* qkv, int T, int heads, int hd,
+                                        int window, float scale, void* out, int out_f16,
+                                        void* stream);
+/* layer_norm (crates/tts-nn/src/lib.rs:1006-1035): y = (x - mean) / sqrt(var + eps) * w + b
+ * over the last dim (b may be NULL); y f32 or f16. */
+TTS_API tts_status tts_layer_norm(tts_ctx* ctx, const float* x, const float* w, const float* b,
+                                  int rows, int dim, float eps, void* y, int y_f16, void* stream);
+/* nlc::depthwise (crates/tts-nn/src/nlc.rs:232-256): causal per-channel conv of x [b][L][C]
+ * with taps w [C][k] and bias [C] (NULL = none). */
+TTS_API tts_status tts_depthwise_conv(tts_ctx* ctx, const float* x, int b, int L, int C,
+                                      const float* w, int k, const float* bias, float* y,
+                                      void* stream);
+/* The epilogue of a projection computed in f32 (Linear's bias, gelu_exact lib.rs:1129, a
+ * per-channel scale such as LayerScale or ConvNeXt's gamma, a residual): z = act(y + bias),
+ * out = res + scale * z; act 0 none, 1 GELU (erf). bias, scale, res may be NULL. */
+TTS_API tts_status tts_bias_act(tts_ctx* ctx, const float* y, int rows, int n, const float* bias,
+                                int act, const float* scale, const float* res, void* out,
+                                int out_f16, void* stream);
+
 /* ---------------------------------------------------------------- checkpoint files
  * Memory-mapped safetensors (the reference's Weights over candle's MmapedSafetensors,
  * crates/tts-nn/src/lib.rs:153-373): the header parsed at open, every tensor a view into the

@@ -517,3 +517,79 @@ def topk_sample(logits: np.ndarray, draws: np.ndarray, k: int, temperature: floa
                 break
         out[r] = pick
     return out
+
+
+# ---------------------------------------------------------------- codec front (numpy)
+def layer_norm(x: np.ndarray, w: np.ndarray, b, eps: float) -> np.ndarray:
+    """layer_norm_plain + affine (crates/tts-nn/src/lib.rs:1006-1035), f64 then f32."""
+    x = np.asarray(x, np.float64)
+    mean = x.mean(-1, keepdims=True)
+    c = x - mean
+    var = (c * c).mean(-1, keepdims=True)
+    y = c / np.sqrt(var + eps) * np.asarray(w, np.float64)
+    if b is not None:
+        y = y + np.asarray(b, np.float64)
+    return y.astype(np.float32)
+
+
+def gelu_exact(x: np.ndarray) -> np.ndarray:
+    """0.5 x (1 + erf(x / sqrt 2)) (lib.rs:1129)."""
+    from scipy.special import erf
+    x = np.asarray(x, np.float64)
+    return (0.5 * x * (1.0 + erf(x / np.sqrt(2.0)))).astype(np.float32)
+
+
+def depthwise(x: np.ndarray, w: np.ndarray, bias) -> np.ndarray:
+    """nlc::depthwise (crates/tts-nn/src/nlc.rs:232-256): x [b, L, C], w [C, k], causal."""
+    b, L, C = x.shape
+    k = w.shape[1]
+    xp = np.concatenate([np.zeros((b, k - 1, C), np.float64), np.asarray(x, np.float64)], 1)
+    y = sum(xp[:, t:t + L] * np.asarray(w[:, t], np.float64) for t in range(k))
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)
+    return y.astype(np.float32)
+
+
+def rope_rows(x: np.ndarray, col0: int, heads: int, hd: int, cos: np.ndarray,
+              sin: np.ndarray, pos0: int = 0) -> np.ndarray:
+    """Half-split rotate_half RoPE (candle_nn::rotary_emb::rope) on heads of x [T, ld]."""
+    y = np.asarray(x, np.float32).copy()
+    T = y.shape[0]
+    half = hd // 2
+    c = cos[pos0:pos0 + T][:, None, :]
+    s = sin[pos0:pos0 + T][:, None, :]
+    blk = y[:, col0:col0 + heads * hd].reshape(T, heads, hd)
+    a, b = blk[..., :half].copy(), blk[..., half:].copy()
+    blk[..., :half] = a * c - b * s
+    blk[..., half:] = b * c + a * s
+    y[:, col0:col0 + heads * hd] = blk.reshape(T, heads * hd)
+    return y
+
+
+def window_attention(qkv: np.ndarray, heads: int, hd: int, window: int, scale: float):
+    """The prefill branch of Stack::forward (qwen3.rs:409-444) with causal_window_mask
+    (lib.rs:1210-1225) for one sequence, gqa 1: qkv [T, 3 heads hd] f32, in f64."""
+    T = qkv.shape[0]
+    q = qkv[:, :heads * hd].reshape(T, heads, hd).astype(np.float64)
+    k = qkv[:, heads * hd:2 * heads * hd].reshape(T, heads, hd).astype(np.float64)
+    v = qkv[:, 2 * heads * hd:].reshape(T, heads, hd).astype(np.float64)
+    s = np.einsum("thd,jhd->htj", q, k) * scale
+    rows = np.arange(T)[:, None]
+    cols = np.arange(T)[None, :]
+    lo = rows + 1 - window if window > 0 else np.zeros_like(rows)
+    mask = (cols > rows) | (cols < lo)
+    s = np.where(mask[None], -np.inf, s)
+    s = s - s.max(-1, keepdims=True)
+    p = np.exp(s)
+    p = p / p.sum(-1, keepdims=True)
+    o = np.einsum("htj,jhd->thd", p, v)
+    return o.reshape(T, heads * hd).astype(np.float32)
+
+
+def rvq_gather(codes: np.ndarray, q0: int, tables: np.ndarray) -> np.ndarray:
+    """Rvq::decode's lookups (codec.rs:285-299): sum over the stack's codebooks, in order."""
+    nq = tables.shape[0]
+    out = np.zeros((codes.shape[0], tables.shape[2]), np.float32)
+    for q in range(nq):
+        out = out + tables[q][codes[:, q0 + q].astype(np.int64)]
+    return out
