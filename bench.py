@@ -807,6 +807,47 @@ def run_prefill(args):
     return 0
 
 
+def run_codec(args):
+    """The codec decoder at the reference's shape (codec.rs:320-424, random-init): codes
+    [T, 16] -> 24 kHz audio through the front (RVQ, pre-conv, 8-layer pre-transformer, x2 x2
+    with ConvNeXt) and the waveform stack (1536 -> 96 channels, x8 x5 x4 x3). One step = one
+    333-frame chunk window (300 frames + 25 of left context + 8 of lookahead, the chunk plan's
+    span); frames/s counts the 300 frames each window contributes."""
+    import torch
+    import ttsnn
+    from qwen3tts.codec_ref import Codec
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    codec = Codec.from_weights(Codec.synthetic_weights(seed=0).__getitem__)
+    T = 333
+    codes = torch.randint(0, 2048, (T, 16), dtype=torch.int32, device=device)
+    for _ in range(args.warmup):
+        codec(codes)
+    torch.cuda.synchronize()
+    ttsnn.check(0)
+    ttsnn.launch_count(reset=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        codec(codes)
+    e1.record()
+    torch.cuda.synchronize()
+    launches = ttsnn.launch_count()
+    s_per = e0.elapsed_time(e1) * 1e-3 / args.steps
+    print(json.dumps({
+        "metric": "codec frames/sec (reference-shape decoder, one GPU)",
+        "value": round(300 / s_per, 1), "unit": "frames/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(s_per * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (random-init weights, random codes)",
+        "config": {"workload": "codec.rs decoder: 16 codebooks x 2048, pre-transformer 8 x 512 "
+                               "(16 x 64 heads, window 72), x2 x2 ConvNeXt at 1024, waveform "
+                               "stack 1536 -> 96 at x8 x5 x4 x3; one 333-frame window",
+                   "window_frames": T},
+        "rtf": round(s_per / (300 / 12.5), 6), "gpu_launches": int(launches)}), flush=True)
+    return 0
+
+
 def run_kernel_case(args):
     """Small standalone cases of one kernel, for ncu captures (a few launches, < 1 GB)."""
     import torch
@@ -1016,7 +1057,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--workload", default="step",
-                    choices=["step", "sweep", "document", "predictor", "frames", "prefill"],
+                    choices=["step", "sweep", "document", "predictor", "frames", "prefill",
+                             "codec"],
                     help="step: the config[2] decode step (headline); sweep: config[3]; "
                          "document: a bounded config[4] sample (talker + codec); predictor: "
                          "the depth predictor's frame; frames: the reference's talker loop "
@@ -1043,6 +1085,8 @@ def main():
         return run_frames(args)
     if args.workload == "prefill":
         return run_prefill(args)
+    if args.workload == "codec":
+        return run_codec(args)
     return run_b200(args)
 
 

@@ -139,3 +139,10 @@ def load_predictor(w: Weights, device="cuda", geo: Geometry = PREDICTOR_GEOMETRY
                           for i in range(steps)]).to(device)
     return Predictor(stack, w.cpu(f"{p}.small_to_mtp_projection.weight").to(device),
                      w.get(f"{p}.small_to_mtp_projection.bias", device), heads, tables)
+
+
+def load_codec(w: Weights, device="cuda"):
+    """`Codec::load` (codec.rs:320-395): the whole decoder from its checkpoint names (folded
+    codebooks, pre-transformer, upsamplers, waveform stack)."""
+    from .codec_ref import Codec
+    return Codec.from_weights(w.cpu, device)
