@@ -169,7 +169,8 @@ __global__ void depthwise_kernel(const float* x, const float* w, const float* bi
 }
 
 // Row epilogue for projections computed in f32: z = act(y + bias); out = res + scale * z (res
-// and scale optional), f32 or f16 out. act 1 is GELU with the exact erf (lib.rs:1129).
+// and scale optional), f32 or f16 out. act 1 is GELU with the exact erf (lib.rs:1129), act 2
+// SiLU (the text projection's, talker.rs:607-616).
 __global__ void bias_act_kernel(const float* y, int rows, int n, const float* bias, int act,
                                 const float* scale, const float* res, void* out, int out_f16) {
   const long total = (long)rows * n;
@@ -178,6 +179,7 @@ __global__ void bias_act_kernel(const float* y, int rows, int n, const float* bi
     const int c = int(e % n);
     float z = y[e] + (bias ? bias[c] : 0.f);
     if (act == 1) z = 0.5f * z * (1.f + erff(z * 0.70710678118654752f));
+    else if (act == 2) z = z / (1.f + expf(-z));  // silu, candle_nn::ops::silu
     if (scale) z = scale[c] * z;
     if (res) z = res[e] + z;
     if (out_f16)

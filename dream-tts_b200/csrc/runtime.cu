@@ -583,7 +583,7 @@ tts_status tts_bias_act(tts_ctx* c, const float* y, int rows, int n, const float
                         const float* scale, const float* res, void* out, int out_f16,
                         void* stream) {
   if (!c || !y || !out) return fail(TTS_ERR_INVALID_ARG, "bias_act: NULL argument");
-  if (rows < 1 || n < 1 || act < 0 || act > 1)
+  if (rows < 1 || n < 1 || act < 0 || act > 2)
     return fail(TTS_ERR_INVALID_ARG, "bias_act: empty shape or unknown activation");
   DeviceGuard g(c->device);
   return counted(launch_bias_act(y, rows, n, bias, act, scale, res, out, out_f16 != 0, S(stream)),

@@ -143,16 +143,16 @@ def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
 
 def bias_act(y: torch.Tensor, bias: torch.Tensor | None = None, gelu: bool = False,
              scale: torch.Tensor | None = None, res: torch.Tensor | None = None,
-             out_f16: bool = False) -> torch.Tensor:
+             out_f16: bool = False, silu: bool = False) -> torch.Tensor:
     """A projection's f32 result finished: act(y + bias) (GELU with the exact erf,
-    `gelu_exact` lib.rs:1129), times a per-channel `scale`, plus `res`."""
+    `gelu_exact` lib.rs:1129, or SiLU), times a per-channel `scale`, plus `res`."""
     yf = y.to(torch.float32).contiguous()
     n = yf.shape[-1]
     rows = yf.numel() // n
     out = torch.empty(yf.shape, device=y.device, dtype=torch.float16 if out_f16 else torch.float32)
     f = lambda t: None if t is None else t.to(torch.float32).contiguous()
     b, sc, r = f(bias), f(scale), f(res)
-    L.call("tts_bias_act", ctx_of(yf), ptr(yf), rows, n, ptr(b), 1 if gelu else 0, ptr(sc),
+    L.call("tts_bias_act", ctx_of(yf), ptr(yf), rows, n, ptr(b), 2 if silu else (1 if gelu else 0), ptr(sc),
            ptr(r), ptr(out), 1 if out_f16 else 0, stream())
     return out
 

@@ -405,7 +405,8 @@ TTS_API tts_status tts_depthwise_conv(tts_ctx* ctx, const float* x, int b, int L
                                       void* stream);
 /* The epilogue of a projection computed in f32 (Linear's bias, gelu_exact lib.rs:1129, a
  * per-channel scale such as LayerScale or ConvNeXt's gamma, a residual): z = act(y + bias),
- * out = res + scale * z; act 0 none, 1 GELU (erf). bias, scale, res may be NULL. */
+ * out = res + scale * z; act 0 none, 1 GELU (erf), 2 SiLU (the text projection's, talker.rs:
+ * 607-616). bias, scale, res may be NULL. */
 TTS_API tts_status tts_bias_act(tts_ctx* ctx, const float* y, int rows, int n, const float* bias,
                                 int act, const float* scale, const float* res, void* out,
                                 int out_f16, void* stream);
