@@ -55,6 +55,13 @@ struct GemmArgs {
   int codebooks;
   PickRule pick;  // EPI_ARGMAX: the talker's pick rule (words == 0: none)
   L2Prefetch pf;  // the next GEMM's first weight blocks
+  // deferred RMSNorm (GemmRequest): producer outputs, consumer row scales
+  const float* norm_w;
+  __half* norm_x16;
+  float* ss_out;
+  const float* ss_in;
+  int ss_tiles;
+  float ss_inv_dim, ss_eps;
 };
 
 
@@ -260,8 +267,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---------------- reduce this CTA's rows across the cluster, in rank order. Rows go four at a
   // time: all their loads (and any residual reads) are issued before the first store.
+  // deferred norm, producer side: this lane's 4 columns of the next norm's weight
+  const float4 nw4 = a.norm_w ? *reinterpret_cast<const float4*>(a.norm_w + tile * kTileM + 4 * lane)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
   for (int j0 = j_first; j0 < a.m; j0 += 4 * stride) {
     float4 acc4[4];
+    // consumer side: lane t < ss_tiles loads tile t's partial sum of squares of row j, issued
+    // ahead of the DSMEM reads (the previous kernel wrote them: L2 reads)
+    float ssp[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = j0 + u * stride;
+      ssp[u] = a.ss_in && j < a.m && lane < a.ss_tiles ? __ldcg(a.ss_in + (size_t)lane * a.m + j)
+                                                       : 0.f;
+    }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int j = j0 + u * stride;
@@ -279,6 +298,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc4[u].z += p.z;
           acc4[u].w += p.w;
         }
+      }
+      if (a.ss_in) {
+        // j is uniform across the warp: every lane takes this branch together
+        const float inv = 1.f / sqrtf(warp_sum(ssp[u]) * a.ss_inv_dim + a.ss_eps);
+        acc4[u].x *= inv;
+        acc4[u].y *= inv;
+        acc4[u].z *= inv;
+        acc4[u].w *= inv;
       }
     }
     if (a.epi == EPI_RESIDUAL) {
@@ -305,6 +332,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         r.w += acc4[u].w;
         *reinterpret_cast<float4*>(static_cast<float*>(a.y) + (size_t)j * a.ldy + tile * kTileM +
                                    4 * lane) = r;
+        if (a.norm_w) {
+          __half2* d = reinterpret_cast<__half2*>(a.norm_x16 + (size_t)j * a.n + tile * kTileM +
+                                                  4 * lane);
+          d[0] = __floats2half2_rn(r.x * nw4.x, r.y * nw4.y);
+          d[1] = __floats2half2_rn(r.z * nw4.z, r.w * nw4.w);
+          const float ss = warp_sum(r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w);
+          if (lane == 0) a.ss_out[(size_t)tile * a.m + j] = ss;
+        }
       }
     } else {
 #pragma unroll
@@ -478,6 +513,11 @@ cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t
     set_error("proj: shared-memory plan exceeds 227 KB for this lane count");
     return cudaErrorInvalidValue;
   }
+  if ((r.norm_w && (r.epi != EPI_RESIDUAL || !r.norm_x16 || !r.ss_out)) ||
+      (r.ss_in && (r.ss_tiles < 1 || r.ss_tiles > 32 || r.ss_dim < 1))) {
+    set_error("proj: deferred norm needs EPI_RESIDUAL with x16 and ss outputs, 1..32 ss tiles");
+    return cudaErrorInvalidValue;
+  }
   CUtensorMap tmW, tmX;
   const bool wmap_ok =
       r.packed ? make_tmap_2d_f16(&tmW, r.w, kBlockK, uint64_t(r.n) / kTileM * (r.k / kBlockK) * kTileM,
@@ -512,6 +552,13 @@ cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t
   a.codebooks = r.vocab > 0 ? r.n / r.vocab : 0;
   a.pick = r.pick;
   a.pf = r.next;
+  a.norm_w = r.norm_w;
+  a.norm_x16 = r.norm_x16;
+  a.ss_out = r.ss_out;
+  a.ss_in = r.ss_in;
+  a.ss_tiles = r.ss_tiles;
+  a.ss_inv_dim = r.ss_dim > 0 ? 1.f / float(r.ss_dim) : 0.f;
+  a.ss_eps = r.ss_eps;
 
   {
     // The opt-in shared-memory limit is a per-device function attribute.

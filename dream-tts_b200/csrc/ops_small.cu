@@ -67,6 +67,34 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* x, const flo
   }
 }
 
+// The deferred norm's first stage (the step input's rows): y16 = f16(x * w) and ss = the row's
+// sum of squares; the projection that reads y16 divides its outputs by the row's RMS.
+__global__ void __launch_bounds__(256) norm_defer_kernel(const float* x, const float* w, int dim,
+                                                         __half* y16, float* ss_out) {
+  __shared__ float red[8];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int row = blockIdx.x;
+  const float* xr = x + (size_t)row * dim;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 4; i < dim; i += blockDim.x * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(xr + i);
+    const float4 g = *reinterpret_cast<const float4*>(w + i);
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    __half2* d = reinterpret_cast<__half2*>(y16 + (size_t)row * dim + i);
+    d[0] = __floats2half2_rn(v.x * g.x, v.y * g.y);
+    d[1] = __floats2half2_rn(v.z * g.z, v.w * g.w);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) ss_out[row] = t;
+  }
+}
+
 // a4 standalone: one warp per (lane, head) over qkv [lanes][(heads + 2 n_kv) * 128] f32.
 __global__ void __launch_bounds__(128) qk_rope_kernel(const float* qkv, QkRopeArgs a, int lanes) {
   pdl_launch_dependents();
@@ -280,6 +308,17 @@ cudaError_t launch_rms_norm(const float* x, const float* w, int rows, int dim, f
   void* args[] = {(void*)&x, (void*)&w, (void*)&dim, (void*)&eps, (void*)&y32,
                   (void*)&y16, (void*)&zero_keys, (void*)&n_keys};
   return launch_ex(reinterpret_cast<void (*)(void*)>(rms_norm_kernel), dim3(rows), dim3(256),
+                   st, pdl, args);
+}
+
+cudaError_t launch_norm_defer(const float* x, const float* w, int rows, int dim, __half* y16,
+                              float* ss, bool pdl, cudaStream_t st) {
+  if (dim % 4 != 0 || rows < 1) {
+    set_error("norm_defer: dim must be a multiple of 4 and rows >= 1");
+    return cudaErrorInvalidValue;
+  }
+  void* args[] = {(void*)&x, (void*)&w, (void*)&dim, (void*)&y16, (void*)&ss};
+  return launch_ex(reinterpret_cast<void (*)(void*)>(norm_defer_kernel), dim3(rows), dim3(256),
                    st, pdl, args);
 }
 

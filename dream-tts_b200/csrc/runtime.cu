@@ -61,6 +61,12 @@ struct tts_stack {
   __half* act = nullptr;      // [max_lanes][ffn]
   float* x_next = nullptr;    // [max_lanes][dim] (own buffer)
   float* feedback = nullptr;  // caller's buffer replacing x_next, or null
+  // Deferred RMSNorm (on unless TTS_DEFER_NORM=0): the O and down projections' epilogues
+  // write the next norm's f16 input h * w and per-tile row sums of squares `ss`
+  // [dim / 128][max_lanes]; the QKV and gate/up projections scale their rows by 1 / RMS. The
+  // step then runs no norm kernel between layers (one for the input, one final).
+  float* ss = nullptr;
+  bool defer_norm = true;
   PickRule pick;              // the codec head's greedy pick rule (words == 0: plain argmax)
   // prefill scratch, grown on demand by tts_stack_prefill: per-row (lane, offset) pairs and
   // lane lengths; per-row block-table rows and positions for one chunk of rows
@@ -628,6 +634,11 @@ tts_status tts_stack_create(tts_ctx* c, const tts_stack_geometry* geo, tts_stack
   if (e == cudaSuccess) e = dmalloc(&s->act, size_t(L) * gm.ffn * 2);
   if (e == cudaSuccess) e = dmalloc(&s->x_next, size_t(L) * gm.dim * 4);
   if (e == cudaSuccess) e = dmalloc(&s->keys, size_t(L) * std::max(1, gm.codebooks) * 8);
+  if (e == cudaSuccess) e = dmalloc(&s->ss, size_t(L) * std::max(1, gm.dim / 128) * 4);
+  {
+    const char* env = getenv("TTS_DEFER_NORM");
+    s->defer_norm = !(env && *env == '0') && gm.dim % 128 == 0 && gm.dim / 128 <= 32;
+  }
   if (e == cudaSuccess) e = cudaMemset(s->keys, 0, size_t(L) * std::max(1, gm.codebooks) * 8);
   if (e == cudaSuccess) e = cudaMemset(s->x_next, 0, size_t(L) * gm.dim * 4);
   // the layer chain serves steps of up to kMaxChainLanes lanes
@@ -720,6 +731,7 @@ tts_status tts_stack_destroy(tts_stack* s) {
   cudaFree(s->act);
   cudaFree(s->x_next);
   cudaFree(s->keys);
+  cudaFree(s->ss);
   cudaFree(s->chain.part);
   cudaFree(s->chain.done);
   cudaFree(s->chain.exit_cnt);
@@ -966,29 +978,57 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
                                    hsel ? nullptr : &s->pick, true, cs),
               "keys_to_codes");
   } else {
+    // RMSNorm deferred into the projections: the norm's input is f16(h * w), the projection's
+    // rows are divided by the RMS in its epilogue, and the O and down projections produce the
+    // next norm's input and sums of squares (every row is complete in their epilogues)
+    const bool defer = s->defer_norm;
+    const int ss_tiles = D / 128;
+    auto consume = [&](GemmRequest& r, int tiles) {
+      r.ss_in = s->ss;
+      r.ss_tiles = tiles;
+      r.ss_dim = D;
+      r.ss_eps = gm.eps;
+    };
+    auto produce = [&](GemmRequest& r, const float* norm_w) {
+      r.norm_w = norm_w;
+      r.norm_x16 = s->xn;
+      r.ss_out = s->ss;
+    };
+    if (defer)
+      TTS_TRY(launch_norm_defer(s->h, s->layers[0].attn_norm, B, D, s->xn, s->ss, true, cs),
+              "rms_norm");
     for (int l = 0; l < gm.layers; ++l) {
       const tts_layer_weights& w = s->layers[l];
       // attention block (qwen3.rs:339-451)
-      TTS_TRY(launch_rms_norm(s->h, w.attn_norm, B, D, gm.eps, nullptr, s->xn, nullptr, 0, true, cs),
-              "rms_norm");
-      TTS_TRY(launch_gemm(req_qkv(l), c->gemm, cs, c->device), "proj");
+      if (!defer)
+        TTS_TRY(launch_rms_norm(s->h, w.attn_norm, B, D, gm.eps, nullptr, s->xn, nullptr, 0, true,
+                                cs),
+                "rms_norm");
+      GemmRequest qkv = req_qkv(l);
+      if (defer) consume(qkv, l == 0 ? 1 : ss_tiles);
+      TTS_TRY(launch_gemm(qkv, c->gemm, cs, c->device), "proj");
       AttnRequest ar = req_attn(l);
       ar.next = pf(w.wo, qw, D);
       TTS_TRY(launch_attn(ar, c->attn, cs), "decode_attention");
       GemmRequest o = req_o(l);
       o.next = pf(w.w_gate_up, D, 2 * gm.ffn);
+      if (defer) produce(o, w.ffn_norm);
       TTS_TRY(launch_gemm(o, c->gemm, cs, c->device), "proj");
       // feed-forward block (qwen3.rs:453-463)
-      TTS_TRY(launch_rms_norm(s->h, w.ffn_norm, B, D, gm.eps, nullptr, s->xn, nullptr, 0, true, cs),
-              "rms_norm");
+      if (!defer)
+        TTS_TRY(launch_rms_norm(s->h, w.ffn_norm, B, D, gm.eps, nullptr, s->xn, nullptr, 0, true,
+                                cs),
+                "rms_norm");
       GemmRequest gu = req_gu(l);
       gu.next = pf(w.w_down, gm.ffn, D);
+      if (defer) consume(gu, ss_tiles);
       TTS_TRY(launch_gemm(gu, c->gemm, cs, c->device), "proj");
       GemmRequest dn = req_dn(l);
       if (l + 1 < gm.layers)
         dn.next = pf(s->layers[l + 1].wqkv, D, nqkv);
       else if (heads)
         dn.next = pf(heads, D, gm.codebooks * gm.vocab);
+      if (defer && l + 1 < gm.layers) produce(dn, s->layers[l + 1].attn_norm);
       TTS_TRY(launch_gemm(dn, c->gemm, cs, c->device), "proj");
     }
     // final norm (qwen3.rs:466), heads + greedy pick, next input

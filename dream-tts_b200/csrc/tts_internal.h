@@ -102,6 +102,17 @@ struct GemmRequest {
   bool pdl = true;
   int force_splits = 0;  // 0 = automatic
   L2Prefetch next;       // optional: the next GEMM's first weight blocks
+  // Deferred RMSNorm. Producer (EPI_RESIDUAL): with norm_w set, the epilogue also writes
+  // norm_x16[j] = f16(h[j] * norm_w) (the next projection's x, [m][n]) and, per 128-column
+  // tile t, ss_out[t * m + j] = the sum of squares of h[j]'s columns in that tile. Consumer:
+  // with ss_in set, every output row j is scaled by 1 / sqrt(sum_t ss_in[t * m + j] / ss_dim +
+  // ss_eps) (t < ss_tiles <= 32) before its epilogue, which completes RMSNorm(h) . W^T.
+  const float* norm_w = nullptr;
+  __half* norm_x16 = nullptr;
+  float* ss_out = nullptr;
+  const float* ss_in = nullptr;
+  int ss_tiles = 0, ss_dim = 0;
+  float ss_eps = 0.f;
 };
 
 struct Workspace {
@@ -187,6 +198,10 @@ size_t attn_static_part_limit();
 int attn_static_counter_limit();
 
 // ------------------------------------------------------------------ small kernels
+// The deferred norm's first stage for rows that no projection produced (the step's input):
+// y16[r] = f16(x[r] * w) and ss[r] = the sum of squares of x[r] (one tile: ss_tiles = 1).
+cudaError_t launch_norm_defer(const float* x, const float* w, int rows, int dim, __half* y16,
+                              float* ss, bool pdl, cudaStream_t st);
 cudaError_t launch_rms_norm(const float* x, const float* w, int rows, int dim, float eps,
                             float* y32, __half* y16, unsigned long long* zero_keys, int n_keys,
                             bool pdl, cudaStream_t st);
