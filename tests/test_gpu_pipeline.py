@@ -13,11 +13,8 @@ from _model import dev_f16, dev_f32, device_predictor, device_stack, make_heads,
 pytestmark = pytest.mark.gpu
 
 
-def test_text_to_audio(tt, orc):
-    from qwen3tts import reference_pick
+def _models(orc):
     from qwen3tts.codec_ref import Codec
-    from qwen3tts.frames import CODEC_EOS, MIN_NEW_TOKENS, REPETITION_PENALTY
-    from qwen3tts.pipeline import Request, Synthesizer
     from qwen3tts.prompt import PromptBuilder, TextProjection
     rng = np.random.default_rng(81)
     dim = 256
@@ -38,6 +35,15 @@ def test_text_to_audio(tt, orc):
                  rates=(2, 2, 2, 2), codebook=2048, inner=64, codebook_dim=128)
     codec = Codec.from_weights(Codec.synthetic_weights(seed=5, **small).__getitem__,
                                rates=small["rates"])
+    return rng, dim, g, Ls, final, head, embed, talker, pg, pLs, pfinal, pw, pred, builder, codec
+
+
+def test_text_to_audio(tt, orc):
+    from qwen3tts import reference_pick
+    from qwen3tts.frames import CODEC_EOS, MIN_NEW_TOKENS, REPETITION_PENALTY
+    from qwen3tts.pipeline import Request, Synthesizer
+    (rng, dim, g, Ls, final, head, embed, talker, pg, pLs, pfinal, pw, pred, builder,
+     codec) = _models(orc)
     synth = Synthesizer(talker, pred, builder, reference_pick(lanes=8), codec, max_lanes=8,
                         capacity=256)
     reqs = [Request([100, 200, 300, 400], spk=torch.randn(dim, device="cuda") * 0.05, max_frames=5),
@@ -76,3 +82,39 @@ def test_text_to_audio(tt, orc):
     wav = synth.decode(frames[0])
     torch.cuda.synchronize()
     assert wav.shape[0] == len(frames[0]) * 64 and torch.isfinite(wav).all()
+
+
+def test_engine_over_the_pipeline(tt, orc):
+    """The engine's schedule (crates/qwen3tts/src/engine.rs:919-1011) over two synthesizers: a
+    batched pool sized for the batch cap and a one-lane pool for the full budget. A run whose
+    lanes reach the cap is redone one segment at a time; every segment's frames then equal the
+    one-lane pool's own output for it."""
+    from qwen3tts import reference_pick
+    from qwen3tts.engine import Engine
+    from qwen3tts.pipeline import Request, Synthesizer
+    (rng, dim, g, Ls, final, head, embed, talker, pg, pLs, pfinal, pw, pred, builder,
+     codec) = _models(orc)
+    batched = Synthesizer(talker, pred, builder, reference_pick(lanes=8), max_lanes=8,
+                          capacity=128)
+    single = Synthesizer(talker, pred, builder, reference_pick(lanes=1), max_lanes=1,
+                         capacity=128)
+    spk = torch.randn(dim, device="cuda") * 0.05
+    reqs = [Request([100 + i, 200, 300 + 7 * i][: 1 + i % 3], spk=spk) for i in range(4)]
+    widths = [builder.build(r.text, spk=r.spk)[0].shape[0] for r in reqs]
+    chars = [50, 80, 20, 80]
+    eng = Engine(batched.generate, lambda r: single.generate([r])[0], budget=7, batch_cap=5)
+    out = eng.run(reqs, widths, chars)
+    torch.cuda.synchronize()
+    tt.check()
+    import dataclasses
+    assert eng.log and all(lg.budgets == [5] * len(lg.segments) for lg in eng.log)
+    for lg in eng.log:
+        if lg.rerun:  # some lane reached the cap: each segment redone with the full budget
+            for i in lg.segments:
+                assert single.generate([dataclasses.replace(reqs[i], max_frames=7)])[0] == out[i]
+        else:         # every lane ended below the cap: the batched run's own frames
+            again = batched.generate([dataclasses.replace(reqs[i], max_frames=5)
+                                      for i in lg.segments])
+            assert again == [out[i] for i in lg.segments]
+            assert all(len(out[i]) < 5 for i in lg.segments)
+    assert all(1 <= len(f) <= 7 for f in out)
