@@ -1049,6 +1049,102 @@ def run_b200(args):
     return 0
 
 
+def run_timeline(args):
+    """Per-CTA phase timeline of one captured config[2] step, from the tracing library (build
+    it with `python dream-tts_b200/build.py --timeline`; run with TTS_LIB=dream-tts_b200/ttsnn/
+    libtts_cuda_tl.so). For each kernel of layers 5 and 20: first CTA entry, dependency release
+    (first/last CTA), main loop done and cross-CTA reduction done (GEMMs), end (median/max over
+    CTAs; for the attention the later of the compute end and the split-pair merges), in us from
+    the layer's first record. Each CTA takes its end time before writing its records; the log's
+    one atomic per CTA still delays its exit a little, so a traced step runs somewhat long."""
+    import ctypes as C
+
+    import torch
+
+    import ttsnn
+    from ttsnn import _lib as L
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cnt = C.c_int(0)
+    if L.load().tts_timeline_read(None, 0, C.byref(cnt), 1) != 0:
+        raise SystemExit("timeline: needs the tracing library (TTS_LIB=.../libtts_cuda_tl.so): "
+                         + L.last_error())
+    stack, kv, lengths, cap = build_device_talker(dev, seed=0, extra_positions=64)
+    codes = torch.zeros(LANES, CB, dtype=torch.int32, device=dev)
+    x = torch.randn(LANES, DIM, device=dev)
+    s = torch.cuda.Stream(dev)
+    with torch.cuda.stream(s):
+        stack.decode_step(kv, x, codes=codes, max_span=cap)
+        g = stack.capture(kv, x, codes=codes, max_span=cap)
+        for _ in range(3):
+            g.replay()
+        s.synchronize()
+        L.call("tts_timeline_read", None, 0, C.byref(cnt), 1)
+        g.replay()
+        s.synchronize()
+    ttsnn.check(0)
+    cap_rec = 1 << 17
+    buf = (C.c_ulonglong * (cap_rec * 4))()
+    L.call("tts_timeline_read", buf, cap_rec, C.byref(cnt), 0)
+    a = np.frombuffer(buf, dtype=np.uint64).reshape(cap_rec, 4)[:cnt.value].astype(np.int64)
+    layers = stack.geo.layers
+    GEMM, ATTN = 0x100, 0x200
+
+    def runs(first_kind):
+        """[launch][cta][record] of the contiguous runs that start with `first_kind`, launches in
+        time order, split evenly (a kernel's grid is the same in every layer)."""
+        idx = np.nonzero(a[:, 0] == first_kind)[0]
+        idx = idx[np.argsort(a[idx, 2])]
+        return idx
+
+    def gemm_phases(epi, n_launch, pick=None):
+        idx = runs(GEMM | epi << 4)
+        per = len(idx) // n_launch
+        out = [idx[i * per:(i + 1) * per] for i in range(n_launch)]
+        return out if pick is None else out[pick::2]
+
+    qkv = gemm_phases(4, layers)
+    gu = gemm_phases(3, layers)
+    o = gemm_phases(2, 2 * layers, 0)
+    dn = gemm_phases(2, 2 * layers, 1)
+    att = runs(ATTN)
+    per = len(att) // layers
+    att = [att[i * per:(i + 1) * per] for i in range(layers)]
+    mg = np.nonzero(a[:, 0] == ATTN | 4)[0]
+    mg = mg[(mg + 1 < len(a)) & (a[np.minimum(mg + 1, len(a) - 1), 0] == ATTN | 5)]
+    merged = {}
+    for i in mg:  # (cta, time) of merge runs, assigned to a launch by time below
+        merged.setdefault(int(a[i, 1]), []).append(int(a[i + 1, 1]))
+    out = {"records": int(cnt.value), "layers": {}}
+    for li in (5, 20):
+        t0 = a[qkv[li], 1].min()
+        f = lambda v: round(float((v - t0) / 1e3), 2)
+        rows = {}
+        for name, idx in (("qkv", qkv[li]), ("attn", att[li]), ("o", o[li]), ("gate/up", gu[li]),
+                          ("down", dn[li])):
+            row = {"entry": f(a[idx, 1].min()),
+                   "released": [f(a[idx + 1, 1].min()), f(a[idx + 1, 1].max())]}
+            if name == "attn":
+                end = a[idx + 3, 1].copy()
+                lo, hi = a[idx + 1, 1].min(), end.max() + 20_000
+                for j, c in enumerate(a[idx + 2, 1]):
+                    for t in merged.get(int(c), []):
+                        if lo <= t <= hi:
+                            end[j] = max(end[j], t)
+                row["end"] = [f(np.median(end)), f(end.max())]
+                row["cta_end_p10_p90"] = [f(np.percentile(end, 10)), f(np.percentile(end, 90))]
+            else:
+                row["main_done"] = [f(np.median(a[idx + 2, 1])), f(a[idx + 2, 1].max())]
+                row["reduced"] = [f(np.median(a[idx + 3, 1])), f(a[idx + 3, 1].max())]
+                row["end"] = [f(np.median(a[idx + 4, 1])), f(a[idx + 4, 1].max())]
+            rows[name] = row
+        out["layers"][str(li)] = rows
+        print(f"layer {li} (us from the QKV projection's first CTA):", file=sys.stderr)
+        for name, row in rows.items():
+            print(f"  {name:8s} " + "  ".join(f"{k} {v}" for k, v in row.items()), file=sys.stderr)
+    print(json.dumps({"timeline": "config[2] step", **out}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1068,6 +1164,8 @@ def main():
     ap.add_argument("--refill", action="store_true")
     ap.add_argument("--kernel", choices=["gemm", "attn", "attn_short", "conv"],
                     help="run a small standalone case of one kernel (for ncu captures)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="per-CTA phase timeline of one step (needs the tracing library)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1075,6 +1173,8 @@ def main():
         return run_reference(args)
     if args.kernel:
         return run_kernel_case(args)
+    if args.timeline:
+        return run_timeline(args)
     if args.workload == "sweep":
         return run_sweep(args)
     if args.workload == "document":

@@ -46,39 +46,52 @@ def _inputs() -> list[str]:
             + [os.path.join(INCLUDE, "tts_cuda.h")])
 
 
-def up_to_date() -> bool:
-    if not os.path.exists(OUT):
+# The tracing variant: the same sources with per-CTA timeline records (TTS_TIMELINE; the
+# records live in one device buffer, so the objects are relocatable and device-linked).
+OUT_TIMELINE = os.path.join(HERE, "ttsnn", "libtts_cuda_tl.so")
+
+
+def up_to_date_at(out: str) -> bool:
+    if not os.path.exists(out):
         return False
-    t = os.path.getmtime(OUT)
+    t = os.path.getmtime(out)
     return all(os.path.getmtime(p) <= t for p in _inputs())
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and up_to_date():
-        return OUT
-    objdir = os.path.join(HERE, "_build")
+def up_to_date() -> bool:
+    return up_to_date_at(OUT)
+
+
+def build(force: bool = False, verbose: bool = False, timeline: bool = False) -> str:
+    out = OUT_TIMELINE if timeline else OUT
+    if not force and up_to_date_at(out):
+        return out
+    objdir = os.path.join(HERE, "_build_tl" if timeline else "_build")
     os.makedirs(objdir, exist_ok=True)
+    extra = ["-rdc=true", "-DTTS_TIMELINE"] if timeline else []
     objs = []
     for s in SOURCES:
         obj = os.path.join(objdir, os.path.splitext(s)[0] + ".o")
-        cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-c", os.path.join(CSRC, s), "-o", obj]
+        cmd = [nvcc(), *NVCC_FLAGS, *extra, "-I", INCLUDE, "-c", os.path.join(CSRC, s), "-o", obj]
         if verbose:
             print(" ".join(cmd))
         subprocess.run(cmd, check=True)
         objs.append(obj)
-    tmp = OUT + ".tmp"
+    tmp = out + ".tmp"
     # --no-undefined: a symbol missing from the objects fails the build, not the first load
-    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xlinker",
-           "--no-undefined", "-o", tmp, *objs]
+    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", *extra[:1],
+           "-Xlinker", "--no-undefined", "-o", tmp, *objs]
     subprocess.run(cmd, check=True)
-    os.replace(tmp, OUT)
-    return OUT
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
+    ap.add_argument("--timeline", action="store_true",
+                    help="build the tracing variant ttsnn/libtts_cuda_tl.so")
     args = ap.parse_args()
-    print(build(force=args.force, verbose=args.verbose))
+    print(build(force=args.force, verbose=args.verbose, timeline=args.timeline))
     sys.exit(0)

@@ -165,6 +165,7 @@ template <int GQA>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+  [[maybe_unused]] const unsigned long long tl_entry = TTS_TL_NOW();
   extern __shared__ uint8_t smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -201,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     reinterpret_cast<uint4*>(&S.qb[0][0][0])[i] = make_uint4(0, 0, 0, 0);
 
   pdl_wait();
+  [[maybe_unused]] const unsigned long long tl_rel = TTS_TL_NOW();
   // ---- spans and the chunk-list offsets of every lane
   for (int b = t; b < a.lanes; b += kThreads) {
     int span = a.spans[b] + a.span_add;
@@ -433,6 +435,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     bar_and(kBarTmem, kTmemBarThreads, true);
     tc_fence_after();
     tmem_dealloc(tmem, 64);
+#ifdef TTS_TIMELINE
+    // the score warp releases TMEM after every chunk's softmax and output MMA: compute ends
+    if (lane == 0) {
+      const uint64_t t_end = TTS_TL_NOW();
+      timeline_recs<4>({kTlAttn | kTlEntry, kTlAttn | kTlReleased, kTlAttn | kTlCta,
+                        kTlAttn | kTlEnd},
+                       {tl_entry, tl_rel, uint64_t(blockIdx.x), t_end});
+    }
+#endif
     return;
   }
 
@@ -514,6 +525,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (lane == 0) a.counters[b * a.n_kv + h] = 0u;
     }
+#ifdef TTS_TIMELINE
+    // the split pairs' merges (this warp's last work; it has none when no pair ends here)
+    if (lane == 0) {
+      const uint64_t t_end = TTS_TL_NOW();
+      timeline_recs<2>({kTlAttn | kTlCta, kTlAttn | kTlMerged}, {uint64_t(blockIdx.x), t_end});
+    }
+#endif
     return;
   }
 

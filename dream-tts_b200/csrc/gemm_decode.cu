@@ -70,6 +70,8 @@ constexpr int kThreads = 256;  // 8 warps: 0..3 producers, 4..7 MMA issuers + ep
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmX, const GemmArgs a) {
+  [[maybe_unused]] const unsigned long long tl_entry = TTS_TL_NOW();
+  [[maybe_unused]] unsigned long long tl_rel = 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -138,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       pdl_wait();  // x is the previous kernel's output
+      if (pp == 0) tl_rel = TTS_TL_NOW();
       if (elect_one()) {
         for (int i = 0; i < pre; ++i) {
           const int kb = kb0 + pp + i * P;
@@ -210,6 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool ok = mbar_wait(done, 0);
   if (!ok && threadIdx.x == 128) atomicOr(a.err, 4);
   tc_fence_after();
+  [[maybe_unused]] const unsigned long long tl_main = TTS_TL_NOW();
   // The producers waited for the previous kernel before loading x, so this returns at once;
   // the residual rows this thread will add are read now, behind the TMEM and cluster steps.
   pdl_wait();
@@ -263,6 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     cluster_sync();
   else
     __syncthreads();
+  [[maybe_unused]] const unsigned long long tl_red = TTS_TL_NOW();
   if (warp == 4) tmem_dealloc(tmem, a.tmem_cols);
 
   // ---------------- reduce this CTA's rows across the cluster, in rank order. Rows go four at a
@@ -350,6 +355,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (S > 1) cluster_sync();  // no CTA leaves while another may still read its shared memory
+#ifdef TTS_TIMELINE
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t_end = TTS_TL_NOW();
+    const int k = kTlGemm | (a.epi << 4);
+    timeline_recs<5>({k | kTlEntry, k | kTlReleased, k | kTlMainDone, k | kTlReduced, k | kTlEnd},
+                     {tl_entry, tl_rel, tl_main, tl_red, t_end});
+  }
+#endif
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {

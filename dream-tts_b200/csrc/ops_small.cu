@@ -29,9 +29,11 @@ cudaError_t launch_ex(void (*kernel)(void*), dim3 grid, dim3 block, cudaStream_t
 __global__ void __launch_bounds__(256) rms_norm_kernel(const float* x, const float* w, int dim,
                                                        float eps, float* y32, __half* y16,
                                                        unsigned long long* keys, int n_keys) {
+  [[maybe_unused]] const unsigned long long tl_entry = TTS_TL_NOW();
   __shared__ float red[8];
   pdl_launch_dependents();
   pdl_wait();
+  [[maybe_unused]] const unsigned long long tl_rel = TTS_TL_NOW();
   const int row = blockIdx.x;
   const float* xr = x + (size_t)row * dim;
   float ss = 0.f;
@@ -65,15 +67,25 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const float* x, const flo
     for (int i = row * blockDim.x + threadIdx.x; i < n_keys; i += gridDim.x * blockDim.x)
       keys[i] = 0ull;
   }
+#ifdef TTS_TIMELINE
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t_end = TTS_TL_NOW();
+    timeline_recs<3>({kTlNorm | kTlEntry, kTlNorm | kTlReleased, kTlNorm | kTlEnd},
+                     {tl_entry, tl_rel, t_end});
+  }
+#endif
 }
 
 // The deferred norm's first stage (the step input's rows): y16 = f16(x * w) and ss = the row's
 // sum of squares; the projection that reads y16 divides its outputs by the row's RMS.
 __global__ void __launch_bounds__(256) norm_defer_kernel(const float* x, const float* w, int dim,
                                                          __half* y16, float* ss_out) {
+  [[maybe_unused]] const unsigned long long tl_entry = TTS_TL_NOW();
   __shared__ float red[8];
   pdl_launch_dependents();
   pdl_wait();
+  [[maybe_unused]] const unsigned long long tl_rel = TTS_TL_NOW();
   const int row = blockIdx.x;
   const float* xr = x + (size_t)row * dim;
   float ss = 0.f;
@@ -93,6 +105,15 @@ __global__ void __launch_bounds__(256) norm_defer_kernel(const float* x, const f
     t = warp_sum(t);
     if (threadIdx.x == 0) ss_out[row] = t;
   }
+#ifdef TTS_TIMELINE
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t_end = TTS_TL_NOW();
+    timeline_recs<3>({kTlNorm | 0x10 | kTlEntry, kTlNorm | 0x10 | kTlReleased,
+                      kTlNorm | 0x10 | kTlEnd},
+                     {tl_entry, tl_rel, t_end});
+  }
+#endif
 }
 
 // a4 standalone: one warp per (lane, head) over qkv [lanes][(heads + 2 n_kv) * 128] f32.

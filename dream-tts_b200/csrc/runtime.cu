@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "../../include/tts_cuda.h"
+#include "tts_common.cuh"
 #include "tts_internal.h"
 
 namespace tts {
@@ -35,6 +36,13 @@ int num_sms(int device) {
 }  // namespace tts
 
 using namespace tts;
+
+#ifdef TTS_TIMELINE
+namespace tts {
+__device__ unsigned long long g_timeline[kTimelineCap * 4];
+__device__ unsigned g_timeline_n;
+}  // namespace tts
+#endif
 
 struct tts_ctx {
   int device = 0;
@@ -191,6 +199,30 @@ using namespace rt;
 extern "C" {
 
 int tts_abi_version(void) { return TTS_CUDA_ABI_VERSION; }
+
+tts_status tts_timeline_read(unsigned long long* records, int cap, int* count, int reset) {
+#ifdef TTS_TIMELINE
+  if (reset) {
+    const unsigned zero = 0;
+    return cuda_status(cudaMemcpyToSymbol(tts::g_timeline_n, &zero, sizeof(zero)), "timeline_read");
+  }
+  if (!records || !count || cap < 0) return fail(TTS_ERR_INVALID_ARG, "timeline_read: NULL argument");
+  unsigned n = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&n, tts::g_timeline_n, sizeof(n));
+  if (e != cudaSuccess) return cuda_status(e, "timeline_read");
+  n = std::min(n, std::min(unsigned(cap), tts::kTimelineCap));
+  *count = int(n);
+  return cuda_status(
+      cudaMemcpyFromSymbol(records, tts::g_timeline, size_t(n) * 4 * sizeof(unsigned long long)),
+      "timeline_read");
+#else
+  (void)records;
+  (void)cap;
+  (void)count;
+  (void)reset;
+  return fail(TTS_ERR_UNSUPPORTED_SHAPE, "timeline_read: library built without TTS_TIMELINE");
+#endif
+}
 const char* tts_last_error(void) { return g_err.c_str(); }
 long long tts_launch_count(int reset) {
   const long long n = g_launches;

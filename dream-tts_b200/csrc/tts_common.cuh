@@ -64,6 +64,41 @@ TTS_DEV uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// Per-CTA timeline records, compiled only with -DTTS_TIMELINE (the library variant built by
+// `build.py --timeline`; the product library has no trace code). A record is (kind, phase time,
+// record time, SM id); kinds are kTl* | phase.
+constexpr int kTlGemm = 0x100;   // | epilogue << 4 | phase
+constexpr int kTlAttn = 0x200;   // | phase
+constexpr int kTlNorm = 0x300;   // | phase (rms_norm; 0x310 | phase: the deferred norm's input)
+constexpr int kTlEntry = 0, kTlReleased = 1, kTlMainDone = 2, kTlReduced = 3, kTlCta = 4,
+              kTlMerged = 5, kTlEnd = 15;  // kTlCta: the phase time field holds blockIdx.x
+#ifdef TTS_TIMELINE
+constexpr unsigned kTimelineCap = 1u << 17;
+extern __device__ unsigned long long g_timeline[kTimelineCap * 4];
+extern __device__ unsigned g_timeline_n;
+// A CTA's records go in one contiguous run (one atomic), so they pair up exactly; callers take
+// their end time before calling, so the log's own cost is outside every phase.
+template <int N>
+TTS_DEV void timeline_recs(const int (&kind)[N], const uint64_t (&t)[N]) {
+  const unsigned i = atomicAdd(&g_timeline_n, unsigned(N));
+  unsigned sm;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+  const uint64_t now = global_ns();
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    if (i + k < kTimelineCap) {
+      g_timeline[(i + k) * 4] = unsigned(kind[k]);
+      g_timeline[(i + k) * 4 + 1] = t[k];
+      g_timeline[(i + k) * 4 + 2] = now;
+      g_timeline[(i + k) * 4 + 3] = sm;
+    }
+  }
+}
+#define TTS_TL_NOW() ::tts::global_ns()
+#else
+#define TTS_TL_NOW() 0ull
+#endif
+
 // Bounded wait: gives up after ~`limit_ns` of wall time (default 2 s) and reports false, so no
 // kernel can spin forever; the caller records an error flag the host reads.
 TTS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull) {

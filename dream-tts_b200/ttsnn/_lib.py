@@ -10,6 +10,8 @@ import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libtts_cuda.so")
+# TTS_LIB selects another build of the same library (the timeline build, for tracing)
+LIB_PATH = os.environ.get("TTS_LIB") or LIB_PATH
 
 TTS_OK = 0
 STATUS = {0: "OK", 1: "INVALID_ARG", 2: "UNSUPPORTED_SHAPE", 3: "CUDA", 4: "TIMEOUT", 5: "OOM"}
@@ -127,6 +129,7 @@ SIGNATURES = {
                          C.POINTER(TextFeed), P, P, P, P],
     "tts_talker_frame_capture": [P, C.POINTER(DecodeState), P, C.POINTER(DecodeState),
                                  C.POINTER(TextFeed), P, P, P, P, C.POINTER(P)],
+    "tts_timeline_read": [P, I, C.POINTER(I), I],
 }
 _RESTYPE = {"tts_last_error": C.c_char_p, "tts_launch_count": C.c_longlong,
             "tts_safetensors_count": C.c_int}

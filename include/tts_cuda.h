@@ -51,6 +51,12 @@ typedef struct tts_graph tts_graph;
 TTS_API int tts_abi_version(void);
 /* Last error message of the calling thread ("" when none). */
 TTS_API const char* tts_last_error(void);
+/* Per-CTA timeline records of the kernels run on the current device since the last reset
+ * (tracing; only in the library built with `build.py --timeline`, which defines TTS_TIMELINE):
+ * copies up to `cap` records of 4 x u64 (kind, phase time ns, record time ns, SM id) into
+ * `records` and their count into *count; `reset` != 0 clears the log instead. The product
+ * library returns TTS_ERR_UNSUPPORTED_SHAPE. No counterpart in the reference (tracing aid). */
+TTS_API tts_status tts_timeline_read(unsigned long long* records, int cap, int* count, int reset);
 
 /* One context per device (and per host thread driving it). Allocates the split-K and
  * attention scratch for up to `max_lanes` rows (1..448). Replaces the candle Device the reference opens
