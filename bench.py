@@ -1133,6 +1133,9 @@ def run_timeline(args):
                             end[j] = max(end[j], t)
                 row["end"] = [f(np.median(end)), f(end.max())]
                 row["cta_end_p10_p90"] = [f(np.percentile(end, 10)), f(np.percentile(end, 90))]
+                by_cta = np.zeros(len(idx))
+                by_cta[a[idx + 2, 1]] = (end - a[idx + 1, 1].min()) / 1e3
+                row["cta_work_us"] = [round(float(x), 2) for x in by_cta]
             else:
                 row["main_done"] = [f(np.median(a[idx + 2, 1])), f(a[idx + 2, 1].max())]
                 row["reduced"] = [f(np.median(a[idx + 3, 1])), f(a[idx + 3, 1].max())]
@@ -1141,7 +1144,9 @@ def run_timeline(args):
         out["layers"][str(li)] = rows
         print(f"layer {li} (us from the QKV projection's first CTA):", file=sys.stderr)
         for name, row in rows.items():
-            print(f"  {name:8s} " + "  ".join(f"{k} {v}" for k, v in row.items()), file=sys.stderr)
+            print(f"  {name:8s} " + "  ".join(f"{k} {v}" for k, v in row.items()
+                                              if k != "cta_work_us"), file=sys.stderr)
+    out["spans"] = [int(p) for p in kv.positions.cpu().tolist()]  # the traced step's spans
     print(json.dumps({"timeline": "config[2] step", **out}))
 
 

@@ -442,13 +442,14 @@ Plan plan_gemm(int m, int k, int n, int device, int force_splits) {
   const int tiles = n / kTileM;
   const int sms = num_sms(device);
   // Many tiles (the heads): two CTAs per SM, one stage per pipeline. Otherwise one CTA per SM
-  // with two stages per pipeline.
+  // with as many stages as 216 KB of rings hold (two per pipeline at decode sizes; three of
+  // 72 KB for 448 rows, whose single pipeline otherwise waits on each stage's load).
   const bool two = tiles > sms;
-  const int budget = two ? 100 * 1024 : 200 * 1024;
+  const int budget = two ? 100 * 1024 : 216 * 1024;
   p.stages = std::max(1, std::min(4, budget / (stage * p.pipes)));
   p.stages = std::max(1, std::min(8, env_int("TTS_GEMM_STAGES", p.stages)));
-  while (p.stages > 1 && size_t(p.stages) * p.pipes * stage > 210 * 1024) --p.stages;
-  while (p.pipes > 1 && size_t(p.stages) * p.pipes * stage > 210 * 1024) --p.pipes;
+  while (p.stages > 1 && size_t(p.stages) * p.pipes * stage > 216 * 1024) --p.stages;
+  while (p.pipes > 1 && size_t(p.stages) * p.pipes * stage > 216 * 1024) --p.pipes;
   const size_t red = size_t(m) * kTileM * sizeof(float);
   const size_t rings = size_t(p.stages) * p.pipes * stage;
   p.smem = std::max(rings, red) + 1024 + 512;
