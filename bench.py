@@ -1069,6 +1069,11 @@ def run_timeline(args):
     if L.load().tts_timeline_read(None, 0, C.byref(cnt), 1) != 0:
         raise SystemExit("timeline: needs the tracing library (TTS_LIB=.../libtts_cuda_tl.so): "
                          + L.last_error())
+    cap_rec = 1 << 21
+    buf = (C.c_ulonglong * (cap_rec * 4))()
+    GEMM, ATTN = 0x100, 0x200
+    if args.workload == "prefill":
+        return timeline_prefill(args, dev, L, C, cnt, buf, cap_rec)
     stack, kv, lengths, cap = build_device_talker(dev, seed=0, extra_positions=64)
     codes = torch.zeros(LANES, CB, dtype=torch.int32, device=dev)
     x = torch.randn(LANES, DIM, device=dev)
@@ -1083,12 +1088,9 @@ def run_timeline(args):
         g.replay()
         s.synchronize()
     ttsnn.check(0)
-    cap_rec = 1 << 17
-    buf = (C.c_ulonglong * (cap_rec * 4))()
     L.call("tts_timeline_read", buf, cap_rec, C.byref(cnt), 0)
     a = np.frombuffer(buf, dtype=np.uint64).reshape(cap_rec, 4)[:cnt.value].astype(np.int64)
     layers = stack.geo.layers
-    GEMM, ATTN = 0x100, 0x200
 
     def runs(first_kind):
         """[launch][cta][record] of the contiguous runs that start with `first_kind`, launches in
@@ -1148,6 +1150,61 @@ def run_timeline(args):
                                               if k != "cta_work_us"), file=sys.stderr)
     out["spans"] = [int(p) for p in kv.positions.cpu().tolist()]  # the traced step's spans
     print(json.dumps({"timeline": "config[2] step", **out}))
+
+
+def timeline_prefill(args, dev, L, C, cnt, buf, cap_rec):
+    """The prefill's GEMM phases (48 lanes x 157 positions in chunks of 448 rows): per
+    projection, the median over its launches of dependency release -> main loop done -> cross-CTA
+    reduction done -> end (median CTA), in us."""
+    import torch
+
+    import ttsnn
+    from qwen3tts import PagedKv
+    prompt = 157
+    stack, _, _, _ = build_device_talker(dev, seed=0, extra_positions=0, lanes_override=0)
+    cap = prompt + 3
+    per = -(-cap // BLOCK)
+    kv = PagedKv(stack.geo, LANES, LANES * per, BLOCK, per, dev)
+    x = torch.randn(LANES * prompt, DIM, device=dev)
+    for i in range(LANES):
+        kv.admit(i, cap, 0)
+
+    def run():
+        for i in range(LANES):
+            kv.positions[i] = 0
+        stack.prefill(kv, [prompt] * LANES, x, max_span=cap)
+
+    run()
+    torch.cuda.synchronize()
+    L.call("tts_timeline_read", None, 0, C.byref(cnt), 1)
+    run()
+    torch.cuda.synchronize()
+    ttsnn.check(0)
+    L.call("tts_timeline_read", buf, cap_rec, C.byref(cnt), 0)
+    a = np.frombuffer(buf, dtype=np.uint64).reshape(cap_rec, 4)[:cnt.value].astype(np.int64)
+    out = {}
+    for name, epi in (("qkv", 4), ("o+down", 2), ("gate/up", 3)):
+        idx = np.nonzero(a[:, 0] == (0x100 | epi << 4))[0]
+        idx = idx[idx + 4 < len(a)]
+        if not len(idx):
+            continue
+        # launches: a launch's CTAs are released together, launches of one kind >= 10 us apart
+        idx = idx[np.argsort(a[idx + 1, 1])]
+        rel_t = a[idx + 1, 1]
+        cuts = [0] + [i for i in range(1, len(idx)) if rel_t[i] - rel_t[i - 1] > 3000] + [len(idx)]
+        ph = []
+        for c0, c1 in zip(cuts[:-1], cuts[1:]):
+            g = idx[c0:c1]
+            rel = a[g + 1, 1].min()
+            ph.append([np.median(a[g + 2, 1]) - rel, np.median(a[g + 3, 1]) - rel,
+                       np.median(a[g + 4, 1]) - rel, a[g + 4, 1].max() - rel])
+        ph = np.median(np.array(ph), 0) / 1e3
+        out[name] = {"launches": len(cuts) - 1, "main_done": round(float(ph[0]), 2),
+                     "reduced": round(float(ph[1]), 2), "end_median": round(float(ph[2]), 2),
+                     "end_max": round(float(ph[3]), 2)}
+        print(f"  {name:8s} {out[name]}  (us after the dependency release)", file=sys.stderr)
+    print(json.dumps({"timeline": "prefill 48 x 157", "gemm": out}))
+    return 0
 
 
 def main():

@@ -67,6 +67,12 @@ struct GemmArgs {
 
 constexpr int kThreads = 256;  // 8 warps: 0..3 producers, 4..7 MMA issuers + epilogue
 
+// kPipe: the epilogue requests each batch's global operands (row-scale partial sums, residual
+// rows, the QKV rows' positions, page numbers and RoPE rows) one batch ahead, so that their
+// round trips overlap the previous batch's reduction and stores. Used where a warp reduces
+// several batches of rows (hundreds of rows: the prefill); at decode sizes each warp has one or
+// two batches and the plain form is used.
+template <bool kPipe>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmX, const GemmArgs a) {
@@ -275,20 +281,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // deferred norm, producer side: this lane's 4 columns of the next norm's weight
   const float4 nw4 = a.norm_w ? *reinterpret_cast<const float4*>(a.norm_w + tile * kTileM + 4 * lane)
                               : make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int j0 = j_first; j0 < a.m; j0 += 4 * stride) {
-    float4 acc4[4];
-    // consumer side: lane t < ss_tiles loads tile t's partial sum of squares of row j, issued
-    // ahead of the DSMEM reads (the previous kernel wrote them: L2 reads)
-    float ssp[4];
+  // the split-K sum of one batch of rows (S partials over DSMEM in rank order), scaled by the
+  // deferred norm's 1/RMS when the row-scale partial sums are given
+  auto reduce_batch = [&](const int (&jr)[4], const float (&ssp)[4], float4 (&acc4)[4]) {
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int j = j0 + u * stride;
-      ssp[u] = a.ss_in && j < a.m && lane < a.ss_tiles ? __ldcg(a.ss_in + (size_t)lane * a.m + j)
-                                                       : 0.f;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int j = j0 + u * stride;
+      const int j = jr[u];
       acc4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (j >= a.m) continue;
       const float* src = red + j * kTileM + 4 * lane;
@@ -313,44 +311,134 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc4[u].w *= inv;
       }
     }
-    if (a.epi == EPI_RESIDUAL) {
-      float4 res[4];
+  };
+  // y[j] = res[j] + acc[j] for a batch, and the next norm's input and sums of squares
+  auto residual_batch = [&](const int (&jr)[4], const float4 (&res)[4], const float4 (&acc4)[4]) {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = j0 + u * stride;
-        if (j0 == j_first)
-          res[u] = res_pre[u];  // read before the reduction
-        else
-          res[u] = j < a.m ? *reinterpret_cast<const float4*>(static_cast<float*>(a.y) +
-                                                              (size_t)j * a.ldy + tile * kTileM +
-                                                              4 * lane)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int u = 0; u < 4; ++u) {
+      const int j = jr[u];
+      if (j >= a.m) continue;
+      float4 r = res[u];
+      r.x += acc4[u].x;
+      r.y += acc4[u].y;
+      r.z += acc4[u].z;
+      r.w += acc4[u].w;
+      *reinterpret_cast<float4*>(static_cast<float*>(a.y) + (size_t)j * a.ldy + tile * kTileM +
+                                 4 * lane) = r;
+      if (a.norm_w) {
+        __half2* d = reinterpret_cast<__half2*>(a.norm_x16 + (size_t)j * a.n + tile * kTileM +
+                                                4 * lane);
+        d[0] = __floats2half2_rn(r.x * nw4.x, r.y * nw4.y);
+        d[1] = __floats2half2_rn(r.z * nw4.z, r.w * nw4.w);
+        const float ss = warp_sum(r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w);
+        if (lane == 0) a.ss_out[(size_t)tile * a.m + j] = ss;
       }
+    }
+  };
+  auto batch_rows = [&](int j0, int (&jr)[4]) {
+    int n = 0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      jr[u] = j0 + u * stride;
+      if (jr[u] < a.m) n = u + 1;
+    }
+    return n;
+  };
+  auto fetch_ss = [&](const int (&jr)[4], float (&d)[4]) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      d[u] = a.ss_in && jr[u] < a.m && lane < a.ss_tiles
+                 ? __ldcg(a.ss_in + (size_t)lane * a.m + jr[u])
+                 : 0.f;
+  };
+  if constexpr (kPipe) {
+    // batch b + 1's operands are requested before batch b's reduction (positions) and before
+    // its stores (page numbers, RoPE rows, which need the positions)
+    int jn[4];
+    int nn = batch_rows(j_first, jn);
+    float ssn[4];
+    float4 resn[4];
+    QkRowsPre qkn;
+    fetch_ss(jn, ssn);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) resn[u] = res_pre[u];  // read before the reduction
+    if (a.epi == EPI_QKROPE) {
+      qkrope_fetch_pos4(a.qk, jn, nn, qkn);
+      qkrope_fetch_rest4(a.qk, tile, jn, nn, lane, qkn);
+    }
+    for (int j0 = j_first; j0 < a.m; j0 += 4 * stride) {
+      int jc[4];
+      float ssc[4];
+      float4 resc[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int j = j0 + u * stride;
-        if (j >= a.m) continue;
-        float4 r = res[u];
-        r.x += acc4[u].x;
-        r.y += acc4[u].y;
-        r.z += acc4[u].z;
-        r.w += acc4[u].w;
-        *reinterpret_cast<float4*>(static_cast<float*>(a.y) + (size_t)j * a.ldy + tile * kTileM +
-                                   4 * lane) = r;
-        if (a.norm_w) {
-          __half2* d = reinterpret_cast<__half2*>(a.norm_x16 + (size_t)j * a.n + tile * kTileM +
-                                                  4 * lane);
-          d[0] = __floats2half2_rn(r.x * nw4.x, r.y * nw4.y);
-          d[1] = __floats2half2_rn(r.z * nw4.z, r.w * nw4.w);
-          const float ss = warp_sum(r.x * r.x + r.y * r.y + r.z * r.z + r.w * r.w);
-          if (lane == 0) a.ss_out[(size_t)tile * a.m + j] = ss;
+        jc[u] = jn[u];
+        ssc[u] = ssn[u];
+        resc[u] = resn[u];
+      }
+      const int nc = nn;
+      const QkRowsPre qkc = qkn;
+      nn = batch_rows(j0 + 4 * stride, jn);
+      if (nn) {
+        fetch_ss(jn, ssn);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          resn[u] = a.epi == EPI_RESIDUAL && u < nn
+                        ? __ldcg(reinterpret_cast<const float4*>(static_cast<float*>(a.y) +
+                                                                 (size_t)jn[u] * a.ldy +
+                                                                 tile * kTileM + 4 * lane))
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.epi == EPI_QKROPE) qkrope_fetch_pos4(a.qk, jn, nn, qkn);
+      }
+      float4 acc4[4];
+      reduce_batch(jc, ssc, acc4);
+      if (nn && a.epi == EPI_QKROPE) qkrope_fetch_rest4(a.qk, tile, jn, nn, lane, qkn);
+      if (a.epi == EPI_RESIDUAL) {
+        residual_batch(jc, resc, acc4);
+      } else if (a.epi == EPI_QKROPE) {
+        float v[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          v[u][0] = acc4[u].x;
+          v[u][1] = acc4[u].y;
+          v[u][2] = acc4[u].z;
+          v[u][3] = acc4[u].w;
         }
-      }
-    } else {
+        qkrope_apply4(a.qk, tile, jc, nc, lane, v, qkc);
+      } else {
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int j = j0 + u * stride;
-        if (j < a.m) epilogue_row(a, tile, j, lane, acc4[u]);
+        for (int u = 0; u < 4; ++u)
+          if (jc[u] < a.m) epilogue_row(a, tile, jc[u], lane, acc4[u]);
+      }
+    }
+  } else {
+    for (int j0 = j_first; j0 < a.m; j0 += 4 * stride) {
+      int jc[4];
+      batch_rows(j0, jc);
+      // lane t < ss_tiles loads tile t's partial sum of squares of each row, ahead of the
+      // DSMEM reads (the previous kernel wrote them: L2 reads)
+      float ssp[4];
+      fetch_ss(jc, ssp);
+      float4 acc4[4];
+      reduce_batch(jc, ssp, acc4);
+      if (a.epi == EPI_RESIDUAL) {
+        float4 res[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int j = jc[u];
+          if (j0 == j_first)
+            res[u] = res_pre[u];  // read before the reduction
+          else
+            res[u] = j < a.m ? *reinterpret_cast<const float4*>(static_cast<float*>(a.y) +
+                                                                (size_t)j * a.ldy +
+                                                                tile * kTileM + 4 * lane)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        residual_batch(jc, res, acc4);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (jc[u] < a.m) epilogue_row(a, tile, jc[u], lane, acc4[u]);
       }
     }
   }
@@ -400,7 +488,8 @@ int max_active_clusters(int device, int splits, size_t smem) {
   auto key = std::make_tuple(device, splits, smem);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  cudaFuncSetAttribute(gemm_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  cudaFuncSetAttribute(gemm_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       227 * 1024);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(1, splits, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -413,7 +502,7 @@ int max_active_clusters(int device, int splits, size_t smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, gemm_decode_kernel, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_decode_kernel<false>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     n = 0;
   }
@@ -583,7 +672,10 @@ cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(mu);
     if (dev >= 0 && dev < 64 && !done[dev]) {
-      cudaFuncSetAttribute(gemm_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      cudaFuncSetAttribute(gemm_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           227 * 1024);
+      cudaFuncSetAttribute(gemm_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           227 * 1024);
       done[dev] = true;
     }
   }
@@ -602,7 +694,11 @@ cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = p.splits > 1 ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, gemm_decode_kernel, tmW, tmX, a);
+  // the look-ahead epilogue where a warp reduces more than two batches of rows (the prefill's
+  // hundreds of rows); TTS_GEMM_PIPE_ROWS overrides the row threshold for A/B measurement
+  static const int pipe_rows = env_int("TTS_GEMM_PIPE_ROWS", 129);
+  if (r.m >= pipe_rows) return cudaLaunchKernelEx(&cfg, gemm_decode_kernel<true>, tmW, tmX, a);
+  return cudaLaunchKernelEx(&cfg, gemm_decode_kernel<false>, tmW, tmX, a);
 }
 
 }  // namespace tts

@@ -69,55 +69,70 @@ __device__ __forceinline__ void qkrope_row(const QkRopeArgs& q, int head, int j,
   }
 }
 
-// Up to four token rows j[0..n) of one head at once, with the same result as qkrope_row on
-// each: every global load of the batch (positions, block table, RoPE table) is issued before
-// the first store, so the rows' load latencies overlap instead of adding up.
-__device__ __forceinline__ void qkrope_rows4(const QkRopeArgs& q, int head, const int j[4], int n,
-                                             int lane, float v[4][4]) {
-  int pos[4];
-#pragma unroll
-  for (int u = 0; u < 4; ++u) pos[u] = u < n ? __ldg(q.positions + j[u]) : -1;
+// The global operands of up to four token rows j[0..n) of one head (positions, page numbers,
+// RoPE rows, the head's norm weights), fetched ahead of qkrope_apply4. The fetch has two
+// levels (page numbers and RoPE rows depend on the positions), so a caller can issue the
+// positions early and the rest later. Positions and block tables are device data written by
+// earlier kernels (read through L2); the RoPE tables and norm weights are constant.
+struct QkRowsPre {
+  int pos[4], blk[4];
   bool ok[4];
-  int blk[4];
-  float4 ct[4], st[4];
+  float4 ct[4], st[4], w4;
+};
+
+__device__ __forceinline__ void qkrope_fetch_pos4(const QkRopeArgs& q, const int j[4], int n,
+                                                  QkRowsPre& p) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) p.pos[u] = u < n ? __ldcg(q.positions + j[u]) : -1;
+}
+
+__device__ __forceinline__ void qkrope_fetch_rest4(const QkRopeArgs& q, int head, const int j[4],
+                                                   int n, int lane, QkRowsPre& p) {
   const bool rot = head < q.heads + q.n_kv;  // q and k heads are normed and rotated
   const int fi = (lane & 15) * 4;
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
-    ok[u] = u < n && pos[u] >= 0 && pos[u] < q.rope_len && pos[u] < q.max_blocks * q.block_size;
-    blk[u] = 0;
-    if (ok[u] && head >= q.heads)
-      blk[u] = __ldg(q.block_table + (size_t)j[u] * q.max_blocks + pos[u] / q.block_size);
-    ct[u] = st[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (ok[u] && rot) {
-      ct[u] = __ldg(reinterpret_cast<const float4*>(q.cos_t + (size_t)pos[u] * 64 + fi));
-      st[u] = __ldg(reinterpret_cast<const float4*>(q.sin_t + (size_t)pos[u] * 64 + fi));
+    const int pos = p.pos[u];
+    p.ok[u] = u < n && pos >= 0 && pos < q.rope_len && pos < q.max_blocks * q.block_size;
+    p.blk[u] = 0;
+    if (p.ok[u] && head >= q.heads)
+      p.blk[u] = __ldcg(q.block_table + (size_t)j[u] * q.max_blocks + pos / q.block_size);
+    p.ct[u] = p.st[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (p.ok[u] && rot) {
+      p.ct[u] = __ldg(reinterpret_cast<const float4*>(q.cos_t + (size_t)pos * 64 + fi));
+      p.st[u] = __ldg(reinterpret_cast<const float4*>(q.sin_t + (size_t)pos * 64 + fi));
     }
   }
-  float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (rot) w4 = __ldg(reinterpret_cast<const float4*>(q.norms + (head < q.heads ? 0 : 128) + 4 * lane));
+  p.w4 = rot ? __ldg(reinterpret_cast<const float4*>(q.norms + (head < q.heads ? 0 : 128) + 4 * lane))
+             : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// qkrope_row on up to four token rows of one head with operands from the fetches above.
+__device__ __forceinline__ void qkrope_apply4(const QkRopeArgs& q, int head, const int j[4], int n,
+                                              int lane, float v[4][4], const QkRowsPre& p) {
+  const bool rot = head < q.heads + q.n_kv;
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
     if (u >= n) break;  // n is warp-uniform
-    if (!ok[u] || (head >= q.heads && (blk[u] < 0 || blk[u] >= q.num_blocks))) {
-      if (u < n && lane == 0 && q.err) atomicOr(q.err, kFlagRopeRange);
+    if (!p.ok[u] || (head >= q.heads && (p.blk[u] < 0 || p.blk[u] >= q.num_blocks))) {
+      if (lane == 0 && q.err) atomicOr(q.err, kFlagRopeRange);
       continue;
     }
-    const int off = pos[u] % q.block_size;
+    const int off = p.pos[u] % q.block_size;
     float* x = v[u];
     if (rot) {
       float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
       ss = warp_sum(ss);
       const float rms = sqrtf(ss / 128.0f + q.eps);
-      x[0] = x[0] / rms * w4.x;
-      x[1] = x[1] / rms * w4.y;
-      x[2] = x[2] / rms * w4.z;
-      x[3] = x[3] / rms * w4.w;
+      x[0] = x[0] / rms * p.w4.x;
+      x[1] = x[1] / rms * p.w4.y;
+      x[2] = x[2] / rms * p.w4.z;
+      x[3] = x[3] / rms * p.w4.w;
       float pr[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) pr[i] = __shfl_xor_sync(0xffffffffu, x[i], 16);
-      const float c4[4] = {ct[u].x, ct[u].y, ct[u].z, ct[u].w};
-      const float s4[4] = {st[u].x, st[u].y, st[u].z, st[u].w};
+      const float c4[4] = {p.ct[u].x, p.ct[u].y, p.ct[u].z, p.ct[u].w};
+      const float s4[4] = {p.st[u].x, p.st[u].y, p.st[u].z, p.st[u].w};
       float o[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i)
@@ -129,18 +144,29 @@ __device__ __forceinline__ void qkrope_rows4(const QkRopeArgs& q, int head, cons
       } else {
         const int h = head - q.heads;
         __half2* dst = reinterpret_cast<__half2*>(
-            q.k_pool + (((size_t)blk[u] * q.n_kv + h) * q.block_size + off) * 128 + 4 * lane);
+            q.k_pool + (((size_t)p.blk[u] * q.n_kv + h) * q.block_size + off) * 128 + 4 * lane);
         dst[0] = __floats2half2_rn(o[0], o[1]);
         dst[1] = __floats2half2_rn(o[2], o[3]);
       }
     } else {
       const int h = head - q.heads - q.n_kv;
       __half2* dst = reinterpret_cast<__half2*>(
-          q.v_pool + (((size_t)blk[u] * q.n_kv + h) * q.block_size + off) * 128 + 4 * lane);
+          q.v_pool + (((size_t)p.blk[u] * q.n_kv + h) * q.block_size + off) * 128 + 4 * lane);
       dst[0] = __floats2half2_rn(x[0], x[1]);
       dst[1] = __floats2half2_rn(x[2], x[3]);
     }
   }
+}
+
+// Up to four token rows j[0..n) of one head at once, with the same result as qkrope_row on
+// each: every global load of the batch is issued before the first store, so the rows' load
+// latencies overlap instead of adding up.
+__device__ __forceinline__ void qkrope_rows4(const QkRopeArgs& q, int head, const int j[4], int n,
+                                             int lane, float v[4][4]) {
+  QkRowsPre p;
+  qkrope_fetch_pos4(q, j, n, p);
+  qkrope_fetch_rest4(q, head, j, n, lane, p);
+  qkrope_apply4(q, head, j, n, lane, v, p);
 }
 
 }  // namespace tts

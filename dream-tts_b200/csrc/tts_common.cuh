@@ -73,7 +73,7 @@ constexpr int kTlNorm = 0x300;   // | phase (rms_norm; 0x310 | phase: the deferr
 constexpr int kTlEntry = 0, kTlReleased = 1, kTlMainDone = 2, kTlReduced = 3, kTlCta = 4,
               kTlMerged = 5, kTlEnd = 15;  // kTlCta: the phase time field holds blockIdx.x
 #ifdef TTS_TIMELINE
-constexpr unsigned kTimelineCap = 1u << 17;
+constexpr unsigned kTimelineCap = 1u << 21;  // 64 MB of records (tracing build only)
 extern __device__ unsigned long long g_timeline[kTimelineCap * 4];
 extern __device__ unsigned g_timeline_n;
 // A CTA's records go in one contiguous run (one atomic), so they pair up exactly; callers take
