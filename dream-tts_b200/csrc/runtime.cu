@@ -83,6 +83,9 @@ struct tts_stack {
   int* pre_table = nullptr;
   size_t pre_table_ints = 0;
   int* pre_pos = nullptr;
+  // layer-major prefill scratch (all of a prompt batch's rows at once), grown on demand
+  unsigned char* pf_buf = nullptr;
+  size_t pf_bytes = 0;
   unsigned long long* keys = nullptr;  // [max_lanes][codebooks]
   // bytes of the next projection's weights each kernel prefetches into L2 (0: none). 12 MB
   // measured best for the talker; the depth predictor's stack runs without (its kernels are
@@ -373,6 +376,27 @@ tts_status tts_proj_forward_packed(tts_ctx* c, const void* x, int m, int k, cons
   r.ldy = ldy;
   r.pdl = false;
   return counted(launch_gemm(r, c->gemm, S(stream), c->device), "proj");
+}
+
+tts_status tts_proj_forward_rows(tts_ctx* c, const void* x, int rows, int k, const void* w, int n,
+                                 int epilogue, void* y, int ldy, void* stream) {
+  if (!c || !x || !w || !y) return fail(TTS_ERR_INVALID_ARG, "proj_rows: NULL argument");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y))
+    return fail(TTS_ERR_INVALID_ARG, "proj_rows: pointers must be 16-byte aligned");
+  std::string why;
+  if (!pf_gemm_supported(rows, k, n, epilogue, &why))
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, "proj_rows: " + why);
+  DeviceGuard g(c->device);
+  PfGemmRequest r;
+  r.x = static_cast<const __half*>(x);
+  r.w = static_cast<const __half*>(w);
+  r.rows = rows;
+  r.k = k;
+  r.n = n;
+  r.epi = epilogue;
+  r.y = y;
+  r.ldy = ldy;
+  return counted(launch_pf_gemm(r, S(stream), c->device, c->gemm.err), "proj_rows");
 }
 
 tts_status tts_rms_norm(tts_ctx* c, const float* x, const float* w, int rows, int dim, float eps,
@@ -771,6 +795,7 @@ tts_status tts_stack_destroy(tts_stack* s) {
   cudaFree(s->pre_map);
   cudaFree(s->pre_table);
   cudaFree(s->pre_pos);
+  cudaFree(s->pf_buf);
   delete s;
   return TTS_OK;
 }
@@ -1120,6 +1145,145 @@ static tts_status capture_graph(cudaStream_t cs, tts_graph** out, Fn&& body) {
 // every lane runs as a decode row of its own (its lane's pages, its own position), in chunks of
 // up to max_lanes rows; the QKV epilogue writes a chunk's K/V before its attention reads them, so
 // each row sees the lane's earlier rows, as the causal mask does.
+// The prompt prefill layer by layer over every row at once (qwen3.rs:294-467 at t > 1): each
+// projection is one prefill-shaped GEMM over all rows (token rows as the MMA's M), the QK-norm,
+// RoPE and KV append run per (row, head), the attention per row in runs of at most max_lanes
+// rows (each row attends to its lane's positions up to its own, already appended at this layer).
+// `s->pre_map` holds the rows' (lane, offset) pairs.
+static bool prefill_layer_major_ok(const tts_stack* s) {
+  const tts_stack_geometry& gm = s->geo;
+  const int D = gm.dim, qw = gm.heads * gm.head_dim, nqkv = (gm.heads + 2 * gm.n_kv) * 128;
+  const char* env = getenv("TTS_PREFILL_DECODE");  // 1: the decode-row path, for A/B
+  if (env && *env == '1') return false;
+  return gm.head_dim == 128 && pf_gemm_supported(1, D, nqkv, EPI_F32, nullptr) &&
+         pf_gemm_supported(1, qw, D, EPI_RESIDUAL, nullptr) &&
+         pf_gemm_supported(1, D, 2 * gm.ffn, EPI_SWIGLU, nullptr) &&
+         pf_gemm_supported(1, gm.ffn, D, EPI_RESIDUAL, nullptr);
+}
+
+static tts_status prefill_layer_major(tts_stack* s, const tts_decode_state* st, long rows,
+                                      const float* x, float* h_out, cudaStream_t cs) {
+  tts_ctx* c = s->ctx;
+  const tts_stack_geometry& gm = s->geo;
+  const int D = gm.dim, qw = gm.heads * gm.head_dim, nqkv = (gm.heads + 2 * gm.n_kv) * 128;
+  const int F = gm.ffn;
+  if (!st->k_pages || !st->v_pages)
+    return fail(TTS_ERR_INVALID_ARG, "stack_prefill: state pointers are NULL");
+  if (st->max_span < 1 || st->max_span > std::min(8192, gm.rope_len))
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE,
+                "stack_prefill: max_span must be in 1..min(8192, rope_len)");
+  for (int l = 0; l < gm.layers; ++l)
+    if (!s->layers[l].wqkv) return fail(TTS_ERR_INVALID_ARG, "stack_prefill: layer weights not set");
+  if (h_out && !s->final_norm) return fail(TTS_ERR_INVALID_ARG, "stack_prefill: final norm not set");
+  auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+  const size_t b_h = up(size_t(rows) * D * 4), b_x16 = up(size_t(rows) * std::max(D, qw) * 2);
+  const size_t b_qkv = up(size_t(rows) * nqkv * 4), b_q = up(size_t(rows) * qw * 4);
+  const size_t b_act = up(size_t(rows) * F * 2), b_tab = up(size_t(rows) * st->max_blocks * 4);
+  const size_t b_pos = up(size_t(rows) * 4);
+  const size_t need = b_h + b_x16 + b_qkv + b_q + b_act + b_tab + b_pos;
+  if (need > s->pf_bytes) {
+    cudaFree(s->pf_buf);
+    s->pf_buf = nullptr;
+    s->pf_bytes = 0;
+    cudaError_t e = dmalloc(&s->pf_buf, need);
+    if (e != cudaSuccess) return cuda_status(e, "stack_prefill");
+    s->pf_bytes = need;
+  }
+  unsigned char* p = s->pf_buf;
+  float* h = reinterpret_cast<float*>(p);
+  __half* x16 = reinterpret_cast<__half*>(p += b_h);
+  float* qkv = reinterpret_cast<float*>(p += b_x16);
+  float* q = reinterpret_cast<float*>(p += b_qkv);
+  __half* act = reinterpret_cast<__half*>(p += b_q);
+  int* table = reinterpret_cast<int*>(p += b_act);
+  int* pos = reinterpret_cast<int*>(p += b_tab);
+  const size_t layer_pages = size_t(st->num_blocks) * gm.n_kv * st->block_size * 128;
+  tts_status rc;
+#define TTS_TRY(expr, op)                     \
+  do {                                        \
+    if ((rc = counted((expr), op)) != TTS_OK) \
+      return rc;                              \
+  } while (0)
+  TTS_TRY(launch_prefill_rows(s->pre_map, int(rows), st->block_table, st->max_blocks,
+                              st->positions, table, pos, cs),
+          "stack_prefill");
+  if ((rc = cuda_status(cudaMemcpyAsync(h, x, size_t(rows) * D * 4, cudaMemcpyDeviceToDevice, cs),
+                        "stack_prefill")) != TTS_OK)
+    return rc;
+  auto proj = [&](const void* w, const __half* xin, int k, int n, int epi, void* y) {
+    PfGemmRequest r;
+    r.x = xin;
+    r.w = static_cast<const __half*>(w);
+    r.rows = int(rows);
+    r.k = k;
+    r.n = n;
+    r.epi = epi;
+    r.y = y;
+    return launch_pf_gemm(r, cs, c->device, c->gemm.err);
+  };
+  for (int l = 0; l < gm.layers; ++l) {
+    const tts_layer_weights& w = s->layers[l];
+    __half* kp = static_cast<__half*>(st->k_pages) + layer_pages * l;
+    __half* vp = static_cast<__half*>(st->v_pages) + layer_pages * l;
+    TTS_TRY(launch_rms_norm(h, w.attn_norm, int(rows), D, gm.eps, nullptr, x16, nullptr, 0, true,
+                            cs),
+            "rms_norm");
+    TTS_TRY(proj(w.wqkv, x16, D, nqkv, EPI_F32, qkv), "proj_rows");
+    QkRopeArgs qa;
+    qa.norms = w.qk_norms;
+    qa.cos_t = s->rope_cos;
+    qa.sin_t = s->rope_sin;
+    qa.positions = pos;
+    qa.block_table = table;
+    qa.max_blocks = st->max_blocks;
+    qa.block_size = st->block_size;
+    qa.num_blocks = st->num_blocks;
+    qa.rope_len = gm.rope_len;
+    qa.err = c->gemm.err;
+    qa.k_pool = kp;
+    qa.v_pool = vp;
+    qa.q_out = q;
+    qa.heads = gm.heads;
+    qa.n_kv = gm.n_kv;
+    qa.eps = gm.eps;
+    TTS_TRY(launch_qk_rope(qkv, qa, int(rows), true, cs), "qk_rope");
+    for (long r0 = 0; r0 < rows; r0 += c->max_lanes) {
+      const int n = int(std::min<long>(c->max_lanes, rows - r0));
+      AttnRequest ar;
+      ar.q = q + size_t(r0) * qw;
+      ar.k_pool = kp;
+      ar.v_pool = vp;
+      ar.block_table = table + size_t(r0) * st->max_blocks;
+      ar.max_blocks = st->max_blocks;
+      ar.block_size = st->block_size;
+      ar.num_blocks = st->num_blocks;
+      ar.err = c->gemm.err;
+      ar.spans = pos + r0;
+      ar.span_add = 1;
+      ar.max_span = st->max_span;
+      ar.window = 0;
+      ar.lanes = n;
+      ar.n_kv = gm.n_kv;
+      ar.gqa = gm.heads / gm.n_kv;
+      ar.out = x16 + size_t(r0) * qw;
+      ar.out_f16 = true;
+      TTS_TRY(launch_attn(ar, c->attn, cs), "decode_attention");
+    }
+    TTS_TRY(proj(w.wo, x16, qw, D, EPI_RESIDUAL, h), "proj_rows");
+    TTS_TRY(launch_rms_norm(h, w.ffn_norm, int(rows), D, gm.eps, nullptr, x16, nullptr, 0, true,
+                            cs),
+            "rms_norm");
+    TTS_TRY(proj(w.w_gate_up, x16, D, 2 * F, EPI_SWIGLU, act), "proj_rows");
+    TTS_TRY(proj(w.w_down, act, F, D, EPI_RESIDUAL, h), "proj_rows");
+  }
+  if (h_out)
+    TTS_TRY(launch_rms_norm(h, s->final_norm, int(rows), D, gm.eps, h_out, nullptr, nullptr, 0,
+                            true, cs),
+            "rms_norm");
+#undef TTS_TRY
+  return TTS_OK;
+}
+
 static tts_status prefill_impl(tts_stack* s, const tts_decode_state* st, const int* lens,
                                const float* x, float* h_out, cudaStream_t cs) {
   tts_ctx* c = s->ctx;
@@ -1168,6 +1332,11 @@ static tts_status prefill_impl(tts_stack* s, const tts_decode_state* st, const i
   if (e != cudaSuccess) return cuda_status(e, "stack_prefill");
   const int D = s->geo.dim;
   tts_status rc;
+  if (prefill_layer_major_ok(s)) {
+    if ((rc = prefill_layer_major(s, st, rows, x, h_out, cs)) != TTS_OK) return rc;
+    return counted(launch_advance_by(st->positions, s->pre_map + 2 * rows, lanes, cs),
+                   "stack_prefill");
+  }
   for (long r0 = 0; r0 < rows; r0 += chunk) {
     const int n = int(std::min<long>(chunk, rows - r0));
     if ((rc = counted(launch_prefill_rows(s->pre_map + 2 * r0, n, st->block_table, st->max_blocks,

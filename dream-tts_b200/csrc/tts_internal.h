@@ -115,6 +115,20 @@ struct GemmRequest {
   float ss_eps = 0.f;
 };
 
+// Prefill-shaped projection (pf_gemm.cu): token rows as the MMA's M, 256 weight rows per tile.
+// w packed as for GemmRequest; epi EPI_F32 (y f32), EPI_RESIDUAL (y f32 +=), EPI_SWIGLU (y f16
+// [rows][n / 2]).
+struct PfGemmRequest {
+  const __half* x = nullptr;  // [rows][k]
+  const __half* w = nullptr;
+  int rows = 0, k = 0, n = 0;
+  int epi = EPI_F32;
+  void* y = nullptr;
+  int ldy = 0;  // 0: n (n / 2 for SwiGLU)
+};
+bool pf_gemm_supported(int rows, int k, int n, int epi, std::string* why);
+cudaError_t launch_pf_gemm(const PfGemmRequest& r, cudaStream_t st, int device, int* err);
+
 struct Workspace {
   int* err = nullptr;  // device error flags (bounded waits that gave up, out-of-range rows)
 };

@@ -70,6 +70,29 @@ class Proj:
 
     __call__ = forward
 
+    def forward_rows(self, x: torch.Tensor, epilogue: int = L.EPI_F32,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+        """The projection shaped for many token rows (tts_proj_forward_rows): x [rows, k] with
+        any rows; epilogue f32, residual (into `out`) or SwiGLU; n % 256 == 0."""
+        if not self.packed:
+            raise ValueError("Proj.forward_rows: needs a packed weight")
+        h = x.to(torch.float16).reshape(-1, self.k).contiguous()
+        rows = h.shape[0]
+        if epilogue == L.EPI_F32:
+            y = out if out is not None else torch.empty(rows, self.n, device=x.device)
+        elif epilogue == L.EPI_RESIDUAL_F32:
+            if out is None:
+                raise ValueError("Proj: the residual epilogue needs `out` (the residual stream)")
+            y = out
+        elif epilogue == L.EPI_SWIGLU_F16:
+            y = out if out is not None else torch.empty(rows, self.n // 2, device=x.device,
+                                                        dtype=torch.float16)
+        else:
+            raise ValueError("Proj.forward_rows: epilogue must be f32, residual or SwiGLU")
+        L.call("tts_proj_forward_rows", ctx_of(x), ptr(h), rows, self.k, ptr(self.w), self.n,
+               epilogue, ptr(y), 0, stream())
+        return y
+
 
 def pack_weight(w: torch.Tensor) -> torch.Tensor:
     """`[n, k]` f16 -> the decode GEMM's streaming layout `[n/128][k/64][128][64]` (returned

@@ -88,6 +88,7 @@ SIGNATURES = {
     "tts_interleave_gate_up": [P, P, P, I, I, P, P],
     "tts_weight_pack": [P, P, I, I, P, P],
     "tts_proj_forward_packed": [P, P, I, I, P, I, I, P, I, P],
+    "tts_proj_forward_rows": [P, P, I, I, P, I, I, P, I, P],
     "tts_rms_norm": [P, P, P, I, I, F, P, P, P],
     "tts_swiglu_mul": [P, P, P, L, P, I, P],
     "tts_snake_beta_nlc": [P, P, I, P, P, L, I, P, I, P],

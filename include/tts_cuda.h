@@ -100,6 +100,12 @@ TTS_API tts_status tts_weight_pack(tts_ctx* ctx, const void* w_f16, int n, int k
 TTS_API tts_status tts_proj_forward_packed(tts_ctx* ctx, const void* x_f16, int m, int k,
                                            const void* w_packed, int n, int epilogue, void* y,
                                            int ldy, void* stream);
+/* The same projection shaped for many token rows (the prompt prefill's Proj::forward at t > 1,
+ * crates/tts-nn/src/lib.rs:510-533): any rows >= 1 (not bounded by max_lanes), n % 256 == 0,
+ * k % 64 == 0, epilogue TTS_EPI_F32, TTS_EPI_RESIDUAL_F32 or TTS_EPI_SWIGLU_F16. */
+TTS_API tts_status tts_proj_forward_rows(tts_ctx* ctx, const void* x_f16, int rows, int k,
+                                         const void* w_packed, int n, int epilogue, void* y,
+                                         int ldy, void* stream);
 
 /* Gate and up projections [ffn][dim] each -> one [2 ffn][dim] weight whose 128-row tiles hold
  * 64 gate rows then the same 64 up rows, the layout TTS_EPI_SWIGLU_F16 consumes. Load-time
