@@ -86,6 +86,41 @@ def test_prefill_matches_decode_steps(tt, orc):
     assert rel(hs.cpu().numpy(), want) < 2e-2
 
 
+@pytest.mark.parametrize("cap,lens,start", [(192, [150, 100, 70, 31], [0, 20, 0, 5]),
+                                             (128, [100, 64, 3, 120], [0, 7, 0, 0])])
+def test_prefill_short_prompts(tt, orc, cap, lens, start):
+    """Short prompts with lanes that already hold positions, through the layer-major prefill:
+    every row's hidden and the written K/V against the oracle's decode steps, as above."""
+    lanes, bs = len(lens), 32
+    g, Ls, final, kc, vc, stack, kv, cos, sin = setup(orc, tt, lanes, cap, bs, 61 + cap)
+    rng = np.random.default_rng(62 + cap)
+    for i in range(lanes):
+        kv.admit(i, cap, 0)
+    pre = [rng.standard_normal((start[i], g.dim), dtype=np.float32) for i in range(lanes)]
+    stack.prefill(kv, start, dev_f32(np.concatenate(pre)), max_span=cap)
+    for i in range(lanes):
+        if start[i]:
+            oracle_prefill(orc, g, Ls, final, kc, vc, i, 0, pre[i], cos, sin)
+    rows = [rng.standard_normal((n, g.dim), dtype=np.float32) for n in lens]
+    x = dev_f32(np.concatenate(rows))
+    h = torch.empty(x.shape[0], g.dim, device="cuda")
+    stack.prefill(kv, lens, x, h_out=h, max_span=cap)
+    torch.cuda.synchronize()
+    tt.check()
+    got = h.cpu().numpy()
+    r0 = 0
+    for i in range(lanes):
+        want = oracle_prefill(orc, g, Ls, final, kc, vc, i, start[i], rows[i], cos, sin)
+        assert rel(got[r0:r0 + lens[i]], want) < 2e-2, i
+        r0 += lens[i]
+    table = kv.table.cpu().numpy()
+    for li in range(g.layers):
+        gk = gather_pages(kv.k[li], table, lanes, g.n_kv, cap, bs)
+        for i in range(lanes):
+            n = start[i] + lens[i]
+            assert rel(orc.f16_value(gk[i, :, :n]), orc.f16_value(kc[li][i, :, :n])) < 2e-2
+
+
 def test_shared_prefix(tt, orc):
     """Lane 0 prefills a 45-position prefix; lanes 1 and 2 share its first page through the
     block table and copy the partly filled second one, then append their own rows: each lane
