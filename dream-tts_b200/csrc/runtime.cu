@@ -86,6 +86,8 @@ struct tts_stack {
   // layer-major prefill scratch (all of a prompt batch's rows at once), grown on demand
   unsigned char* pf_buf = nullptr;
   size_t pf_bytes = 0;
+  int* pf_blocks = nullptr;  // the prompt attention's query blocks [n][4]
+  size_t pf_blocks_ints = 0;
   unsigned long long* keys = nullptr;  // [max_lanes][codebooks]
   // bytes of the next projection's weights each kernel prefetches into L2 (0: none). 12 MB
   // measured best for the talker; the depth predictor's stack runs without (its kernels are
@@ -796,6 +798,7 @@ tts_status tts_stack_destroy(tts_stack* s) {
   cudaFree(s->pre_table);
   cudaFree(s->pre_pos);
   cudaFree(s->pf_buf);
+  cudaFree(s->pf_blocks);
   delete s;
   return TTS_OK;
 }
@@ -1161,8 +1164,8 @@ static bool prefill_layer_major_ok(const tts_stack* s) {
          pf_gemm_supported(1, gm.ffn, D, EPI_RESIDUAL, nullptr);
 }
 
-static tts_status prefill_layer_major(tts_stack* s, const tts_decode_state* st, long rows,
-                                      const float* x, float* h_out, cudaStream_t cs) {
+static tts_status prefill_layer_major(tts_stack* s, const tts_decode_state* st, const int* lens,
+                                      long rows, const float* x, float* h_out, cudaStream_t cs) {
   tts_ctx* c = s->ctx;
   const tts_stack_geometry& gm = s->geo;
   const int D = gm.dim, qw = gm.heads * gm.head_dim, nqkv = (gm.heads + 2 * gm.n_kv) * 128;
@@ -1221,6 +1224,40 @@ static tts_status prefill_layer_major(tts_stack* s, const tts_decode_state* st, 
     r.y = y;
     return launch_pf_gemm(r, cs, c->device, c->gemm.err);
   };
+  // the prompt attention (a lane's query rows in blocks of 64 against its keys), opt-in with
+  // TTS_PREFILL_ATTN=1 where it applies (GQA 2, spans <= 256); by default the decode attention
+  // runs per prompt row
+  const char* pa_env = getenv("TTS_PREFILL_ATTN");
+  const bool use_pfa = pa_env && *pa_env == '1' &&
+                       pf_attn_supported(gm.heads, gm.n_kv, st->block_size, st->max_span);
+  int n_qblocks = 0;
+  if (use_pfa) {
+    std::vector<int> qb;
+    long base = 0;
+    for (int b = 0; b < st->lanes; ++b) {
+      for (int i0 = 0; i0 < lens[b]; i0 += 64) {
+        qb.push_back(b);
+        qb.push_back(int(base + i0));
+        qb.push_back(i0);
+        qb.push_back(std::min(64, lens[b] - i0));
+      }
+      base += lens[b];
+    }
+    n_qblocks = int(qb.size() / 4);
+    if (qb.size() > s->pf_blocks_ints) {
+      cudaFree(s->pf_blocks);
+      s->pf_blocks = nullptr;
+      s->pf_blocks_ints = 0;
+      cudaError_t e = dmalloc(&s->pf_blocks, qb.size() * 4);
+      if (e != cudaSuccess) return cuda_status(e, "stack_prefill");
+      s->pf_blocks_ints = qb.size();
+    }
+    // a pageable source: the copy has read it when the call returns
+    if ((rc = cuda_status(cudaMemcpyAsync(s->pf_blocks, qb.data(), qb.size() * 4,
+                                          cudaMemcpyHostToDevice, cs),
+                          "stack_prefill")) != TTS_OK)
+      return rc;
+  }
   for (int l = 0; l < gm.layers; ++l) {
     const tts_layer_weights& w = s->layers[l];
     __half* kp = static_cast<__half*>(st->k_pages) + layer_pages * l;
@@ -1247,7 +1284,26 @@ static tts_status prefill_layer_major(tts_stack* s, const tts_decode_state* st, 
     qa.n_kv = gm.n_kv;
     qa.eps = gm.eps;
     TTS_TRY(launch_qk_rope(qkv, qa, int(rows), true, cs), "qk_rope");
-    for (long r0 = 0; r0 < rows; r0 += c->max_lanes) {
+    if (use_pfa) {
+      PfAttnRequest pa;
+      pa.q = q;
+      pa.blocks = s->pf_blocks;
+      pa.n_blocks = n_qblocks;
+      pa.positions = st->positions;
+      pa.block_table = st->block_table;
+      pa.max_blocks = st->max_blocks;
+      pa.block_size = st->block_size;
+      pa.num_blocks = st->num_blocks;
+      pa.heads = gm.heads;
+      pa.n_kv = gm.n_kv;
+      pa.max_span = st->max_span;
+      pa.k_pool = kp;
+      pa.v_pool = vp;
+      pa.out = x16;
+      pa.err = c->gemm.err;
+      TTS_TRY(launch_pf_attn(pa, cs), "prefill_attention");
+    }
+    for (long r0 = 0; r0 < rows && !use_pfa; r0 += c->max_lanes) {
       const int n = int(std::min<long>(c->max_lanes, rows - r0));
       AttnRequest ar;
       ar.q = q + size_t(r0) * qw;
@@ -1333,7 +1389,7 @@ static tts_status prefill_impl(tts_stack* s, const tts_decode_state* st, const i
   const int D = s->geo.dim;
   tts_status rc;
   if (prefill_layer_major_ok(s)) {
-    if ((rc = prefill_layer_major(s, st, rows, x, h_out, cs)) != TTS_OK) return rc;
+    if ((rc = prefill_layer_major(s, st, lens, rows, x, h_out, cs)) != TTS_OK) return rc;
     return counted(launch_advance_by(st->positions, s->pre_map + 2 * rows, lanes, cs),
                    "stack_prefill");
   }

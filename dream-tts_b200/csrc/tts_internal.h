@@ -129,6 +129,24 @@ struct PfGemmRequest {
 bool pf_gemm_supported(int rows, int k, int n, int epi, std::string* why);
 cudaError_t launch_pf_gemm(const PfGemmRequest& r, cudaStream_t st, int device, int* err);
 
+// Prompt attention for the layer-major prefill (pf_attn.cu): one CTA per (block of <= 64 new
+// positions of a lane, kv head); GQA 2, spans <= 256, block_size % 8 == 0.
+struct PfAttnRequest {
+  const float* q = nullptr;    // [rows][heads][128]
+  const int* blocks = nullptr; // [n_blocks][4]: lane, first row, first new-position offset, rows
+  int n_blocks = 0;
+  const int* positions = nullptr;  // [lanes] positions held before this prefill
+  const int* block_table = nullptr;
+  int max_blocks = 0, block_size = 0, num_blocks = 0;
+  int heads = 0, n_kv = 0, max_span = 0;
+  const __half* k_pool = nullptr;  // this layer's pages
+  const __half* v_pool = nullptr;
+  __half* out = nullptr;  // [rows][heads][128]
+  int* err = nullptr;
+};
+bool pf_attn_supported(int heads, int n_kv, int block_size, int max_span);
+cudaError_t launch_pf_attn(const PfAttnRequest& r, cudaStream_t st);
+
 struct Workspace {
   int* err = nullptr;  // device error flags (bounded waits that gave up, out-of-range rows)
 };
