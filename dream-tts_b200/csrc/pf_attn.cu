@@ -13,6 +13,8 @@
 //
 // 128 threads: thread t owns query row t (TMEM lane t) through the softmax and the output; one
 // elected lane of warp 0 issues the copies and the MMAs. Every wait is bounded (error flags).
+#include <mutex>
+
 #include "tts_common.cuh"
 #include "tts_internal.h"
 
@@ -335,12 +337,17 @@ cudaError_t launch_pf_attn(const PfAttnRequest& r, cudaStream_t st) {
   a.out = r.out;
   a.err = r.err;
   const size_t smem = sizeof(PaSmem) + 1024;
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(pf_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-    attr_done[dev] = true;
+  {
+    // the opt-in shared-memory limit is a per-device function attribute
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !done[dev]) {
+      cudaFuncSetAttribute(pf_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      done[dev] = true;
+    }
   }
   pf_attn_kernel<<<dim3(r.n_blocks, r.n_kv), kPaThreads, smem, st>>>(tmK, tmV, a);
   return cudaGetLastError();
