@@ -748,10 +748,11 @@ def run_frames(args):
 
 def run_prefill(args):
     """Prompt prefill (Stack::forward at t > 1, qwen3.rs:294-467) at config[2]'s talker shape:
-    48 lanes x 157 prompt positions (the reference's ICL width) through the 28 layers, as
-    chunks of 448 decode rows sharing each lane's pages. value = prompt tokens per second over
-    the whole call (its row plan upload included). Roofline: tensor (2 x tokens x 1.41 G
-    weights FLOP, the attention's share is < 1 %)."""
+    48 lanes x 157 prompt positions (the reference's ICL width) through the 28 layers, layer by
+    layer over all rows: prefill-shaped projections over the 7,536 rows, each row's attention
+    over its lane's pages. value = prompt tokens per second over the whole call (its row plan
+    upload included). Roofline: tensor (2 x tokens x 1.41 G weights FLOP, the attention's share
+    is < 1 %)."""
     import torch
     import ttsnn
     from qwen3tts import PagedKv
@@ -798,7 +799,8 @@ def run_prefill(args):
             "ms_per_step": round(s_per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (random-init weights)",
             "config": {"workload": "prefill of 48 lanes x 157 positions through the config[2] "
-                                   "talker (28 layers), chunks of 448 rows", "tokens": tokens},
+                                   "talker (28 layers), layer-major over all rows",
+                       "tokens": tokens},
             "roofline": {"bound": "tensor", "achieved": round(flops / s_per / 1e12, 1),
                          "peak": tpeak, "unit": "TFLOP/s",
                          "frac": round(flops / s_per / 1e12 / tpeak, 4), "traffic": None,
