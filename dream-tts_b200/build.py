@@ -9,6 +9,7 @@ link time.
 from __future__ import annotations
 
 import argparse
+import concurrent.futures
 import os
 import shutil
 import subprocess
@@ -23,7 +24,7 @@ SOURCES = ["runtime.cu", "gemm_decode.cu", "attn_decode.cu", "chain.cu", "ops_sm
            "predictor.cu", "attn_short.cu", "topk_sample.cu", "safetensors.cpp",
            "codec_front.cu", "pf_gemm.cu", "pf_attn.cu",
            "conv_nlc.cu"]
-HEADERS = ["tts_common.cuh", "tts_internal.h", "qkrope_row.cuh", "gemm_epilogue.cuh",
+HEADERS = ["tts_common.cuh", "tts_internal.h", "qkrope_row.cuh", "gemm_epilogue.cuh", "pick_rule.cuh",
            "l2_prefetch.cuh"]
 
 NVCC_FLAGS = [
@@ -69,14 +70,30 @@ def build(force: bool = False, verbose: bool = False, timeline: bool = False) ->
     objdir = os.path.join(HERE, "_build_tl" if timeline else "_build")
     os.makedirs(objdir, exist_ok=True)
     extra = ["-rdc=true", "-DTTS_TIMELINE"] if timeline else []
+    headers = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(INCLUDE, "tts_cuda.h")]
+    newest_header = max(os.path.getmtime(h) for h in headers)
+    jobs = []
     objs = []
     for s in SOURCES:
+        src = os.path.join(CSRC, s)
         obj = os.path.join(objdir, os.path.splitext(s)[0] + ".o")
-        cmd = [nvcc(), *NVCC_FLAGS, *extra, "-I", INCLUDE, "-c", os.path.join(CSRC, s), "-o", obj]
+        objs.append(obj)
+        # an object is reused when it is newer than its source and every header
+        if (not force and os.path.exists(obj)
+                and os.path.getmtime(obj) >= max(os.path.getmtime(src), newest_header)):
+            continue
+        cmd = [nvcc(), *NVCC_FLAGS, *extra, "-I", INCLUDE, "-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd))
-        subprocess.run(cmd, check=True)
-        objs.append(obj)
+        jobs.append(cmd)
+    # the sources compile independently: run them side by side
+    with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 1)) as ex:
+        for r in list(ex.map(lambda c: subprocess.run(c, capture_output=True, text=True), jobs)):
+            if r.returncode != 0:
+                sys.stderr.write(r.stdout + r.stderr)
+                raise subprocess.CalledProcessError(r.returncode, r.args)
+            elif verbose and (r.stdout or r.stderr):
+                sys.stderr.write(r.stdout + r.stderr)
     tmp = out + ".tmp"
     # --no-undefined: a symbol missing from the objects fails the build, not the first load
     cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", *extra[:1],

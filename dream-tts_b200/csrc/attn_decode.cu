@@ -775,49 +775,51 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-// Scratch for launch_attn_static: the split-KV partials followed by the per-(lane, kv head)
-// arrival counters, in one fixed device array so that callers which must not allocate device
-// memory can still run the attention. Every GPU that loads the library holds this array until
-// the process exits. All calls share it and it keeps the last call's contents, so the counters
-// are cleared on every call, and calls that overlap on the GPU (two streams, two threads) race.
+// Scratch for launch_attn_static, one fixed device array so that callers which must not
+// allocate device memory can still run the attention: the split-KV partials, then a 256-byte
+// status block whose first word collects the kernel's error flags (bounded waits that gave up,
+// spans or pages out of range), then the per-(lane, kv head) arrival counters. Every GPU that
+// loads the library holds this array until the process exits. All calls share it and it keeps
+// the last call's contents, so the status word and the counters are cleared on every call, and
+// calls that overlap on the GPU (two streams, two threads) race.
 constexpr size_t kStaticPartBytes = size_t(4) << 20;  // 4 MiB of partials
+constexpr size_t kStaticStatusBytes = 256;             // the status word, padded
 constexpr int kStaticCounters = 4096;                  // lanes * n_kv
-static __device__ __align__(256) unsigned char g_attn_static_scratch[kStaticPartBytes + kStaticCounters * sizeof(unsigned)];
+static __device__ __align__(256) unsigned char
+    g_attn_static_scratch[kStaticPartBytes + kStaticStatusBytes + kStaticCounters * sizeof(unsigned)];
 
 size_t attn_part_bytes(int lanes, int n_kv, int gqa, int max_span) {
   const int chunks = (max_span + kChunk - 1) / kChunk;
   return size_t(lanes) * n_kv * chunks * gqa * 130 * sizeof(float);
 }
 
+// Why the kernels cannot take request `r` ("" when they can); the caller prefixes its op name.
+std::string attn_shape_error(const AttnRequest& r) {
+  if (r.gqa != 1 && r.gqa != 2 && r.gqa != 4 && r.gqa != 8) return "gqa must be 1, 2, 4 or 8";
+  if (r.lanes < 1 || r.n_kv < 1 || r.max_span < 1 || r.block_size < 1) return "empty shape";
+  if (r.lanes > kMaxLanes) return "at most " + std::to_string(kMaxLanes) + " lanes per call";
+  if (r.max_span <= kShortSpanMax) return "";
+  if ((r.max_span + kChunk - 1) / kChunk > kMaxChunks)
+    return "max_span exceeds " + std::to_string(kMaxChunks * kChunk);
+  if (r.max_blocks != 1 && r.block_size % 8)
+    return "block_size must be a multiple of 8 (or one page per lane)";
+  return "";
+}
+
 cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream_t st) {
-  if (r.gqa != 1 && r.gqa != 2 && r.gqa != 4 && r.gqa != 8) {
-    set_error("decode_attention: gqa must be 1, 2, 4 or 8");
-    return cudaErrorInvalidValue;
-  }
-  if (r.lanes < 1 || r.n_kv < 1 || r.max_span < 1 || r.block_size < 1) {
-    set_error("decode_attention: empty shape");
-    return cudaErrorInvalidValue;
-  }
-  if (r.lanes > kMaxLanes) {
-    set_error("decode_attention: at most 512 lanes per call");
+  const std::string why = attn_shape_error(r);
+  if (!why.empty()) {
+    set_error("decode_attention: " + why);
     return cudaErrorInvalidValue;
   }
   if (r.max_span <= kShortSpanMax) return launch_attn_short(r, st);
   const int chunks = (r.max_span + kChunk - 1) / kChunk;
-  if (chunks > kMaxChunks) {
-    set_error("decode_attention: max_span exceeds 8192");
-    return cudaErrorInvalidValue;
-  }
   // TMA boxes copy runs of whole rows; a run never crosses a page, so the box height divides
   // the page size (or the lane's single page holds every position).
   int box = 0;
   if (r.max_blocks == 1) {
     box = kChunk;
   } else {
-    if (r.block_size % 8) {
-      set_error("decode_attention: block_size must be a multiple of 8 (or one page per lane)");
-      return cudaErrorInvalidValue;
-    }
     box = 8;
     while (box < kChunk && r.block_size % (box * 2) == 0) box *= 2;
   }
@@ -891,18 +893,45 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
 
 size_t attn_static_part_limit() { return kStaticPartBytes; }
 int attn_static_counter_limit() { return kStaticCounters; }
+cudaError_t attn_static_base(void** base);
 
 cudaError_t launch_attn_static(const AttnRequest& r, cudaStream_t st) {
-  if (attn_part_bytes(r.lanes, r.n_kv, r.gqa, r.max_span) > kStaticPartBytes ||
-      r.lanes * r.n_kv > kStaticCounters) {
-    set_error("decode_attention_static: lanes x kv heads x chunks of max_span need " +
-              std::to_string(attn_part_bytes(r.lanes, r.n_kv, r.gqa, r.max_span)) +
-              " bytes of partials (limit " + std::to_string(kStaticPartBytes) +
-              ") and lanes x kv heads <= " + std::to_string(kStaticCounters));
+  // every refusal is decided here, before anything is launched, and named after this op
+  std::string why = attn_shape_error(r);
+  if (why.empty() && (attn_part_bytes(r.lanes, r.n_kv, r.gqa, r.max_span) > kStaticPartBytes ||
+                      r.lanes * r.n_kv > kStaticCounters))
+    why = "lanes x kv heads x chunks of max_span need " +
+          std::to_string(attn_part_bytes(r.lanes, r.n_kv, r.gqa, r.max_span)) +
+          " bytes of partials (limit " + std::to_string(kStaticPartBytes) +
+          ") and lanes x kv heads <= " + std::to_string(kStaticCounters);
+  if (!why.empty()) {
+    set_error("decode_attention_static: " + why);
     return cudaErrorInvalidValue;
   }
-  // The host-side name of the array is not a device address: resolve it once per device, with
-  // that device current, and pass the resolved pointer to the kernel.
+  void* base = nullptr;
+  cudaError_t e = attn_static_base(&base);
+  if (e != cudaSuccess) return e;
+  AttnWorkspace w;
+  w.part = static_cast<float*>(base);
+  w.part_bytes = kStaticPartBytes;
+  unsigned char* status = static_cast<unsigned char*>(base) + kStaticPartBytes;
+  w.counters = reinterpret_cast<unsigned*>(status + kStaticStatusBytes);
+  w.n_counters = kStaticCounters;
+  AttnRequest rr = r;
+  rr.err = reinterpret_cast<int*>(status);
+  // The status word and the counters must start at zero. A previous call leaves the counters at
+  // zero, but one that was cut short (a bounded wait that gave up) may not; the status word
+  // holds the previous call's flags. One clear covers both (they are adjacent).
+  e = cudaMemsetAsync(status, 0, kStaticStatusBytes + size_t(r.lanes) * r.n_kv * sizeof(unsigned),
+                      st);
+  if (e != cudaSuccess) return e;
+  return launch_attn(rr, w, st);
+}
+
+// The device address of the fixed array on the current device. The host-side name of a
+// __device__ array is not a device address: it is resolved once per device, with that device
+// current, and cached (a device reset invalidates the cache; the process must not reuse it).
+cudaError_t attn_static_base(void** base) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -912,31 +941,33 @@ cudaError_t launch_attn_static(const AttnRequest& r, cudaStream_t st) {
   }
   static std::mutex mu;
   static void* scratch[64] = {nullptr};
-  void* base = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (!scratch[dev]) {
-      void* p = nullptr;
-      e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
-      if (e != cudaSuccess) {
-        set_error(std::string("decode_attention_static: cudaGetSymbolAddress failed: ") +
-                  cudaGetErrorString(e));
-        return e;
-      }
-      scratch[dev] = p;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!scratch[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
+    if (e != cudaSuccess) {
+      set_error(std::string("decode_attention_static: cudaGetSymbolAddress failed: ") +
+                cudaGetErrorString(e));
+      return e;
     }
-    base = scratch[dev];
+    scratch[dev] = p;
   }
-  AttnWorkspace w;
-  w.part = static_cast<float*>(base);
-  w.part_bytes = kStaticPartBytes;
-  w.counters = reinterpret_cast<unsigned*>(static_cast<unsigned char*>(base) + kStaticPartBytes);
-  w.n_counters = kStaticCounters;
-  // The counters must start at zero; a previous call leaves them at zero, but one that was cut
-  // short (a bounded wait that gave up elsewhere in the stream) may not, so clear them here.
-  e = cudaMemsetAsync(w.counters, 0, size_t(r.lanes) * r.n_kv * sizeof(unsigned), st);
+  *base = scratch[dev];
+  return cudaSuccess;
+}
+
+// Reads the status word of the last static call on the current device (after `st` has run it).
+cudaError_t attn_static_status(cudaStream_t st, int* flags) {
+  void* base = nullptr;
+  cudaError_t e = attn_static_base(&base);
   if (e != cudaSuccess) return e;
-  return launch_attn(r, w, st);
+  int v = 0;
+  e = cudaMemcpyAsync(&v, static_cast<unsigned char*>(base) + kStaticPartBytes, sizeof(int),
+                      cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return e;
+  *flags = v;
+  return cudaSuccess;
 }
 
 }  // namespace tts

@@ -53,7 +53,7 @@ struct GemmArgs {
   unsigned long long* keys;
   int vocab;
   int codebooks;
-  PickRule pick;  // EPI_ARGMAX: the talker's pick rule (words == 0: none)
+  PickRule pick;  // EPI_ARGMAX: the talker's pick rule (vocab == 0: none)
   L2Prefetch pf;  // the next GEMM's first weight blocks
   // deferred RMSNorm (GemmRequest): producer outputs, consumer row scales
   const float* norm_w;

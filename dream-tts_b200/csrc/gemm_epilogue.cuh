@@ -1,6 +1,7 @@
 // Epilogue of one token row of a 128-row weight tile, shared by the decode GEMM and the layer
 // chain: lane l holds rows 4l .. 4l + 3 of the tile for token row j.
 #pragma once
+#include "pick_rule.cuh"
 #include "qkrope_row.cuh"
 #include "tts_common.cuh"
 #include "tts_internal.h"
@@ -71,22 +72,7 @@ __device__ __forceinline__ void epilogue_row(const A& a, int tile, int j, int la
       const int cb = (tile * kTileRows) / a.vocab;
       const int id0 = f0 - cb * a.vocab;
       float v[4] = {acc.x, acc.y, acc.z, acc.w};
-      if (a.pick.words) {
-        // banned ids first (eos too while the row is young), then the repetition penalty on
-        // the finite logits of ids the row has emitted (talker.rs:160-180)
-        const int w = id0 >> 5, sh = id0 & 31;  // the 4 ids share one word
-        const uint32_t ban = a.pick.ban ? a.pick.ban[w] >> sh : 0u;
-        const uint32_t seen = a.pick.seen ? a.pick.seen[(size_t)j * a.pick.words + w] >> sh : 0u;
-        const bool young = a.pick.frames && a.pick.frames[j] < a.pick.min_new;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          if (((ban >> i) & 1u) || (young && id0 + i == a.pick.eos)) {
-            v[i] = -INFINITY;
-          } else if ((seen >> i) & 1u) {
-            v[i] = v[i] > 0.f ? __fdiv_rn(v[i], a.pick.penalty) : v[i] * a.pick.penalty;
-          }
-        }
-      }
+      if (a.pick.vocab) pick_rule4(a.pick, j, id0, v);
       unsigned long long best = 0;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {

@@ -2,6 +2,7 @@
 // greedy argmax, code gather + embedding sum, position advance. Each is one coalesced pass;
 // the talker step fuses most of them into the GEMM epilogues and keeps only RMSNorm, the code
 // gather and the position advance as launches.
+#include "pick_rule.cuh"
 #include "qkrope_row.cuh"
 #include "tts_common.cuh"
 #include "tts_internal.h"
@@ -215,6 +216,43 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float* logits, int n,
   }
 }
 
+// The talker's greedy pick over rows of logits (sample_with_u with greedy on,
+// crates/qwen3tts/src/talker.rs:154-189): the rule of pick_rule4 on every id, then the last of
+// equal maxima. With `record` the pick joins the row's history as the decode loop's push does
+// (talker.rs:984-996). One block per row; the rule's state is indexed by the row.
+__global__ void __launch_bounds__(256) pick_kernel(const float* logits, int vocab, PickRule pick,
+                                                   int record, uint32_t* out) {
+  __shared__ unsigned long long red[8];
+  const int row = blockIdx.x;
+  const float* lr = logits + (size_t)row * vocab;
+  unsigned long long best = 0;
+  for (int id0 = threadIdx.x * 4; id0 < vocab; id0 += blockDim.x * 4) {
+    const float4 x = *reinterpret_cast<const float4*>(lr + id0);
+    float v[4] = {x.x, x.y, x.z, x.w};
+    pick_rule4(pick, row, id0, v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const unsigned long long key =
+          (static_cast<unsigned long long>(float_order_key(v[i])) << 32) | unsigned(id0 + i);
+      best = key > best ? key : best;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = red[w] > best ? red[w] : best;
+    best = red[0] > best ? red[0] : best;
+    const unsigned c = unsigned(best & 0xffffffffu);
+    out[row] = c;
+    if (record) pick_record(pick, row, c);
+  }
+}
+
 // Codes from the heads GEMM's argmax keys, and the next step's input as the sum of each
 // codebook's embedding row (the talker's codec_embed lookup + the predictor's gather_sum,
 // crates/qwen3tts/src/talker.rs:1019-1023, 528-550). Resets the keys for the next step.
@@ -231,14 +269,9 @@ __global__ void __launch_bounds__(256) keys_to_codes_kernel(const unsigned long 
   const int row = blockIdx.x;
   // the step's last reader of the positions has finished: advance this lane's
   if (positions && threadIdx.x == 0) positions[row] += 1;
-  // the pick rule's history (one codebook): the pick joins the row's seen ids unless it is eos
-  // (talker.rs:990-996), and the row has one more frame
-  if (pick.words && threadIdx.x == 0) {
-    const unsigned c = unsigned(keys[row] & 0xffffffffu);
-    if (pick.seen && int(c) != pick.eos && c < unsigned(pick.words * 32))
-      pick.seen[(size_t)row * pick.words + (c >> 5)] |= 1u << (c & 31);
-    if (pick.frames) pick.frames[row] += 1;
-  }
+  // the pick rule's history (one codebook): the pick joins the row's history unless it is eos
+  // (talker.rs:984-996), and the row has one more frame
+  if (pick.vocab && threadIdx.x == 0) pick_record(pick, row, unsigned(keys[row] & 0xffffffffu));
   if (threadIdx.x < codebooks) {
     const unsigned c = unsigned(keys[(size_t)row * codebooks + threadIdx.x] & 0xffffffffu);
     sc[threadIdx.x] = int(c < unsigned(vocab) ? c : 0);
@@ -375,13 +408,23 @@ cudaError_t launch_argmax(const float* logits, int rows, int n, const uint8_t* b
   return cudaGetLastError();
 }
 
+cudaError_t launch_pick(const float* logits, int rows, const PickRule& pick, bool record,
+                        uint32_t* out, cudaStream_t st) {
+  if (pick.vocab < 32 || pick.vocab % 32) {
+    set_error("talker_pick: vocab must be a positive multiple of 32");
+    return cudaErrorInvalidValue;
+  }
+  pick_kernel<<<rows, 256, 0, st>>>(logits, pick.vocab, pick, record ? 1 : 0, out);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_keys_to_codes(const unsigned long long* keys, int rows, int codebooks,
                                  int vocab, const __half* embed, const float* embed32, int dim,
                                  uint32_t* codes, float* x_next, unsigned long long* keys_reset,
                                  int* positions, const PickRule* pick, bool pdl,
                                  cudaStream_t st) {
   PickRule pr = pick ? *pick : PickRule{};
-  if (pr.words && codebooks != 1) {
+  if (pr.vocab && codebooks != 1) {
     set_error("keys_to_codes: a pick rule takes one codebook");
     return cudaErrorInvalidValue;
   }

@@ -75,7 +75,7 @@ struct tts_stack {
   // step then runs no norm kernel between layers (one for the input, one final).
   float* ss = nullptr;
   bool defer_norm = true;
-  PickRule pick;              // the codec head's greedy pick rule (words == 0: plain argmax)
+  PickRule pick;              // the codec head's greedy pick rule (vocab == 0: plain argmax)
   // prefill scratch, grown on demand by tts_stack_prefill: per-row (lane, offset) pairs and
   // lane lengths; per-row block-table rows and positions for one chunk of rows
   int* pre_map = nullptr;
@@ -541,6 +541,24 @@ tts_status tts_decode_attention_static(const float* q, int lanes, int gqa,
   return counted(launch_attn_static(r, S(stream)), "decode_attention_static");
 }
 
+tts_status tts_decode_attention_static_check(void* stream) {
+  int code = 0;
+  const cudaError_t e = attn_static_status(S(stream), &code);
+  if (e != cudaSuccess) return cuda_status(e, "decode_attention_static_check");
+  if (code & kFlagWaitMask)
+    return fail(TTS_ERR_TIMEOUT, "decode_attention_static: device wait gave up (code " +
+                                     std::to_string(code) + "): the output is not valid");
+  if (code) {
+    std::string what;
+    if (code & kFlagSpanRange) what += " a span outside 1..max_span or the block table;";
+    if (code & kFlagPageRange) what += " a block-table page outside the pool;";
+    return fail(TTS_ERR_INVALID_ARG, "decode_attention_static: device data out of range (code " +
+                                         std::to_string(code) + "):" + what +
+                                         " those positions were clamped or read as zero");
+  }
+  return TTS_OK;
+}
+
 tts_status tts_argmax(tts_ctx* c, const float* logits, int rows, int n,
                       const unsigned char* banned, unsigned int* out, void* stream) {
   if (!c || !logits || !out) return fail(TTS_ERR_INVALID_ARG, "argmax: NULL argument");
@@ -745,30 +763,57 @@ tts_status tts_stack_set_head(tts_stack* s, const float* final_norm, const void*
   return TTS_OK;
 }
 
+// Checks a caller's pick rule for a vocabulary of `vocab` ids and converts it.
+static tts_status pick_rule_of(const tts_pick_rule* rule, int vocab, const char* op,
+                               PickRule* out) {
+  if (vocab < 32 || vocab % 32)
+    return fail(TTS_ERR_UNSUPPORTED_SHAPE, std::string(op) + ": vocab must be a multiple of 32");
+  if (!(rule->penalty > 0.f) || rule->min_new < 0 || rule->eos >= vocab)
+    return fail(TTS_ERR_INVALID_ARG, std::string(op) + ": penalty > 0, min_new >= 0, eos < vocab");
+  if ((rule->min_new > 0 && rule->eos >= 0 && !rule->frames) ||
+      (rule->penalty != 1.f && !rule->counts))
+    return fail(TTS_ERR_INVALID_ARG,
+                std::string(op) + ": min_new needs frames, a penalty needs the counts");
+  if ((rule->ban && !aligned16(rule->ban)) || (rule->counts && !aligned16(rule->counts)))
+    return fail(TTS_ERR_INVALID_ARG, std::string(op) + ": ban and counts must be 16-byte aligned");
+  PickRule p;
+  p.ban = rule->ban;
+  p.counts = rule->counts;
+  p.frames = rule->frames;
+  p.penalty = rule->penalty;
+  p.eos = rule->eos;
+  p.min_new = rule->min_new;
+  p.vocab = vocab;
+  *out = p;
+  return TTS_OK;
+}
+
 tts_status tts_stack_set_pick(tts_stack* s, const tts_pick_rule* rule) {
   if (!s) return fail(TTS_ERR_INVALID_ARG, "stack_set_pick: stack is NULL");
   if (!rule) {
     s->pick = PickRule{};
     return TTS_OK;
   }
-  if (s->geo.codebooks != 1 || s->geo.vocab % 32)
+  if (s->geo.codebooks != 1)
     return fail(TTS_ERR_UNSUPPORTED_SHAPE, "stack_set_pick: needs one codebook head");
-  if (!(rule->penalty > 0.f) || rule->min_new < 0 || rule->eos >= s->geo.vocab)
-    return fail(TTS_ERR_INVALID_ARG, "stack_set_pick: penalty > 0, min_new >= 0, eos < vocab");
-  if ((rule->min_new > 0 && rule->eos >= 0 && !rule->frames) ||
-      (rule->penalty != 1.f && !rule->seen))
-    return fail(TTS_ERR_INVALID_ARG,
-                "stack_set_pick: min_new needs frames, a penalty needs the seen bits");
   PickRule p;
-  p.ban = rule->ban;
-  p.seen = rule->seen;
-  p.frames = rule->frames;
-  p.penalty = rule->penalty;
-  p.eos = rule->eos;
-  p.min_new = rule->min_new;
-  p.words = s->geo.vocab / 32;
+  const tts_status st = pick_rule_of(rule, s->geo.vocab, "stack_set_pick", &p);
+  if (st != TTS_OK) return st;
   s->pick = p;
   return TTS_OK;
+}
+
+tts_status tts_talker_pick(tts_ctx* c, const float* logits, int rows, int vocab,
+                           const tts_pick_rule* rule, int record, unsigned int* out,
+                           void* stream) {
+  if (!c || !logits || !rule || !out) return fail(TTS_ERR_INVALID_ARG, "talker_pick: NULL argument");
+  if (rows < 1) return fail(TTS_ERR_INVALID_ARG, "talker_pick: rows must be >= 1");
+  if (!aligned16(logits)) return fail(TTS_ERR_INVALID_ARG, "talker_pick: logits must be 16-byte aligned");
+  PickRule p;
+  const tts_status st = pick_rule_of(rule, vocab, "talker_pick", &p);
+  if (st != TTS_OK) return st;
+  DeviceGuard g(c->device);
+  return counted(launch_pick(logits, rows, p, record != 0, out, S(stream)), "talker_pick");
 }
 
 tts_status tts_stack_set_feedback(tts_stack* s, float* x_next) {

@@ -73,16 +73,16 @@ L2Prefetch gemm_prefetch_plan(const void* w_packed, int m, int k, int n, int dev
 
 // The talker's greedy pick rule (crates/qwen3tts/src/talker.rs:154-189, 940, 971-981), applied
 // to the codec head's logits before the argmax: ids with their bit set in `ban` are excluded,
-// `eos` too while frames[row] < min_new, and ids with their bit set in the row's `seen` are
-// divided (if positive) or multiplied (if negative) by `penalty`. The code gather then marks
-// the pick in `seen` (unless it is eos) and counts the row's frame.
+// `eos` too while frames[row] < min_new, and each id's logit is divided (if positive) or
+// multiplied (if negative) by `penalty` once per time the row has emitted it (counts). The code
+// gather then records the pick (unless it is eos) and counts the row's frame (pick_rule.cuh).
 struct PickRule {
-  const uint32_t* ban = nullptr;  // [words]
-  uint32_t* seen = nullptr;       // [rows][words]
+  const uint32_t* ban = nullptr;  // [vocab / 32] bits
+  uint16_t* counts = nullptr;     // [rows][vocab]: times each id was emitted (saturating)
   int* frames = nullptr;          // [rows]
   float penalty = 1.f;
   int eos = -1, min_new = 0;
-  int words = 0;                  // vocab / 32
+  int vocab = 0;                  // ids per row, a multiple of 32 (0: no rule)
 };
 
 struct GemmRequest {
@@ -228,6 +228,9 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
 cudaError_t launch_attn_static(const AttnRequest& r, cudaStream_t st);
 size_t attn_static_part_limit();
 int attn_static_counter_limit();
+// The error flags the last launch_attn_static on the current device left in its status word
+// (synchronises `st` first).
+cudaError_t attn_static_status(cudaStream_t st, int* flags);
 
 // ------------------------------------------------------------------ small kernels
 // The deferred norm's first stage for rows that no projection produced (the step's input):
@@ -243,6 +246,8 @@ cudaError_t launch_swiglu(const float* g, const float* u, void* y, bool y_f16, l
                           cudaStream_t st);
 cudaError_t launch_snake(const void* x, bool x_f16, const float* alpha, const float* brecip,
                          long rows, int chan, void* y, bool y_f16, cudaStream_t st);
+cudaError_t launch_pick(const float* logits, int rows, const PickRule& pick, bool record,
+                        uint32_t* out, cudaStream_t st);
 cudaError_t launch_argmax(const float* logits, int rows, int n, const uint8_t* banned,
                           uint32_t* out, cudaStream_t st);
 cudaError_t launch_keys_to_codes(const unsigned long long* keys, int rows, int codebooks,

@@ -171,10 +171,11 @@ class PagedKv:
 
 class PickState:
     """The talker's greedy pick rule on the device (talker.rs:154-189, 940, 971-981): `banned`
-    ids never picked, `eos` banned while a lane has fewer than `min_new` frames, and logits of
-    ids a lane has emitted divided (positive) or multiplied (negative) by `penalty`. The seen
-    bits int32 [lanes, vocab / 32] and frame counts int32 [lanes] live on the device and are
-    updated by every step; `reset(lane)` clears a lane slot for a new segment."""
+    ids never picked, `eos` banned while a lane has fewer than `min_new` frames, and each id's
+    logit divided (positive) or multiplied (negative) by `penalty` once per time the lane has
+    emitted it. The per-id emission counts u16 [lanes, vocab] (held as int16) and frame counts
+    int32 [lanes] live on the device and are updated by every step; `reset(lane)` clears a lane
+    slot for a new segment."""
 
     def __init__(self, vocab: int, lanes: int, banned, eos: int = -1, min_new: int = 0,
                  penalty: float = 1.0, device: torch.device | str = "cuda"):
@@ -187,14 +188,21 @@ class PickState:
             bits[int(i) >> 5] |= np.uint32(1 << (int(i) & 31))
         self.vocab, self.eos, self.min_new, self.penalty = vocab, eos, min_new, penalty
         self.ban = torch.from_numpy(bits.view(np.int32)).to(device)
-        self.seen = torch.zeros(lanes, words, dtype=torch.int32, device=device)
+        self.counts = torch.zeros(lanes, vocab, dtype=torch.int16, device=device)
         self.frames = torch.zeros(lanes, dtype=torch.int32, device=device)
-        self.c = L.PickRule(self.ban.data_ptr(), self.seen.data_ptr(), self.frames.data_ptr(),
+        self.c = L.PickRule(self.ban.data_ptr(), self.counts.data_ptr(), self.frames.data_ptr(),
                             float(penalty), int(eos), int(min_new))
 
     def reset(self, lane: int) -> None:
-        self.seen[lane].zero_()
+        self.counts[lane].zero_()
         self.frames[lane] = 0
+
+    def history(self, lane: int) -> dict[int, int]:
+        """The lane's emitted ids and how often each was emitted (the reference's `seen` list
+        as a multiset)."""
+        c = self.counts[lane].to(torch.int32) & 0xFFFF
+        nz = torch.nonzero(c).flatten().tolist()
+        return {int(i): int(c[i]) for i in nz}
 
 
 class Graph:

@@ -57,7 +57,7 @@ class PredictorWeights(C.Structure):
 
 
 class PickRule(C.Structure):
-    _fields_ = [("ban", C.c_void_p), ("seen", C.c_void_p), ("frames", C.c_void_p),
+    _fields_ = [("ban", C.c_void_p), ("counts", C.c_void_p), ("frames", C.c_void_p),
                 ("penalty", C.c_float), ("eos", C.c_int), ("min_new", C.c_int)]
 
 
@@ -95,6 +95,7 @@ SIGNATURES = {
     "tts_qk_rope_append": [P, P, I, I, P, P, P, I, P, C.POINTER(KvCache), F, P, P],
     "tts_decode_attention": [P, P, I, I, C.POINTER(KvCache), P, I, I, P, I, P],
     "tts_decode_attention_static": [P, I, I, C.POINTER(KvCache), P, I, I, P, I, P],
+    "tts_decode_attention_static_check": [P],
     "tts_argmax": [P, P, I, I, P, P, P],
     "tts_conv1d_nlc": [P, P, I, I, I, P, I, I, I, I, P, P, P, P, P, P],
     "tts_stack_create": [P, C.POINTER(StackGeometry), C.POINTER(P)],
@@ -112,6 +113,7 @@ SIGNATURES = {
     "tts_predictor_graph_capture": [P, C.POINTER(DecodeState), P, P, C.POINTER(TextFeed), P, P,
                                     P, C.POINTER(P)],
     "tts_stack_set_pick": [P, C.POINTER(PickRule)],
+    "tts_talker_pick": [P, P, I, I, C.POINTER(PickRule), I, P, P],
     "tts_topk_sample": [P, P, I, I, P, I, F, P, P],
     "tts_predictor_set_sampling": [P, P, I, I, F],
     "tts_stack_prefill": [P, C.POINTER(DecodeState), P, P, P, P],

@@ -23,6 +23,19 @@ def argmax(logits: torch.Tensor, banned: torch.Tensor | None = None) -> torch.Te
     return out
 
 
+def talker_pick(logits: torch.Tensor, rule, record: bool = False) -> torch.Tensor:
+    """sample_with_u's greedy branch (crates/qwen3tts/src/talker.rs:154-189) on `[rows, vocab]`
+    f32 under a pick rule (`rule.c`, a PickRule; counts and frames indexed by row): banned ids
+    and a young eos at -inf, each id's logit penalised once per time the row emitted it, the
+    last of equal maxima. With `record`, the picks join the rows' histories (talker.rs:984-996)."""
+    x = logits.to(torch.float32).contiguous()
+    rows, n = x.shape
+    out = torch.empty(rows, dtype=torch.int32, device=x.device)
+    L.call("tts_talker_pick", ctx_of(x), ptr(x), rows, n, rule.c, 1 if record else 0, ptr(out),
+           stream())
+    return out
+
+
 MAX_N = 4096
 MAX_K = 64
 

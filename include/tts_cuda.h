@@ -172,18 +172,32 @@ TTS_API tts_status tts_decode_attention(tts_ctx* ctx, const float* q, int lanes,
  * unbounded time, or a host engine that reserves all device memory up front in its own arena
  * and cannot let a library allocate behind its back. It needs no tts_ctx (creating one
  * allocates) and calls no allocator: its scratch is one fixed device array inside the library,
- * 4 MiB of split-KV partials plus 4096 arrival counters, which every GPU that loads the library
- * holds until the process exits. Limits: lanes * n_kv * ceil(max_span / 128) * gqa * 520 bytes
- * must fit in 4 MiB (e.g. 48 lanes x 8 kv heads x gqa 2 up to max_span 1280) and
- * lanes * n_kv <= 4096; larger requests return TTS_ERR_UNSUPPORTED_SHAPE. The first call on a
- * device looks up the array's device address with that device current, so make the first call
- * before any stream capture. All calls share the array and it keeps the last call's contents:
- * the counters are cleared at the start of every call, and calls that overlap on the GPU (two
- * streams or threads at once) race. Out-of-range pages are masked, not reported. */
+ * 4 MiB of split-KV partials, a status word and 4096 arrival counters, which every GPU that
+ * loads the library holds until the process exits. It runs on the current device.
+ * Limits: lanes <= 512; gqa in {1, 2, 4, 8}; max_span <= 8192; block_size a multiple of 8 unless
+ * max_blocks == 1; lanes * n_kv * ceil(max_span / 128) * gqa * 520 bytes must fit in 4 MiB (e.g.
+ * 48 lanes x 8 kv heads x gqa 2 up to max_span 1280) and lanes * n_kv <= 4096. A request beyond
+ * a limit returns TTS_ERR_UNSUPPORTED_SHAPE before anything is launched.
+ * Set-up: CUDA loads the library's device code lazily, so the first call on a device may load
+ * it (creating the array) and looks up the array's device address with that device current;
+ * that step can allocate and synchronise. Make one call per device at set-up, outside the
+ * real-time thread and before any stream capture. The address stays cached for the process:
+ * after a device reset the library must not be used again.
+ * All calls share the array and it keeps the last call's contents: the status word and the
+ * counters are cleared at the start of every call, and calls that overlap on the GPU (two
+ * streams or threads at once) race. Device-side problems (a bounded wait that gave up, a span
+ * or a page out of range) do not change the return code, which is decided on the host; they
+ * are recorded in the status word, read by tts_decode_attention_static_check. */
 TTS_API tts_status tts_decode_attention_static(const float* q, int lanes, int gqa,
                                                const tts_kv_cache* kv, const int* spans,
                                                int max_span, int window, void* out,
                                                int out_f16, void* stream);
+/* Synchronises `stream` and reports the status word of the last tts_decode_attention_static call
+ * on the current device: TTS_ERR_TIMEOUT if a bounded device-side wait gave up (the output is not
+ * valid), TTS_ERR_INVALID_ARG if a span was clamped or a page outside the pool read as zero,
+ * else TTS_OK. Allocates nothing. Part of the static entry point above (no reference
+ * counterpart). */
+TTS_API tts_status tts_decode_attention_static_check(void* stream);
 
 /* ---------------------------------------------------------------- sampling
  * Greedy pick of sample_with_u: crates/qwen3tts/src/talker.rs:154-189. banned[n] (nullable)
@@ -251,20 +265,31 @@ TTS_API tts_status tts_stack_set_feedback(tts_stack* s, float* x_next);
 
 /* The talker's greedy pick over its codec head (crates/qwen3tts/src/talker.rs:154-189, 940,
  * 971-981), for a stack with one codebook head: ids whose bit is set in `ban` are never picked,
- * nor `eos` while the lane's frames < min_new; ids set in the lane's `seen` bits have their
- * logit divided (if positive) or multiplied (if negative) by `penalty` first. Each step marks
- * its pick in `seen` (unless it is eos) and adds one to the lane's `frames`. All device
- * memory, caller-owned; a lane slot reused for a new segment is cleared by the caller. NULL
- * restores the plain argmax. */
+ * nor `eos` while the lane's frames < min_new; then each id's finite logit is divided (if
+ * positive) or multiplied (if negative) by `penalty` once for every time the lane has emitted
+ * it (`counts`), one f32 operation per occurrence as the reference's loop over its history
+ * with repeats does; then the last of equal maxima wins. Each step adds its pick to the lane's
+ * `counts` (unless it is eos; saturating at 65535) and adds one to the lane's `frames`. All
+ * device memory, caller-owned, 16-byte aligned; a lane slot reused for a new segment is
+ * cleared by the caller. NULL restores the plain argmax. */
 typedef struct tts_pick_rule {
-  const unsigned int* ban; /* [vocab / 32] bits, or NULL */
-  unsigned int* seen;      /* [max_lanes][vocab / 32] bits, or NULL (needs penalty == 1) */
-  int* frames;             /* [max_lanes], or NULL (needs min_new == 0 or eos < 0) */
-  float penalty;           /* repetition penalty, 1 = none */
-  int eos;                 /* the end id (-1: none) */
-  int min_new;             /* frames before eos may be picked */
+  const unsigned int* ban;  /* [vocab / 32] bits, or NULL */
+  unsigned short* counts;   /* [max_lanes][vocab] times each id was emitted, or NULL (needs
+                               penalty == 1) */
+  int* frames;              /* [max_lanes], or NULL (needs min_new == 0 or eos < 0) */
+  float penalty;            /* repetition penalty, 1 = none */
+  int eos;                  /* the end id (-1: none) */
+  int min_new;              /* frames before eos may be picked */
 } tts_pick_rule;
 TTS_API tts_status tts_stack_set_pick(tts_stack* s, const tts_pick_rule* rule);
+/* sample_with_u with greedy on (crates/qwen3tts/src/talker.rs:154-189) over rows of logits f32
+ * [rows][vocab] (vocab % 32 == 0), under `rule` (tts_pick_rule above; counts and frames are
+ * indexed by row): out u32 [rows]. With record != 0 each pick is then added to its row's
+ * counts (unless it is eos) and the row's frames advance, as the decode loop's push does
+ * (talker.rs:984-996). The same arithmetic as the codec head's pick inside the decode step. */
+TTS_API tts_status tts_talker_pick(tts_ctx* ctx, const float* logits, int rows, int vocab,
+                                   const tts_pick_rule* rule, int record, unsigned int* out,
+                                   void* stream);
 TTS_API tts_status tts_stack_destroy(tts_stack* s);
 
 /* Decode-time cache state of one group of lanes, all layers: pages f16

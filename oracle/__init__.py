@@ -252,9 +252,11 @@ def decode_step(x: np.ndarray, layers: list[Layer], final_norm: np.ndarray, kcac
     return rms_norm(h, final_norm, g.eps)
 
 
-def heads_pick(hidden: np.ndarray, heads_bits: np.ndarray, g: Geometry):
-    """Codebook heads `[codebooks * vocab, dim]` f16 and the greedy pick per head."""
-    logits = proj(hidden, heads_bits)
+def heads_pick(hidden: np.ndarray, heads_bits: np.ndarray, g: Geometry, round_f16: bool = False):
+    """Codebook heads `[codebooks * vocab, dim]` f16 and the greedy pick per head. With
+    `round_f16` the logits are rounded to f16 as the CPU arm's `matmul_2d(..).to_dtype(f32)`
+    leaves them (crates/tts-nn/src/lib.rs:519-528), which makes exact ties common."""
+    logits = proj(hidden, heads_bits, round_f16)
     b = hidden.shape[0]
     codes = argmax(logits.reshape(b, g.codebooks, g.vocab))
     return logits, codes
@@ -410,18 +412,30 @@ def predictor_frame(hidden: np.ndarray, code0_embed: np.ndarray, layers: list[La
 
 
 # ---------------------------------------------------------------- the talker's frame
-def talker_pick(logits: np.ndarray, banned, seen: list[set], frames: np.ndarray, eos: int,
+def penalize(x: np.float32, times: int, penalty: np.float32) -> np.float32:
+    """The repetition penalty of sample_with_u (crates/qwen3tts/src/talker.rs:167-179) applied
+    for `times` occurrences of one id in the history: each occurrence, while the logit is finite,
+    divides it by the penalty if positive, else multiplies it, one f32 operation at a time."""
+    for _ in range(times):
+        if not np.isfinite(x):
+            break
+        x = np.float32(x / penalty) if x > 0 else np.float32(x * penalty)
+    return x
+
+
+def talker_pick(logits: np.ndarray, banned, seen: list, frames: np.ndarray, eos: int,
                 min_new: int, penalty: float, forced: np.ndarray | None = None,
                 tie_tol: float = 0.0):
     """sample_with_u with greedy on (crates/qwen3tts/src/talker.rs:154-189) for each row: banned
-    ids (and eos while the row has fewer than `min_new` frames, :971-981) to -inf, then each
-    seen id's finite logit divided (positive) or multiplied (negative) by `penalty`, then the
-    last of equal maxima. `forced` picks within `tie_tol` of the row's maximum are followed
-    (near-ties resolved the other way by a different accumulation order). Returns
-    (picks, ties, mismatches)."""
+    ids (and eos while the row has fewer than `min_new` frames, :971-981) to -inf, then the
+    repetition penalty once per entry of the row's history `seen[r]` (a list of emitted ids with
+    repeats, as `seen[lane].push(c)` builds it, :987), then the last of equal maxima. `forced`
+    picks within `tie_tol` of the row's maximum are followed (near-ties resolved the other way
+    by a different accumulation order). Returns (picks, ties, mismatches)."""
     b, n = logits.shape
     picks = np.zeros(b, np.uint32)
     ties = mismatches = 0
+    pen = np.float32(penalty)
     for r in range(b):
         l = logits[r].astype(np.float32).copy()
         for i in banned:
@@ -429,9 +443,14 @@ def talker_pick(logits: np.ndarray, banned, seen: list[set], frames: np.ndarray,
         if frames[r] < min_new and 0 <= eos < n:
             l[eos] = -np.inf
         if penalty != 1.0:
+            # every occurrence of an id acts on that id's logit alone, so the entries can be
+            # grouped by id without changing any result
+            times: dict[int, int] = {}
             for i in seen[r]:
-                if np.isfinite(l[i]):
-                    l[i] = np.float32(l[i] / np.float32(penalty)) if l[i] > 0 else np.float32(l[i] * np.float32(penalty))
+                if 0 <= int(i) < n:
+                    times[int(i)] = times.get(int(i), 0) + 1
+            for i, t in times.items():
+                l[i] = penalize(l[i], t, pen)
         best = int(np.flatnonzero(l == l.max())[-1])
         if forced is not None and int(forced[r]) != best:
             f = int(forced[r])
@@ -447,7 +466,8 @@ def talker_pick(logits: np.ndarray, banned, seen: list[set], frames: np.ndarray,
 @dataclass
 class TalkerState:
     """One group's talker-side state: per-layer caches [b, n_kv, cap, hd] f16 bits, positions,
-    the pick rule's seen ids and frame counts, and the next input rows."""
+    the pick rule's history (per lane, the emitted ids with repeats) and frame counts, and the
+    next input rows."""
     kc: list
     vc: list
     pos: np.ndarray
@@ -460,22 +480,24 @@ def talker_frame(st: TalkerState, layers: list[Layer], final_norm: np.ndarray, g
                  codec_head: np.ndarray, codec_embed: np.ndarray, banned, eos: int,
                  min_new: int, penalty: float, p_layers: list[Layer], p_final: np.ndarray,
                  pw: PredictorWeights, pg: Geometry, text_rows: np.ndarray, pad: np.ndarray,
-                 forced0=None, forced=None, tie_tol: float = 0.0):
+                 forced0=None, forced=None, tie_tol: float = 0.0,
+                 tie_tol0: float | None = None):
     """One iteration of Talker::generate_batch with greedy picks (talker.rs:953-1057), started
     from the step that feeds the talker stack: Stack::forward on `st.x` at each lane's
     position, codec head, pick, code 0's codec_embed row, the predictor's frame on the hidden
     state and that row, then the sum plus the lane's text row (trailing row frames - 1, else the
-    pad row) as the next input. Updates `st`; returns (code0, codes, ties, mismatches)."""
+    pad row) as the next input. `tie_tol0` (default `tie_tol`) is the near-tie band of code 0's
+    pick, `tie_tol` the predictor's. Updates `st`; returns (code0, codes, ties, mismatches)."""
     cap = st.kc[0].shape[2]
     cos, sin = rope_table(cap + 1, g.head_dim, g.rope_base)
     h = decode_step(st.x, layers, final_norm, st.kc, st.vc, st.pos, cos, sin, g)
     st.pos = st.pos + 1
     logits = proj(h, codec_head)
     code0, t0, m0 = talker_pick(logits, banned, st.seen, st.frames, eos, min_new, penalty,
-                                forced0, tie_tol)
+                                forced0, tie_tol if tie_tol0 is None else tie_tol0)
     for r, c in enumerate(code0):
         if int(c) != eos:
-            st.seen[r].add(int(c))
+            st.seen[r].append(int(c))
     st.frames = st.frames + 1
     code0_embed = f16_value(codec_embed[code0.astype(np.int64)])
     codes, total, t1, m1 = predictor_frame(h, code0_embed, p_layers, p_final, pw, pg, forced,

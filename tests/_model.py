@@ -12,17 +12,30 @@ def make_layer(orc, rng, g):
     return orc.synthetic_layer(rng, g)
 
 
+def normal_f16_table(rng, shape):
+    """~N(0, 1) f16 bits drawn from a seeded table of 65,536 normal values: the same
+    distribution as drawing each element, fast enough for the benchmark's multi-GB caches."""
+    import oracle
+    table = oracle.f16_bits(rng.standard_normal(65536, dtype=np.float32))
+    n = int(np.prod(shape))
+    return table[np.frombuffer(rng.bytes(2 * n), np.uint16)].reshape(shape)
+
+
 def make_talker(orc, lanes, layers, dim, heads, n_kv, ffn, cap, seed, codebooks=0, vocab=0,
-                lengths=None):
+                lengths=None, fast_kv=False):
     rng = np.random.default_rng(seed)
     g = orc.Geometry(dim=dim, layers=layers, heads=heads, n_kv=n_kv, ffn=ffn,
                      codebooks=codebooks, vocab=vocab)
     Ls = [make_layer(orc, rng, g) for _ in range(layers)]
     final = rng.uniform(0.8, 1.2, dim).astype(np.float32)
-    kc = [orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
-          for _ in range(layers)]
-    vc = [orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
-          for _ in range(layers)]
+    if fast_kv:
+        kc = [normal_f16_table(rng, (lanes, n_kv, cap, 128)) for _ in range(layers)]
+        vc = [normal_f16_table(rng, (lanes, n_kv, cap, 128)) for _ in range(layers)]
+    else:
+        kc = [orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
+              for _ in range(layers)]
+        vc = [orc.f16_bits(rng.standard_normal((lanes, n_kv, cap, 128), dtype=np.float32))
+              for _ in range(layers)]
     if lengths is None:
         pos = rng.integers(cap // 2, cap - 1, lanes).astype(np.int32)
     else:

@@ -3,8 +3,14 @@ B200 against the CPU oracle's composition: per frame the talker step with its co
 the pick rule (banned top ids except eos, eos held back for the first frames, repetition
 penalty), code 0's codec_embed row, the depth predictor's residual codes and the next input
 (their embedding sum plus the lane's text row). Several frames in a row, so the pick rule's
-history (seen ids, frame counts) and the text rows are exercised. Bar: every pick equal to the
-oracle's except near-ties (followed by the oracle), and the next input equal for equal picks."""
+history (each lane's emitted ids with repeats, frame counts) and the text rows are exercised; a
+long run (128 frames) over a head whose leading rows are proportional to each other makes the
+penalty, applied once per occurrence of an id, decide most picks. Bar: every code-0 pick equal
+to the oracle's with no tie allowance; the predictor's picks equal except near-ties (followed
+by the oracle); the next input equal for equal picks; the device's per-id counts equal to the
+oracle's history."""
+from collections import Counter
+
 import numpy as np
 import pytest
 import torch
@@ -13,7 +19,7 @@ from _model import dev_f16, dev_f32, device_predictor, device_stack, make_predic
 
 pytestmark = pytest.mark.gpu
 
-LANES, CAP, BS = 5, 64, 32
+LANES, CAP, BS = 5, 192, 32
 VOCAB, EOS, MIN_NEW, PENALTY = 384, 300, 2, 1.05
 BANNED = [i for i in range(256, 384) if i != EOS]
 
@@ -24,7 +30,7 @@ def rel(a, b):
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
 
 
-def build(orc, seed):
+def build(orc, seed, group=False):
     lengths = np.array([3, 9, 20, 31, 40], np.int32)  # cached positions before the first step
     g, Ls, final, kc, vc, pos, x = make_talker(orc, LANES, 2, 256, 4, 2, 512, CAP, seed,
                                                codebooks=1, vocab=VOCAB, lengths=lengths)
@@ -36,6 +42,11 @@ def build(orc, seed):
     head[11] = head[10] * 1.02
     head[EOS] = head[10] * 1.04
     head[290] = head[10] * 2.0
+    if group:
+        # eight rows proportional to row 10: their logits keep fixed ratios frame after frame,
+        # so which of them leads depends on how often each was emitted
+        for i in range(8):
+            head[40 + i] = head[10] * (1.0 + 0.012 * i)
     head = orc.f16_bits(head)
     embed = orc.f16_bits(rng.standard_normal((VOCAB, g.dim), dtype=np.float32) * 0.02)
     for L_ in (kc, vc):
@@ -75,17 +86,16 @@ def device_loop(orc, m):
 
 def oracle_state(orc, m):
     return orc.TalkerState(kc=[a.copy() for a in m["kc"]], vc=[a.copy() for a in m["vc"]],
-                           pos=m["lengths"].copy(), seen=[set() for _ in range(LANES)],
+                           pos=m["lengths"].copy(), seen=[[] for _ in range(LANES)],
                            frames=np.zeros(LANES, np.int64), x=m["x"].copy())
 
 
-def test_frame_loop_matches_oracle(tt, orc):
-    m = build(orc, 41)
+def run_frames(tt, orc, m, frames, tie_tol, tie_tol0=None):
     loop, talker, pred = device_loop(orc, m)
     st = oracle_state(orc, m)
     ties = 0
-    picked = set()
-    for f in range(6):
+    picked = []
+    for f in range(frames):
         loop.frame(LANES)
         torch.cuda.synchronize()
         tt.check()
@@ -94,18 +104,38 @@ def test_frame_loop_matches_oracle(tt, orc):
         want0, want, t, mism = orc.talker_frame(
             st, m["Ls"], m["final"], m["g"], m["head"], m["embed"], BANNED, EOS, MIN_NEW,
             PENALTY, m["pLs"], m["pfinal"], m["pw"], m["pg"], m["text"], m["pad"],
-            forced0=c0, forced=codes, tie_tol=2e-3)
+            forced0=c0, forced=codes, tie_tol=tie_tol, tie_tol0=tie_tol0)
         assert mism == 0, (f, c0, want0, codes, want)
         ties += t
         assert np.array_equal(want0, c0) and np.array_equal(want, codes)
         assert not any(int(c) in BANNED for c in c0)
         if f < MIN_NEW:
             assert EOS not in c0.tolist()
-        picked.update(c0.tolist())
+        picked.append(c0)
         assert rel(loop.feedback.cpu().numpy(), st.x) < 1e-6
         assert loop.pick.frames.cpu().tolist() == [f + 1] * LANES
+    assert loop.kv.positions.cpu().numpy().tolist() == (m["lengths"] + frames).tolist()
+    for lane in range(LANES):
+        assert loop.pick.history(lane) == dict(Counter(st.seen[lane])), lane
+    return np.stack(picked), ties
+
+
+def test_frame_loop_matches_oracle(tt, orc):
+    m = build(orc, 41)
+    _, ties = run_frames(tt, orc, m, 6, 2e-3)
     assert ties <= 3
-    assert loop.kv.positions.cpu().numpy().tolist() == (m["lengths"] + 6).tolist()
+
+
+def test_frame_loop_penalty_decides_long_run(tt, orc):
+    """128 frames over a head with eight proportional leading rows: ids repeat many times, and
+    the penalty's per-occurrence count decides which of them leads."""
+    m = build(orc, 43, group=True)
+    # no tie allowance for code 0 (the pick the rule makes); the predictor's near-ties as above
+    picks, ties = run_frames(tt, orc, m, 128, 2e-3, tie_tol0=0.0)
+    group = (picks >= 40) & (picks < 48)
+    assert group.mean() > 0.2
+    per_lane = [Counter(p.tolist()) for p in picks.T]
+    assert max(max(c.values()) for c in per_lane) >= 5  # ids emitted many times
 
 
 def test_frame_loop_graph_matches_eager(tt, orc):

@@ -68,7 +68,7 @@ def test_text_to_audio(tt, orc):
         vc = [np.zeros((1, g.n_kv, cap, 128), np.uint16) for _ in Ls]
         for t in range(P.shape[0] - 1):
             orc.decode_step(P[t:t + 1], Ls, final, kc, vc, np.array([t], np.int32), cos, sin, g)
-        st = orc.TalkerState(kc, vc, np.array([P.shape[0] - 1], np.int32), [set()],
+        st = orc.TalkerState(kc, vc, np.array([P.shape[0] - 1], np.int32), [[]],
                              np.zeros(1, np.int64), P[-1:].copy())
         rows = np.broadcast_to(pad, (1, max(trailing.shape[0], 1), dim)).copy()
         rows[0, :trailing.shape[0]] = trailing.cpu().numpy()

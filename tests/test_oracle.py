@@ -313,7 +313,7 @@ def test_talker_pick_rule(orc):
                        [-1.0, -2.0, -1.02, -9.0, -9.0],
                        [2.0, 2.0, 1.0, 0.0, 2.0]], np.float32)
     banned = [3]
-    seen = [set(), {4}, {0}, set()]
+    seen = [[], [4], [0], []]
     frames = np.array([0, 5, 5, 5])
     picks, _, _ = orc.talker_pick(logits, banned, seen, frames, eos=4, min_new=2, penalty=1.05)
     # row 0: 3 banned, eos (4) too young -> 1; row 1: eos old enough but seen: 4/1.05 = 3.81 > 3
@@ -322,6 +322,37 @@ def test_talker_pick_rule(orc):
     forced = np.array([2, 4, 2, 0], np.uint32)
     p2, ties, mism = orc.talker_pick(logits, banned, seen, frames, 4, 2, 1.05, forced, 0.2)
     assert p2.tolist() == [2, 4, 2, 0] and ties == 2 and mism == 0
+
+
+def test_talker_pick_penalty_per_occurrence(orc):
+    """The history keeps repeats (talker.rs:987 pushes every non-eos pick), and the penalty
+    loop runs once per entry (talker.rs:167-179): an id emitted k times is divided (or
+    multiplied) k times in sequence, in f32, which is not the same as one power of the
+    penalty."""
+    logits = np.array([[4.0, 3.7, -8.0, 1.0],
+                       [4.0, 3.7, -8.0, 1.0],
+                       [-1.0, -1.06, -1.2, -3.0],
+                       [-1.0, -1.06, -1.2, -3.0]], np.float32)
+    seen = [[0], [0, 3, 0], [0, 0], [1, 0, 0, 0, 1]]
+    frames = np.array([9, 9, 9, 9])
+    picks, _, _ = orc.talker_pick(logits, [], seen, frames, eos=-1, min_new=0, penalty=1.05)
+    # row 0: 4/1.05 = 3.81 > 3.7 -> 0; row 1: 4/1.05/1.05 = 3.63 < 3.7 -> 1; row 2: -1 * 1.05^2
+    # = -1.1025 < -1.06 -> 1; row 3: id 0 -> -1.157..., id 1 -> -1.06 * 1.05^2 = -1.1687 -> 0
+    assert picks.tolist() == [0, 1, 1, 0]
+    # sequential f32 operations, not a power: find inputs where the two differ and check that
+    # the oracle follows the sequence
+    pen = np.float32(1.05)
+    rng = np.random.default_rng(3)
+    xs = (rng.standard_normal(4000) * 10).astype(np.float32)
+    differ = 0
+    for x in xs:
+        seq = x
+        for _ in range(7):
+            seq = np.float32(seq / pen) if seq > 0 else np.float32(seq * pen)
+        pw = np.float32(x / np.float32(pen ** 7)) if x > 0 else np.float32(x * np.float32(pen ** 7))
+        assert orc.penalize(x, 7, pen) == seq
+        differ += int(seq != pw)
+    assert differ > 100
 
 
 def test_topk_sample_walk(orc):

@@ -2,7 +2,9 @@
 (a real-time audio thread, where cudaMalloc can stall the whole device, or a host engine that
 owns all device memory in its own arena). Its scratch lives in a fixed device array inside the
 library. Checked through the C ABI against the context-based tts_decode_attention on two calls
-in a row, within the attention tests' tolerance. This file is collected last on purpose."""
+in a row, within the attention tests' tolerance, on the short-span path, a request just under
+the array's limit and a windowed call; free device memory must not move across static calls
+after the first. This file is collected last on purpose."""
 import ctypes as C
 
 import numpy as np
@@ -11,7 +13,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-LANES, N_KV, GQA, BS = 12, 8, 2, 32
+N_KV, BS = 8, 32
 
 
 def rel(a, b):
@@ -20,55 +22,126 @@ def rel(a, b):
     return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
 
 
-def paged_inputs(seed, spans):
+def paged_inputs(seed, spans, gqa, max_span):
+    lanes = len(spans)
     rng = np.random.default_rng(seed)
-    per = 36  # 36 pages of 32 positions = 1152 >= every span
-    nb = LANES * per + 7
-    table = rng.permutation(nb)[:LANES * per].reshape(LANES, per).astype(np.int32)
-    k = torch.randn(nb, N_KV, BS, 128, device="cuda").half()
-    v = torch.randn(nb, N_KV, BS, 128, device="cuda").half()
-    q = torch.randn(LANES, N_KV * GQA, 128, device="cuda") * 0.1
+    per = -(-max_span // BS)
+    nb = lanes * per + 7
+    table = rng.permutation(nb)[:lanes * per].reshape(lanes, per).astype(np.int32)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    k = torch.randn(nb, N_KV, BS, 128, device="cuda", generator=g).half()
+    v = torch.randn(nb, N_KV, BS, 128, device="cuda", generator=g).half()
+    q = torch.randn(lanes, N_KV * gqa, 128, device="cuda", generator=g) * 0.1
     t = torch.from_numpy(table).cuda()
     s = torch.tensor(spans, dtype=torch.int32, device="cuda")
     return q, k, v, t, s, per, nb
 
 
-def test_static_scratch_matches_context_entry_point(tt):
+def both(tt, spans, gqa, max_span, window, seed):
+    """One call of each entry point on the same inputs; returns (static, context) outputs."""
     from ttsnn import _lib as L
     lib = L.load()
-    torch.cuda.set_device(0)
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-    ctx = tt.ctx(0)
-    max_span = 1100
-    # two calls in a row with different spans: multi-chunk lanes use the partials and counters
-    for call, spans in enumerate(([1, 31, 256, 257, 600, 1100, 5, 64, 999, 300, 512, 700],
-                                  [1100, 2, 700, 33, 1024, 255, 129, 900, 1, 513, 64, 1099])):
-        q, k, v, t, s, per, nb = paged_inputs(100 + call, spans)
-        kv = L.KvCache(k.data_ptr(), v.data_ptr(), t.data_ptr(), per, BS, nb, N_KV, 128)
-        want = torch.empty(LANES, N_KV * GQA * 128, device="cuda")
-        got = torch.full_like(want, float("nan"))
-        rc = lib.tts_decode_attention(ctx, C.c_void_p(q.data_ptr()), LANES, GQA, C.byref(kv),
-                                      C.c_void_p(s.data_ptr()), max_span, 0,
-                                      C.c_void_p(want.data_ptr()), 0, stream)
-        assert rc == 0, L.last_error()
-        rc = lib.tts_decode_attention_static(C.c_void_p(q.data_ptr()), LANES, GQA, C.byref(kv),
-                                             C.c_void_p(s.data_ptr()), max_span, 0,
-                                             C.c_void_p(got.data_ptr()), 0, stream)
-        assert rc == 0, L.last_error()
-        torch.cuda.synchronize()
+    lanes = len(spans)
+    q, k, v, t, s, per, nb = paged_inputs(seed, spans, gqa, max_span)
+    kv = L.KvCache(k.data_ptr(), v.data_ptr(), t.data_ptr(), per, BS, nb, N_KV, 128)
+    want = torch.empty(lanes, N_KV * gqa * 128, device="cuda")
+    got = torch.full_like(want, float("nan"))
+    rc = lib.tts_decode_attention(tt.ctx(0), C.c_void_p(q.data_ptr()), lanes, gqa, C.byref(kv),
+                                  C.c_void_p(s.data_ptr()), max_span, window,
+                                  C.c_void_p(want.data_ptr()), 0, stream)
+    assert rc == 0, L.last_error()
+    rc = lib.tts_decode_attention_static(C.c_void_p(q.data_ptr()), lanes, gqa, C.byref(kv),
+                                         C.c_void_p(s.data_ptr()), max_span, window,
+                                         C.c_void_p(got.data_ptr()), 0, stream)
+    assert rc == 0, L.last_error()
+    assert lib.tts_decode_attention_static_check(stream) == 0, L.last_error()
+    torch.cuda.synchronize()
+    return got, want
+
+
+CASES = [
+    # (spans, gqa, max_span, window): multi-chunk lanes use the partials and the counters
+    ([1, 31, 256, 257, 600, 1100, 5, 64, 999, 300, 512, 700], 2, 1100, 0),
+    ([1100, 2, 700, 33, 1024, 255, 129, 900, 1, 513, 64, 1099], 2, 1100, 0),
+    ([64, 1, 17, 33, 63, 2, 50, 64], 2, 64, 0),                       # short-span kernel
+    ([1 + (i * 181) % 1280 for i in range(47)] + [1280], 2, 1280, 0),  # 3.99 of the 4 MiB
+    ([1100, 700, 90, 1024, 300, 2, 513, 999], 4, 1100, 200),           # window, gqa 4
+]
+
+
+@pytest.mark.parametrize("case", range(len(CASES)))
+def test_static_scratch_matches_context_entry_point(tt, case):
+    spans, gqa, max_span, window = CASES[case]
+    torch.cuda.set_device(0)
+    for call in range(2):  # two calls in a row: the array keeps the first call's contents
+        got, want = both(tt, spans, gqa, max_span, window, 100 + 10 * case + call)
         assert torch.isfinite(got).all(), f"call {call}: output not fully written"
         assert rel(got.cpu().numpy(), want.cpu().numpy()) < 1e-5, f"call {call}"
 
 
-def test_static_scratch_rejects_oversize(tt):
+def test_static_calls_allocate_nothing(tt):
     from ttsnn import _lib as L
     lib = L.load()
-    q, k, v, t, s, per, nb = paged_inputs(7, [1] * LANES)
+    spans, gqa, max_span, window = CASES[0]
+    got, _ = both(tt, spans, gqa, max_span, window, 5)  # set-up call on this device
+    q, k, v, t, s, per, nb = paged_inputs(6, spans, gqa, max_span)
     kv = L.KvCache(k.data_ptr(), v.data_ptr(), t.data_ptr(), per, BS, nb, N_KV, 128)
-    out = torch.empty(512, N_KV * GQA * 128, device="cuda")
-    # 512 lanes x 8 kv heads x 32 chunks x 2 x 520 B is far beyond the 4 MiB of partials
-    rc = lib.tts_decode_attention_static(C.c_void_p(q.data_ptr()), 512, GQA, C.byref(kv),
-                                         C.c_void_p(s.data_ptr()), 8192, 0,
-                                         C.c_void_p(out.data_ptr()), 0, None)
-    assert rc == 2
-    assert "limit" in L.last_error()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    reserved0 = torch.cuda.memory_reserved()
+    for _ in range(20):
+        rc = lib.tts_decode_attention_static(C.c_void_p(q.data_ptr()), len(spans), gqa,
+                                             C.byref(kv), C.c_void_p(s.data_ptr()), max_span,
+                                             window, C.c_void_p(got.data_ptr()), 0, stream)
+        assert rc == 0, L.last_error()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0 and torch.cuda.memory_reserved() == reserved0
+
+
+def test_static_scratch_rejects_out_of_limit_requests(tt):
+    from ttsnn import _lib as L
+    lib = L.load()
+    q, k, v, t, s, per, nb = paged_inputs(7, [1] * 12, 2, 1100)
+    out = torch.empty(520, N_KV * 2 * 128, device="cuda")
+
+    def call(lanes, gqa, max_span, block_size=BS, max_blocks=None):
+        kv = L.KvCache(k.data_ptr(), v.data_ptr(), t.data_ptr(),
+                       per if max_blocks is None else max_blocks, block_size, nb, N_KV, 128)
+        return lib.tts_decode_attention_static(C.c_void_p(q.data_ptr()), lanes, gqa,
+                                               C.byref(kv), C.c_void_p(s.data_ptr()), max_span,
+                                               0, C.c_void_p(out.data_ptr()), 0, None)
+
+    # 512 lanes x 8 kv heads x 64 chunks x 2 x 520 B is far beyond the 4 MiB of partials
+    assert call(512, 2, 8192) == 2 and "limit" in L.last_error()
+    # refusals the kernel launcher makes are reported under this op's name, as unsupported
+    assert call(513, 1, 129) == 2
+    assert "decode_attention_static" in L.last_error() and "512 lanes" in L.last_error()
+    assert call(12, 2, 1100, block_size=12) == 2 and "multiple of 8" in L.last_error()
+    assert call(12, 3, 1100) == 2 and "gqa" in L.last_error()
+
+
+def test_static_status_word_reports_device_data_out_of_range(tt):
+    from ttsnn import _lib as L
+    lib = L.load()
+    spans = [300, 5000, 40, 700]  # 5000 is beyond max_span: the kernel clamps it and records it
+    gqa, max_span = 2, 1100
+    q, k, v, t, s, per, nb = paged_inputs(8, [min(x, max_span) for x in spans], gqa, max_span)
+    s = torch.tensor(spans, dtype=torch.int32, device="cuda")
+    kv = L.KvCache(k.data_ptr(), v.data_ptr(), t.data_ptr(), per, BS, nb, N_KV, 128)
+    out = torch.empty(len(spans), N_KV * gqa * 128, device="cuda")
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = lib.tts_decode_attention_static(C.c_void_p(q.data_ptr()), len(spans), gqa, C.byref(kv),
+                                         C.c_void_p(s.data_ptr()), max_span, 0,
+                                         C.c_void_p(out.data_ptr()), 0, stream)
+    assert rc == 0, L.last_error()
+    assert lib.tts_decode_attention_static_check(stream) == 1
+    assert "span" in L.last_error()
+    # the next call clears the word
+    s.clamp_(max=max_span)
+    rc = lib.tts_decode_attention_static(C.c_void_p(q.data_ptr()), len(spans), gqa, C.byref(kv),
+                                         C.c_void_p(s.data_ptr()), max_span, 0,
+                                         C.c_void_p(out.data_ptr()), 0, stream)
+    assert rc == 0 and lib.tts_decode_attention_static_check(stream) == 0, L.last_error()
