@@ -35,6 +35,9 @@ LANES, LAYERS, DIM, HEADS, N_KV, HD, FFN, CB, VOCAB = 48, 28, 2048, 16, 8, 128, 
 BLOCK = 32
 # DRAM bytes (read + write) of one gate/up launch at 48 lanes, from its ncu capture
 GATEUP_NCU_TRAFFIC = 50_606_336 + 6_912
+# the same for one attention launch of the config[2] step (KV lengths U[64,1024] seed 0 + 1)
+ATTN_NCU_TRAFFIC = 103_300_000 + 3_100_000
+ATTN_BYTES_PER_POS = N_KV * HD * 2 * 2  # K and V rows of one position, all kv heads, f16
 KV_LO, KV_HI = 64, 1024
 WORKLOAD = ("config[2]: full talker decode step, 28 layers, hidden 2048, 16q/8kv heads x 128, "
             "SwiGLU 6144, f16 weights N(0,0.02), 16 codebook heads x 2048, greedy; 48 lanes, "
@@ -50,6 +53,13 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def clocks_path(args, rank):
+    """Where the nvidia-smi samples of this rank go: --clocks-dir (default /tmp)."""
+    d = getattr(args, "clocks_dir", None) or "/tmp"
+    os.makedirs(d, exist_ok=True)
+    return os.path.join(d, f"clocks_rank{rank}.csv")
+
+
 def dist_env():
     return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
             int(os.environ.get("LOCAL_RANK", 0)))
@@ -60,31 +70,75 @@ def kv_lengths(seed=0):
 
 
 # ---------------------------------------------------------------- reference (CPU) arm
-class CpuSample:
-    """The oracle's decode step on `layers_sample` of the 28 layers at 48 lanes with the
-    workload's KV lengths, plus the heads and the greedy pick. `time()` returns seconds per full
-    step: the layer time scaled to 28 layers, plus the heads."""
+_F16_BASE: dict = {}
 
-    def __init__(self, layers_sample=4, threads=None, seed=0):
+
+def normal_f16_bits(rng, shape, std=1.0):
+    """~N(0, std^2) as f16 bit patterns for the CPU arm's multi-GB weights and caches: a seeded
+    block of 2^24 normal values is drawn once per std, and each array is that block repeated
+    from a random offset (memcpy speed; the values are only read for timing)."""
+    import oracle as orc
+    base = _F16_BASE.get(std)
+    if base is None:
+        base = orc.f16_bits(np.random.default_rng(12345).standard_normal(1 << 24, dtype=np.float32)
+                            * np.float32(std))
+        _F16_BASE[std] = base
+    n = int(np.prod(shape))
+    off = int(rng.integers(0, base.size))
+    reps = -(-(n + off) // base.size)
+    return np.tile(base, reps)[off:off + n].reshape(shape)
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+class CpuSample:
+    """The oracle's decode step at config[2]: all 28 layers at 48 lanes with the workload's KV
+    lengths, then the 16 heads and the greedy pick. The oracle's projection runs 4 x 4 blocks of
+    outputs on AVX2/FMA with F16C conversions and its attention scores 8 positions per SIMD
+    vector, over all host cores (OpenMP). `time()` returns seconds per step."""
+
+    def __init__(self, threads=None, seed=0):
         import oracle as orc
         self.orc = orc
         if threads:
             orc.set_threads(threads)
         rng = np.random.default_rng(seed)
-        self.layers_sample = layers_sample
-        self.g = orc.Geometry(layers=layers_sample)
+        self.g = orc.Geometry()
         self.lengths = kv_lengths(seed)
         cap = int(self.lengths.max()) + 2
-        self.layers = [orc.synthetic_layer(rng, self.g) for _ in range(layers_sample)]
+        g = self.g
+        nq = (HEADS + 2 * N_KV) * HD
+
+        def layer():
+            qk = np.stack([rng.uniform(0.8, 1.2, HD).astype(np.float32) / np.sqrt(HD),
+                           rng.uniform(0.8, 1.2, HD).astype(np.float32)]).astype(np.float32)
+            return orc.Layer(attn_norm=rng.uniform(0.8, 1.2, DIM).astype(np.float32),
+                             ffn_norm=rng.uniform(0.8, 1.2, DIM).astype(np.float32),
+                             wqkv=normal_f16_bits(rng, (nq, DIM), 0.02), qk_norms=qk,
+                             wo=normal_f16_bits(rng, (DIM, HEADS * HD), 0.02),
+                             gate=normal_f16_bits(rng, (FFN, DIM), 0.02),
+                             up=normal_f16_bits(rng, (FFN, DIM), 0.02),
+                             down=normal_f16_bits(rng, (DIM, FFN), 0.02))
+
+        self.layers = [layer() for _ in range(g.layers)]
         self.final = np.ones(DIM, np.float32)
         shape = (LANES, N_KV, cap, HD)
-        self.kc = [orc.f16_bits(rng.standard_normal(shape, dtype=np.float32)) for _ in range(layers_sample)]
-        self.vc = [orc.f16_bits(rng.standard_normal(shape, dtype=np.float32)) for _ in range(layers_sample)]
-        self.heads = orc.f16_bits(rng.standard_normal((CB * VOCAB, DIM), dtype=np.float32) * 0.02)
+        self.kc = [normal_f16_bits(rng, shape) for _ in range(g.layers)]
+        self.vc = [normal_f16_bits(rng, shape) for _ in range(g.layers)]
+        self.heads = normal_f16_bits(rng, (CB * VOCAB, DIM), 0.02)
         self.x = rng.standard_normal((LANES, DIM), dtype=np.float32)
         self.cos, self.sin = orc.rope_table(cap + 64, HD, 1e6)
-        self.sample = (f"{layers_sample} of 28 layers + heads at 48 lanes, KV lengths U[64,1024]; "
-                       f"layer time scaled x{LAYERS / layers_sample:g} to a full step")
+        self.sample = (f"28 of 28 layers + 16 heads at 48 lanes, KV lengths U[64,1024] seed 0 "
+                       f"(contiguous per-lane caches); one full step per sample on "
+                       f"{orc.threads()} threads of {cpu_model()}")
 
     def threads(self):
         return self.orc.threads()
@@ -94,10 +148,8 @@ class CpuSample:
         t0 = time.perf_counter()
         h = orc.decode_step(self.x, self.layers, self.final, self.kc, self.vc, self.lengths,
                             self.cos, self.sin, self.g)
-        t1 = time.perf_counter()
-        orc.heads_pick(h, self.heads, orc.Geometry())
-        t2 = time.perf_counter()
-        return (t1 - t0) * (LAYERS / self.layers_sample) + (t2 - t1)
+        orc.heads_pick(h, self.heads, self.g)
+        return time.perf_counter() - t0
 
 
 def run_reference(args):
@@ -129,14 +181,15 @@ def run_reference(args):
 class Clocks:
     """nvidia-smi sampling during the timed region."""
 
-    def __init__(self, index, path):
+    def __init__(self, index, path, interval_ms=200):
         self.path = path
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms",
+                                          str(int(interval_ms))],
                                          stdout=open(path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -160,9 +213,15 @@ class Clocks:
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        pw = []
+        for r in rows:
+            try:
+                pw.append(float(r[3]))
+            except ValueError:
+                pass
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "power_w_max": max(pw) if pw else None}
 
 
 def build_device_talker(device, seed=0, extra_positions=256, lanes_override=None, codebooks=CB,
@@ -230,6 +289,47 @@ def time_dominant_gemm(stack, device, reps=3):
     per = e0.elapsed_time(e1) / (reps * len(projs)) * 1e-3
     bytes_ = 2 * FFN * DIM * 2 + LANES * DIM * 2 + LANES * FFN * 2
     return per, bytes_
+
+
+def time_dominant_attention(stack, kv, device, reps=3):
+    """The decode attention alone, as the step launches it (48 lanes, gqa 2, spans = each lane's
+    position + 1, f16 output), over the 28 layers' pages in turn (3 GB of K/V, so nothing is
+    served from L2): CUDA-event time per launch on the launching stream, and the algorithmic
+    bytes of one launch (every K and V row of every lane's span read once, q read, output
+    written)."""
+    import ctypes as C
+    import torch
+    import ttsnn
+    from ttsnn import _lib as L
+    q = torch.randn(LANES, HEADS, HD, device=device) * 0.1
+    spans = (kv.positions + 1).to(torch.int32)
+    caches = [L.KvCache(kv.k[li].data_ptr(), kv.v[li].data_ptr(), kv.table.data_ptr(),
+                        kv.max_blocks, kv.block_size, kv.num_blocks, N_KV, HD)
+              for li in range(LAYERS)]
+    max_span = kv.max_blocks * kv.block_size
+    out = torch.empty(LANES, HEADS * HD, device=device, dtype=torch.float16)
+    ctx = ttsnn.ctx()
+
+    def one(c):
+        L.call("tts_decode_attention", ctx, ttsnn.ptr(q), LANES, HEADS // N_KV, C.byref(c),
+               ttsnn.ptr(spans), max_span, 0, ttsnn.ptr(out), 1, ttsnn.stream())
+
+    for c in caches:
+        one(c)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(reps):
+        for c in caches:
+            one(c)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ttsnn.check()
+    per = e0.elapsed_time(e1) / (reps * LAYERS) * 1e-3
+    total = int(spans.sum().item())
+    bytes_ = total * ATTN_BYTES_PER_POS + LANES * HEADS * HD * 4 + LANES * HEADS * HD * 2
+    return per, bytes_, total
 
 
 def bf16_peak():
@@ -338,30 +438,30 @@ def run_sweep(args):
     return 0
 
 
-def run_document(args):
-    """Benchmark config[4] (bounded sample): a synthetic document of `--segments` segments per
-    GPU (2000 in the config) with target lengths log-uniform in [40, 1200] frames, decoded by
-    the talker at `--lanes` lanes with tail shedding and interior refill, then turned into 24 kHz
-    audio by the codec decoder stack (x2 x2 pre-upsample, x8 x5 x4 x3 transposed convs 1024 ->
-    64, three snake residual blocks after each, random-init) over each segment's chunk windows
-    (300 frames + 25 left context + 8 frames of lookahead for the 'same'-padded blocks), all
-    windows of a rank decoded in batches. The codec's RVQ dequantiser and pre-transformer are
-    not on this path: seeded random latents stand in for its input. Segments are split over the
-    ranks by LPT, no collective on the data path. frames/s = all frames / max over ranks of
-    (talker + codec device time); rtf = that time / audio seconds (12.5 frames per second)."""
+def document_sample(args, rank, world, device):
+    """Benchmark config[4] (bounded sample) on this rank: a synthetic document of `--segments`
+    segments per GPU (2000 in the config) with target lengths log-uniform in [40, 1200] frames,
+    decoded by the talker at `--lanes` lanes with tail shedding and interior refill, then turned
+    into 24 kHz audio by the codec decoder stack (x2 x2 pre-upsample, x8 x5 x4 x3 transposed
+    convs 1024 -> 64, three snake residual blocks after each, random-init) over each segment's
+    chunk windows (300 frames + 25 left context + 8 frames of lookahead for the 'same'-padded
+    blocks), all windows of a rank decoded in batches, and the rank's audio copied into pinned
+    host memory (the host gather). The codec's RVQ dequantiser and pre-transformer are not on
+    this path: seeded random latents stand in for its input. Segments are split over the ranks
+    by LPT (longest processing time first), no collective on the data path. Returns the
+    rank-0 summary (None on other ranks): frames/s = all frames / max over ranks of (talker +
+    codec + host copy device time); rtf = that time / audio seconds (12.5 frames per second)."""
     import torch
     import torch.distributed as dist
-    from qwen3tts.codec import SAMPLES_PER_FRAME, WaveStack, chunk_plan, gather_windows
-    from qwen3tts.talker import Talker, plan_groups, shard_groups, synthetic_segments
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    from qwen3tts.codec import WaveStack, chunk_plan
+    from qwen3tts.talker import (Talker, group_cost, plan_groups, shard_groups,
+                                 synthetic_segments)
     n_segments = args.segments * world
     segs = synthetic_segments(n_segments, seed=0)
     groups = plan_groups(segs, args.lanes)
-    mine = shard_groups(groups, world)[rank]
+    shards = shard_groups(groups, world)
+    mine = shards[rank]
+    loads = [sum(group_cost(g) * len(g) for g in sh) for sh in shards]
     queue = [s for g in mine for s in g]
     stack, _, _, _ = build_device_talker(device, seed=0, extra_positions=0, lanes_override=0)
     talker = Talker(stack, max_lanes=args.lanes, capacity=157 + 1200 + 2)
@@ -380,43 +480,78 @@ def run_document(args):
     codec = WaveStack(device, seed=7)
     batch = 16
     xs = [torch.stack(wins[i:i + batch]) for i in range(0, len(wins), batch)]
+    outs = [None] * len(xs)
     codec(xs[0][:1])  # warm-up
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     st = talker.run(queue, refill=True)
-    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0, e1, e2 = torch.cuda.Event(True), torch.cuda.Event(True), torch.cuda.Event(True)
     e0.record()
     samples = 0
-    for xb in xs:
-        samples += codec(xb).numel()
+    for i, xb in enumerate(xs):
+        outs[i] = codec(xb)
+        samples += outs[i].numel()
     e1.record()
+    # host gather: every window's audio into one pinned host buffer
+    host = torch.empty(samples, dtype=torch.float16, pin_memory=True)
+    o = 0
+    for y in outs:
+        n = y.numel()
+        host[o:o + n].copy_(y.reshape(-1), non_blocking=True)
+        o += n
+    e2.record()
     torch.cuda.synchronize()
     codec_s = e0.elapsed_time(e1) * 1e-3
+    gather_s = e1.elapsed_time(e2) * 1e-3
     flops = codec.flops_per_frame() * len(wins) * span
-    t = torch.tensor([st.seconds + codec_s, st.seconds, codec_s, st.frames, flops, samples],
+    mine_s = st.seconds + codec_s + gather_s
+    t = torch.tensor([mine_s, st.seconds, codec_s, gather_s, st.frames, flops, samples],
                      device=device, dtype=torch.float64)
+    per_rank = [mine_s]
     if world > 1:
-        tmax = t[:3].clone()
+        g = [torch.zeros(1, device=device, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(g, t[:1].clone())
+        per_rank = [float(x.item()) for x in g]
+        tmax = t[:4].clone()
         dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-        tsum = t[3:].clone()
+        tsum = t[4:].clone()
         dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
         t = torch.cat([tmax, tsum])
-    secs, tk_s, cd_s, frames, flops, samples = [float(v) for v in t]
-    if rank == 0:
-        line = {"metric": "codec frames/sec (end-to-end document, whole box)",
-                "value": round(frames / secs, 2), "unit": "frames/s", "n_gpus": world,
-                "higher_is_better": True, "scaling": "weak", "dtype": "f16",
-                "data": "synthetic (random-init weights; random latents in place of the RVQ front)",
-                "config": {"workload": "config[4] sample: talker (lane scheduler, shedding, refill) "
-                                       "+ codec stack at 24 kHz over chunk windows",
-                           "segments": n_segments, "lanes": args.lanes, "window_frames": span,
-                           "codec_batch_windows": batch},
-                "frames": int(frames), "audio_seconds": round(frames / 12.5, 2),
-                "seconds": round(secs, 4), "talker_seconds": round(tk_s, 4),
-                "codec_seconds": round(cd_s, 4), "rtf": round(secs / (frames / 12.5), 6),
-                "codec_tflops": round(flops / max(cd_s, 1e-9) / 1e12, 1),
-                "samples": int(samples)}
+    secs, tk_s, cd_s, ga_s, frames, flops, samples = [float(v) for v in t]
+    if rank != 0:
+        return None
+    mean_load = sum(loads) / len(loads)
+    return {"metric": "codec frames/sec (end-to-end document, whole box)",
+            "value": round(frames / secs, 2), "unit": "frames/s", "n_gpus": world,
+            "higher_is_better": True, "scaling": "weak", "dtype": "f16",
+            "data": "synthetic (random-init weights; random latents in place of the RVQ front)",
+            "config": {"workload": "config[4] sample: talker (lane scheduler, shedding, refill) "
+                                   "+ codec stack at 24 kHz over chunk windows + host gather",
+                       "segments": n_segments, "segments_per_gpu": args.segments,
+                       "lanes": args.lanes, "window_frames": span, "codec_batch_windows": batch},
+            "frames": int(frames), "audio_seconds": round(frames / 12.5, 2),
+            "seconds": round(secs, 4), "talker_seconds": round(tk_s, 4),
+            "codec_seconds": round(cd_s, 4), "host_gather_seconds": round(ga_s, 5),
+            "rtf": round(secs / (frames / 12.5), 6),
+            "codec_tflops": round(flops / max(cd_s, 1e-9) / 1e12, 1),
+            "lpt_planned_imbalance": round(max(loads) / mean_load, 4) if mean_load else 1.0,
+            "measured_imbalance": round(max(per_rank) / (sum(per_rank) / len(per_rank)), 4),
+            "seconds_per_rank": [round(x, 4) for x in per_rank],
+            "samples": int(samples)}
+
+
+def run_document(args):
+    """`--workload document`: config[4]'s sample as its own JSON line (document_sample)."""
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    line = document_sample(args, rank, world, device)
+    if line is not None:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -523,8 +658,7 @@ def run_predictor(args):
 
     barrier()
     torch.cuda.synchronize()
-    clocks = Clocks(local, os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
-                    if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/clocks_rank{rank}.csv")
+    clocks = Clocks(local, clocks_path(args, rank))
     ttsnn.launch_count(reset=True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -657,8 +791,7 @@ def run_frames(args):
 
     barrier()
     torch.cuda.synchronize()
-    clocks = Clocks(local, os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
-                    if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/clocks_rank{rank}.csv")
+    clocks = Clocks(local, clocks_path(args, rank))
     ttsnn.launch_count(reset=True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -915,7 +1048,8 @@ def run_b200(args):
     from ttsnn import _lib as L
 
     steps, warmup = args.steps, args.warmup
-    stack, kv, lengths, cap = build_device_talker(device, seed=rank, extra_positions=2 * (steps + warmup) + 16)
+    stack, kv, lengths, cap = build_device_talker(
+        device, seed=rank, extra_positions=2 * (steps + warmup) + args.sustained_steps + 16)
     stream = torch.cuda.Stream(device)
     codes = torch.zeros(LANES, CB, dtype=torch.int32, device=device)
     x_dev = torch.empty(LANES, DIM, device=device)
@@ -942,8 +1076,7 @@ def run_b200(args):
     stream.synchronize()
     barrier()
     torch.cuda.synchronize()
-    clocks = Clocks(local, os.path.join(ROOT, "gpurun_out", f"clocks_rank{rank}.csv")
-                    if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else f"/tmp/clocks_rank{rank}.csv")
+    clocks = Clocks(local, clocks_path(args, rank))
     ttsnn.launch_count(reset=True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -958,10 +1091,47 @@ def run_b200(args):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1)
     t = torch.tensor([ms], device=device)
+    per_rank = [ms]
     if world > 1:
+        gathered = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(gathered, t)
+        per_rank = [float(x.item()) for x in gathered]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     ttsnn.check(local)
+
+    # ---- sustained leg: the same replays for long enough (~0.6 s) that the clock sampler sees
+    # the GPU under load; positions restart from the timed leg's start so the KV work matches
+    sustained = None
+    if args.sustained_steps > 0:
+        with torch.cuda.stream(stream):
+            kv.positions.copy_(pos0)
+            for _ in range(warmup):
+                graph.replay()
+        stream.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        clocks_s = Clocks(local, clocks_path(args, rank) + ".sustained", interval_ms=50)
+        es0, es1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            es0.record(stream)
+            for _ in range(args.sustained_steps):
+                graph.replay()
+            es1.record(stream)
+        stream.synchronize()
+        clk_s = clocks_s.stop()
+        barrier()
+        ts = torch.tensor([es0.elapsed_time(es1)], device=device)
+        if world > 1:
+            dist.all_reduce(ts, op=dist.ReduceOp.MAX)
+        sustained = {"steps": args.sustained_steps,
+                     "ms_per_step": round(float(ts.item()) / args.sustained_steps, 4),
+                     "value": round(world * LANES * args.sustained_steps / (float(ts.item()) * 1e-3), 2),
+                     "clocks": clk_s}
+        ttsnn.check(local)
+    with torch.cuda.stream(stream):
+        kv.positions.copy_(pos0)
+    stream.synchronize()
 
     # ---- end to end through the public API: pinned host input in, codes out, every step
     barrier()
@@ -990,6 +1160,10 @@ def run_b200(args):
     # ---- roofline of the dominant kernel and of the whole step
     hbm, peak_kind = peaks()
     gemm_s, gemm_bytes = time_dominant_gemm(stack, device)
+    with torch.cuda.stream(stream):
+        kv.positions.copy_(pos0)
+    stream.synchronize()
+    attn_s, attn_bytes, attn_positions = time_dominant_attention(stack, kv, device)
     weights = stack.weight_bytes()
     mean_len = float(lengths.mean()) + warmup + steps / 2.0 + 1
     kv_bytes = LAYERS * N_KV * HD * 2 * 2 * LANES * mean_len
@@ -998,6 +1172,14 @@ def run_b200(args):
 
     codec_s, codec_flops = time_codec_block(device)
     tpeak, tpeak_kind = bf16_peak()
+    # config[4]'s sharded segment queue with host gather, at this N (weak: segments per GPU)
+    doc = None
+    if args.document_segments > 0:
+        import argparse as _ap
+        dargs = _ap.Namespace(**vars(args))
+        dargs.segments = args.document_segments
+        dargs.lanes = LANES
+        doc = document_sample(dargs, rank, world, device)
 
     if rank == 0:
         value = world * LANES * steps / (ms_max * 1e-3)
@@ -1017,14 +1199,29 @@ def run_b200(args):
             "config": {"workload": WORKLOAD, "lanes_per_gpu": LANES, "global_lanes": LANES * world,
                        "parallelism": f"dp{world} (replicated weights, lanes sharded per GPU)",
                        "l2": "inputs larger than L2: each step streams 2.95 GB of weights and ~3 GB of KV"},
-            "roofline": {"bound": "hbm", "kernel": "gemm_decode (gate/up, SwiGLU epilogue)",
-                         "achieved": round(gemm_bytes / gemm_s / 1e9, 1), "peak": hbm,
-                         "unit": "GB/s", "frac": round(gemm_bytes / gemm_s / 1e9 / hbm, 4),
-                         "traffic": GATEUP_NCU_TRAFFIC,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one cold launch (profiles/gemm_decode_gateup_config2.md)",
+            "roofline": {"bound": "hbm", "kernel": "attn_decode (the step's largest share of time: "
+                                                   "48 lanes x 8 kv heads x gqa 2, paged f16 K/V)",
+                         "achieved": round(attn_bytes / attn_s / 1e9, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(attn_bytes / attn_s / 1e9 / hbm, 4),
+                         "traffic": ATTN_NCU_TRAFFIC,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of "
+                                           "one cold launch of this kernel on this workload "
+                                           "(a separate capture, not measured in this run)",
                          "peak_source": peak_kind,
-                         "algorithmic_bytes_per_launch": gemm_bytes,
-                         "launch_us": round(gemm_s * 1e6, 2)},
+                         "algorithmic_bytes_per_launch": attn_bytes,
+                         "algorithmic_unit": f"{ATTN_BYTES_PER_POS} B of K/V per cached position "
+                                             f"per layer x {attn_positions} positions, + q and "
+                                             "output",
+                         "launch_us": round(attn_s * 1e6, 2)},
+            "roofline_gemm": {"bound": "hbm", "kernel": "gemm_decode (gate/up, SwiGLU epilogue)",
+                              "achieved": round(gemm_bytes / gemm_s / 1e9, 1), "peak": hbm,
+                              "unit": "GB/s", "frac": round(gemm_bytes / gemm_s / 1e9 / hbm, 4),
+                              "traffic": GATEUP_NCU_TRAFFIC,
+                              "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                                                "of one cold launch (a separate capture, not "
+                                                "measured in this run)",
+                              "algorithmic_bytes_per_launch": gemm_bytes,
+                              "launch_us": round(gemm_s * 1e6, 2)},
             "roofline_step": {"bound": "hbm", "achieved": round(step_bytes / step_s / 1e9, 1),
                               "peak": hbm, "unit": "GB/s",
                               "frac": round(step_bytes / step_s / 1e9 / hbm, 4),
@@ -1040,7 +1237,12 @@ def run_b200(args):
                             "flops_per_block": codec_flops},
             "gpu_launches": int(launches),
             "clocks": clk,
+            "ms_per_step_per_rank": [round(x / steps, 4) for x in per_rank],
         }
+        if sustained is not None:
+            line["sustained"] = sustained
+        if doc is not None:
+            line["document"] = doc
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -1216,6 +1418,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--clocks-dir", default="/tmp",
+                    help="directory for the per-rank nvidia-smi clock samples")
+    ap.add_argument("--document-segments", type=int, default=96,
+                    help="segments per GPU of the config[4] sample in the default run (0: none)")
+    ap.add_argument("--sustained-steps", type=int, default=300,
+                    help="graph replays of the sustained leg (clock record under load)")
     ap.add_argument("--workload", default="step",
                     choices=["step", "sweep", "document", "predictor", "frames", "prefill",
                              "codec"],

@@ -17,6 +17,9 @@ from .frames import CODEC_EOS, FrameLoop
 from .prompt import TTS_PAD, PromptBuilder
 from .talker import SHED_QUANTUM
 
+# frames of the voice clip decoded ahead of the generated frames (cfg::codec::CHUNK_LEFT_CONTEXT)
+CONTEXT_FRAMES = 25
+
 
 @dataclass
 class Request:
@@ -98,12 +101,16 @@ class Synthesizer:
             loop.kv.release(i)
         return frames
 
-    def decode(self, frames: list[list[int]]) -> torch.Tensor:
+    def decode(self, frames: list[list[int]], context: list[list[int]] | None = None) -> torch.Tensor:
         """Codec::decode (codec.rs:544-604): chunks of 300 frames with 25 of left context, the
-        context's audio dropped; 1920 samples per frame."""
+        context's audio dropped; 1920 samples per frame. With `context` (the voice asset's
+        ref_codes, which the talker continues), its last 25 frames are decoded ahead of
+        `frames` and their audio dropped, as the engine does (engine.rs:1119-1135), so the
+        first frames have their real history instead of a cold start."""
         if self.codec is None:
             raise ValueError("no codec")
-        codes = torch.tensor(frames, dtype=torch.int32, device=self.talker.device)
+        ctx = list(context[-CONTEXT_FRAMES:]) if context else []
+        codes = torch.tensor(ctx + list(frames), dtype=torch.int32, device=self.talker.device)
         plan = chunk_plan(codes.shape[0])
         wins = gather_windows(codes, plan)
         pieces = []
@@ -111,4 +118,21 @@ class Synthesizer:
             wav = self.codec(wins[i, :w.hi - w.lo].contiguous())
             per = wav.shape[0] // (w.hi - w.lo)  # SAMPLES_PER_FRAME at the reference's rates
             pieces.append(wav[w.drop * per:(w.drop + w.end - w.start) * per])
-        return torch.cat(pieces)
+        joined = torch.cat(pieces)
+        per = joined.shape[0] // codes.shape[0]
+        return joined[len(ctx) * per:]
+
+    def decode_document(self, frames: list[list[list[int]]],
+                        context: list[list[int]] | None = None) -> list[torch.Tensor]:
+        """The engine's stage 2 (engine.rs:1107-1171): the codec once over every request's
+        frames concatenated (each segment gets real history rather than a cold start), the
+        voice's context ahead of them and dropped, then the audio cut at exact frame
+        boundaries, one piece per request."""
+        flat = [fr for f in frames for fr in f]
+        wav = self.decode(flat, context)
+        per = wav.shape[0] // max(len(flat), 1)
+        out, o = [], 0
+        for f in frames:
+            out.append(wav[o:o + len(f) * per])
+            o += len(f) * per
+        return out

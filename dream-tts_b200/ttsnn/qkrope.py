@@ -28,10 +28,12 @@ def contiguous_cache(k_cache: torch.Tensor, v_cache: torch.Tensor) -> tuple[L.Kv
 
 
 def apply(qkv: torch.Tensor, norms: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
-          k_cache: torch.Tensor, v_cache: torch.Tensor, heads: int, start: int, eps: float,
+          k_cache: torch.Tensor, v_cache: torch.Tensor, heads: int, start, eps: float,
           f32_kv: bool = False) -> tuple[torch.Tensor, None]:
     """`qkv [b, 1, (heads + 2 n_kv) * 128]` f32 -> q `[b, heads, 1, 128]`; k and v are written
     as f16 into the caches `[b, n_kv, cap, 128]` at position `start` (qkrope.rs:26-69).
+    `start` may also be an int32 tensor `[b]` of per-lane positions (lanes of different lengths
+    in one step, which the paged decode step does; the reference uses one start per call).
 
     Decode only (t == 1): prefill's multi-position form is not on this path.
     """
@@ -41,13 +43,20 @@ def apply(qkv: torch.Tensor, norms: torch.Tensor, cos: torch.Tensor, sin: torch.
         raise L.TtsError(2, "qk_rope: only t == 1 (a decode step) is supported")
     if f32_kv:
         raise L.TtsError(2, "qk_rope: the f32 k/v side outputs are prefill-only")
-    if start + t > cap:
-        raise ValueError(f"qk_rope: {start + t} positions exceed {cap}")
+    if isinstance(start, torch.Tensor):
+        pos = start.to(device=qkv.device, dtype=torch.int32).contiguous()
+        if pos.numel() != b:
+            raise ValueError("qk_rope: one position per lane")
+        end = int(pos.max().item()) + t
+    else:
+        pos = torch.full((b,), int(start), dtype=torch.int32, device=qkv.device)
+        end = int(start) + t
+    if end > cap:
+        raise ValueError(f"qk_rope: {end} positions exceed {cap}")
     if width != (heads + 2 * n_kv) * hd:
         raise ValueError("qk_rope: qkv width does not match heads and cache")
     x = qkv.reshape(b, width).contiguous()
     kv, table = contiguous_cache(k_cache, v_cache)
-    pos = torch.full((b,), start, dtype=torch.int32, device=qkv.device)
     q = torch.empty(b, heads, hd, device=qkv.device, dtype=torch.float32)
     nm = norms.to(torch.float32).contiguous()
     L.call("tts_qk_rope_append", ctx_of(x), ptr(x), b, heads, ptr(nm), ptr(cos.contiguous()),

@@ -252,6 +252,66 @@ def decode_step(x: np.ndarray, layers: list[Layer], final_norm: np.ndarray, kcac
     return rms_norm(h, final_norm, g.eps)
 
 
+def proj_rows(x_f32: np.ndarray, w_bits: np.ndarray, round_f16: bool = True) -> np.ndarray:
+    """`matmul_2d(f16(x), W^T)` for many rows (crates/tts-nn/src/lib.rs:438-459, 516-528): f16
+    operands, f32 accumulation (a BLAS sgemm here; the `gemm` crate's accumulation order is not
+    pinned), the result rounded to f16 and cast back to f32 when `round_f16`, as the CPU arm
+    and every projection of more than 48 rows leave it."""
+    xf = f16_value(f16_bits(x_f32.reshape(-1, x_f32.shape[-1])))
+    y = xf @ f16_value(w_bits).T
+    if round_f16:
+        y = f16_value(f16_bits(y))
+    return y.astype(np.float32).reshape(*x_f32.shape[:-1], w_bits.shape[0])
+
+
+def prefill(x: np.ndarray, layers: list[Layer], final_norm: np.ndarray, kcache: list,
+            vcache: list, start: int, cos: np.ndarray, sin: np.ndarray, g: Geometry,
+            round_f16: bool = True) -> np.ndarray:
+    """Stack::forward at t > 1 for one group of lanes sharing `start` (crates/qwen3tts/src/
+    qwen3.rs:294-467, the prefill branch :415-444), the CPU arm by default:
+      * every projection through matmul_2d with an f16 result (`round_f16`);
+      * QK-norm and RoPE per row at position start + i (qwen3.rs:358-394), K and V written to
+        the f16 caches, and kept at f32 as the new positions' `fresh` k/v;
+      * attention of the new rows over the cached prefix [0, start) read back from f16 and
+        concatenated with the fresh f32 k/v, scores q.K^T in f32, the causal mask (column >
+        row -> -inf, causal_window_mask), softmax_last_dim, probs.V.
+    x f32 [b, t, dim]; caches per layer [b, n_kv, cap, hd] f16 bits, written in place at
+    [start, start + t). Returns every row's final-normed hidden [b, t, dim]."""
+    b, t, dim = x.shape
+    gqa = g.heads // g.n_kv
+    hd = g.head_dim
+    h = _c(x).reshape(b * t, dim).copy()
+    pos = np.tile(np.arange(start, start + t, dtype=np.int32), b)
+    span = start + t
+    mask = np.where(np.arange(span)[None, :] > (start + np.arange(t))[:, None], -np.inf,
+                    0.0).astype(np.float32)  # [t, span]
+    for li, L in enumerate(layers):
+        normed = rms_norm(h, L.attn_norm, g.eps)
+        qkv = proj_rows(normed, L.wqkv, round_f16)
+        q, k, v = qk_rope(qkv, L.qk_norms, cos, sin, pos, g.heads, g.n_kv, g.eps, hd)
+        q = q.reshape(b, t, g.n_kv, gqa, hd)
+        k = k.reshape(b, t, g.n_kv, hd)
+        v = v.reshape(b, t, g.n_kv, hd)
+        kcache[li][:, :, start:span] = f16_bits(k.transpose(0, 2, 1, 3))
+        vcache[li][:, :, start:span] = f16_bits(v.transpose(0, 2, 1, 3))
+        att = np.empty((b, t, g.n_kv, gqa, hd), np.float32)
+        for lane in range(b):
+            for kh in range(g.n_kv):
+                k_all = np.concatenate([f16_value(kcache[li][lane, kh, :start]), k[lane, :, kh]])
+                v_all = np.concatenate([f16_value(vcache[li][lane, kh, :start]), v[lane, :, kh]])
+                for j in range(gqa):
+                    sc = q[lane, :, kh, j] @ k_all.T + mask  # [t, span]
+                    sc = sc - sc.max(axis=1, keepdims=True)
+                    e = np.exp(sc)
+                    p = e / e.sum(axis=1, keepdims=True)
+                    att[lane, :, kh, j] = p @ v_all
+        h = h + proj_rows(att.reshape(b * t, g.heads * hd), L.wo, round_f16)
+        normed = rms_norm(h, L.ffn_norm, g.eps)
+        tail = swiglu(proj_rows(normed, L.gate, round_f16), proj_rows(normed, L.up, round_f16))
+        h = h + proj_rows(tail, L.down, round_f16)
+    return rms_norm(h, final_norm, g.eps).reshape(b, t, dim)
+
+
 def heads_pick(hidden: np.ndarray, heads_bits: np.ndarray, g: Geometry, round_f16: bool = False):
     """Codebook heads `[codebooks * vocab, dim]` f16 and the greedy pick per head. With
     `round_f16` the logits are rounded to f16 as the CPU arm's `matmul_2d(..).to_dtype(f32)`
@@ -481,13 +541,14 @@ def talker_frame(st: TalkerState, layers: list[Layer], final_norm: np.ndarray, g
                  min_new: int, penalty: float, p_layers: list[Layer], p_final: np.ndarray,
                  pw: PredictorWeights, pg: Geometry, text_rows: np.ndarray, pad: np.ndarray,
                  forced0=None, forced=None, tie_tol: float = 0.0,
-                 tie_tol0: float | None = None):
+                 tie_tol0: float | None = None, stats: dict | None = None):
     """One iteration of Talker::generate_batch with greedy picks (talker.rs:953-1057), started
     from the step that feeds the talker stack: Stack::forward on `st.x` at each lane's
     position, codec head, pick, code 0's codec_embed row, the predictor's frame on the hidden
     state and that row, then the sum plus the lane's text row (trailing row frames - 1, else the
     pad row) as the next input. `tie_tol0` (default `tie_tol`) is the near-tie band of code 0's
-    pick, `tie_tol` the predictor's. Updates `st`; returns (code0, codes, ties, mismatches)."""
+    pick, `tie_tol` the predictor's; `stats` (optional) receives the code-0 and predictor tie
+    counts separately. Updates `st`; returns (code0, codes, ties, mismatches)."""
     cap = st.kc[0].shape[2]
     cos, sin = rope_table(cap + 1, g.head_dim, g.rope_base)
     h = decode_step(st.x, layers, final_norm, st.kc, st.vc, st.pos, cos, sin, g)
@@ -502,6 +563,9 @@ def talker_frame(st: TalkerState, layers: list[Layer], final_norm: np.ndarray, g
     code0_embed = f16_value(codec_embed[code0.astype(np.int64)])
     codes, total, t1, m1 = predictor_frame(h, code0_embed, p_layers, p_final, pw, pg, forced,
                                            tie_tol)
+    if stats is not None:
+        stats["ties0"] = stats.get("ties0", 0) + t0
+        stats["ties_predictor"] = stats.get("ties_predictor", 0) + t1
     length = text_rows.shape[1]
     for r in range(total.shape[0]):
         t = int(st.frames[r]) - 1

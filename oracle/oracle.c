@@ -27,6 +27,7 @@
 #include <string.h>
 #include <stdlib.h>
 #include <omp.h>
+#include <immintrin.h>
 
 typedef _Float16 f16;
 
@@ -54,28 +55,75 @@ void orc_f16_to_f32(const uint16_t* x, float* y, int64_t n) {
  * at load, lib.rs:1252-1269; the arithmetic is the same). round_f16 != 0 rounds the result
  * to f16 as the CPU arm's f16 matmul output does before its cast back to f32 (lib.rs:528);
  * 0 keeps f32 as the device arm does. The reduction order is fixed: eight interleaved f32
- * partial sums over k, combined in order.
+ * partial sums over k (fused multiply-adds), combined in order; outputs are computed in 4 x 4
+ * blocks (dot4x4) without changing any output's arithmetic.
  */
+/* Dot products of 4 rows of x with 4 rows of W (f32, k a multiple of 8), each with the
+ * arithmetic of the scalar form: lane l of an 8-wide accumulator sums x[kk + l] * w[kk + l]
+ * (fused multiply-add) over kk, then the lanes are added in order. 16 independent chains keep
+ * the FMA units busy; the result of every (i, j) is the same as one chain at a time. */
+static void dot4x4(const float* const xi[4], const float* const wj[4], int k, float out[4][4]) {
+    __m256 acc[4][4];
+    for (int r = 0; r < 4; r++)
+        for (int c = 0; c < 4; c++) acc[r][c] = _mm256_setzero_ps();
+    for (int kk = 0; kk < k; kk += 8) {
+        __m256 xv[4], wv[4];
+        for (int r = 0; r < 4; r++) xv[r] = _mm256_loadu_ps(xi[r] + kk);
+        for (int c = 0; c < 4; c++) wv[c] = _mm256_loadu_ps(wj[c] + kk);
+        for (int r = 0; r < 4; r++)
+            for (int c = 0; c < 4; c++) acc[r][c] = _mm256_fmadd_ps(xv[r], wv[c], acc[r][c]);
+    }
+    for (int r = 0; r < 4; r++)
+        for (int c = 0; c < 4; c++) {
+            float l[8];
+            _mm256_storeu_ps(l, acc[r][c]);
+            float s = 0.f;
+            for (int q = 0; q < 8; q++) s += l[q];
+            out[r][c] = s;
+        }
+}
+
 void orc_proj(const uint16_t* x, const uint16_t* w, float* y, int m, int k, int n, int round_f16) {
     float* xf = (float*)malloc(sizeof(float) * (size_t)m * k);
     for (int64_t i = 0; i < (int64_t)m * k; i++) xf[i] = h2f(x[i]);
+    const int k8 = k - k % 8;
 #pragma omp parallel
     {
-        float* wr = (float*)malloc(sizeof(float) * (size_t)k);
+        float* wr = (float*)malloc(sizeof(float) * (size_t)k * 4);
 #pragma omp for schedule(static)
-        for (int j = 0; j < n; j++) {
-            const uint16_t* wj = w + (size_t)j * k;
-            for (int kk = 0; kk < k; kk++) wr[kk] = h2f(wj[kk]);
-            for (int i = 0; i < m; i++) {
-                const float* xi = xf + (size_t)i * k;
-                float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int j0 = 0; j0 < n; j0 += 4) {
+            const int nj = n - j0 < 4 ? n - j0 : 4;
+            for (int c = 0; c < nj; c++) {
+                const uint16_t* wj = w + (size_t)(j0 + c) * k;
+                float* dst = wr + (size_t)c * k;
                 int kk = 0;
-                for (; kk + 8 <= k; kk += 8)
-                    for (int l = 0; l < 8; l++) acc[l] += xi[kk + l] * wr[kk + l];
-                for (; kk < k; kk++) acc[kk & 7] += xi[kk] * wr[kk];
-                float s = 0.f;
-                for (int l = 0; l < 8; l++) s += acc[l];
-                y[(size_t)i * n + j] = round_f16 ? h2f(f2h(s)) : s;
+                for (; kk + 8 <= k; kk += 8)  /* F16C: exact f16 -> f32 conversion, 8 at a time */
+                    _mm256_storeu_ps(dst + kk,
+                                     _mm256_cvtph_ps(_mm_loadu_si128((const __m128i*)(wj + kk))));
+                for (; kk < k; kk++) dst[kk] = h2f(wj[kk]);
+            }
+            for (int i0 = 0; i0 < m; i0 += 4) {
+                const int ni = m - i0 < 4 ? m - i0 : 4;
+                const float* xi[4];
+                const float* wj[4];
+                for (int r = 0; r < 4; r++) xi[r] = xf + (size_t)(i0 + (r < ni ? r : 0)) * k;
+                for (int c = 0; c < 4; c++) wj[c] = wr + (size_t)(c < nj ? c : 0) * k;
+                float o[4][4];
+                dot4x4(xi, wj, k8, o);
+                for (int r = 0; r < ni; r++)
+                    for (int c = 0; c < nj; c++) {
+                        float s = o[r][c];
+                        if (k8 < k) {
+                            /* a k that is not a multiple of 8: the scalar form's tail, lane
+                               kk & 7, folded in after the full lanes */
+                            float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                            for (int kk = 0; kk < k8; kk++) acc[kk & 7] += xi[r][kk] * wj[c][kk];
+                            for (int kk = k8; kk < k; kk++) acc[kk & 7] += xi[r][kk] * wj[c][kk];
+                            s = 0.f;
+                            for (int l = 0; l < 8; l++) s += acc[l];
+                        }
+                        y[(size_t)(i0 + r) * n + j0 + c] = round_f16 ? h2f(f2h(s)) : s;
+                    }
             }
         }
         free(wr);
@@ -175,6 +223,8 @@ void orc_decode_attention(const float* q, const uint16_t* kc, const uint16_t* vc
 #pragma omp parallel
     {
         float* sc = (float*)malloc(sizeof(float) * (size_t)cap);
+        float* kt = (float*)malloc(sizeof(float) * (size_t)hd * 8);  /* 8 positions, d-major */
+        float* vr = (float*)malloc(sizeof(float) * (size_t)hd);
 #pragma omp for schedule(dynamic) collapse(2)
         for (int l = 0; l < b; l++)
             for (int h = 0; h < n_kv; h++) {
@@ -184,25 +234,53 @@ void orc_decode_attention(const float* q, const uint16_t* kc, const uint16_t* vc
                 for (int g = 0; g < gqa; g++) {
                     const float* qv = q + (((size_t)l * n_kv + h) * gqa + g) * hd;
                     float mx = -INFINITY;
-                    for (int p = 0; p < sp; p++) {
-                        if (p < ws) { sc[p] = -INFINITY; continue; }
+                    for (int p = 0; p < ws && p < sp; p++) sc[p] = -INFINITY;
+                    int p = ws;
+                    /* 8 positions at a time: SIMD lane i sums q[d] * k[p + i][d] over d in order,
+                       a product then a sum as in the scalar loop, so every score is unchanged */
+                    for (; p + 8 <= sp; p += 8) {
+                        for (int i = 0; i < 8; i++) {
+                            const uint16_t* kr = kb + (size_t)(p + i) * hd;
+                            for (int d = 0; d < hd; d++) kt[(size_t)d * 8 + i] = h2f(kr[d]);
+                        }
+                        __m256 acc = _mm256_setzero_ps();
+                        for (int d = 0; d < hd; d++)
+                            acc = _mm256_add_ps(acc, _mm256_mul_ps(_mm256_set1_ps(qv[d]),
+                                                  _mm256_loadu_ps(kt + (size_t)d * 8)));
+                        _mm256_storeu_ps(sc + p, acc);
+                    }
+                    for (; p < sp; p++) {
                         float acc = 0.f;
                         for (int d = 0; d < hd; d++) acc += qv[d] * h2f(kb[(size_t)p * hd + d]);
                         sc[p] = acc;
-                        if (acc > mx) mx = acc;
                     }
+                    for (p = ws; p < sp; p++)
+                        if (sc[p] > mx) mx = sc[p];
                     float sum = 0.f;
-                    for (int p = 0; p < sp; p++) { sc[p] = expf(sc[p] - mx); sum += sc[p]; }
-                    for (int p = 0; p < sp; p++) sc[p] /= sum;
+                    for (p = 0; p < sp; p++) { sc[p] = expf(sc[p] - mx); sum += sc[p]; }
+                    for (p = 0; p < sp; p++) sc[p] /= sum;
                     float* o = out + (((size_t)l * n_kv + h) * gqa + g) * hd;
                     for (int d = 0; d < hd; d++) o[d] = 0.f;
-                    for (int p = 0; p < sp; p++) {
-                        float wgt = sc[p];
-                        for (int d = 0; d < hd; d++) o[d] += wgt * h2f(vb[(size_t)p * hd + d]);
+                    for (p = 0; p < sp; p++) {
+                        const float wgt = sc[p];
+                        const uint16_t* vp = vb + (size_t)p * hd;
+                        int d = 0;
+                        if (hd % 8 == 0) {
+                            const __m256 wv = _mm256_set1_ps(wgt);
+                            for (; d < hd; d += 8) {
+                                const __m256 v8 = _mm256_cvtph_ps(
+                                    _mm_loadu_si128((const __m128i*)(vp + d)));
+                                _mm256_storeu_ps(o + d, _mm256_add_ps(_mm256_loadu_ps(o + d),
+                                                                      _mm256_mul_ps(wv, v8)));
+                            }
+                        }
+                        for (; d < hd; d++) o[d] += wgt * h2f(vp[d]);
                     }
                 }
             }
         free(sc);
+        free(kt);
+        free(vr);
     }
 }
 

@@ -43,10 +43,11 @@ def build(orc, seed, group=False):
     head[EOS] = head[10] * 1.04
     head[290] = head[10] * 2.0
     if group:
-        # eight rows proportional to row 10: their logits keep fixed ratios frame after frame,
-        # so which of them leads depends on how often each was emitted
+        # eight rows proportional to row 10 and three times its size: their logits keep fixed
+        # ratios frame after frame and lead whenever they are positive, so which of them leads
+        # depends on how often each was emitted
         for i in range(8):
-            head[40 + i] = head[10] * (1.0 + 0.012 * i)
+            head[40 + i] = head[10] * 3.0 * (1.0 + 0.012 * i)
     head = orc.f16_bits(head)
     embed = orc.f16_bits(rng.standard_normal((VOCAB, g.dim), dtype=np.float32) * 0.02)
     for L_ in (kc, vc):
@@ -90,7 +91,7 @@ def oracle_state(orc, m):
                            frames=np.zeros(LANES, np.int64), x=m["x"].copy())
 
 
-def run_frames(tt, orc, m, frames, tie_tol, tie_tol0=None):
+def run_frames(tt, orc, m, frames, tie_tol, tie_tol0=None, stats=None):
     loop, talker, pred = device_loop(orc, m)
     st = oracle_state(orc, m)
     ties = 0
@@ -104,7 +105,7 @@ def run_frames(tt, orc, m, frames, tie_tol, tie_tol0=None):
         want0, want, t, mism = orc.talker_frame(
             st, m["Ls"], m["final"], m["g"], m["head"], m["embed"], BANNED, EOS, MIN_NEW,
             PENALTY, m["pLs"], m["pfinal"], m["pw"], m["pg"], m["text"], m["pad"],
-            forced0=c0, forced=codes, tie_tol=tie_tol, tie_tol0=tie_tol0)
+            forced0=c0, forced=codes, tie_tol=tie_tol, tie_tol0=tie_tol0, stats=stats)
         assert mism == 0, (f, c0, want0, codes, want)
         ties += t
         assert np.array_equal(want0, c0) and np.array_equal(want, codes)
@@ -128,12 +129,19 @@ def test_frame_loop_matches_oracle(tt, orc):
 
 def test_frame_loop_penalty_decides_long_run(tt, orc):
     """128 frames over a head with eight proportional leading rows: ids repeat many times, and
-    the penalty's per-occurrence count decides which of them leads."""
+    the penalty's per-occurrence count decides which of them leads. Code 0 may differ from the
+    oracle only on a near-tie of 1e-4 (absolute, on logits of order 1): an f32 accumulation-
+    order difference after a hundred frames of hidden-state drift. A difference the rule makes
+    is a factor of 1.05 per occurrence, hundreds of times that band, so no rule-decided pick
+    can pass as a tie; at most two such near-ties in 640 picks."""
     m = build(orc, 43, group=True)
-    # no tie allowance for code 0 (the pick the rule makes); the predictor's near-ties as above
-    picks, ties = run_frames(tt, orc, m, 128, 2e-3, tie_tol0=0.0)
+    stats = {}
+    picks, ties = run_frames(tt, orc, m, 128, 2e-3, tie_tol0=1e-4, stats=stats)
+    print(f"long run: code-0 near-ties {stats.get('ties0', 0)} of {picks.size}, predictor "
+          f"near-ties {stats.get('ties_predictor', 0)}")
+    assert stats.get("ties0", 0) <= 2
     group = (picks >= 40) & (picks < 48)
-    assert group.mean() > 0.2
+    assert group.mean() > 0.25, group.mean()
     per_lane = [Counter(p.tolist()) for p in picks.T]
     assert max(max(c.values()) for c in per_lane) >= 5  # ids emitted many times
 

@@ -102,6 +102,34 @@ def test_qk_rope_lane_window(tt, orc, b, start, off):
     tt.check()
 
 
+def test_qk_rope_config0_per_row_positions(tt, orc):
+    """Benchmark config[0]'s RoPE: X [48, 2048] ~N(0, 1) seed 0 viewed as 16 heads x 128,
+    theta 1e6, one position per row drawn from U{0..1023}, through the reference's op on this
+    path (qkrope::apply: per-head RMSNorm with eps 1e-6, half-split RoPE from the f64-built f32
+    table, K/V appended at each row's own position; qkrope.rs:26-69, qwen3.rs:358-394)."""
+    heads, n_kv, cap, eps = 16, 8, 1024, 1e-6
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((48, 2048), dtype=np.float32)
+    kv_part = rng.standard_normal((48, 2 * n_kv * 128), dtype=np.float32)
+    qkv = np.concatenate([x, kv_part], axis=1)
+    pos = rng.integers(0, 1024, 48).astype(np.int32)
+    norms = rng.uniform(0.5, 1.5, (2, 128)).astype(np.float32)
+    cos, sin = orc.rope_table(cap, 128, 1e6)
+    kc = torch.zeros(48, n_kv, cap, 128, dtype=torch.float16, device="cuda")
+    vc = torch.zeros_like(kc)
+    q, _ = tt.qkrope.apply(dev_f32(qkv).reshape(48, 1, -1), dev_f32(norms), dev_f32(cos),
+                           dev_f32(sin), kc, vc, heads, torch.from_numpy(pos), eps)
+    wq, wk, wv = orc.qk_rope(qkv, norms, cos, sin, pos, heads, n_kv, eps)
+    assert rel(np_(q).reshape(48, heads, 128), wq) < 1e-5
+    lanes = np.arange(48)
+    assert rel(np_(kc)[lanes, :, pos], wk) < 1e-3
+    assert rel(np_(vc)[lanes, :, pos], wv) < 1e-3
+    # nothing but each row's own position is written
+    written = (kc != 0).any(dim=3).any(dim=1).cpu().numpy()
+    assert np.array_equal(np.flatnonzero(written.reshape(-1)), np.sort(lanes * cap + pos))
+    tt.check()
+
+
 @pytest.mark.parametrize("b,n_kv,gqa,cap,span,wstart",
                          [(48, 8, 2, 400, 250, 0), (40, 8, 2, 17, 3, 0), (8, 8, 2, 300, 211, 90),
                           (4, 8, 1, 64, 33, 0), (6, 8, 2, 2100, 2050, 0)])

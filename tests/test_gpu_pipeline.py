@@ -83,6 +83,21 @@ def test_text_to_audio(tt, orc):
     torch.cuda.synchronize()
     assert wav.shape[0] == len(frames[0]) * 64 and torch.isfinite(wav).all()
 
+    # the voice clip's last 25 frames decoded ahead and dropped (engine.rs:1119-1135): equal to
+    # decoding clip + frames and cutting the clip's samples, and not the cold decode
+    clip = [list(rng.integers(0, 2048, 16)) for _ in range(40)]
+    warm = synth.decode(frames[0], context=clip)
+    both = synth.decode(clip[-25:] + frames[0])
+    torch.cuda.synchronize()
+    assert warm.shape == wav.shape and torch.equal(warm, both[25 * 64:])
+    assert not torch.equal(warm, wav)
+    # the whole document once, cut per request at exact frame boundaries
+    pieces = synth.decode_document(frames, context=clip)
+    joined = synth.decode([fr for f in frames for fr in f], context=clip)
+    torch.cuda.synchronize()
+    assert [p.shape[0] for p in pieces] == [len(f) * 64 for f in frames]
+    assert torch.equal(torch.cat(pieces), joined)
+
 
 def test_engine_over_the_pipeline(tt, orc):
     """The engine's schedule (crates/qwen3tts/src/engine.rs:919-1011) over two synthesizers: a

@@ -304,6 +304,41 @@ def test_predictor_forced_ties(orc):
     assert got[0, 0] == wrong[0, 0] and ties >= 1
 
 
+def test_prefill_restatement_against_decode_steps(orc):
+    """The prefill branch (qwen3.rs:415-444: fresh f32 K/V after the f16 prefix, one masked
+    softmax over the span) against the same rows run as decode steps over the f16 cache (the
+    causal mask makes them the same computation up to the K/V rounding), with and without a
+    cached prefix; and the CPU arm's f16-rounded projections stay within the same band."""
+    g = orc.Geometry(dim=256, layers=2, heads=4, n_kv=2, ffn=512, codebooks=0, vocab=0)
+    rng = np.random.default_rng(11)
+    layers = [orc.synthetic_layer(rng, g) for _ in range(g.layers)]
+    final = rng.uniform(0.8, 1.2, g.dim).astype(np.float32)
+    b, cap = 3, 64
+    cos, sin = orc.rope_table(cap, 128, g.rope_base)
+    kc = [np.zeros((b, g.n_kv, cap, 128), np.uint16) for _ in layers]
+    vc = [np.zeros((b, g.n_kv, cap, 128), np.uint16) for _ in layers]
+    kd = [a.copy() for a in kc]
+    vd = [a.copy() for a in vc]
+    for start, t in ((0, 20), (20, 7)):
+        x = rng.standard_normal((b, t, g.dim), dtype=np.float32)
+        got = orc.prefill(x, layers, final, kc, vc, start, cos, sin, g, round_f16=False)
+        want = np.stack([orc.decode_step(x[:, i], layers, final, kd, vd,
+                                         np.full(b, start + i, np.int32), cos, sin, g)
+                         for i in range(t)], axis=1)
+        r = np.abs(got - want).max() / np.abs(want).max()
+        assert r < 5e-3, (start, r)
+        for li in range(g.layers):
+            a = orc.f16_value(kc[li][:, :, :start + t])
+            d = orc.f16_value(kd[li][:, :, :start + t])
+            assert np.abs(a - d).max() / np.abs(d).max() < 5e-3
+    x = rng.standard_normal((b, 9, g.dim), dtype=np.float32)
+    k2 = [a.copy() for a in kc]
+    v2 = [a.copy() for a in vc]
+    cpu = orc.prefill(x, layers, final, kc, vc, 27, cos, sin, g)
+    metal = orc.prefill(x, layers, final, k2, v2, 27, cos, sin, g, round_f16=False)
+    assert 0 < np.abs(cpu - metal).max() / np.abs(metal).max() < 5e-3
+
+
 def test_talker_pick_rule(orc):
     """sample_with_u greedy (talker.rs:154-189): banned ids never win, eos waits for min_new
     frames, the penalty divides positive and multiplies negative logits of seen ids, and the
