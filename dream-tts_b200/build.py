@@ -23,7 +23,7 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 SOURCES = ["runtime.cu", "gemm_decode.cu", "attn_decode.cu", "chain.cu", "ops_small.cu",
            "predictor.cu", "attn_short.cu", "topk_sample.cu", "safetensors.cpp",
            "codec_front.cu", "pf_gemm.cu", "pf_attn.cu",
-           "conv_nlc.cu"]
+           "conv_nlc.cu", "kv_pool.cu"]
 HEADERS = ["tts_common.cuh", "tts_internal.h", "qkrope_row.cuh", "gemm_epilogue.cuh", "pick_rule.cuh",
            "l2_prefetch.cuh"]
 

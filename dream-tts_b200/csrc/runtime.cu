@@ -146,6 +146,8 @@ tts_status counted(cudaError_t e, const char* op) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+int ctx_device(const tts_ctx* c) { return c->device; }
+
 cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
 
 struct DeviceGuard {

@@ -84,7 +84,10 @@ class LayerTensors:
 class PagedKv:
     """KV pages for one group of lanes: pools f16 [layers][num_blocks][n_kv][block_size][128],
     block table int32 [lanes][max_blocks], positions int32 [lanes] (each lane's cached length).
-    Pages come from a host-side free list when a lane is admitted."""
+    The buffers are torch tensors; the page bookkeeping (free list, per-lane pages, reference
+    counts of shared prefix pages, table rows and positions) is the native pool's
+    (tts_kv_pool_*), the same allocator a host engine binds through the C ABI. Admissions are
+    ordered on the current stream."""
 
     def __init__(self, geo: Geometry, lanes: int, num_blocks: int, block_size: int,
                  max_blocks: int, device: torch.device | str = "cuda"):
@@ -98,34 +101,24 @@ class PagedKv:
         self.v = torch.zeros(shape, dtype=torch.float16, device=device)
         self.table = torch.zeros(lanes, max_blocks, dtype=torch.int32, device=device)
         self.positions = torch.zeros(lanes, dtype=torch.int32, device=device)
-        self._free = list(range(num_blocks - 1, -1, -1))
-        self._owned: dict[int, list[int]] = {}
-        self._refs: dict[int, int] = {}  # lanes holding each page (shared prefixes)
-
-    def _take(self, n: int) -> list[int]:
-        if n > len(self._free):
-            raise MemoryError("KV pool exhausted")
-        pages = [self._free.pop() for _ in range(n)]
-        for p in pages:
-            self._refs[p] = 1
-        return pages
-
-    def _set_row(self, lane: int, pages: list[int], length: int) -> None:
-        self._owned[lane] = pages
-        row = torch.zeros(self.max_blocks, dtype=torch.int32)
-        row[:len(pages)] = torch.tensor(pages, dtype=torch.int32)
-        self.table[lane].copy_(row)
-        self.positions[lane] = length
+        desc = L.KvPoolDesc(geo.layers, geo.n_kv, geo.head_dim, block_size, num_blocks, lanes,
+                            max_blocks, self.k.data_ptr(), self.v.data_ptr(),
+                            self.table.data_ptr(), self.positions.data_ptr())
+        h = C.c_void_p()
+        dev = self.k.device.index if self.k.device.index is not None else torch.cuda.current_device()
+        L.call("tts_kv_pool_create", ctx(dev), C.byref(desc), C.byref(h))
+        self.handle = h
 
     def admit(self, lane: int, capacity: int, length: int = 0) -> list[int]:
         """Give `lane` pages for `capacity` positions; it holds `length` of them already."""
-        need = -(-capacity // self.block_size)
-        if need > self.max_blocks:
-            raise ValueError(f"lane needs {need} pages, the table holds {self.max_blocks}")
-        self.release(lane)
-        pages = self._take(need)
-        self._set_row(lane, pages, length)
-        return pages
+        L.call("tts_kv_pool_admit", self.handle, int(lane), int(capacity), int(length), stream())
+        return self.pages(lane)
+
+    def admit_pages(self, lane: int, pages, length: int = 0) -> None:
+        """Admit `lane` with the given free pages (block-table order)."""
+        arr = (C.c_int * len(pages))(*[int(p) for p in pages])
+        L.call("tts_kv_pool_admit_pages", self.handle, int(lane), arr, len(pages), int(length),
+               stream())
 
     def share_prefix(self, src: int, lane: int, length: int, capacity: int) -> list[int]:
         """Admit `lane` with the first `length` cached positions of lane `src` (the shared
@@ -133,33 +126,24 @@ class PagedKv:
         into each lane, crates/qwen3tts/src/qwen3.rs:261-284): its full pages are shared
         through the block table, only a partly filled last page is copied, and fresh pages
         cover the rest of `capacity`. `src` must hold at least `length` positions."""
-        bs = self.block_size
-        need = -(-capacity // bs)
-        if need > self.max_blocks or length > capacity:
-            raise ValueError("share_prefix: capacity exceeds the block table or the prefix")
-        full, part = divmod(length, bs)
-        src_pages = self._owned[src]
-        self.release(lane)
-        shared = src_pages[:full]
-        for p in shared:
-            self._refs[p] += 1
-        own = self._take(need - full)
-        if part:
-            # the partly filled page: a copy, since this lane writes its own rows after it
-            self.k[:, own[0]].copy_(self.k[:, src_pages[full]])
-            self.v[:, own[0]].copy_(self.v[:, src_pages[full]])
-        self._set_row(lane, shared + own, length)
-        return shared + own
+        L.call("tts_kv_pool_share_prefix", self.handle, int(src), int(lane), int(length),
+               int(capacity), stream())
+        return self.pages(lane)
 
     def release(self, lane: int) -> None:
-        for p in self._owned.pop(lane, []):
-            self._refs[p] -= 1
-            if self._refs[p] == 0:
-                del self._refs[p]
-                self._free.append(p)
+        L.call("tts_kv_pool_release", self.handle, int(lane))
+
+    def pages(self, lane: int) -> list[int]:
+        n = C.c_int(0)
+        buf = (C.c_int * self.max_blocks)()
+        L.call("tts_kv_pool_lane_pages", self.handle, int(lane), buf, self.max_blocks, C.byref(n))
+        return list(buf[:n.value])
+
+    def page_refs(self, page: int) -> int:
+        return int(L.load().tts_kv_pool_page_refs(self.handle, int(page)))
 
     def free_pages(self) -> int:
-        return len(self._free)
+        return int(L.load().tts_kv_pool_free_pages(self.handle))
 
     def state(self, lanes: int | None = None, max_span: int | None = None) -> L.DecodeState:
         n = self.lanes if lanes is None else lanes
@@ -167,6 +151,14 @@ class PagedKv:
         return L.DecodeState(n, self.positions.data_ptr(), self.table.data_ptr(),
                              self.max_blocks, self.block_size, self.num_blocks,
                              self.k.data_ptr(), self.v.data_ptr(), ms)
+
+    def __del__(self):
+        try:
+            if getattr(self, "handle", None):
+                L.load().tts_kv_pool_destroy(self.handle)
+                self.handle = None
+        except Exception:
+            pass
 
 
 class PickState:

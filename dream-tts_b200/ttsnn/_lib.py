@@ -56,6 +56,13 @@ class PredictorWeights(C.Structure):
                 ("embed_dim", C.c_int)]
 
 
+class KvPoolDesc(C.Structure):
+    _fields_ = [("layers", C.c_int), ("n_kv", C.c_int), ("head_dim", C.c_int),
+                ("block_size", C.c_int), ("num_blocks", C.c_int), ("max_lanes", C.c_int),
+                ("max_blocks", C.c_int), ("k_pages", C.c_void_p), ("v_pages", C.c_void_p),
+                ("block_table", C.c_void_p), ("positions", C.c_void_p)]
+
+
 class PickRule(C.Structure):
     _fields_ = [("ban", C.c_void_p), ("counts", C.c_void_p), ("frames", C.c_void_p),
                 ("penalty", C.c_float), ("eos", C.c_int), ("min_new", C.c_int)]
@@ -133,9 +140,20 @@ SIGNATURES = {
     "tts_talker_frame_capture": [P, C.POINTER(DecodeState), P, C.POINTER(DecodeState),
                                  C.POINTER(TextFeed), P, P, P, P, C.POINTER(P)],
     "tts_timeline_read": [P, I, C.POINTER(I), I],
+    "tts_kv_pool_create": [P, C.POINTER(KvPoolDesc), C.POINTER(P)],
+    "tts_kv_pool_destroy": [P],
+    "tts_kv_pool_admit": [P, I, I, I, P],
+    "tts_kv_pool_admit_pages": [P, I, C.POINTER(I), I, I, P],
+    "tts_kv_pool_share_prefix": [P, I, I, I, I, P],
+    "tts_kv_pool_release": [P, I],
+    "tts_kv_pool_free_pages": [P],
+    "tts_kv_pool_page_refs": [P, I],
+    "tts_kv_pool_lane_pages": [P, I, C.POINTER(I), I, C.POINTER(I)],
+    "tts_kv_pool_state": [P, I, I, C.POINTER(DecodeState)],
 }
 _RESTYPE = {"tts_last_error": C.c_char_p, "tts_launch_count": C.c_longlong,
-            "tts_safetensors_count": C.c_int}
+            "tts_safetensors_count": C.c_int, "tts_kv_pool_free_pages": C.c_int,
+            "tts_kv_pool_page_refs": C.c_int}
 
 _lib = None
 

@@ -308,6 +308,60 @@ typedef struct tts_decode_state {
   int max_span;
 } tts_decode_state;
 
+/* ---------------------------------------------------------------- KV page pool
+ * The page allocator of the paged KV cache. The reference keeps one contiguous cache per lane,
+ * narrows it when lanes are shed and broadcast-copies a shared prompt prefix into every lane
+ * (crates/qwen3tts/src/qwen3.rs:122-212 State/Cache/narrow_to, :261-284 fill_prefix); here a
+ * lane owns a row of a block table of fixed-size pages from one pool. Full pages of a shared
+ * prefix are shared by reference count, only a partly filled last page is copied. The pool
+ * keeps the free list and reference counts on the host; admissions write the lane's table row
+ * and position with one stream-ordered launch (no host wait), so they may be interleaved with
+ * decode steps on the same stream. Not thread-safe: one pool per host thread, as the
+ * reference's dispatcher. */
+typedef struct tts_kv_pool tts_kv_pool;
+typedef struct tts_kv_pool_desc {
+  int layers, n_kv, head_dim; /* the stack's geometry */
+  int block_size;             /* positions per page */
+  int num_blocks;             /* pages in the pool */
+  int max_lanes, max_blocks;  /* block table [max_lanes][max_blocks] */
+  /* Device buffers, or NULL for the pool to allocate (and free on destroy):
+   * pages f16 [layers][num_blocks][n_kv][block_size][head_dim] (both or neither), the block
+   * table int32 [max_lanes][max_blocks], positions int32 [max_lanes]. */
+  void* k_pages;
+  void* v_pages;
+  int* block_table;
+  int* positions;
+} tts_kv_pool_desc;
+TTS_API tts_status tts_kv_pool_create(tts_ctx* ctx, const tts_kv_pool_desc* desc,
+                                      tts_kv_pool** out);
+TTS_API tts_status tts_kv_pool_destroy(tts_kv_pool* pool);
+/* Gives `lane` ceil(capacity / block_size) pages (its previous pages are released first); the
+ * lane holds `length` positions already (its position is set to `length`). TTS_ERR_OOM when the
+ * pool has too few free pages. */
+TTS_API tts_status tts_kv_pool_admit(tts_kv_pool* pool, int lane, int capacity, int length,
+                                     void* stream);
+/* Admits `lane` with the given free pages, in block-table order (a caller that lays out its own
+ * pages, e.g. to scatter a prefilled cache). */
+TTS_API tts_status tts_kv_pool_admit_pages(tts_kv_pool* pool, int lane, const int* pages, int n,
+                                           int length, void* stream);
+/* Admits `lane` holding the first `length` positions of lane `src` (the shared prompt prefix,
+ * qwen3.rs:261-284): src's full pages are shared, a partly filled page is copied (every layer,
+ * K and V, stream-ordered), fresh pages cover the rest of `capacity`. */
+TTS_API tts_status tts_kv_pool_share_prefix(tts_kv_pool* pool, int src, int lane, int length,
+                                            int capacity, void* stream);
+/* Releases the lane's pages: a page returns to the free list when its last lane lets it go. */
+TTS_API tts_status tts_kv_pool_release(tts_kv_pool* pool, int lane);
+TTS_API int tts_kv_pool_free_pages(const tts_kv_pool* pool);
+/* Lanes holding `page` (0 = free), -1 for a page outside the pool. */
+TTS_API int tts_kv_pool_page_refs(const tts_kv_pool* pool, int page);
+/* The lane's pages in block-table order: up to `cap` into `pages`, their count into *n. */
+TTS_API tts_status tts_kv_pool_lane_pages(const tts_kv_pool* pool, int lane, int* pages,
+                                          int cap, int* n);
+
+/* The decode state of the pool's first `lanes` lanes (max_span <= 0: the table's capacity). */
+TTS_API tts_status tts_kv_pool_state(const tts_kv_pool* pool, int lanes, int max_span,
+                                     tts_decode_state* out);
+
 /* One talker decode step: Stack::forward at t == 1 (qwen3.rs:294-467, the whole layer loop and
  * the final norm), then the codebook heads and a greedy pick per head (talker.rs:956-998), then
  * the sum of the picked codes' embedding rows as the next input (talker.rs:1019-1023, 528-550).

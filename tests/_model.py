@@ -93,9 +93,8 @@ def paged_from_contiguous(geo, kc, vc, pos, block_size, seed, spare_blocks=3, ca
     rng = np.random.default_rng(seed)
     order = rng.permutation(num_blocks)
     table = order[:lanes * per_lane].reshape(lanes, per_lane).astype(np.int32)
-    kv.table.copy_(torch.from_numpy(table))
-    kv.positions.copy_(torch.from_numpy(np.asarray(pos, np.int32)))
-    kv._free = [int(b) for b in order[lanes * per_lane:]]
+    for i in range(lanes):
+        kv.admit_pages(i, table[i].tolist(), int(pos[i]))
     for li in range(len(kc)):
         for src, pool in ((kc[li], kv.k), (vc[li], kv.v)):
             padded = np.zeros((lanes, n_kv, per_lane * block_size, hd), np.uint16)

@@ -187,6 +187,6 @@ def test_shared_prefix(tt, orc):
     shared = int(kv.table[0, 0])
     kv.release(0)
     kv.release(1)
-    assert shared not in kv._free
+    assert kv.page_refs(shared) == 1
     kv.release(2)
-    assert shared in kv._free and kv.free_pages() > free_before
+    assert kv.page_refs(shared) == 0 and kv.free_pages() > free_before
