@@ -1345,6 +1345,11 @@ def run_timeline(args):
             else:
                 row["main_done"] = [f(np.median(a[idx + 2, 1])), f(a[idx + 2, 1].max())]
                 row["reduced"] = [f(np.median(a[idx + 3, 1])), f(a[idx + 3, 1].max())]
+                if len(a) > int(idx.max()) + 6 and ((a[idx + 5, 0] & 0xf) == 6).all():
+                    ok = a[idx + 5, 1] > 0  # the kPipe form has no first-batch stamp
+                    if ok.any():
+                        row["epi_first_batch"] = f(np.median(a[idx + 5, 1][ok]))
+                    row["epi_loop_done"] = f(np.median(a[idx + 6, 1]))
                 row["end"] = [f(np.median(a[idx + 4, 1])), f(a[idx + 4, 1].max())]
             rows[name] = row
         out["layers"][str(li)] = rows

@@ -62,10 +62,21 @@ struct GemmArgs {
   const float* ss_in;
   int ss_tiles;
   float ss_inv_dim, ss_eps;
+  // Epilogue operands staged into shared memory by one bulk copy each, issued right after the
+  // dependency wait so that they land during the main loop (their global round trips, slow
+  // while the weight stream holds the memory system, otherwise stall the epilogue): the
+  // row-scale partial sums [ss_tiles][m] and, for the QKV epilogue, the per-step row
+  // operands (QkRopeArgs::rows_desc / rows_rope) and the two norm weights. 0: not staged.
+  int ops_ss;     // bytes of row-scale sums (a multiple of 16)
+  int ops_rows;   // 1: desc [m] int4 + rope [m][128] f32 + norms [256] f32
+  int ops_bytes;  // all staged bytes
 };
 
 
 constexpr int kThreads = 256;  // 8 warps: 0..3 producers, 4..7 MMA issuers + epilogue
+// The staged epilogue operands start this far past the stage rings / partial tile (the
+// barriers and the TMEM address sit in between).
+constexpr uint32_t kOpsOffset = 1024;
 
 // kPipe: the epilogue requests each batch's global operands (row-scale partial sums, residual
 // rows, the QKV rows' positions, page numbers and RoPE rows) one batch ahead, so that their
@@ -77,7 +88,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_decode_kernel(const __grid_constant__ CUtensorMap tmW,
                        const __grid_constant__ CUtensorMap tmX, const GemmArgs a) {
   [[maybe_unused]] const unsigned long long tl_entry = TTS_TL_NOW();
-  [[maybe_unused]] unsigned long long tl_rel = 0;
+  [[maybe_unused]] unsigned long long tl_rel = 0, tl_a = 0, tl_b = 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -96,7 +107,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + body);  // [P][SP]
   uint64_t* empty = full + P * SP;                              // [P][SP]
   uint64_t* done = empty + P * SP;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  uint64_t* ops_bar = done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ops_bar + 1);
+  // the staged epilogue operands (GemmArgs::ops_*), past the barriers
+  uint8_t* ops = smem + body + kOpsOffset;
+  const float* ss_s = reinterpret_cast<const float*>(ops);
+  const int4* desc_s = reinterpret_cast<const int4*>(ops + a.ops_ss);
+  const float* rope_s = reinterpret_cast<const float*>(ops + a.ops_ss + a.m * 16);
+  const float* norms_s = rope_s + a.m * 128;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -107,6 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(done, P);
+    mbar_init(ops_bar, 1);
     fence_barrier_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmX);
@@ -153,6 +172,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* st = ring + i * stage_bytes + kWBytes;
           for (int g = 0; g < a.groups; ++g)
             tma_load_2d(st + g * a.ng * 128, &tmX, &fl[i], kb * kBlockK, g * a.ng);
+        }
+        if (pp == 0 && a.ops_bytes) {
+          // the epilogue's operands: written by earlier kernels, complete once the wait
+          // returned; they arrive while the weights stream
+          mbar_arrive_expect_tx(ops_bar, uint32_t(a.ops_bytes));
+          if (a.ops_ss) bulk_load(ops, a.ss_in, uint32_t(a.ops_ss), ops_bar);
+          if (a.ops_rows) {
+            bulk_load(ops + a.ops_ss, a.qk.rows_desc, uint32_t(a.m) * 16u, ops_bar);
+            bulk_load(ops + a.ops_ss + a.m * 16, a.qk.rows_rope, uint32_t(a.m) * 512u, ops_bar);
+            bulk_load(ops + a.ops_ss + a.m * 16 + a.m * 512, a.qk.norms, 1024u, ops_bar);
+          }
         }
       }
       __syncwarp();
@@ -344,11 +374,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     return n;
   };
+  // staged operands: every thread waits for their bulk copies (long landed by now)
+  if (a.ops_bytes && !mbar_wait(ops_bar, 0) && threadIdx.x == 0) atomicOr(a.err, 4);
   auto fetch_ss = [&](const int (&jr)[4], float (&d)[4]) {
 #pragma unroll
     for (int u = 0; u < 4; ++u)
       d[u] = a.ss_in && jr[u] < a.m && lane < a.ss_tiles
-                 ? __ldcg(a.ss_in + (size_t)lane * a.m + jr[u])
+                 ? (a.ops_ss ? ss_s[lane * a.m + jr[u]]
+                             : __ldcg(a.ss_in + (size_t)lane * a.m + jr[u]))
                  : 0.f;
   };
   if constexpr (kPipe) {
@@ -421,6 +454,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       fetch_ss(jc, ssp);
       float4 acc4[4];
       reduce_batch(jc, ssp, acc4);
+#ifdef TTS_TIMELINE
+      if (j0 == j_first) tl_a = TTS_TL_NOW();
+#endif
       if (a.epi == EPI_RESIDUAL) {
         float4 res[4];
 #pragma unroll
@@ -435,6 +471,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                              : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         residual_batch(jc, res, acc4);
+      } else if (a.epi == EPI_QKROPE && a.ops_rows) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (jc[u] < a.m) {
+            float v[4] = {acc4[u].x, acc4[u].y, acc4[u].z, acc4[u].w};
+            qkrope_row_staged(a.qk, tile, jc[u], lane, v, desc_s[jc[u]],
+                              rope_s + (size_t)jc[u] * 128, norms_s);
+          }
       } else {
 #pragma unroll
         for (int u = 0; u < 4; ++u)
@@ -442,14 +486,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   }
+#ifdef TTS_TIMELINE
+  tl_b = TTS_TL_NOW();
+#endif
   if (S > 1) cluster_sync();  // no CTA leaves while another may still read its shared memory
 #ifdef TTS_TIMELINE
   __syncthreads();
   if (threadIdx.x == 0) {
     const uint64_t t_end = TTS_TL_NOW();
     const int k = kTlGemm | (a.epi << 4);
-    timeline_recs<5>({k | kTlEntry, k | kTlReleased, k | kTlMainDone, k | kTlReduced, k | kTlEnd},
-                     {tl_entry, tl_rel, tl_main, tl_red, t_end});
+    timeline_recs<7>({k | kTlEntry, k | kTlReleased, k | kTlMainDone, k | kTlReduced, k | kTlEnd,
+                      k | kTlEpiFirst, k | kTlEpiLoop},
+                     {tl_entry, tl_rel, tl_main, tl_red, t_end, tl_a, tl_b});
   }
 #endif
 }
@@ -663,6 +711,31 @@ cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t
   a.ss_tiles = r.ss_tiles;
   a.ss_inv_dim = r.ss_dim > 0 ? 1.f / float(r.ss_dim) : 0.f;
   a.ss_eps = r.ss_eps;
+  // Stage the epilogue's global operands (GemmArgs::ops_*) where the decode epilogue (the
+  // plain form) reads them, every source is 16-byte aligned, and the extra shared memory
+  // leaves the CTAs per SM unchanged. TTS_GEMM_STAGE_OPS=0 turns it off (A/B).
+  size_t smem = p.smem;
+  {
+    static const int stage_on = env_int("TTS_GEMM_STAGE_OPS", 1);
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    static const int pipe_rows_s = env_int("TTS_GEMM_PIPE_ROWS", 129);
+    const bool plain = r.m < pipe_rows_s;
+    int ss_b = 0, rows = 0;
+    if (stage_on && plain && r.ss_in && al16(r.ss_in))
+      ss_b = (r.ss_tiles * r.m * 4 + 15) / 16 * 16;
+    if (stage_on && plain && r.epi == EPI_QKROPE && r.qk.rows_desc && r.qk.rows_rope &&
+        al16(r.qk.rows_desc) && al16(r.qk.rows_rope) && al16(r.qk.norms))
+      rows = 1;
+    const int bytes = ss_b + (rows ? r.m * 16 + r.m * 512 + 1024 : 0);
+    const size_t with = p.smem - 512 + kOpsOffset + size_t(bytes);
+    const size_t one_cta = 114 * 1024;  // above this, one CTA per SM either way
+    if (bytes > 0 && with <= 227 * 1024 && (p.smem > one_cta || with <= one_cta)) {
+      a.ops_ss = ss_b;
+      a.ops_rows = rows;
+      a.ops_bytes = bytes;
+      smem = with;
+    }
+  }
 
   {
     // The opt-in shared-memory limit is a per-device function attribute.
@@ -683,7 +756,7 @@ cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(tiles, p.splits, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = p.smem;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

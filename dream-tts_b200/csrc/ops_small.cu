@@ -253,6 +253,27 @@ __global__ void __launch_bounds__(256) pick_kernel(const float* logits, int voca
   }
 }
 
+// Per decode step, each row's QK-rope operands, read once here instead of by every layer's
+// QKV epilogue: the position (-1 when outside the RoPE table or the row's block table), the page
+// holding it (-1 when the table entry is outside the pool), its offset in the page, and the
+// RoPE table's cos and sin rows at that position. Out-of-range rows are flagged once; the
+// epilogue skips them as qkrope_row does (a q head only needs the position).
+__global__ void __launch_bounds__(64) qk_rows_kernel(QkRopeArgs a, int4* desc, float* rope) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int j = blockIdx.x, t = threadIdx.x;
+  const int pos = a.positions[j];
+  const bool ok = pos >= 0 && pos < a.rope_len && pos < a.max_blocks * a.block_size;
+  int blk = ok ? a.block_table[(size_t)j * a.max_blocks + pos / a.block_size] : -1;
+  if (blk < 0 || blk >= a.num_blocks) blk = -1;
+  if (t == 0) {
+    desc[j] = make_int4(ok ? pos : -1, blk, ok ? pos % a.block_size : 0, 0);
+    if ((!ok || blk < 0) && a.err) atomicOr(a.err, kFlagRopeRange);
+  }
+  rope[(size_t)j * 128 + t] = ok ? a.cos_t[(size_t)pos * 64 + t] : 0.f;
+  rope[(size_t)j * 128 + 64 + t] = ok ? a.sin_t[(size_t)pos * 64 + t] : 0.f;
+}
+
 // Codes from the heads GEMM's argmax keys, and the next step's input as the sum of each
 // codebook's embedding row (the talker's codec_embed lookup + the predictor's gather_sum,
 // crates/qwen3tts/src/talker.rs:1019-1023, 528-550). Resets the keys for the next step.
@@ -416,6 +437,14 @@ cudaError_t launch_pick(const float* logits, int rows, const PickRule& pick, boo
   }
   pick_kernel<<<rows, 256, 0, st>>>(logits, pick.vocab, pick, record ? 1 : 0, out);
   return cudaGetLastError();
+}
+
+cudaError_t launch_qk_rows(const QkRopeArgs& a, int rows, int4* desc, float* rope, bool pdl,
+                           cudaStream_t st) {
+  QkRopeArgs args = a;
+  void* params[] = {(void*)&args, (void*)&desc, (void*)&rope};
+  return launch_ex(reinterpret_cast<void (*)(void*)>(qk_rows_kernel), dim3(rows), dim3(64), st,
+                   pdl, params);
 }
 
 cudaError_t launch_keys_to_codes(const unsigned long long* keys, int rows, int codebooks,

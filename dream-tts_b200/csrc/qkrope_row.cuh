@@ -69,6 +69,53 @@ __device__ __forceinline__ void qkrope_row(const QkRopeArgs& q, int head, int j,
   }
 }
 
+// qkrope_row with the row's operands already in shared memory (the decode GEMM stages the
+// per-step QkRopeArgs::rows_desc / rows_rope and the norm weights ahead of its epilogue): the
+// same arithmetic in the same order, no global loads. d = {position or -1, page or -1, offset
+// in the page}; rows out of range were flagged when the operands were built.
+__device__ __forceinline__ void qkrope_row_staged(const QkRopeArgs& q, int head, int j, int lane,
+                                                  float v[4], int4 d, const float* rope_row,
+                                                  const float* norms) {
+  if (d.x < 0) return;                       // position outside the table (warp-uniform)
+  if (head >= q.heads && d.y < 0) return;    // page outside the pool: k and v rows skipped
+  const int blk = d.y, off = d.z;
+  if (head < q.heads + q.n_kv) {
+    const float* w = norms + (head < q.heads ? 0 : 128) + 4 * lane;
+    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+    ss = warp_sum(ss);
+    const float rms = sqrtf(ss / 128.0f + q.eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = v[i] / rms * w[i];
+    float pr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pr[i] = __shfl_xor_sync(0xffffffffu, v[i], 16);
+    const int fi = (lane & 15) * 4;
+    const float* ct = rope_row + fi;
+    const float* st = rope_row + 64 + fi;
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      o[i] = lane < 16 ? v[i] * ct[i] - pr[i] * st[i] : v[i] * ct[i] + pr[i] * st[i];
+    if (head < q.heads) {
+      float4* dst =
+          reinterpret_cast<float4*>(q.q_out + ((size_t)j * q.heads + head) * 128 + 4 * lane);
+      *dst = make_float4(o[0], o[1], o[2], o[3]);
+    } else {
+      const int h = head - q.heads;
+      __half2* dst = reinterpret_cast<__half2*>(
+          q.k_pool + (((size_t)blk * q.n_kv + h) * q.block_size + off) * 128 + 4 * lane);
+      dst[0] = __floats2half2_rn(o[0], o[1]);
+      dst[1] = __floats2half2_rn(o[2], o[3]);
+    }
+  } else {
+    const int h = head - q.heads - q.n_kv;
+    __half2* dst = reinterpret_cast<__half2*>(
+        q.v_pool + (((size_t)blk * q.n_kv + h) * q.block_size + off) * 128 + 4 * lane);
+    dst[0] = __floats2half2_rn(v[0], v[1]);
+    dst[1] = __floats2half2_rn(v[2], v[3]);
+  }
+}
+
 // The global operands of up to four token rows j[0..n) of one head (positions, page numbers,
 // RoPE rows, the head's norm weights), fetched ahead of qkrope_apply4. The fetch has two
 // levels (page numbers and RoPE rows depend on the positions), so a caller can issue the

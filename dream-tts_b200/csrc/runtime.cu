@@ -75,6 +75,10 @@ struct tts_stack {
   // step then runs no norm kernel between layers (one for the input, one final).
   float* ss = nullptr;
   bool defer_norm = true;
+  // each lane's QK-rope operands for the step (launch_qk_rows), read by every layer's QKV
+  // epilogue from shared memory: int4 [max_lanes] and f32 [max_lanes][128]
+  int4* qk_desc = nullptr;
+  float* qk_rope = nullptr;
   PickRule pick;              // the codec head's greedy pick rule (vocab == 0: plain argmax)
   // prefill scratch, grown on demand by tts_stack_prefill: per-row (lane, offset) pairs and
   // lane lengths; per-row block-table rows and positions for one chunk of rows
@@ -712,7 +716,9 @@ tts_status tts_stack_create(tts_ctx* c, const tts_stack_geometry* geo, tts_stack
   if (e == cudaSuccess) e = dmalloc(&s->act, size_t(L) * gm.ffn * 2);
   if (e == cudaSuccess) e = dmalloc(&s->x_next, size_t(L) * gm.dim * 4);
   if (e == cudaSuccess) e = dmalloc(&s->keys, size_t(L) * std::max(1, gm.codebooks) * 8);
-  if (e == cudaSuccess) e = dmalloc(&s->ss, size_t(L) * std::max(1, gm.dim / 128) * 4);
+  if (e == cudaSuccess) e = dmalloc(&s->ss, size_t(L) * std::max(1, gm.dim / 128) * 4 + 16);
+  if (e == cudaSuccess) e = dmalloc(&s->qk_desc, size_t(L) * sizeof(int4));
+  if (e == cudaSuccess) e = dmalloc(&s->qk_rope, size_t(L) * 128 * 4);
   {
     const char* env = getenv("TTS_DEFER_NORM");
     s->defer_norm = !(env && *env == '0') && gm.dim % 128 == 0 && gm.dim / 128 <= 32;
@@ -837,6 +843,8 @@ tts_status tts_stack_destroy(tts_stack* s) {
   cudaFree(s->x_next);
   cudaFree(s->keys);
   cudaFree(s->ss);
+  cudaFree(s->qk_desc);
+  cudaFree(s->qk_rope);
   cudaFree(s->chain.part);
   cudaFree(s->chain.done);
   cudaFree(s->chain.exit_cnt);
@@ -913,6 +921,11 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
   auto pf = [&](const void* w, int k, int n) {
     return pf_budget ? gemm_prefetch_plan(w, B, k, n, c->device, pf_budget) : L2Prefetch{};
   };
+  // each lane's QK-rope operands once per step for every layer's QKV epilogue (the
+  // separate-kernel path; TTS_QK_ROWS=0 turns it off for A/B measurement)
+  const char* rows_env = getenv("TTS_QK_ROWS");
+  const char* chain_env0 = getenv("TTS_CHAIN");
+  const bool rows_on = !(rows_env && *rows_env == '0') && !(chain_env0 && *chain_env0 == '1');
   auto pages = [&](int l, bool v) {
     return (v ? static_cast<__half*>(st->v_pages) : static_cast<__half*>(st->k_pages)) +
            layer_pages * l;
@@ -944,6 +957,10 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
     r.qk.heads = gm.heads;
     r.qk.n_kv = gm.n_kv;
     r.qk.eps = gm.eps;
+    if (rows_on) {
+      r.qk.rows_desc = s->qk_desc;
+      r.qk.rows_rope = s->qk_rope;
+    }
     return r;
   };
   auto req_o = [&](int l) {
@@ -1101,6 +1118,8 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
       r.norm_x16 = s->xn;
       r.ss_out = s->ss;
     };
+    if (rows_on) TTS_TRY(launch_qk_rows(req_qkv(0).qk, B, s->qk_desc, s->qk_rope, true, cs),
+                         "qk_rows");
     if (defer)
       TTS_TRY(launch_norm_defer(s->h, s->layers[0].attn_norm, B, D, s->xn, s->ss, true, cs),
               "rms_norm");

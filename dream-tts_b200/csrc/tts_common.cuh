@@ -72,6 +72,8 @@ constexpr int kTlAttn = 0x200;   // | phase
 constexpr int kTlNorm = 0x300;   // | phase (rms_norm; 0x310 | phase: the deferred norm's input)
 constexpr int kTlEntry = 0, kTlReleased = 1, kTlMainDone = 2, kTlReduced = 3, kTlCta = 4,
               kTlMerged = 5, kTlEnd = 15;  // kTlCta: the phase time field holds blockIdx.x
+// GEMM epilogue (warp 0): its first batch of rows reduced, every batch done
+constexpr int kTlEpiFirst = 6, kTlEpiLoop = 7;
 #ifdef TTS_TIMELINE
 constexpr unsigned kTimelineCap = 1u << 21;  // 64 MB of records (tracing build only)
 extern __device__ unsigned long long g_timeline[kTimelineCap * 4];
@@ -162,6 +164,14 @@ TTS_DEV void tma_load_4d(void* smem_dst, const void* desc, uint64_t* bar, int c0
 }
 // Prefetch `bytes` (a multiple of 16, from a 16-byte aligned address) into L2; no completion
 // to wait for.
+// One contiguous global -> shared copy by the bulk-copy engine (no multicast): both addresses
+// 16-byte aligned, `bytes` a multiple of 16; completes on `bar`'s transaction count.
+TTS_DEV void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
 TTS_DEV void l2_prefetch_bulk(const void* src, uint32_t bytes, uint64_t policy) {
   asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(
                    reinterpret_cast<uint64_t>(src)),

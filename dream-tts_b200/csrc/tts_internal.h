@@ -57,6 +57,12 @@ struct QkRopeArgs {
   int heads = 0;
   int n_kv = 0;
   float eps = 1e-6f;
+  // Optional, per step (launch_qk_rows): each row's operands read once for every layer, which
+  // the decode GEMM stages into shared memory ahead of its epilogue. rows_desc [rows] =
+  // {position or -1 when outside the RoPE table or the block table, page or -1 when outside
+  // the pool, offset in the page, 0}; rows_rope [rows][128] = the RoPE cos row then sin row.
+  const int4* rows_desc = nullptr;
+  const float* rows_rope = nullptr;
 };
 
 // The next projection's packed weights, for an L2 prefetch issued at the end of a kernel's own
@@ -248,6 +254,10 @@ cudaError_t launch_snake(const void* x, bool x_f16, const float* alpha, const fl
                          long rows, int chan, void* y, bool y_f16, cudaStream_t st);
 cudaError_t launch_pick(const float* logits, int rows, const PickRule& pick, bool record,
                         uint32_t* out, cudaStream_t st);
+// Each row's QK-rope operands for a decode step (QkRopeArgs::rows_desc / rows_rope) from
+// the positions, the block table and the RoPE tables; flags out-of-range rows once.
+cudaError_t launch_qk_rows(const QkRopeArgs& a, int rows, int4* desc, float* rope, bool pdl,
+                           cudaStream_t st);
 cudaError_t launch_argmax(const float* logits, int rows, int n, const uint8_t* banned,
                           uint32_t* out, cudaStream_t st);
 cudaError_t launch_keys_to_codes(const unsigned long long* keys, int rows, int codebooks,
