@@ -1339,6 +1339,10 @@ def run_timeline(args):
                             end[j] = max(end[j], t)
                 row["end"] = [f(np.median(end)), f(end.max())]
                 row["cta_end_p10_p90"] = [f(np.percentile(end, 10)), f(np.percentile(end, 90))]
+                if len(a) > int(idx.max()) + 6 and ((a[idx + 4, 0] & 0xf) == 6).all():
+                    row["first_s"] = f(np.median(a[idx + 4, 1]))
+                    row["first_p"] = f(np.median(a[idx + 5, 1]))
+                    row["last_p"] = [f(np.median(a[idx + 6, 1])), f(a[idx + 6, 1].max())]
                 by_cta = np.zeros(len(idx))
                 by_cta[a[idx + 2, 1]] = (end - a[idx + 1, 1].min()) / 1e3
                 row["cta_work_us"] = [round(float(x), 2) for x in by_cta]
@@ -1350,6 +1354,10 @@ def run_timeline(args):
                     if ok.any():
                         row["epi_first_batch"] = f(np.median(a[idx + 5, 1][ok]))
                     row["epi_loop_done"] = f(np.median(a[idx + 6, 1]))
+                    if len(a) > int(idx.max()) + 7 and ((a[idx + 7, 0] & 0xf) == 8).all():
+                        ok2 = a[idx + 7, 1] > 0
+                        if ok2.any():
+                            row["epi_first_again"] = f(np.median(a[idx + 7, 1][ok2]))
                 row["end"] = [f(np.median(a[idx + 4, 1])), f(a[idx + 4, 1].max())]
             rows[name] = row
         out["layers"][str(li)] = rows

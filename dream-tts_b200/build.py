@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "ttsnn", "libtts_cuda.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["runtime.cu", "gemm_decode.cu", "attn_decode.cu", "chain.cu", "ops_small.cu",
+SOURCES = ["runtime.cu", "gemm_decode.cu", "attn_decode.cu", "ops_small.cu",
            "predictor.cu", "attn_short.cu", "topk_sample.cu", "safetensors.cpp",
            "codec_front.cu", "pf_gemm.cu", "pf_attn.cu",
            "conv_nlc.cu", "kv_pool.cu"]

@@ -93,6 +93,7 @@ struct AttnSmem {
   uint32_t inv_v[kStages];
   uint32_t tmem;
   int last;
+  unsigned long long tl_p0, tl_plast;  // tracing build: first and last P handed to the O MMA
   int span[kMaxLanes];
   int cnt[kMaxLanes];         // chunk-list items of each lane (chunks x n_kv)
   int prefix[kMaxLanes + 1];  // chunk-list offset of each lane
@@ -396,6 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ================= score warp: S(j) = K(j) . Q^T when K(j) and its segment's q are in place
     bool ok = true;
     long long ns = 0;  // MMA groups issued
+    [[maybe_unused]] unsigned long long tl_s0 = 0;
     Cursor x = first;
     for (long long j = 0; j < n && ok; ++j) {
       const int s = int(j % kStages);
@@ -423,6 +425,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&S.empty_k[s]);
       }
       __syncwarp();
+#ifdef TTS_TIMELINE
+      if (j == 0) tl_s0 = TTS_TL_NOW();
+#endif
       ++ns;
       cursor_next(x, S.span, a);
     }
@@ -439,9 +444,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the score warp releases TMEM after every chunk's softmax and output MMA: compute ends
     if (lane == 0) {
       const uint64_t t_end = TTS_TL_NOW();
-      timeline_recs<4>({kTlAttn | kTlEntry, kTlAttn | kTlReleased, kTlAttn | kTlCta,
-                        kTlAttn | kTlEnd},
-                       {tl_entry, tl_rel, uint64_t(blockIdx.x), t_end});
+      timeline_recs<7>({kTlAttn | kTlEntry, kTlAttn | kTlReleased, kTlAttn | kTlCta,
+                        kTlAttn | kTlEnd, kTlAttn | kTlAttnFirstS, kTlAttn | kTlAttnFirstP,
+                        kTlAttn | kTlAttnLastP},
+                       {tl_entry, tl_rel, uint64_t(blockIdx.x), t_end, tl_s0, S.tl_p0,
+                        S.tl_plast});
     }
 #endif
     return;
@@ -737,6 +744,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_proxy_async();
     __syncwarp();
     if (lane == 0) mbar_arrive(&S.p_full[j & 1]);
+#ifdef TTS_TIMELINE
+    if (t == 0 && j == 0) S.tl_p0 = TTS_TL_NOW();
+    if (t == 0 && j + 1 == n) S.tl_plast = TTS_TL_NOW();
+#endif
     // ---- the previous item, now that this item's P is out, and the segment it ended
     if (pend) {
       if (fin) {

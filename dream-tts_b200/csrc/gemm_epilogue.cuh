@@ -1,5 +1,5 @@
-// Epilogue of one token row of a 128-row weight tile, shared by the decode GEMM and the layer
-// chain: lane l holds rows 4l .. 4l + 3 of the tile for token row j.
+// Epilogue of one token row of a 128-row weight tile of the decode GEMM: lane l holds rows
+// 4l .. 4l + 3 of the tile for token row j.
 #pragma once
 #include "pick_rule.cuh"
 #include "qkrope_row.cuh"
@@ -15,12 +15,13 @@ constexpr int kTileRows = 128;
 // rows of the epilogue from overlapping (measured ~3x slower per row).
 __device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-// One token row of one 128-row tile: lane owns rows 4*lane .. 4*lane + 3.
+// One token row of one 128-row tile: lane owns rows 4*lane .. 4*lane + 3. `epi` is the
+// epilogue kind (a compile-time constant where the caller's kernel is specialised on it).
 template <typename A>
 __device__ __forceinline__ void epilogue_row(const A& a, int tile, int j, int lane,
-                                             float4 acc) {
+                                             float4 acc, int epi) {
   const int f0 = tile * kTileRows + 4 * lane;
-  switch (a.epi) {
+  switch (epi) {
     case EPI_F32: {
       float* y = static_cast<float*>(a.y) + (size_t)j * a.ldy + f0;
       *reinterpret_cast<float4*>(y) = acc;
@@ -33,7 +34,7 @@ __device__ __forceinline__ void epilogue_row(const A& a, int tile, int j, int la
       break;
     }
     case EPI_RESIDUAL: {
-      // an L2 read: within the layer chain other CTAs wrote this row earlier in the kernel
+      // an L2 read of the residual stream
       float4* y = reinterpret_cast<float4*>(static_cast<float*>(a.y) + (size_t)j * a.ldy + f0);
       float4 r = __ldcg(y);
       r.x += acc.x;
@@ -90,62 +91,6 @@ __device__ __forceinline__ void epilogue_row(const A& a, int tile, int j, int la
     }
     default:
       break;
-  }
-}
-
-// Token rows j0, j0 + step, ... (below m) of one tile, read from a [m][128] f32 tile in shared
-// memory, four rows at a time: a batch's global loads (residual rows, RoPE tables) are issued
-// before its first store.
-template <typename A>
-__device__ __forceinline__ void epilogue_rows(const A& a, int tile, int j0, int step, int m,
-                                              int lane, const float* red) {
-  for (int jb = j0; jb < m; jb += 4 * step) {
-    int j[4];
-    float4 acc[4];
-    int n = 0;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      j[u] = jb + u * step;
-      acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j[u] < m) {
-        acc[u] = *reinterpret_cast<const float4*>(red + j[u] * kTileRows + 4 * lane);
-        n = u + 1;
-      }
-    }
-    if (a.epi == EPI_RESIDUAL) {
-      float4 r[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        r[u] = u < n ? __ldcg(reinterpret_cast<const float4*>(static_cast<float*>(a.y) +
-                                                              (size_t)j[u] * a.ldy + tile * kTileRows +
-                                                              4 * lane))
-                     : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (u >= n) break;
-        float4 o = r[u];
-        o.x += acc[u].x;
-        o.y += acc[u].y;
-        o.z += acc[u].z;
-        o.w += acc[u].w;
-        *reinterpret_cast<float4*>(static_cast<float*>(a.y) + (size_t)j[u] * a.ldy +
-                                   tile * kTileRows + 4 * lane) = o;
-      }
-    } else if (a.epi == EPI_QKROPE) {
-      float v[4][4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        v[u][0] = acc[u].x;
-        v[u][1] = acc[u].y;
-        v[u][2] = acc[u].z;
-        v[u][3] = acc[u].w;
-      }
-      qkrope_rows4(a.qk, tile, j, n, lane, v);
-    } else {
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        if (u < n) epilogue_row(a, tile, j[u], lane, acc[u]);
-    }
   }
 }
 

@@ -205,15 +205,5 @@ __device__ __forceinline__ void qkrope_apply4(const QkRopeArgs& q, int head, con
   }
 }
 
-// Up to four token rows j[0..n) of one head at once, with the same result as qkrope_row on
-// each: every global load of the batch is issued before the first store, so the rows' load
-// latencies overlap instead of adding up.
-__device__ __forceinline__ void qkrope_rows4(const QkRopeArgs& q, int head, const int j[4], int n,
-                                             int lane, float v[4][4]) {
-  QkRowsPre p;
-  qkrope_fetch_pos4(q, j, n, p);
-  qkrope_fetch_rest4(q, head, j, n, lane, p);
-  qkrope_apply4(q, head, j, n, lane, v, p);
-}
 
 }  // namespace tts

@@ -97,9 +97,6 @@ struct tts_stack {
   // measured best for the talker; the depth predictor's stack runs without (its kernels are
   // latency-bound, and the prefetch measured 6% slower per frame at 48 lanes).
   size_t pf_budget = size_t(12) << 20;
-  // layer chain (steps of up to 128 lanes): phase counters and partial tiles
-  ChainWorkspace chain;
-  int chain_lanes = 0;  // lanes the partial buffer is sized for (0: no chain)
 };
 
 // The depth predictor: its stack, weights, the doubled resize weight and per-frame scratch
@@ -725,24 +722,6 @@ tts_status tts_stack_create(tts_ctx* c, const tts_stack_geometry* geo, tts_stack
   }
   if (e == cudaSuccess) e = cudaMemset(s->keys, 0, size_t(L) * std::max(1, gm.codebooks) * 8);
   if (e == cudaSuccess) e = cudaMemset(s->x_next, 0, size_t(L) * gm.dim * 4);
-  // the layer chain serves steps of up to kMaxChainLanes lanes
-  s->chain_lanes = std::min(L, kMaxChainLanes);
-  {
-    const int nqkv = (gm.heads + 2 * gm.n_kv) * 128;
-    int tiles = std::max(std::max(nqkv, gm.dim), 2 * gm.ffn) / 128;
-    if (gm.codebooks > 0) tiles = std::max(tiles, gm.codebooks * gm.vocab / 128);
-    s->chain.max_tiles = tiles;
-    s->chain.part_bytes = chain_part_bytes(s->chain_lanes, num_sms(c->device));
-    s->chain.err = c->gemm.err;
-    const size_t cnt_bytes = size_t(2) * kMaxChainPhases * tiles * sizeof(unsigned);
-    if (e == cudaSuccess) e = dmalloc(&s->chain.part, s->chain.part_bytes);
-    if (e == cudaSuccess) e = dmalloc(&s->chain.done, kMaxChainPhases * sizeof(unsigned long long));
-    if (e == cudaSuccess) e = dmalloc(&s->chain.exit_cnt, sizeof(unsigned));
-    if (e == cudaSuccess) e = dmalloc(&s->chain.tile_cnt, cnt_bytes);
-    if (e == cudaSuccess) e = cudaMemset(s->chain.done, 0, kMaxChainPhases * sizeof(unsigned long long));
-    if (e == cudaSuccess) e = cudaMemset(s->chain.exit_cnt, 0, sizeof(unsigned));
-    if (e == cudaSuccess) e = cudaMemset(s->chain.tile_cnt, 0, cnt_bytes);
-  }
   if (e != cudaSuccess) {
     tts_stack_destroy(s);
     return cuda_status(e, "stack_create");
@@ -845,10 +824,6 @@ tts_status tts_stack_destroy(tts_stack* s) {
   cudaFree(s->ss);
   cudaFree(s->qk_desc);
   cudaFree(s->qk_rope);
-  cudaFree(s->chain.part);
-  cudaFree(s->chain.done);
-  cudaFree(s->chain.exit_cnt);
-  cudaFree(s->chain.tile_cnt);
   cudaFree(s->pre_map);
   cudaFree(s->pre_table);
   cudaFree(s->pre_pos);
@@ -924,8 +899,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
   // each lane's QK-rope operands once per step for every layer's QKV epilogue (the
   // separate-kernel path; TTS_QK_ROWS=0 turns it off for A/B measurement)
   const char* rows_env = getenv("TTS_QK_ROWS");
-  const char* chain_env0 = getenv("TTS_CHAIN");
-  const bool rows_on = !(rows_env && *rows_env == '0') && !(chain_env0 && *chain_env0 == '1');
+  const bool rows_on = !(rows_env && *rows_env == '0');
   auto pages = [&](int l, bool v) {
     return (v ? static_cast<__half*>(st->v_pages) : static_cast<__half*>(st->k_pages)) +
            layer_pages * l;
@@ -1042,66 +1016,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
   };
   const int nkeys = heads ? B * gm.codebooks : 0;
 
-  // Opt-in (TTS_CHAIN=1): the layer chain runs everything between two attentions as one
-  // persistent kernel, per layer the attention, then [O, norm, gate/up, down, next norm, next
-  // QKV] (or the final norm and the heads after the last layer). Measured on B200 at 48 lanes
-  // it is slower than the separate kernels (its cross-CTA reductions and phase barriers cost
-  // more per projection than a kernel boundary under programmatic dependent launch), so the
-  // separate kernels are the default.
-  const char* chain_env = getenv("TTS_CHAIN");
-  const bool use_chain = B <= s->chain_lanes && chain_env && *chain_env == '1' &&
-                         !(hsel && hsel->draws);
-  if (use_chain) {
-    auto gemm_ph = [](const GemmRequest& g) {
-      ChainPhaseRequest p;
-      p.kind = CHAIN_GEMM;
-      p.gemm = g;
-      return p;
-    };
-    auto norm_ph = [&](const float* wn, float* y32, unsigned long long* zk, int nk) {
-      ChainPhaseRequest p;
-      p.kind = CHAIN_NORM;
-      p.norm_src = s->h;
-      p.norm_w = wn;
-      p.norm_dst16 = s->xn;
-      p.norm_dst32 = y32;
-      p.zero_keys = zk;
-      p.n_keys = nk;
-      return p;
-    };
-    ChainRequest k0;
-    k0.m = B;
-    k0.dim = D;
-    k0.eps = gm.eps;
-    k0.nph = 2;
-    k0.ph[0] = norm_ph(s->layers[0].attn_norm, nullptr, nullptr, 0);
-    k0.ph[1] = gemm_ph(req_qkv(0));
-    TTS_TRY(launch_chain(k0, s->chain, cs, c->device), "layer_chain");
-    for (int l = 0; l < gm.layers; ++l) {
-      TTS_TRY(launch_attn(req_attn(l), c->attn, cs), "decode_attention");
-      ChainRequest kr;
-      kr.m = B;
-      kr.dim = D;
-      kr.eps = gm.eps;
-      kr.ph[kr.nph++] = gemm_ph(req_o(l));
-      kr.ph[kr.nph++] = norm_ph(s->layers[l].ffn_norm, nullptr, nullptr, 0);
-      kr.ph[kr.nph++] = gemm_ph(req_gu(l));
-      kr.ph[kr.nph++] = gemm_ph(req_dn(l));
-      if (l + 1 < gm.layers) {
-        kr.ph[kr.nph++] = norm_ph(s->layers[l + 1].attn_norm, nullptr, nullptr, 0);
-        kr.ph[kr.nph++] = gemm_ph(req_qkv(l + 1));
-      } else {
-        kr.ph[kr.nph++] = norm_ph(s->final_norm, h_out, heads ? s->keys : nullptr, nkeys);
-        if (heads) kr.ph[kr.nph++] = gemm_ph(req_heads());
-      }
-      TTS_TRY(launch_chain(kr, s->chain, cs, c->device), "layer_chain");
-    }
-    if (heads)
-      TTS_TRY(launch_keys_to_codes(s->keys, B, gm.codebooks, gm.vocab, embed16, embed32, D, codes,
-                                   feed ? next : nullptr, nullptr, st->positions,
-                                   hsel ? nullptr : &s->pick, true, cs),
-              "keys_to_codes");
-  } else {
+  {
     // RMSNorm deferred into the projections: the norm's input is f16(h * w), the projection's
     // rows are divided by the RMS in its epilogue, and the O and down projections produce the
     // next norm's input and sums of squares (every row is complete in their epilogues)

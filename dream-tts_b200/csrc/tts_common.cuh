@@ -74,6 +74,8 @@ constexpr int kTlEntry = 0, kTlReleased = 1, kTlMainDone = 2, kTlReduced = 3, kT
               kTlMerged = 5, kTlEnd = 15;  // kTlCta: the phase time field holds blockIdx.x
 // GEMM epilogue (warp 0): its first batch of rows reduced, every batch done
 constexpr int kTlEpiFirst = 6, kTlEpiLoop = 7;
+// attention: first score MMAs issued, first and last P handed to the output MMA
+constexpr int kTlAttnFirstS = 6, kTlAttnFirstP = 7, kTlAttnLastP = 8;
 #ifdef TTS_TIMELINE
 constexpr unsigned kTimelineCap = 1u << 21;  // 64 MB of records (tracing build only)
 extern __device__ unsigned long long g_timeline[kTimelineCap * 4];

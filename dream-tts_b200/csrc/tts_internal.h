@@ -20,8 +20,7 @@ const char* last_error();
 constexpr int kFlagGemmWait = 1 | 2 | 4;
 constexpr int kFlagConvWait = 16 | 32 | 64 | 128 | 4096 | 8192;
 constexpr int kFlagAttnWait = 2048;
-constexpr int kFlagChainWait = 16384;
-constexpr int kFlagWaitMask = kFlagGemmWait | kFlagConvWait | kFlagAttnWait | kFlagChainWait;
+constexpr int kFlagWaitMask = kFlagGemmWait | kFlagConvWait | kFlagAttnWait;
 // Device data outside what the launch covers (the rows involved are skipped or read as zero):
 constexpr int kFlagRopeRange = 256;   // position outside the RoPE table, block table or pool
 constexpr int kFlagSpanRange = 512;   // attention span outside 1..min(max_span, table)
@@ -161,42 +160,7 @@ constexpr int kMaxGemmRows = 448;
 bool gemm_supported(int m, int k, int n, int epi, std::string* why);
 cudaError_t launch_gemm(const GemmRequest& r, const Workspace& wsp, cudaStream_t st, int device);
 
-// ------------------------------------------------------------------ layer chain
-// A run of projections and RMS norms as one persistent kernel (chain.cu).
-constexpr int kMaxChainPhases = 6;
-constexpr int kMaxChainLanes = 128;
-enum ChainKind : int { CHAIN_GEMM = 0, CHAIN_NORM = 1 };
-struct ChainPhaseRequest {
-  int kind = CHAIN_GEMM;
-  GemmRequest gemm;  // CHAIN_GEMM: packed weights, x [m][k] f16, epilogue as for launch_gemm
-  // CHAIN_NORM: dst16[r] (and dst32[r] when set) = src[r] / rms(src[r]) * w; zeroes keys
-  const float* norm_src = nullptr;
-  const float* norm_w = nullptr;
-  __half* norm_dst16 = nullptr;
-  float* norm_dst32 = nullptr;
-  unsigned long long* zero_keys = nullptr;
-  int n_keys = 0;
-};
-struct ChainRequest {
-  int m = 0, dim = 0;  // lanes; row width of the norm phases
-  float eps = 1e-6f;
-  int nph = 0;
-  ChainPhaseRequest ph[kMaxChainPhases];
-  bool pdl = true;
-};
-struct ChainWorkspace {
-  unsigned long long* done = nullptr;  // [kMaxChainPhases], zero between launches
-  unsigned* exit_cnt = nullptr;        // zero between launches
-  unsigned* tile_cnt = nullptr;        // [2][kMaxChainPhases][max_tiles], zero between launches
-  int max_tiles = 0;
-  float* part = nullptr;
-  size_t part_bytes = 0;
-  int* err = nullptr;
-};
-bool chain_supported(int m, std::string* why);
-size_t chain_part_bytes(int m, int grid);
-cudaError_t launch_chain(const ChainRequest& r, const ChainWorkspace& w, cudaStream_t st,
-                         int device);
+
 
 // ------------------------------------------------------------------ decode attention
 struct AttnRequest {

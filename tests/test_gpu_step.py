@@ -153,16 +153,3 @@ def test_step_config2_48_lanes_28_layers(tt, orc):
           f"({cpu_exact:.4f} exact, {cpu_ties:.4f} on f16 ties)")
     assert cpu_h < 2e-2 and cpu_l < 2e-2
     assert cpu_agree >= 0.995, cpu_agree
-
-
-def test_step_layer_chain_opt_in(tt, orc, monkeypatch):
-    """The opt-in layer chain (TTS_CHAIN=1: the projections and norms between attentions as one
-    persistent kernel with stream-K split tiles) against the oracle, and bit-identical from
-    run to run (its split-tile sums are in a fixed order)."""
-    monkeypatch.setenv("TTS_CHAIN", "1")
-    lengths = [0, 5, 100, 300, 511, 64, 1, 800, 129, 40, 7, 333]
-    r = run_case(tt, orc, 12, 2, 2048, 16, 8, 6144, lengths, 4, 2048, 32, 51)
-    check_case(orc, r, 12, 32)
-    h1 = r["h"].clone()
-    r2 = run_case(tt, orc, 12, 2, 2048, 16, 8, 6144, lengths, 4, 2048, 32, 51)
-    assert torch.equal(r2["h"], h1)
