@@ -1343,6 +1343,11 @@ def run_timeline(args):
                     row["first_s"] = f(np.median(a[idx + 4, 1]))
                     row["first_p"] = f(np.median(a[idx + 5, 1]))
                     row["last_p"] = [f(np.median(a[idx + 6, 1])), f(a[idx + 6, 1].max())]
+                    order = np.argsort(a[idx + 2, 1])  # by CTA index
+                    row["per_cta"] = {k: [f(v) for v in a[idx + o, 1][order]]
+                                      for k, o in (("released", 1), ("first_s", 4),
+                                                   ("first_p", 5), ("last_p", 6))}
+                    row["per_cta"]["end"] = [f(v) for v in end[order]]
                 by_cta = np.zeros(len(idx))
                 by_cta[a[idx + 2, 1]] = (end - a[idx + 1, 1].min()) / 1e3
                 row["cta_work_us"] = [round(float(x), 2) for x in by_cta]
@@ -1364,7 +1369,8 @@ def run_timeline(args):
         print(f"layer {li} (us from the QKV projection's first CTA):", file=sys.stderr)
         for name, row in rows.items():
             print(f"  {name:8s} " + "  ".join(f"{k} {v}" for k, v in row.items()
-                                              if k != "cta_work_us"), file=sys.stderr)
+                                              if k not in ("cta_work_us", "per_cta")),
+                  file=sys.stderr)
     out["spans"] = [int(p) for p in kv.positions.cpu().tolist()]  # the traced step's spans
     print(json.dumps({"timeline": "config[2] step", **out}))
 

@@ -26,6 +26,7 @@
 // merges the segments in chunk order, so results are deterministic and the softmax warps never
 // wait on a global fence or atomic.
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "tts_common.cuh"
@@ -68,7 +69,9 @@ struct AttnArgs {
   unsigned* counters;
   void* out;
   int out_f16;
-  L2Prefetch pf;  // the next GEMM's first weight blocks
+  int early_meta;  // spans, work split and first pages before the dependency wait
+  int merge_last;  // the last segment of a split pair merged by the softmax warps when it can
+  L2Prefetch pf;   // the next GEMM's first weight blocks
 };
 
 // One K or V tile of a chunk: dims 0-63 / 64-127, each 128 rows x 128 B, 128-byte swizzle.
@@ -93,6 +96,7 @@ struct AttnSmem {
   uint32_t inv_v[kStages];
   uint32_t tmem;
   int last;
+  int merge_here;  // the CTA's last segment is merged by the softmax warps
   unsigned long long tl_p0, tl_plast;  // tracing build: first and last P handed to the O MMA
   int span[kMaxLanes];
   int cnt[kMaxLanes];         // chunk-list items of each lane (chunks x n_kv)
@@ -162,6 +166,18 @@ TTS_DEV void zero_rows(Tile& tile, int vlo, int vhi, uint32_t inv, int box, int 
   }
 }
 
+// One step of merging a pair's parts in chunk order: the running (max, sum, output) takes part
+// (cm, cl, ov). Explicit roundings, so the epilogue warp's merge and the softmax warps' merge of
+// a CTA's last segment give the same bits whichever of them runs.
+TTS_DEV void merge_step(float& mm, float& ll, float& oo, float cm, float cl, float ov) {
+  const float mn = fmaxf(mm, cm);
+  const float f0 = (mm == -INFINITY) ? 0.f : expf(mm - mn);
+  const float f1 = expf(cm - mn);
+  ll = __fmaf_rn(ll, f0, __fmul_rn(cl, f1));
+  oo = __fmaf_rn(oo, f0, __fmul_rn(ov, f1));
+  mm = mn;
+}
+
 template <int GQA>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmK,
@@ -202,8 +218,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int i = t; i < int(sizeof(S.qb) + sizeof(S.pb)) / 16; i += kThreads)
     reinterpret_cast<uint4*>(&S.qb[0][0][0])[i] = make_uint4(0, 0, 0, 0);
 
-  pdl_wait();
-  [[maybe_unused]] const unsigned long long tl_rel = TTS_TL_NOW();
+  // With early_meta the spans and the block table are final already: the work split and the
+  // first page lookups go ahead of the dependency wait. Every warp that reads what the previous
+  // kernel wrote (q, K/V rows) or writes what earlier kernels read (partials, counters, the
+  // output) waits first.
+  if (!a.early_meta) pdl_wait();
+  [[maybe_unused]] unsigned long long tl_rel = TTS_TL_NOW();
   // ---- spans and the chunk-list offsets of every lane
   for (int b = t; b < a.lanes; b += kThreads) {
     int span = a.spans[b] + a.span_add;
@@ -309,6 +329,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     Cursor x = first;
     Boxes next = n > 0 ? lookup(x) : Boxes{}, prev{};
+    if (a.early_meta) {
+      pdl_wait();  // K/V rows of this step (the newest position) are the previous kernel's
+      tl_rel = TTS_TL_NOW();
+    }
     bool ok = true;
     long long nk = 0, nv = 0;  // tiles issued
     for (long long k = 0; k <= n && ok; ++k) {
@@ -457,6 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kEpiWarp) {
     // ================= epilogue warp: arrival counts and merges of split pairs. Only the
     // first and the last segment of a CTA's range can hold part of a pair.
+    if (a.early_meta) pdl_wait();
     int expect = 0;
     if (n > 0) {
       Cursor x = first;
@@ -472,6 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (a.err && lane == 0) atomicOr(a.err, kFlagAttnWait);
         break;
       }
+      if (S.seg_info[k].len == 0) continue;  // merged by the softmax warps (finish_last)
       const int b = S.seg_info[k].b, h = S.seg_info[k].h;
       const int nch = lane_range(S.span[b], a.window).nch;
       unsigned last = 0;
@@ -506,15 +532,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           // slots are 130 floats (8-byte aligned): four scalar loads
           const float4 ov = make_float4(__ldcg(pp + lane * 4), __ldcg(pp + lane * 4 + 1),
                                         __ldcg(pp + lane * 4 + 2), __ldcg(pp + lane * 4 + 3));
-          const float mn = fmaxf(mm[g], cm);
-          const float f0 = (mm[g] == -INFINITY) ? 0.f : expf(mm[g] - mn);
-          const float f1 = expf(cm - mn);
-          ll[g] = ll[g] * f0 + cl * f1;
-          oo[g][0] = oo[g][0] * f0 + ov.x * f1;
-          oo[g][1] = oo[g][1] * f0 + ov.y * f1;
-          oo[g][2] = oo[g][2] * f0 + ov.z * f1;
-          oo[g][3] = oo[g][3] * f0 + ov.w * f1;
-          mm[g] = mn;
+          const float ov4[4] = {ov.x, ov.y, ov.z, ov.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float m_u = mm[g], l_u = ll[g];
+            merge_step(m_u, l_u, oo[g][u], cm, cl, ov4[u]);
+            if (u == 3) {
+              mm[g] = m_u;
+              ll[g] = l_u;
+            }
+          }
         }
       }
       const size_t out_base = (size_t)b * heads * 128 + (size_t)h * GQA * 128;
@@ -543,6 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ================= softmax warps 0-3 (thread t: TMEM lane t = chunk row t = output dim t)
+  if (a.early_meta) pdl_wait();  // q is the previous kernel's output
   const int heads = a.n_kv * GQA;
   const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
   bool ok = true;
@@ -669,6 +697,72 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++n_partial;
     }
   };
+  // The CTA's last segment. When it closes a pair split across CTAs and every other part has
+  // arrived already (the next CTA processed its part at the start of its range), it is merged
+  // here from registers: one acquire load and one read of the other parts, instead of a partial
+  // write, the epilogue warp's arrival count and a merge that reads this part back.
+  auto finish_last = [&](const float* m, const float* l, const float* o_acc) {
+    const bool whole = prev.c_first == 0 && prev.c_last + 1 == prev.nch;
+    if (whole || n_partial >= 2 || !a.merge_last) {
+      finish_segment(m, l, o_acc);
+      return;
+    }
+    const unsigned key = unsigned(prev.b * a.n_kv + prev.h);
+    const unsigned len = unsigned(prev.c_last - prev.c_first + 1);
+    if (t == 0)
+      S.merge_here = (ld_acquire_u32(&a.counters[key]) + len == unsigned(prev.nch)) ? 1 : 0;
+    bar_and(kBarSoftmax, kSoftmax, true);
+    if (!S.merge_here) {
+      finish_segment(m, l, o_acc);
+      return;
+    }
+    const size_t pbase = ((size_t)prev.b * a.n_kv + prev.h) * a.max_chunks;
+    const long long base = S.prefix[prev.b] + (long long)prev.h * prev.nch;
+    const long long total = S.prefix[a.lanes];
+    float mm[GQA], ll[GQA], oo[GQA];
+#pragma unroll
+    for (int g = 0; g < GQA; ++g) {
+      mm[g] = -INFINITY;
+      ll[g] = 0.f;
+      oo[g] = 0.f;
+    }
+    for (int cc = 0; cc < prev.nch; ++cc) {
+      const bool st = cc == 0 || owner_of(base + cc, total, gridDim.x) !=
+                                     owner_of(base + cc - 1, total, gridDim.x);
+      if (!st) continue;
+#pragma unroll
+      for (int g = 0; g < GQA; ++g) {
+        float cm, cl, ov;
+        if (cc == prev.c_first) {
+          cm = m[g];
+          cl = l[g];
+          ov = o_acc[g];
+        } else {
+          const float* pp = a.part + ((pbase + cc) * GQA + g) * 130;
+          cm = __ldcg(pp + 128);
+          cl = __ldcg(pp + 129);
+          ov = __ldcg(pp + t);
+        }
+        merge_step(mm[g], ll[g], oo[g], cm, cl, ov);
+      }
+    }
+    const size_t out_base = (size_t)prev.b * heads * 128 + (size_t)prev.h * GQA * 128;
+#pragma unroll
+    for (int g = 0; g < GQA; ++g) {
+      const float r = oo[g] / ll[g];
+      const size_t oi = out_base + g * 128 + t;
+      if (a.out_f16)
+        static_cast<__half*>(a.out)[oi] = __float2half_rn(r);
+      else
+        static_cast<float*>(a.out)[oi] = r;
+    }
+    if (t == 0) {
+      a.counters[key] = 0u;  // every other part has counted in: no one else reads it
+      S.seg_info[n_partial].len = 0;  // the epilogue warp has nothing left for this segment
+    }
+    mbar_arrive(&S.seg_done[n_partial]);
+    ++n_partial;
+  };
 
   for (long long j = 0; j < n; ++j) {
     const int s = int(j % kStages);
@@ -774,7 +868,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (ok && pend) {
     if (bar_and(kBarSoftmax, kSoftmax, ok)) {
       fold(n - 1, l_run, acc);
-      finish_segment(m_run, l_run, acc);
+      finish_last(m_run, l_run, acc);
     } else {
       ok = false;
     }
@@ -865,6 +959,12 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
   a.counters = w.counters;
   a.out = r.out;
   a.out_f16 = r.out_f16 ? 1 : 0;
+  a.early_meta = (r.early_meta && r.pdl) ? 1 : 0;
+  {
+    // TTS_ATTN_MERGE_LAST=0: every split pair merged by the epilogue warp (A/B)
+    const char* e = getenv("TTS_ATTN_MERGE_LAST");
+    a.merge_last = (e && *e == '0') ? 0 : 1;
+  }
   a.pf = r.next;
 
   int dev = 0;

@@ -266,6 +266,9 @@ __global__ void __launch_bounds__(kPaThreads, 1)
     __syncwarp();
   }
   if (ok) ok = mbar_wait(&S.o_bar, 0);
+  // one verdict for the whole CTA: the TMEM loads below are warp-collective, and each thread's
+  // bounded wait could give up on its own
+  ok = __syncthreads_and(ok);
   tc_fence_after();
   if (ok) {
     // every lane of a warp issues the TMEM loads (warp-collective, aligned); only rows of the

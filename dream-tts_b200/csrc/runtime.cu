@@ -883,6 +883,13 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
 
   float* next = hsel && hsel->feed_h ? s->h : (s->feedback ? s->feedback : s->x_next);
   const float* src = x ? x : next;
+  // The step begins with a copy into the residual stream (a full stream dependency on
+  // everything earlier, the position advance included), and none of its kernels writes the
+  // positions or the block table before the final code gather: the attention may split its
+  // work and resolve its pages before its dependency wait. TTS_ATTN_EARLY_META=0: off (A/B).
+  const bool step_copies_input = !(hsel && hsel->in_h);
+  const char* early_env = getenv("TTS_ATTN_EARLY_META");
+  const bool early_meta_on = !(early_env && *early_env == '0');
   if (!(hsel && hsel->in_h) &&
       (rc = cuda_status(cudaMemcpyAsync(s->h, src, size_t(B) * D * 4, cudaMemcpyDeviceToDevice, cs),
                         "decode_step")) != TTS_OK)
@@ -1050,6 +1057,7 @@ static tts_status step_impl(tts_stack* s, const tts_decode_state* st, const floa
       TTS_TRY(launch_gemm(qkv, c->gemm, cs, c->device), "proj");
       AttnRequest ar = req_attn(l);
       ar.next = pf(w.wo, qw, D);
+      ar.early_meta = step_copies_input && early_meta_on;
       TTS_TRY(launch_attn(ar, c->attn, cs), "decode_attention");
       GemmRequest o = req_o(l);
       o.next = pf(w.w_gate_up, D, 2 * gm.ffn);

@@ -196,6 +196,12 @@ TTS_DEV uint64_t l2_policy_evict_last() {
 TTS_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 TTS_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
+// A load with acquire semantics at GPU scope (pairs with a writer's fence + atomic).
+TTS_DEV unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 // ------------------------------------------------------------------ thread-block clusters
 TTS_DEV uint32_t cluster_rank() {
   uint32_t r;

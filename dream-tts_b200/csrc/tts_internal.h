@@ -180,6 +180,12 @@ struct AttnRequest {
   void* out = nullptr;  // [lanes][n_kv*gqa*128]
   bool out_f16 = true;
   bool pdl = true;
+  // The caller guarantees that the spans and the block table are final when the kernel starts
+  // (nothing launched earlier in the stream still writes them): the kernel then splits its work
+  // and resolves its first pages before waiting for the previous kernel (PDL); every K/V load
+  // still waits. The talker's decode step: it starts with a copy (a full stream dependency on
+  // the previous step's position advance) and its kernels write neither.
+  bool early_meta = false;
   L2Prefetch next;  // optional: the next GEMM's first weight blocks
 };
 struct AttnWorkspace {
