@@ -1213,11 +1213,11 @@ static tts_status prefill_layer_major(tts_stack* s, const tts_decode_state* st, 
     r.y = y;
     return launch_pf_gemm(r, cs, c->device, c->gemm.err);
   };
-  // the prompt attention (a lane's query rows in blocks of 64 against its keys), opt-in with
-  // TTS_PREFILL_ATTN=1 where it applies (GQA 2, spans <= 256); by default the decode attention
-  // runs per prompt row
+  // the prompt attention (a lane's query rows in blocks of 64 against its keys) where it
+  // applies (GQA 2, max_span <= 256: every lane's keys fit its two TMEM chunks); elsewhere, or
+  // with TTS_PREFILL_ATTN=0, the decode attention runs per prompt row
   const char* pa_env = getenv("TTS_PREFILL_ATTN");
-  const bool use_pfa = pa_env && *pa_env == '1' &&
+  const bool use_pfa = !(pa_env && *pa_env == '0') &&
                        pf_attn_supported(gm.heads, gm.n_kv, st->block_size, st->max_span);
   int n_qblocks = 0;
   if (use_pfa) {
