@@ -36,7 +36,7 @@ BLOCK = 32
 # DRAM bytes (read + write) of one gate/up launch at 48 lanes, from its ncu capture
 GATEUP_NCU_TRAFFIC = 50_606_336 + 6_912
 # the same for one attention launch of the config[2] step (KV lengths U[64,1024] seed 0 + 1)
-ATTN_NCU_TRAFFIC = 103_300_000 + 3_100_000
+ATTN_NCU_TRAFFIC = 103_285_760 + 3_062_016
 ATTN_BYTES_PER_POS = N_KV * HD * 2 * 2  # K and V rows of one position, all kv heads, f16
 KV_LO, KV_HI = 64, 1024
 WORKLOAD = ("config[2]: full talker decode step, 28 layers, hidden 2048, 16q/8kv heads x 128, "
