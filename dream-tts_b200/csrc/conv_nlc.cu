@@ -18,10 +18,21 @@
 // rather than once per tap. Rows before 0 or past len are zero-filled by TMA, and snake(0) = 0,
 // so padding matches the reference's pad-then-activate order.
 //
-// Persistent: one CTA per SM loops over (position block, batch, output-channel slice) tiles.
-// Warp roles (320 threads): warp 0 issues the weight tiles (B ring), warp 1 the MMAs (each
+// CTA pairs: where a tile is 256 output channels, two CTAs of a cluster share it
+// (tcgen05 cta_group::2). Each holds its own positions' halo and half of every weight tile (128
+// rows), and the even CTA issues M = 256 MMAs that read both CTAs' shared memory and write both
+// CTAs' TMEM. Each SM then streams half the weight bytes per MMA and the MMA issuer drives two
+// SMs. The odd CTA's halo and epilogue warps report to the even CTA's barriers (remote
+// arrivals); its weight loads count on the even CTA's barrier; the MMAs' completions arrive in
+// both CTAs (multicast commits). The issue loop precomputes each tap's descriptors (one thread
+// issues every MMA, and rebuilding descriptors per MMA made issue, not the tensor pipe, the
+// limit).
+//
+// Persistent: one CTA (pair) per SM (pair of SMs) loops over (position block, batch,
+// output-channel slice) tiles.
+// Warp roles (384 threads): warp 0 issues the weight tiles (B ring), warp 1 the MMAs (each
 // from one elected lane of the converged warp), warps 2..5 run the epilogue of one tile while
-// warps 6..9 load the next tile's halos (A ring, one halo per sub-tile) and apply the snake, so
+// warps 6..11 load the next tile's halos (A ring, one halo per sub-tile) and apply the snake, so
 // a tile's loads and snake overlap the previous tile's epilogue. Every wait is bounded; a wait
 // that gives up sets an error flag the host reads.
 #include <algorithm>
@@ -36,9 +47,10 @@ namespace {
 
 constexpr int kRows = 128;      // output positions per sub-tile (the MMA's M)
 constexpr int kCB = 64;         // input channels per halo
-constexpr int kHaloWarp0 = 6;   // warps 6..9 load and transform the halos
-constexpr int kHaloThreads = 128;
-constexpr int kThreads = 320;
+constexpr int kHaloWarp0 = 6;   // warps 6..11 load and transform the halos
+constexpr int kHaloThreads = 192;
+// 12 warps: three per SM sub-partition, which caps registers at 168 per thread (as ten would)
+constexpr int kThreads = 384;
 
 struct ConvArgs {
   int b, len, cin, cout, k, dil, pad_left;
@@ -46,11 +58,16 @@ struct ConvArgs {
   int nh, nper;  // MMAs per K step and sub-tile, and N of each
   int ms;        // 128-position sub-tiles per CTA (1 or 2), one accumulator each
   int acc_stride;  // TMEM columns between the sub-tiles' accumulators
+  int nbuf;        // accumulator sets (1 or 2): with 2, tile t's epilogue drains one set while
+                   // tile t + 1's MMAs fill the other
+  int buf_stride;  // TMEM columns between the sets
   int R;         // halo rows covering every sub-tile (multiple of 8)
   int H, nrb;    // rows per halo TMA box and boxes per 8-channel slab (R = H * nrb)
   int as, bs;    // halo and weight ring depths
   int tmem_cols;
   const float* bias;
+  int bias_v4;  // bias is 16-byte aligned: read 4 channels per load
+  int snake_v4;  // alpha and 1/beta are 16-byte aligned: read 4 channels per load
   const float* alpha;
   const float* brecip;
   const __half* res;
@@ -61,41 +78,50 @@ struct ConvArgs {
 // SnakeBeta on 8 f16 channels in place. The fast hardware sine is used: its absolute error
 // (about 2^-21 near the origin, growing slowly with the argument) stays far below the f16
 // rounding of the result, while the accurate sinf's range reduction made the snake, applied to
-// every halo element, cost as much as the MMAs it feeds.
-__device__ __forceinline__ void snake8(uint4& u, const float* alpha, const float* brecip) {
+// every halo element, cost as much as the MMAs it feeds. The channels' alpha and 1/beta are
+// in registers (loaded once per 8-channel slab of a halo).
+__device__ __forceinline__ void snake8r(uint4& u, const float (&al)[8], const float (&br)[8]) {
   __half2* h = reinterpret_cast<__half2*>(&u);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     float2 f = __half22float2(h[q]);
-    const float s0 = __sinf(__ldg(alpha + 2 * q) * f.x);
-    const float s1 = __sinf(__ldg(alpha + 2 * q + 1) * f.y);
-    f.x = f.x + __ldg(brecip + 2 * q) * (s0 * s0);
-    f.y = f.y + __ldg(brecip + 2 * q + 1) * (s1 * s1);
+    const float s0 = __sinf(al[2 * q] * f.x);
+    const float s1 = __sinf(al[2 * q + 1] * f.y);
+    f.x = f.x + br[2 * q] * (s0 * s0);
+    f.y = f.y + br[2 * q + 1] * (s1 * s1);
     h[q] = __floats2half2_rn(f.x, f.y);
   }
 }
 
+// kPair: CTA pairs (2-CTA clusters) share each weight tile; see the file comment.
+template <bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_nlc_kernel(const __grid_constant__ CUtensorMap tmX,
                     const __grid_constant__ CUtensorMap tmW, const ConvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  constexpr int P = kPair ? 2 : 1;  // CTAs per tile
+  const uint32_t rank = kPair ? cluster_rank() : 0u;
+  const bool leader = rank == 0;  // the CTA that issues the MMAs
   const int kAStages = a.as, kBStages = a.bs;
   const int ncb = a.cin / kCB;
-  const int nx = (a.len + kRows * a.ms - 1) / (kRows * a.ms);
+  const int span = kRows * a.ms * P;  // positions per tile (each CTA kRows * ms of them)
+  const int nx = (a.len + span - 1) / span;
   const int nz = a.cout / a.cout_cta;
   const int ntiles = nx * a.b * nz;
-  // this CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
-  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  // this CTA's (pair's) tiles: unit, unit + units, ...
+  const int unit = blockIdx.x / P, units = gridDim.x / P;
+  const int my_tiles = unit < ntiles ? (ntiles - 1 - unit) / units + 1 : 0;
   auto tile_of = [&](int t, int& l0, int& bb, int& co0) {
-    const int id = blockIdx.x + t * gridDim.x;
-    l0 = (id % nx) * kRows * a.ms;
+    const int id = unit + t * units;
+    l0 = (id % nx) * span + int(rank) * kRows * a.ms;  // this CTA's first position
     bb = (id / nx) % a.b;
     co0 = (id / (nx * a.b)) * a.cout_cta;
   };
-  const uint32_t a_bytes = uint32_t(a.R) * kCB * 2;        // one halo: 8 slabs x R rows x 16 B
-  const uint32_t b_bytes = uint32_t(a.cout_cta) * kCB * 2;  // cout_cta rows x 128 B
+  const uint32_t a_bytes = uint32_t(a.R) * kCB * 2;  // one halo: 8 slabs x R rows x 16 B
+  // this CTA's weight rows per step: all cout_cta, or its half of them in a pair
+  const uint32_t b_bytes = uint32_t(a.cout_cta / P) * kCB * 2;
   uint8_t* a_base = smem;
   uint8_t* b_base = smem + kAStages * a_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + kBStages * b_bytes);
@@ -104,33 +130,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty_a = bars + 2 * kAStages;
   uint64_t* full_b = bars + 3 * kAStages;
   uint64_t* empty_b = full_b + kBStages;
-  uint64_t* tmem_full = empty_b + kBStages;  // MMAs of a tile done
-  uint64_t* tmem_empty = tmem_full + 1;      // its accumulators read by the epilogue
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 1);
+  uint64_t* tmem_full = empty_b + kBStages;  // [2] MMAs of a tile done (per accumulator set)
+  uint64_t* tmem_empty = tmem_full + 2;      // [2] its accumulators read by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // tracing build: each role's summed wait (or busy) times, recorded at the end
+  [[maybe_unused]] const unsigned long long tl_entry = TTS_TL_NOW();
+  [[maybe_unused]] unsigned long long tl_w0 = 0, tl_w1 = 0, tl_w2 = 0, tl_t = 0;
   if (threadIdx.x == 0) {
+    // in a pair the MMA-side barriers that count both CTAs live in the leader: ready_a
+    // (both CTAs' halo threads), full_b (both halves' bytes), tmem_empty (both epilogues)
     for (int s = 0; s < kAStages; ++s) {
       mbar_init(&full_a[s], 1);
-      mbar_init(&ready_a[s], kHaloThreads);
+      mbar_init(&ready_a[s], kHaloThreads * P);
       mbar_init(&empty_a[s], 1);
     }
     for (int s = 0; s < kBStages; ++s) {
       mbar_init(&full_b[s], 1);
       mbar_init(&empty_b[s], 1);
     }
-    mbar_init(tmem_full, 1);
-    mbar_init(tmem_empty, 4);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&tmem_full[s], 1);
+      mbar_init(&tmem_empty[s], 4 * P);
+    }
     fence_barrier_init();
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmW);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, a.tmem_cols);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(tmem_slot, a.tmem_cols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, a.tmem_cols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  // a pair's barriers and TMEM exist in both CTAs before either signals the other
+  if constexpr (kPair)
+    cluster_sync();
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_launch_dependents();
@@ -142,7 +184,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int total = my_tiles * steps;
     for (int g = 0; g < total; ++g) {
       const int s = g % kBStages;
-      if (g >= kBStages && !mbar_wait_warp(&empty_b[s], ((g / kBStages) + 1) & 1)) {
+      tl_t = TTS_TL_NOW();
+      const bool ok_e = g < kBStages || mbar_wait_warp(&empty_b[s], ((g / kBStages) + 1) & 1);
+      tl_w0 += TTS_TL_NOW() - tl_t;
+      if (!ok_e) {
         if (lane == 0) atomicOr(a.err, 16);
         break;
       }
@@ -151,28 +196,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_of(g / steps, l0, bb, co0);
         const int i = g % steps, cb = i / a.k, t = i % a.k;
         uint8_t* dst = b_base + s * b_bytes;
-        mbar_arrive_expect_tx(&full_b[s], b_bytes);
-        for (int h = 0; h < a.nh; ++h)
-          tma_load_2d(dst + h * a.nper * 128, &tmW, &full_b[s], t * a.cin + cb * kCB,
-                      co0 + h * a.nper);
+        if constexpr (kPair) {
+          // this CTA's half of the tile's rows; both halves count on the leader's barrier,
+          // which expects both
+          const uint32_t fb = cluster_addr(&full_b[s], 0);
+          if (leader) mbar_arrive_expect_tx(&full_b[s], b_bytes * 2);
+          for (int h = 0; h < a.nh; ++h)
+            tma_load_2d_pair(dst + h * (a.nper / 2) * 128, &tmW, fb, t * a.cin + cb * kCB,
+                             co0 + h * a.nper + int(rank) * (a.nper / 2));
+        } else {
+          mbar_arrive_expect_tx(&full_b[s], b_bytes);
+          for (int h = 0; h < a.nh; ++h)
+            tma_load_2d(dst + h * a.nper * 128, &tmW, &full_b[s], t * a.cin + cb * kCB,
+                        co0 + h * a.nper);
+        }
       }
       __syncwarp();
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer: the accumulators of one tile at a time
-    const uint32_t idesc = idesc_f16_f32(kRows, a.nper);
+  } else if (warp == 1 && (!kPair || leader)) {
+    // ---------------- MMA issuer: the accumulators of one tile at a time (in a pair, M = 256:
+    // 128 positions of each CTA, N = a.nper with half of the weight rows in each CTA)
+    const uint32_t idesc = idesc_f16_f32(kRows * P, a.nper);
+    // the MMAs' completion arrives in both CTAs of a pair
+    auto commit = [&](uint64_t* bar) {
+      if constexpr (kPair)
+        umma_commit_pair(bar, 3);
+      else
+        umma_commit(bar);
+    };
     const uint32_t slab = uint32_t(a.R) * 16;
     bool ok = true;
     int gc = 0, g = 0;  // global halo and step counters
     for (int tl = 0; tl < my_tiles && ok; ++tl) {
-      if (tl > 0 && !mbar_wait_warp(tmem_empty, (tl - 1) & 1)) {
+      // accumulator set tl % nbuf, used for the (tl / nbuf)-th time
+      const int buf = tl % a.nbuf, use = tl / a.nbuf;
+      const uint32_t acc0 = tmem + uint32_t(buf * a.buf_stride);
+      tl_t = TTS_TL_NOW();
+      const bool ok_t = use == 0 || mbar_wait_warp(&tmem_empty[buf], (use - 1) & 1);
+      tl_w0 += TTS_TL_NOW() - tl_t;
+      if (!ok_t) {
         if (lane == 0) atomicOr(a.err, 32);
         break;
       }
       tc_fence_after();
       for (int cb = 0; cb < ncb && ok; ++cb, ++gc) {
         const int sa = gc % kAStages;
-        if (!mbar_wait_warp(&ready_a[sa], (gc / kAStages) & 1)) {
+        tl_t = TTS_TL_NOW();
+        const bool ok_a = mbar_wait_warp(&ready_a[sa], (gc / kAStages) & 1);
+        tl_w1 += TTS_TL_NOW() - tl_t;
+        if (!ok_a) {
           if (lane == 0) atomicOr(a.err, 32);
           ok = false;
           break;
@@ -181,7 +253,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < a.k; ++t, ++g) {
           const int i = cb * a.k + t;
           const int sb = g % kBStages;
-          if (!mbar_wait_warp(&full_b[sb], (g / kBStages) & 1)) {
+          tl_t = TTS_TL_NOW();
+          const bool ok_b = mbar_wait_warp(&full_b[sb], (g / kBStages) & 1);
+          tl_w2 += TTS_TL_NOW() - tl_t;
+          if (!ok_b) {
             if (lane == 0) atomicOr(a.err, 64);
             ok = false;
             break;
@@ -189,29 +264,56 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           if (elect_one()) {
             const uint32_t hb = smem_u32(b_base + sb * b_bytes);
+            auto mma = [&](uint32_t d, uint64_t ad, uint64_t bd, uint32_t acc) {
+              if constexpr (kPair)
+                umma_f16_pair(d, ad, bd, idesc, acc);
+              else
+                umma_f16(d, ad, bd, idesc, acc);
+            };
+            // The descriptors of this tap's first MMA; the others differ only in the start
+            // address field (bits 0-13, in 16-byte units, no carry below 256 KB): +32 B per
+            // 16 channels of the weight rows, +2 slabs per 16 channels of the halo, +128 rows
+            // per sub-tile. One thread issues every MMA, so its issue loop is kept this short.
+            const uint64_t a_t = desc_k_interleave(ha + t * a.dil * 16, slab);
+            const uint64_t b_0 = desc_k_sw128(hb);
+            const uint64_t a_kk = 2 * (slab >> 4), a_j = (kRows * 16) >> 4;
+            if (a.ms == 2 && a.nh == 1) {
 #pragma unroll
-            for (int kk = 0; kk < kCB / 16; ++kk) {
-              for (int h = 0; h < a.nh; ++h) {
-                const uint64_t bd = desc_k_sw128(hb + h * a.nper * 128 + kk * 32);
-                for (int j = 0; j < a.ms; ++j) {
-                  // sub-tile j starts 128 rows into the shared halo
-                  const uint64_t ad = desc_k_interleave(
-                      ha + 2 * kk * slab + (j * kRows + t * a.dil) * 16, slab);
-                  umma_f16(tmem + j * a.acc_stride + h * a.nper, ad, bd, idesc, (i | kk) != 0);
+              for (int kk = 0; kk < kCB / 16; ++kk) {
+                const uint64_t bd = b_0 + uint64_t(kk * 2);
+                const uint64_t ad = a_t + uint64_t(kk) * a_kk;
+                const uint32_t acc = (i | kk) != 0;
+                mma(acc0, ad, bd, acc);
+                mma(acc0 + a.acc_stride, ad + a_j, bd, acc);
+              }
+            } else if (a.ms == 1 && a.nh == 1) {
+#pragma unroll
+              for (int kk = 0; kk < kCB / 16; ++kk)
+                mma(acc0, a_t + uint64_t(kk) * a_kk, b_0 + uint64_t(kk * 2), (i | kk) != 0);
+            } else {
+#pragma unroll
+              for (int kk = 0; kk < kCB / 16; ++kk) {
+                for (int h = 0; h < a.nh; ++h) {
+                  const uint64_t bd =
+                      b_0 + uint64_t((h * (a.nper / P) * 128) >> 4) + uint64_t(kk * 2);
+                  for (int j = 0; j < a.ms; ++j)
+                    // sub-tile j starts 128 rows into the shared halo
+                    mma(acc0 + j * a.acc_stride + h * a.nper,
+                        a_t + uint64_t(kk) * a_kk + uint64_t(j) * a_j, bd, (i | kk) != 0);
                 }
               }
             }
-            umma_commit(&empty_b[sb]);
+            commit(&empty_b[sb]);
           }
           __syncwarp();
         }
         if (ok) {
-          if (elect_one()) umma_commit(&empty_a[sa]);
+          if (elect_one()) commit(&empty_a[sa]);
           __syncwarp();
         }
       }
       if (ok) {
-        if (elect_one()) umma_commit(tmem_full);
+        if (elect_one()) commit(&tmem_full[buf]);
         __syncwarp();
       }
     }
@@ -242,33 +344,90 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int gi = 0; gi < std::min(total, kAStages - 1); ++gi) issue(gi);
     for (int gi = 0; gi < total; ++gi) {
       const int s = gi % kAStages;
-      if (!mbar_wait(&full_a[s], (gi / kAStages) & 1)) {
+      tl_t = TTS_TL_NOW();
+      const bool ok_h = mbar_wait(&full_a[s], (gi / kAStages) & 1);
+      tl_w0 += TTS_TL_NOW() - tl_t;
+      tl_t = TTS_TL_NOW();
+      if (!ok_h) {
         if (tt == 0) atomicOr(a.err, 4096);
       }
       if (a.alpha) {
         uint8_t* halos = a_base + s * a_bytes;
         const int cb = gi % ncb;
-        for (int c = tt; c < 8 * a.R; c += kHaloThreads) {
-          const int gq = c / a.R;
-          const int ch = cb * kCB + gq * 8;
-          uint4* p = reinterpret_cast<uint4*>(halos) + c;
-          uint4 u = *p;
-          snake8(u, a.alpha + ch, a.brecip + ch);
-          *p = u;
+        uint4* p = reinterpret_cast<uint4*>(halos);
+        // Elements c = slab * R + row, two per thread per pass (kHaloThreads apart: the
+        // sine's latency dominates), the slab tracked as the row wraps rather than divided
+        // out (R >= 128: a step of kHaloThreads wraps at most twice).
+        auto ab = [&](int g, float (&al)[8], float (&br)[8]) {
+          const int ch = cb * kCB + g * 8;
+          if (a.snake_v4) {
+            const float4* a4 = reinterpret_cast<const float4*>(a.alpha + ch);
+            const float4* b4 = reinterpret_cast<const float4*>(a.brecip + ch);
+            const float4 a0 = __ldg(a4), a1 = __ldg(a4 + 1), b0 = __ldg(b4), b1 = __ldg(b4 + 1);
+            al[0] = a0.x, al[1] = a0.y, al[2] = a0.z, al[3] = a0.w;
+            al[4] = a1.x, al[5] = a1.y, al[6] = a1.z, al[7] = a1.w;
+            br[0] = b0.x, br[1] = b0.y, br[2] = b0.z, br[3] = b0.w;
+            br[4] = b1.x, br[5] = b1.y, br[6] = b1.z, br[7] = b1.w;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              al[e] = __ldg(a.alpha + ch + e);
+              br[e] = __ldg(a.brecip + ch + e);
+            }
+          }
+        };
+        int g0 = 0, r0 = tt;
+        while (r0 >= a.R) r0 -= a.R, ++g0;
+        while (g0 < kCB / 8) {
+          int g1 = g0, r1 = r0 + kHaloThreads;
+          while (r1 >= a.R) r1 -= a.R, ++g1;
+          const bool two = g1 < kCB / 8;
+          uint4 u0 = p[g0 * a.R + r0];
+          uint4 u1 = two ? p[g1 * a.R + r1] : make_uint4(0, 0, 0, 0);
+          float al0[8], br0[8], al1[8], br1[8];
+          ab(g0, al0, br0);
+          ab(two ? g1 : g0, al1, br1);
+          snake8r(u0, al0, br0);
+          snake8r(u1, al1, br1);
+          p[g0 * a.R + r0] = u0;
+          if (two) p[g1 * a.R + r1] = u1;
+          g0 = g1;
+          r0 = r1 + kHaloThreads;
+          while (r0 >= a.R) r0 -= a.R, ++g0;
         }
+        tl_w1 += TTS_TL_NOW() - tl_t;
+        tl_t = TTS_TL_NOW();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tl_w2 += TTS_TL_NOW() - tl_t;
+        tl_t = TTS_TL_NOW();
       }
-      mbar_arrive(&ready_a[s]);
+      tl_w1 += TTS_TL_NOW() - tl_t;
+      // the halo is ready for the MMAs (in a pair: on the leader's barrier)
+      if (kPair && !leader)
+        mbar_arrive_cluster(cluster_addr(&ready_a[s], 0));
+      else
+        mbar_arrive(&ready_a[s]);
       if (warp == kHaloWarp0 && gi + kAStages - 1 < total) issue(gi + kAStages - 1);
     }
-  } else {
+  } else if (warp >= 2) {
     // ---------------- epilogue (warps 2..5: TMEM lane quadrant = warp % 4), one tile at a time
     const int quad = warp & 3;
     // 64 columns per TMEM wait; the residual of the next 64 columns is read while this batch
     // is finished, so the row's residual loads overlap instead of adding up
     auto finish16 = [&](float* v, const uint4* rr, int c0, int co0, size_t row, bool live) {
       if (!live) return;
-      if (a.bias) {
+      if (a.bias && a.bias_v4) {
+        // four 16-byte loads (the same addresses across the warp: broadcasts)
+        const float4* b4 = reinterpret_cast<const float4*>(a.bias + co0 + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 b = __ldg(b4 + q);
+          v[4 * q] += b.x;
+          v[4 * q + 1] += b.y;
+          v[4 * q + 2] += b.z;
+          v[4 * q + 3] += b.w;
+        }
+      } else if (a.bias) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) v[i] += __ldg(a.bias + co0 + c0 + i);
       }
@@ -294,7 +453,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     const int c64 = a.cout_cta / 64 * 64;  // columns done 64 at a time
     for (int tl = 0; tl < my_tiles; ++tl) {
-      if (!mbar_wait(tmem_full, tl & 1) && lane == 0) atomicOr(a.err, 8192);
+      const int buf = tl % a.nbuf;
+      tl_t = TTS_TL_NOW();
+      if (!mbar_wait(&tmem_full[buf], (tl / a.nbuf) & 1) && lane == 0) atomicOr(a.err, 8192);
+      tl_w0 += TTS_TL_NOW() - tl_t;
+      tl_t = TTS_TL_NOW();
       tc_fence_after();
       int l0, bb, co0;
       tile_of(tl, l0, bb, co0);
@@ -302,7 +465,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int l = l0 + j * kRows + quad * 32 + lane;
         const bool live = l < a.len;
         const size_t row = ((size_t)bb * a.len + (live ? l : 0)) * a.cout + co0;
-        const uint32_t acc = tmem + (uint32_t(quad * 32) << 16) + uint32_t(j * a.acc_stride);
+        const uint32_t acc = tmem + (uint32_t(quad * 32) << 16) +
+                             uint32_t(buf * a.buf_stride + j * a.acc_stride);
         const uint4* rp = reinterpret_cast<const uint4*>(a.res + row);  // 8 channels per uint4
         const bool rd = a.res && live;
         uint4 rnext[8];
@@ -335,14 +499,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the accumulators may be overwritten by the next tile's MMAs
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(tmem_empty);
+      if (lane == 0) {
+        // in a pair the leader's MMAs wait for both CTAs' epilogues
+        if (kPair && !leader)
+          mbar_arrive_cluster(cluster_addr(&tmem_empty[buf], 0));
+        else
+          mbar_arrive(&tmem_empty[buf]);
+      }
+      tl_w1 += TTS_TL_NOW() - tl_t;
     }
   }
+#ifdef TTS_TIMELINE
+  if (lane == 0 && (warp <= 2 || warp == kHaloWarp0)) {
+    const uint64_t t_end = TTS_TL_NOW();
+    const int k = kTlConv | (warp << 4);
+    timeline_recs<6>({k | kTlCta, k | kTlEntry, k | 1, k | 2, k | 3, k | kTlEnd},
+                     {uint64_t(blockIdx.x), tl_entry, tl_w0, tl_w1, tl_w2, t_end});
+  }
+#endif
   tc_fence_before();
-  __syncthreads();
+  // a pair: neither CTA leaves (or frees TMEM) while the other may still signal its barriers
+  if constexpr (kPair)
+    cluster_sync();
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, a.tmem_cols);
+    if constexpr (kPair)
+      tmem_dealloc_pair(tmem, a.tmem_cols);
+    else
+      tmem_dealloc(tmem, a.tmem_cols);
   }
 }
 
@@ -421,9 +607,31 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     const char* v = getenv("TTS_CONV_SUBTILES");
     if (v && *v == '1') a.ms = 1;
   }
+  // CTA pairs where a tile is 256 output channels (one N = 256 MMA per 16 input channels): the
+  // two CTAs of a cluster take 128 * ms positions each and half of every weight tile, and
+  // the even one issues M = 256 MMAs for both. TTS_CONV_PAIR=0 keeps one CTA per tile and
+  // TTS_CONV_ACC_SETS=2 double-buffers the accumulators with one sub-tile per CTA (A/B
+  // measurement; both measured slower on the codec's block).
+  a.nbuf = 1;
+  bool pair = false;
+  {
+    const char* vp = getenv("TTS_CONV_PAIR");
+    const char* vs = getenv("TTS_CONV_ACC_SETS");
+    const bool pair_on = !(vp && *vp == '0');
+    const bool two_sets = vs && *vs == '2';
+    if (pair_on && a.cout_cta == 256 && a.nh == 1) pair = true;
+    // a pair's tile spans 2 * 128 * ms positions: one sub-tile each for short inputs
+    if (pair && a.ms == 2 && r.len <= 2 * kRows) a.ms = 1;
+    if (two_sets && a.cout_cta <= 256) {
+      a.ms = 1;
+      a.nbuf = 2;
+    }
+  }
+  const int P = pair ? 2 : 1;
   a.acc_stride = 32;
   while (a.acc_stride < a.cout_cta) a.acc_stride *= 2;
-  a.tmem_cols = a.acc_stride * a.ms;
+  a.buf_stride = a.acc_stride * a.ms;
+  a.tmem_cols = a.buf_stride * a.nbuf;
   // one halo for all sub-tiles: ms * 128 + (k-1)*dil rows, loaded as nrb boxes of H rows
   // (a box is at most 256 rows; H a multiple of 8 keeps every box 128-byte aligned)
   {
@@ -435,12 +643,13 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
   // ring depths: the weight tiles are the steady stream (one per tap), halos one per 64 input
   // channels; fill what fits in 224 KB, at least two of each
   {
-    const size_t halo = size_t(a.R) * kCB * 2, wt = size_t(a.cout_cta) * kCB * 2;
+    const size_t halo = size_t(a.R) * kCB * 2, wt = size_t(a.cout_cta / P) * kCB * 2;
     const size_t budget = 224 * 1024;
+    const size_t bs_max = wt <= 16384 ? 6 : 4;
     a.as = 2;
-    a.bs = int(std::min<size_t>(4, (budget - 2 * halo) / wt));
+    a.bs = int(std::min<size_t>(bs_max, (budget - 2 * halo) / wt));
     if (a.bs < 2) a.bs = 2;
-    if (a.bs >= 4 && 3 * halo + 4 * wt <= budget) a.as = 3;
+    if (a.bs >= 4 && 3 * halo + size_t(a.bs) * wt <= budget) a.as = 3;
     // TTS_CONV_AS / TTS_CONV_BS override the ring depths (A/B measurement)
     const char* va = getenv("TTS_CONV_AS");
     const char* vb = getenv("TTS_CONV_BS");
@@ -448,6 +657,11 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     if (vb && *vb) a.bs = std::max(2, std::min(6, atoi(vb)));
   }
   a.bias = r.bias;
+  a.bias_v4 = (reinterpret_cast<uintptr_t>(r.bias) & 15u) == 0 ? 1 : 0;
+  a.snake_v4 = ((reinterpret_cast<uintptr_t>(r.alpha) | reinterpret_cast<uintptr_t>(r.brecip)) &
+                15u) == 0
+                   ? 1
+                   : 0;
   a.alpha = r.alpha;
   a.brecip = r.brecip;
   a.res = r.res;
@@ -471,12 +685,12 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     }
   }
   if (!make_tmap_2d_f16(&tmW, r.w, uint64_t(r.k) * r.cin, uint64_t(r.cout),
-                        uint64_t(r.k) * r.cin * 2, kCB, a.nper, true)) {
+                        uint64_t(r.k) * r.cin * 2, kCB, a.nper / P, true)) {
     set_error("conv1d: weight tensor map rejected");
     return cudaErrorInvalidValue;
   }
-  const size_t smem = size_t(a.as) * a.R * kCB * 2 + size_t(a.bs) * a.cout_cta * kCB * 2 +
-                      1024 + 256;
+  const size_t smem = size_t(a.as) * a.R * kCB * 2 +
+                      size_t(a.bs) * (a.cout_cta / P) * kCB * 2 + 1024 + 256;
   {
     // The opt-in shared-memory limit is a per-device function attribute.
     static std::mutex mu;
@@ -485,7 +699,8 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lock(mu);
     if (dev >= 0 && dev < 64 && !done[dev]) {
-      cudaFuncSetAttribute(conv_nlc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      for (auto fn_k : {conv_nlc_kernel<false>, conv_nlc_kernel<true>})
+        cudaFuncSetAttribute(fn_k, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
       done[dev] = true;
     }
   }
@@ -494,25 +709,43 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     return cudaErrorInvalidValue;
   }
   cudaLaunchConfig_t cfg{};
-  // persistent: one CTA per SM (or per tile when there are fewer), each looping over tiles
-  const long long ntiles = (long long)((r.len + kRows * a.ms - 1) / (kRows * a.ms)) * r.b *
-                           (r.cout / a.cout_cta);
+  // persistent: one CTA (pair) per SM (pair of SMs), or per tile when there are fewer, each
+  // looping over tiles
+  const int span = kRows * a.ms * P;
+  const long long ntiles = (long long)((r.len + span - 1) / span) * r.b * (r.cout / a.cout_cta);
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   if (ntiles > (1ll << 31) - 1) {
     set_error("conv1d: too many tiles");
     return cudaErrorInvalidValue;
   }
-  cfg.gridDim = dim3(unsigned(std::min<long long>(ntiles, std::max(1, sms))), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = r.pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, conv_nlc_kernel, tmX, tmW, a);
+  if (!pair) {
+    cfg.gridDim = dim3(unsigned(std::min<long long>(ntiles, std::max(1, sms))), 1, 1);
+    return cudaLaunchKernelEx(&cfg, conv_nlc_kernel<false>, tmX, tmW, a);
+  }
+  // as many pairs as can be resident at once (a pair's SMs share a GPC)
+  cfg.numAttrs = 2;
+  int clusters = 0;
+  cfg.gridDim = dim3(2 * unsigned(std::max(1, sms / 2)), 1, 1);
+  if (cudaOccupancyMaxActiveClusters(&clusters, conv_nlc_kernel<true>, &cfg) != cudaSuccess ||
+      clusters < 1) {
+    cudaGetLastError();
+    clusters = std::max(1, sms / 2);
+  }
+  cfg.gridDim = dim3(2 * unsigned(std::min<long long>(ntiles, clusters)), 1, 1);
+  return cudaLaunchKernelEx(&cfg, conv_nlc_kernel<true>, tmX, tmW, a);
 }
 
 }  // namespace tts

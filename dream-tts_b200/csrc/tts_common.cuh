@@ -70,6 +70,8 @@ TTS_DEV uint64_t global_ns() {
 constexpr int kTlGemm = 0x100;   // | epilogue << 4 | phase
 constexpr int kTlAttn = 0x200;   // | phase
 constexpr int kTlNorm = 0x300;   // | phase (rms_norm; 0x310 | phase: the deferred norm's input)
+// conv_nlc: | warp << 4 | field; fields 1..3 are per-role sums of wait (or busy) time
+constexpr int kTlConv = 0x400;
 constexpr int kTlEntry = 0, kTlReleased = 1, kTlMainDone = 2, kTlReduced = 3, kTlCta = 4,
               kTlMerged = 5, kTlEnd = 15;  // kTlCta: the phase time field holds blockIdx.x
 // GEMM epilogue (warp 0): its first batch of rows reduced, every batch done
@@ -261,6 +263,67 @@ TTS_DEV void umma_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
           smem_u32(bar))
+      : "memory");
+}
+
+// ---- CTA pairs (cta_group::2): the even CTA of a 2-CTA cluster issues M = 256 MMAs whose A
+// rows and B rows are split between the two CTAs' shared memory (128 A rows and N/2 B rows
+// each, at the same offsets) and whose accumulators land in both CTAs' TMEM (each its own 128
+// lanes, all N columns). Allocation is collective: one warp with the same warp index in each
+// CTA of the pair allocates, relinquishes and frees.
+TTS_DEV void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+TTS_DEV void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+TTS_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+TTS_DEV void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on `bar` (same offset) in every CTA of `cta_mask` once the pair MMAs issued so far
+// have completed.
+TTS_DEV void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+// The shared::cluster address of `local` (an address in this CTA's shared memory) in CTA
+// `rank` of the cluster.
+TTS_DEV uint32_t cluster_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+// Arrive on an mbarrier of any CTA of the cluster, releasing this thread's prior writes at
+// cluster scope.
+TTS_DEV void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   bar_cluster_addr)
+               : "memory");
+}
+// 2D tile load into this CTA's shared memory whose completion is counted on an mbarrier in
+// either CTA of the pair (`bar_cluster_addr`, a shared::cluster address).
+TTS_DEV void tma_load_2d_pair(void* smem_dst, const void* desc, uint32_t bar_cluster_addr, int c0,
+                              int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
       : "memory");
 }
 
