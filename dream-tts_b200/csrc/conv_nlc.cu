@@ -51,6 +51,10 @@ constexpr int kHaloWarp0 = 6;   // warps 6..11 load and transform the halos
 constexpr int kHaloThreads = 192;
 // 12 warps: three per SM sub-partition, which caps registers at 168 per thread (as ten would)
 constexpr int kThreads = 384;
+// TMA epilogue: per epilogue warp, two residual boxes and one output box of 32 rows x 64
+// channels (f16, 128-byte swizzle: 4 KB each)
+constexpr int kEpiBox = 32 * 64 * 2;
+constexpr int kEpiWarpBytes = 3 * kEpiBox;
 
 struct ConvArgs {
   int b, len, cin, cout, k, dil, pad_left;
@@ -68,6 +72,7 @@ struct ConvArgs {
   const float* bias;
   int bias_v4;  // bias is 16-byte aligned: read 4 channels per load
   int snake_v4;  // alpha and 1/beta are 16-byte aligned: read 4 channels per load
+  int tma_epi;   // residual rows in and output rows out by TMA boxes (else per-thread rows)
   const float* alpha;
   const float* brecip;
   const __half* res;
@@ -97,7 +102,9 @@ __device__ __forceinline__ void snake8r(uint4& u, const float (&al)[8], const fl
 template <bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     conv_nlc_kernel(const __grid_constant__ CUtensorMap tmX,
-                    const __grid_constant__ CUtensorMap tmW, const ConvArgs a) {
+                    const __grid_constant__ CUtensorMap tmW,
+                    const __grid_constant__ CUtensorMap tmR,
+                    const __grid_constant__ CUtensorMap tmY, const ConvArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -124,7 +131,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t b_bytes = uint32_t(a.cout_cta / P) * kCB * 2;
   uint8_t* a_base = smem;
   uint8_t* b_base = smem + kAStages * a_bytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(b_base + kBStages * b_bytes);
+  // the TMA epilogue's boxes (4 warps), then the barriers
+  uint8_t* e_base = b_base + kBStages * b_bytes;
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(e_base + (a.tma_epi ? 4 * kEpiWarpBytes : 0));
   uint64_t* full_a = bars;
   uint64_t* ready_a = bars + kAStages;
   uint64_t* empty_a = bars + 2 * kAStages;
@@ -132,7 +142,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty_b = full_b + kBStages;
   uint64_t* tmem_full = empty_b + kBStages;  // [2] MMAs of a tile done (per accumulator set)
   uint64_t* tmem_empty = tmem_full + 2;      // [2] its accumulators read by the epilogue
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  uint64_t* res_bar = tmem_empty + 2;        // [4 warps][2] residual boxes landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // tracing build: each role's summed wait (or busy) times, recorded at the end
@@ -154,9 +165,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tmem_full[s], 1);
       mbar_init(&tmem_empty[s], 4 * P);
     }
+    for (int s = 0; s < 8; ++s) mbar_init(&res_bar[s], 1);
     fence_barrier_init();
     tma_prefetch_desc(&tmX);
     tma_prefetch_desc(&tmW);
+    if (a.tma_epi) {
+      tma_prefetch_desc(&tmR);
+      tma_prefetch_desc(&tmY);
+    }
   }
   if (warp == 1) {
     if constexpr (kPair) {
@@ -290,6 +306,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int kk = 0; kk < kCB / 16; ++kk)
                 mma(acc0, a_t + uint64_t(kk) * a_kk, b_0 + uint64_t(kk * 2), (i | kk) != 0);
+            } else if (a.ms == 1 && a.nh == 2) {
+              // two N = nper MMAs per 16 channels on the same halo rows
+              const uint64_t b_h = uint64_t(((a.nper / P) * 128) >> 4);
+#pragma unroll
+              for (int kk = 0; kk < kCB / 16; ++kk) {
+                const uint64_t ad = a_t + uint64_t(kk) * a_kk;
+                const uint32_t acc = (i | kk) != 0;
+                mma(acc0, ad, b_0 + uint64_t(kk * 2), acc);
+                mma(acc0 + a.nper, ad, b_0 + b_h + uint64_t(kk * 2), acc);
+              }
             } else {
 #pragma unroll
               for (int kk = 0; kk < kCB / 16; ++kk) {
@@ -452,6 +478,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       yp[1] = o[1];
     };
     const int c64 = a.cout_cta / 64 * 64;  // columns done 64 at a time
+    // TMA epilogue: this warp's boxes and residual barriers; rk counts its 64-column batches
+    // (batch k uses residual box k & 1, for the (k >> 1)-th time)
+    uint8_t* rbox = e_base + (warp - 2) * kEpiWarpBytes;
+    uint8_t* obox = rbox + 2 * kEpiBox;
+    uint64_t* rbar = res_bar + 2 * (warp - 2);
+    uint32_t rk = 0;
+    // byte offset of row r's 16-byte chunk q in a 128-byte-swizzled box
+    auto swz = [](int r, int q) { return r * 128 + ((q ^ (r & 7)) << 4); };
     for (int tl = 0; tl < my_tiles; ++tl) {
       const int buf = tl % a.nbuf;
       tl_t = TTS_TL_NOW();
@@ -464,6 +498,80 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < a.ms; ++j) {
         const int l = l0 + j * kRows + quad * 32 + lane;
         const bool live = l < a.len;
+        if (a.tma_epi) {
+          // the warp's 32 rows as boxes of 64 channels: residual in by TMA one batch ahead,
+          // the finished f16 rows out by TMA (rows past len are neither read nor written)
+          const int lw = l0 + j * kRows + quad * 32;
+          if (lw >= a.len) continue;  // no row of this warp exists (warp-uniform)
+          const uint32_t acc = tmem + (uint32_t(quad * 32) << 16) +
+                               uint32_t(buf * a.buf_stride + j * a.acc_stride);
+          const int nb = a.cout_cta / 64;
+          auto load_res = [&](int b, uint32_t k) {
+            if (lane == 0 && a.res) {
+              // the box's previous contents were read before the warp's last sync
+              fence_proxy_async();
+              mbar_arrive_expect_tx(&rbar[k & 1], kEpiBox);
+              tma_load_3d(rbox + (k & 1) * kEpiBox, &tmR, &rbar[k & 1], co0 + 64 * b, lw, bb);
+            }
+          };
+          load_res(0, rk);
+          for (int b = 0; b < nb; ++b, ++rk) {
+            if (b + 1 < nb) load_res(b + 1, rk + 1);
+            float v[4][16];
+            tmem_ld16x4(acc + 64 * b, acc + 64 * b + 16, acc + 64 * b + 32, acc + 64 * b + 48, v);
+            if (a.bias) {
+              // the same addresses across the warp: broadcasts
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int e = 0; e < 16; e += 4) {
+                  const float* bp = a.bias + co0 + 64 * b + 16 * i + e;
+                  const float4 b4 = a.bias_v4 ? __ldg(reinterpret_cast<const float4*>(bp))
+                                              : make_float4(__ldg(bp), __ldg(bp + 1),
+                                                            __ldg(bp + 2), __ldg(bp + 3));
+                  v[i][e] += b4.x;
+                  v[i][e + 1] += b4.y;
+                  v[i][e + 2] += b4.z;
+                  v[i][e + 3] += b4.w;
+                }
+            }
+            if (a.res) {
+              if (!mbar_wait(&rbar[rk & 1], (rk >> 1) & 1) && lane == 0) atomicOr(a.err, 16384);
+              const uint8_t* rb = rbox + (rk & 1) * kEpiBox;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const uint4 u = *reinterpret_cast<const uint4*>(rb + swz(lane, q));
+                const __half2* h2 = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = __half22float2(h2[e]);
+                  v[q >> 1][(q & 1) * 8 + 2 * e] += f.x;
+                  v[q >> 1][(q & 1) * 8 + 2 * e + 1] += f.y;
+                }
+              }
+            }
+            // the output box is free once the previous store has read it
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              uint4 o;
+              __half2* oh = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                oh[e] = __floats2half2_rn(v[q >> 1][(q & 1) * 8 + 2 * e],
+                                          v[q >> 1][(q & 1) * 8 + 2 * e + 1]);
+              *reinterpret_cast<uint4*>(obox + swz(lane, q)) = o;
+            }
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&tmY, obox, co0 + 64 * b, lw, bb);
+              bulk_commit_group();
+            }
+          }
+          continue;
+        }
         const size_t row = ((size_t)bb * a.len + (live ? l : 0)) * a.cout + co0;
         const uint32_t acc = tmem + (uint32_t(quad * 32) << 16) +
                              uint32_t(buf * a.buf_stride + j * a.acc_stride);
@@ -508,6 +616,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tl_w1 += TTS_TL_NOW() - tl_t;
     }
+    // every output box written before the CTA ends
+    if (lane == 0 && a.tma_epi) bulk_wait_all();
+    __syncwarp();
   }
 #ifdef TTS_TIMELINE
   if (lane == 0 && (warp <= 2 || warp == kHaloWarp0)) {
@@ -607,11 +718,14 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     const char* v = getenv("TTS_CONV_SUBTILES");
     if (v && *v == '1') a.ms = 1;
   }
-  // CTA pairs where a tile is 256 output channels (one N = 256 MMA per 16 input channels): the
-  // two CTAs of a cluster take 128 * ms positions each and half of every weight tile, and
-  // the even one issues M = 256 MMAs for both. TTS_CONV_PAIR=0 keeps one CTA per tile and
+  // CTA pairs: the two CTAs of a cluster take 128 * ms positions each and half of every weight
+  // tile, and the even one issues M = 256 MMAs for both. Where the output channels come in
+  // 512s a pair's tile is 128 positions per CTA x 512 channels (two N = 256 MMAs per 16 input
+  // channels on the same halo rows, so each input row is loaded and activated once per 512
+  // output channels); where a tile is 256 channels, 2 x 128 positions per CTA x 256 channels.
+  // TTS_CONV_WIDE=0 turns the 512-channel tile off, TTS_CONV_PAIR=0 keeps one CTA per tile,
   // TTS_CONV_ACC_SETS=2 double-buffers the accumulators with one sub-tile per CTA (A/B
-  // measurement; both measured slower on the codec's block).
+  // measurement; each measured slower on the codec's block).
   a.nbuf = 1;
   bool pair = false;
   {
@@ -620,6 +734,14 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     const bool pair_on = !(vp && *vp == '0');
     const bool two_sets = vs && *vs == '2';
     if (pair_on && a.cout_cta == 256 && a.nh == 1) pair = true;
+    const char* vw = getenv("TTS_CONV_WIDE");
+    if (pair_on && !(vw && *vw == '0') && r.cout % 512 == 0 && !two_sets) {
+      pair = true;
+      a.cout_cta = 512;
+      a.nh = 2;
+      a.nper = 256;
+      a.ms = 1;
+    }
     // a pair's tile spans 2 * 128 * ms positions: one sub-tile each for short inputs
     if (pair && a.ms == 2 && r.len <= 2 * kRows) a.ms = 1;
     if (two_sets && a.cout_cta <= 256) {
@@ -640,16 +762,32 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     a.H = ((need + a.nrb - 1) / a.nrb + 7) / 8 * 8;
     a.R = a.H * a.nrb;
   }
+  // TMA epilogue where the tile's channels come in 64-channel boxes and the output and residual
+  // rows are 16-byte aligned (TTS_CONV_TMA_EPI=0: per-thread rows, A/B measurement)
+  {
+    const char* v = getenv("TTS_CONV_TMA_EPI");
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    a.tma_epi = !(v && *v == '0') && a.cout_cta % 64 == 0 && r.cout % 8 == 0 && al16(r.y) &&
+                        (!r.res || al16(r.res))
+                    ? 1
+                    : 0;
+  }
   // ring depths: the weight tiles are the steady stream (one per tap), halos one per 64 input
-  // channels; fill what fits in 224 KB, at least two of each
+  // channels; fill what fits in 224 KB beside the epilogue's boxes: three halos where four or
+  // more weight stages still fit, else two; at least two of each
   {
     const size_t halo = size_t(a.R) * kCB * 2, wt = size_t(a.cout_cta / P) * kCB * 2;
-    const size_t budget = 224 * 1024;
+    const size_t budget = 224 * 1024 - (a.tma_epi ? 4 * kEpiWarpBytes : 0);
     const size_t bs_max = wt <= 16384 ? 6 : 4;
-    a.as = 2;
-    a.bs = int(std::min<size_t>(bs_max, (budget - 2 * halo) / wt));
-    if (a.bs < 2) a.bs = 2;
-    if (a.bs >= 4 && 3 * halo + size_t(a.bs) * wt <= budget) a.as = 3;
+    const size_t bs_min3 = wt <= 16384 ? 4 : 3;  // weight stages that justify a third halo
+    if (budget > 3 * halo && (budget - 3 * halo) / wt >= bs_min3) {
+      a.as = 3;
+      a.bs = int(std::min<size_t>(bs_max, (budget - 3 * halo) / wt));
+    } else {
+      a.as = 2;
+      a.bs = budget > 2 * halo ? int(std::min<size_t>(bs_max, (budget - 2 * halo) / wt)) : 2;
+      if (a.bs < 2) a.bs = 2;
+    }
     // TTS_CONV_AS / TTS_CONV_BS override the ring depths (A/B measurement)
     const char* va = getenv("TTS_CONV_AS");
     const char* vb = getenv("TTS_CONV_BS");
@@ -689,8 +827,28 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     set_error("conv1d: weight tensor map rejected");
     return cudaErrorInvalidValue;
   }
+  // The epilogue's residual and output maps over [b][len][cout] f16: a box is 64 channels x 32
+  // rows of one batch entry (rows past len are zero-filled on load and not written on store).
+  CUtensorMap tmR{}, tmY{};
+  if (a.tma_epi) {
+    auto rows_map = [&](CUtensorMap* m, const void* ptr) {
+      cuuint64_t dims[3] = {cuuint64_t(r.cout), cuuint64_t(r.len), cuuint64_t(r.b)};
+      cuuint64_t strides[2] = {cuuint64_t(r.cout) * 2, cuuint64_t(r.len) * r.cout * 2};
+      cuuint32_t box[3] = {64, 32, 1};
+      cuuint32_t estr[3] = {1, 1, 1};
+      return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    if (!rows_map(&tmY, r.y) || (r.res && !rows_map(&tmR, r.res))) {
+      set_error("conv1d: epilogue tensor map rejected");
+      return cudaErrorInvalidValue;
+    }
+  }
   const size_t smem = size_t(a.as) * a.R * kCB * 2 +
-                      size_t(a.bs) * (a.cout_cta / P) * kCB * 2 + 1024 + 256;
+                      size_t(a.bs) * (a.cout_cta / P) * kCB * 2 +
+                      (a.tma_epi ? 4 * kEpiWarpBytes : 0) + 1024 + 512;
   {
     // The opt-in shared-memory limit is a per-device function attribute.
     static std::mutex mu;
@@ -733,7 +891,7 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
   cfg.numAttrs = 1;
   if (!pair) {
     cfg.gridDim = dim3(unsigned(std::min<long long>(ntiles, std::max(1, sms))), 1, 1);
-    return cudaLaunchKernelEx(&cfg, conv_nlc_kernel<false>, tmX, tmW, a);
+    return cudaLaunchKernelEx(&cfg, conv_nlc_kernel<false>, tmX, tmW, tmR, tmY, a);
   }
   // as many pairs as can be resident at once (a pair's SMs share a GPC)
   cfg.numAttrs = 2;
@@ -745,7 +903,7 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     clusters = std::max(1, sms / 2);
   }
   cfg.gridDim = dim3(2 * unsigned(std::min<long long>(ntiles, clusters)), 1, 1);
-  return cudaLaunchKernelEx(&cfg, conv_nlc_kernel<true>, tmX, tmW, a);
+  return cudaLaunchKernelEx(&cfg, conv_nlc_kernel<true>, tmX, tmW, tmR, tmY, a);
 }
 
 }  // namespace tts

@@ -166,6 +166,27 @@ TTS_DEV void tma_load_4d(void* smem_dst, const void* desc, uint64_t* bar, int c0
       "r"(c3)
       : "memory");
 }
+TTS_DEV void tma_load_3d(void* smem_dst, const void* desc, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+// Shared -> global tile store (elements outside the tensor map's extents are not written);
+// tracked by the issuing thread's bulk async-groups.
+TTS_DEV void tma_store_3d(const void* desc, const void* smem_src, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(desc)),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+TTS_DEV void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// This thread's committed bulk stores have finished reading their shared-memory sources.
+TTS_DEV void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// This thread's committed bulk stores are complete (written to global memory).
+TTS_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Prefetch `bytes` (a multiple of 16, from a 16-byte aligned address) into L2; no completion
 // to wait for.
 // One contiguous global -> shared copy by the bulk-copy engine (no multicast): both addresses
