@@ -1348,6 +1348,9 @@ def run_timeline(args):
                                       for k, o in (("released", 1), ("first_s", 4),
                                                    ("first_p", 5), ("last_p", 6))}
                     row["per_cta"]["end"] = [f(v) for v in end[order]]
+                    if len(a) > int(idx.max()) + 8 and ((a[idx + 7, 0] & 0xf) == 9).all():
+                        row["q_wait"] = f(np.median(a[idx + 7, 1]))
+                        row["q_ready"] = f(np.median(a[idx + 8, 1]))
                 by_cta = np.zeros(len(idx))
                 by_cta[a[idx + 2, 1]] = (end - a[idx + 1, 1].min()) / 1e3
                 row["cta_work_us"] = [round(float(x), 2) for x in by_cta]

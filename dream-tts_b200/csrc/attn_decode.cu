@@ -98,6 +98,7 @@ struct AttnSmem {
   int last;
   int merge_here;  // the CTA's last segment is merged by the softmax warps
   unsigned long long tl_p0, tl_plast;  // tracing build: first and last P handed to the O MMA
+  unsigned long long tl_q0, tl_q1;     // tracing build: softmax warps past the wait, q staged
   int span[kMaxLanes];
   int cnt[kMaxLanes];         // chunk-list items of each lane (chunks x n_kv)
   int prefix[kMaxLanes + 1];  // chunk-list offset of each lane
@@ -468,11 +469,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // the score warp releases TMEM after every chunk's softmax and output MMA: compute ends
     if (lane == 0) {
       const uint64_t t_end = TTS_TL_NOW();
-      timeline_recs<7>({kTlAttn | kTlEntry, kTlAttn | kTlReleased, kTlAttn | kTlCta,
+      timeline_recs<9>({kTlAttn | kTlEntry, kTlAttn | kTlReleased, kTlAttn | kTlCta,
                         kTlAttn | kTlEnd, kTlAttn | kTlAttnFirstS, kTlAttn | kTlAttnFirstP,
-                        kTlAttn | kTlAttnLastP},
+                        kTlAttn | kTlAttnLastP, kTlAttn | kTlAttnQWait, kTlAttn | kTlAttnQReady},
                        {tl_entry, tl_rel, uint64_t(blockIdx.x), t_end, tl_s0, S.tl_p0,
-                        S.tl_plast});
+                        S.tl_plast, S.tl_q0, S.tl_q1});
     }
 #endif
     return;
@@ -571,6 +572,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ================= softmax warps 0-3 (thread t: TMEM lane t = chunk row t = output dim t)
   if (a.early_meta) pdl_wait();  // q is the previous kernel's output
+#ifdef TTS_TIMELINE
+  if (t == 0) S.tl_q0 = TTS_TL_NOW();
+#endif
   const int heads = a.n_kv * GQA;
   const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
   bool ok = true;
@@ -610,6 +614,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (n > 0) {
     load_q(cur);
     store_q(0);
+#ifdef TTS_TIMELINE
+    if (t == 0) S.tl_q1 = TTS_TL_NOW();
+#endif
     seg1 = next_segment(cur, pos1);
     if (pos1 < n) {
       load_q(seg1);

@@ -78,6 +78,8 @@ constexpr int kTlEntry = 0, kTlReleased = 1, kTlMainDone = 2, kTlReduced = 3, kT
 constexpr int kTlEpiFirst = 6, kTlEpiLoop = 7;
 // attention: first score MMAs issued, first and last P handed to the output MMA
 constexpr int kTlAttnFirstS = 6, kTlAttnFirstP = 7, kTlAttnLastP = 8;
+// attention: the softmax warps past the dependency wait, and q staged for the first scores
+constexpr int kTlAttnQWait = 9, kTlAttnQReady = 10;
 #ifdef TTS_TIMELINE
 constexpr unsigned kTimelineCap = 1u << 21;  // 64 MB of records (tracing build only)
 extern __device__ unsigned long long g_timeline[kTimelineCap * 4];
