@@ -390,11 +390,13 @@ def time_codec_block(device, reps=5):
 def run_sweep(args):
     """Benchmark config[3]: a document of segments with target lengths log-uniform in [40, 1200]
     frames, grouped longest-first into runs of `--lanes` lanes, groups split over the ranks by
-    LPT (no collective on the data path), each rank decoding its shard with tail shedding
-    (`--refill` reuses finished lanes). frames/s = all frames / max over ranks of device time."""
+    LPT (no collective on the data path), each rank decoding its shard with tail shedding;
+    with `--refill` (finished lanes reused) single segments are split by LPT on their frames and
+    each rank groups its own. frames/s = all frames / max over ranks of device time."""
     import torch
     import torch.distributed as dist
-    from qwen3tts.talker import Talker, plan_groups, shard_groups, synthetic_segments
+    from qwen3tts.talker import (Talker, plan_groups, shard_groups, shard_segments,
+                                 synthetic_segments)
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
@@ -402,8 +404,10 @@ def run_sweep(args):
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
     n_segments = args.segments * world
     segs = synthetic_segments(n_segments, seed=0)
-    groups = plan_groups(segs, args.lanes)
-    mine = shard_groups(groups, world)[rank]
+    if args.refill:
+        mine = plan_groups(shard_segments(segs, world)[rank], args.lanes)
+    else:
+        mine = shard_groups(plan_groups(segs, args.lanes), world)[rank]
     queue = [s for g in mine for s in g]
     stack, _, _, _ = build_device_talker(device, seed=0, extra_positions=0, lanes_override=0)
     cap = 157 + 1200 + 2
@@ -448,20 +452,19 @@ def document_sample(args, rank, world, device):
     blocks), all windows of a rank decoded in batches, and the rank's audio copied into pinned
     host memory (the host gather). The codec's RVQ dequantiser and pre-transformer are not on
     this path: seeded random latents stand in for its input. Segments are split over the ranks
-    by LPT (longest processing time first), no collective on the data path. Returns the
+    one by one by LPT on their frames (shard_segments: a refilling talker's time follows its
+    frames), each rank grouping its own longest-first; no collective on the data path. Returns the
     rank-0 summary (None on other ranks): frames/s = all frames / max over ranks of (talker +
     codec + host copy device time); rtf = that time / audio seconds (12.5 frames per second)."""
     import torch
     import torch.distributed as dist
     from qwen3tts.codec import WaveStack, chunk_plan
-    from qwen3tts.talker import (Talker, group_cost, plan_groups, shard_groups,
-                                 synthetic_segments)
+    from qwen3tts.talker import Talker, plan_groups, shard_segments, synthetic_segments
     n_segments = args.segments * world
     segs = synthetic_segments(n_segments, seed=0)
-    groups = plan_groups(segs, args.lanes)
-    shards = shard_groups(groups, world)
-    mine = shards[rank]
-    loads = [sum(group_cost(g) * len(g) for g in sh) for sh in shards]
+    shards = shard_segments(segs, world)
+    mine = plan_groups(shards[rank], args.lanes)
+    loads = [sum(s.frames for s in sh) for sh in shards]
     queue = [s for g in mine for s in g]
     stack, _, _, _ = build_device_talker(device, seed=0, extra_positions=0, lanes_override=0)
     talker = Talker(stack, max_lanes=args.lanes, capacity=157 + 1200 + 2)

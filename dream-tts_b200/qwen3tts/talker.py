@@ -77,6 +77,22 @@ def shard_groups(groups: list[list[Segment]], world: int) -> list[list[list[Segm
     return shards
 
 
+def shard_segments(segments: list[Segment], world: int) -> list[list[Segment]]:
+    """Longest-processing-time-first assignment of single segments to `world` GPUs by frame
+    count (each segment, longest first, to the least-loaded GPU, ties to the lowest rank), for
+    ranks that decode with interior refill: a refilling talker's time follows its frames, not
+    its groups, and whole groups are too coarse a unit when a rank holds only a few of them.
+    Deterministic, so every rank computes the same split without talking to the others. Each
+    rank then plans its own groups (plan_groups) over its segments."""
+    shards: list[list[Segment]] = [[] for _ in range(world)]
+    load = [0] * world
+    for s in sorted(segments, key=lambda s: (-s.frames, s.index)):
+        r = min(range(world), key=lambda i: (load[i], i))
+        shards[r].append(s)
+        load[r] += s.frames
+    return shards
+
+
 def shed_widths(frames: list[int], quantum: int = SHED_QUANTUM) -> list[int]:
     """Live width at each step of a group whose lanes run `frames[i]` steps, with the finished
     tail shed (crates/qwen3tts/src/talker.rs:1002-1017). Lanes arrive longest-first, so the
