@@ -36,7 +36,9 @@
 // a tile's loads and snake overlap the previous tile's epilogue. Every wait is bounded; a wait
 // that gives up sets an error flag the host reads.
 #include <algorithm>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "tts_common.cuh"
 #include "tts_internal.h"
@@ -893,14 +895,27 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     cfg.gridDim = dim3(unsigned(std::min<long long>(ntiles, std::max(1, sms))), 1, 1);
     return cudaLaunchKernelEx(&cfg, conv_nlc_kernel<false>, tmX, tmW, tmR, tmY, a);
   }
-  // as many pairs as can be resident at once (a pair's SMs share a GPC)
+  // as many pairs as can be resident at once (a pair's SMs share a GPC); the occupancy query
+  // depends only on the device and the shared memory, so it runs once per pair of them
   cfg.numAttrs = 2;
   int clusters = 0;
-  cfg.gridDim = dim3(2 * unsigned(std::max(1, sms / 2)), 1, 1);
-  if (cudaOccupancyMaxActiveClusters(&clusters, conv_nlc_kernel<true>, &cfg) != cudaSuccess ||
-      clusters < 1) {
-    cudaGetLastError();
-    clusters = std::max(1, sms / 2);
+  {
+    static std::mutex mu;
+    static std::map<std::pair<int, size_t>, int> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_pair(device, smem);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      clusters = it->second;
+    } else {
+      cfg.gridDim = dim3(2 * unsigned(std::max(1, sms / 2)), 1, 1);
+      if (cudaOccupancyMaxActiveClusters(&clusters, conv_nlc_kernel<true>, &cfg) != cudaSuccess ||
+          clusters < 1) {
+        cudaGetLastError();
+        clusters = std::max(1, sms / 2);
+      }
+      cache.emplace(key, clusters);
+    }
   }
   cfg.gridDim = dim3(2 * unsigned(std::min<long long>(ntiles, clusters)), 1, 1);
   return cudaLaunchKernelEx(&cfg, conv_nlc_kernel<true>, tmX, tmW, tmR, tmY, a);
