@@ -31,11 +31,15 @@ def case(rng, orc, b, length, cin, cout, k):
 
 
 # (b, len, cin, cout, k, dil, pad) — crates/tts-nn/src/nlc.rs:367-372 shapes where the kernel's
-# channel rules allow (cin % 64), lengths not a multiple of the 128-row tile, "same" and causal
+# channel rules allow (cin % 64), lengths not a multiple of the 128-row tile, "same" and causal;
+# 256- and 512-channel outputs run on CTA pairs, 64-channel multiples on the TMA epilogue
 @pytest.mark.parametrize("b,length,cin,cout,k,dil,pad", [
     (1, 300, 64, 64, 7, 1, 6), (1, 4200, 128, 96, 7, 9, 54), (1, 4096, 64, 96, 7, 1, 6),
     (1, 5000, 128, 192, 7, 3, 18), (1, 4097, 64, 96, 1, 1, 0), (2, 1000, 256, 256, 7, 3, 9),
-    (3, 777, 512, 512, 7, 9, 27), (1, 130, 64, 1024, 3, 1, 2)])
+    (3, 777, 512, 512, 7, 9, 27), (1, 130, 64, 1024, 3, 1, 2),
+    # CTA pairs with few rows: 512 channels shorter than one CTA's 128 positions (the odd CTA
+    # has no live row), and 256-channel tiles short enough for one sub-tile per CTA
+    (1, 50, 64, 512, 3, 1, 2), (2, 200, 128, 256, 7, 1, 6)])
 def test_conv_plain(tt, orc, b, length, cin, cout, k, dil, pad):
     rng = np.random.default_rng(length + cin)
     x, w, bias = case(rng, orc, b, length, cin, cout, k)
