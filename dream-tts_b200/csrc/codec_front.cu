@@ -2,6 +2,9 @@
 // small row-wise kernels its RVQ dequantiser, pre-transformer and ConvNeXt upsamplers need
 // besides the projections and convolutions (gemm_decode.cu, conv_nlc.cu). Each is one coalesced
 // pass (or one warp per row) over activations that stay in HBM/L2 between launches.
+#include <cstdlib>
+#include <mutex>
+
 #include "tts_common.cuh"
 #include "tts_internal.h"
 
@@ -103,6 +106,86 @@ __global__ void window_attn_kernel(const float* qkv, int T, int ld, int heads, i
       static_cast<__half*>(out)[oi] = __float2half_rn(r);
     else
       static_cast<float*>(out)[oi] = r;
+  }
+}
+
+// The same attention for a window > 0, by tiles: one CTA per (block of 32 query rows, head)
+// stages the block's q rows and the K and V rows its windows reach ([t0 + 1 - window, t0 + 31])
+// in shared memory (K and V rows padded to hd + 1 floats, so the lanes of a warp, one key each,
+// read different banks), then a warp per query row runs window_attn_kernel's arithmetic in
+// its order (each score a sequential dot product, the softmax online per pass of 32 keys, the
+// values summed key by key): the same results, from shared memory instead of every lane
+// reading its own key row from global memory.
+constexpr int kWinRows = 32;  // query rows per CTA
+__global__ void __launch_bounds__(256) window_attn_tiled_kernel(const float* qkv, int T, int ld,
+                                                                int heads, int hd, int window,
+                                                                float scale, void* out,
+                                                                int out_f16) {
+  extern __shared__ float wsm[];
+  const int h = blockIdx.y;
+  const int t0 = blockIdx.x * kWinRows;
+  const int t1 = min(T, t0 + kWinRows);  // query rows [t0, t1)
+  const int k0 = max(0, t0 + 1 - window);  // key rows [k0, t1)
+  const int nk_rows = t1 - k0;
+  const int pitch = hd + 1;
+  float* qs = wsm;                          // [kWinRows][hd]
+  float* ks = qs + kWinRows * hd;           // [nk_rows][pitch]
+  float* vs = ks + (kWinRows + window - 1) * pitch;
+  const int kcol = heads * hd + h * hd, vcol = 2 * heads * hd + h * hd;
+  for (int i = threadIdx.x; i < (t1 - t0) * hd; i += blockDim.x) {
+    const int r = i / hd, d = i % hd;
+    qs[r * hd + d] = qkv[(size_t)(t0 + r) * ld + (size_t)h * hd + d];
+  }
+  for (int i = threadIdx.x; i < nk_rows * hd; i += blockDim.x) {
+    const int r = i / hd, d = i % hd;
+    const float* row = qkv + (size_t)(k0 + r) * ld;
+    ks[r * pitch + d] = row[kcol + d];
+    vs[r * pitch + d] = row[vcol + d];
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = t0 + warp; t < t1; t += blockDim.x >> 5) {
+    const int lo = max(0, t + 1 - window);
+    const float* q = qs + (t - t0) * hd;
+    float m = -INFINITY, l = 0.f;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j0 = lo; j0 <= t; j0 += 32) {
+      const int j = j0 + lane;
+      float s = -INFINITY;
+      if (j <= t) {
+        const float* kr = ks + (j - k0) * pitch;
+        float acc = 0.f;
+        for (int d = 0; d < hd; ++d) acc += q[d] * kr[d];
+        s = acc * scale;
+      }
+      const float pm = warp_max(s);
+      const float mn = fmaxf(m, pm);
+      const float corr = m == -INFINITY ? 0.f : expf(m - mn);
+      const float p = j <= t ? expf(s - mn) : 0.f;
+      l = l * corr + warp_sum(p);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) o[u] *= corr;
+      const int nk = min(32, t + 1 - j0);
+      for (int i = 0; i < nk; ++i) {
+        const float pi = __shfl_sync(0xffffffffu, p, i);
+        const float* vr = vs + (j0 + i - k0) * pitch;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (lane + 32 * u < hd) o[u] += pi * vr[lane + 32 * u];
+      }
+      m = mn;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int d = lane + 32 * u;
+      if (d >= hd) break;
+      const float r = o[u] / l;
+      const size_t oi = (size_t)t * heads * hd + (size_t)h * hd + d;
+      if (out_f16)
+        static_cast<__half*>(out)[oi] = __float2half_rn(r);
+      else
+        static_cast<float*>(out)[oi] = r;
+    }
   }
 }
 
@@ -210,6 +293,29 @@ cudaError_t launch_window_attn(const float* qkv, int T, int ld, int heads, int h
   if (hd > 128 || hd < 1) {
     set_error("window_attention: head_dim must be in 1..128");
     return cudaErrorInvalidValue;
+  }
+  // the tiled form where the window's rows fit in shared memory (TTS_WINDOW_TILED=0: the
+  // per-row form, A/B measurement)
+  const char* tv = getenv("TTS_WINDOW_TILED");
+  const size_t smem = (size_t(kWinRows) * hd + size_t(2) * (kWinRows + window - 1) * (hd + 1)) *
+                      sizeof(float);
+  if (!(tv && *tv == '0') && window > 0 && smem <= 200 * 1024) {
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      if (dev >= 0 && dev < 64 && !done[dev]) {
+        cudaFuncSetAttribute(window_attn_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024);
+        done[dev] = true;
+      }
+    }
+    const dim3 grid((T + kWinRows - 1) / kWinRows, heads);
+    window_attn_tiled_kernel<<<grid, 256, smem, st>>>(qkv, T, ld, heads, hd, window, scale, out,
+                                                      out_f16 ? 1 : 0);
+    return cudaGetLastError();
   }
   const long warps = (long)T * heads;
   window_attn_kernel<<<int((warps + 7) / 8), 256, 0, st>>>(qkv, T, ld, heads, hd, window, scale,
