@@ -5,9 +5,10 @@ projections), the causal pre-conv, the 8-layer pre-transformer (dim 512, 16 head
 upsampling stages (causal transposed conv + ConvNeXt: depthwise k7, LayerNorm, 4x MLP with
 GELU, gamma, residual), giving the [T * 4, 1024] latent the waveform stack takes.
 
-Projections run on the decode GEMM (f16 weights, f32 accumulate; rows in chunks of 448), the
-convolutions on the conv kernel, and the row ops (lookups, RoPE, windowed attention, LayerNorm,
-depthwise conv, bias/GELU/scale/residual epilogues) on the kernels of csrc/codec_front.cu.
+Projections run on the prefill-shaped GEMM for many rows, else the decode GEMM (f16 weights,
+f32 accumulate; rows in chunks of 448), the convolutions on the conv kernel, and the row ops
+(lookups, RoPE, windowed attention, LayerNorm, depthwise conv, bias/GELU/scale/residual
+epilogues) on the kernels of csrc/codec_front.cu.
 """
 from __future__ import annotations
 
@@ -22,11 +23,18 @@ from ttsnn._ctx import ctx_of, ptr, stream
 from .codec import Conv, TransConv
 
 MAX_ROWS = 448  # rows per projection call (the decode GEMM's limit)
+# Above this many rows a projection runs on the prefill-shaped GEMM (tokens as the MMA's M, all
+# rows in one launch) where its shape allows; below it the decode GEMM streams the weights.
+ROWS_GEMM_MIN = 129
 
 
 def proj_rows(p: ttsnn.Proj, x: torch.Tensor, epilogue: int = L.EPI_F32) -> torch.Tensor:
-    """A projection over any number of rows, in chunks the GEMM takes."""
+    """A projection over any number of rows: one prefill-shaped GEMM for many rows (packed
+    weight, n a multiple of 256, f32 or SwiGLU output), else the decode GEMM in chunks it takes."""
     rows = x.shape[0]
+    if (rows >= ROWS_GEMM_MIN and p.packed and p.n % 256 == 0
+            and epilogue in (L.EPI_F32, L.EPI_SWIGLU_F16)):
+        return p.forward_rows(x, epilogue)
     outs = [p.forward(x[r:r + MAX_ROWS], epilogue) for r in range(0, rows, MAX_ROWS)]
     return outs[0] if len(outs) == 1 else torch.cat(outs)
 
