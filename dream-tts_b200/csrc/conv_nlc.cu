@@ -755,6 +755,13 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
   a.acc_stride = 32;
   while (a.acc_stride < a.cout_cta) a.acc_stride *= 2;
   a.buf_stride = a.acc_stride * a.ms;
+  // a second accumulator set wherever two fit in TMEM's 512 columns (tiles of <= 128 output
+  // channels): the next tile's MMAs then run while this tile's epilogue drains the other set
+  // (TTS_CONV_ACC_SETS=1 keeps one, A/B measurement)
+  {
+    const char* vs = getenv("TTS_CONV_ACC_SETS");
+    if (a.nbuf == 1 && 2 * a.buf_stride <= 512 && !(vs && *vs == '1')) a.nbuf = 2;
+  }
   a.tmem_cols = a.buf_stride * a.nbuf;
   // one halo for all sub-tiles: ms * 128 + (k-1)*dil rows, loaded as nrb boxes of H rows
   // (a box is at most 256 rows; H a multiple of 8 keeps every box 128-byte aligned)
