@@ -735,7 +735,11 @@ cudaError_t launch_conv(const ConvRequest& r, cudaStream_t st, int device, int* 
     const char* vs = getenv("TTS_CONV_ACC_SETS");
     const bool pair_on = !(vp && *vp == '0');
     const bool two_sets = vs && *vs == '2';
+    // pairs for 256-channel tiles and for tiles of two MMAs per 16 input channels (e.g. 384
+    // channels as two N = 192 MMAs: 0.1348 -> 0.1224 ms at 4 x 10000 positions); single-MMA
+    // tiles below 256 channels stay on one CTA (128 channels: 0.230 vs 0.237 ms in pairs)
     if (pair_on && a.cout_cta == 256 && a.nh == 1) pair = true;
+    if (pair_on && a.nh == 2 && a.nper % 32 == 0) pair = true;
     const char* vw = getenv("TTS_CONV_WIDE");
     if (pair_on && !(vw && *vw == '0') && r.cout % 512 == 0 && !two_sets) {
       pair = true;
