@@ -149,10 +149,14 @@ TTS_DEV void chunk_rows(const Cursor& x, int& vlo, int& vhi) {
   vhi = min(x.lr.span - p0, kChunk);
 }
 
-// Which CTA of `grid` owns item x of a list of `total` split as [total*i/grid, total*(i+1)/grid).
-TTS_DEV int owner_of(long long x, long long total, int grid) {
-  return int(((x + 1) * grid + total - 1) / total) - 1;
+// Which CTA of `grid` owns item x of a list of `total` split as [total*i/grid, total*(i+1)/grid),
+// and where CTA i's range starts. 32-bit arithmetic (the host keeps total x grid below 2^31): a
+// 64-bit division is a long software sequence, and the split pairs' merges run these on the
+// attention's critical path.
+TTS_DEV int owner_of(unsigned x, unsigned total, unsigned grid) {
+  return int(((x + 1u) * grid + total - 1u) / total) - 1;
 }
+TTS_DEV unsigned range_lo(unsigned i, unsigned total, unsigned grid) { return total * i / grid; }
 
 // Zeroes rows of a K or V tile: rows outside [vlo, vhi), and rows of boxes flagged in `inv`
 // (pages outside the pool). Thread `tid` of a group of `n` takes every n-th 16-byte piece.
@@ -260,8 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
 
   const long long total = S.prefix[a.lanes];
-  const long long lo = total * blockIdx.x / gridDim.x;
-  const long long hi = total * (blockIdx.x + 1) / gridDim.x;
+  const long long lo = range_lo(blockIdx.x, unsigned(total), gridDim.x);
+  const long long hi = range_lo(blockIdx.x + 1, unsigned(total), gridDim.x);
   const long long n = hi - lo;  // items of this CTA
   const uint32_t tmem = S.tmem;
 
@@ -522,10 +526,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int u = 0; u < 4; ++u) oo[g][u] = 0.f;
       }
-      for (int cc = 0; cc < nch; ++cc) {
-        const bool st = cc == 0 || owner_of(base + cc, total, gridDim.x) !=
-                                       owner_of(base + cc - 1, total, gridDim.x);
-        if (!st) continue;
+      // the pair's parts in chunk order: chunk 0 and each later CTA's range start in the pair
+      const unsigned tot = unsigned(total), gr = gridDim.x;
+      const int o0 = owner_of(unsigned(base), tot, gr);
+      const int o1 = owner_of(unsigned(base + nch - 1), tot, gr);
+      int last_cc = -1;
+      for (int ci = o0; ci <= o1; ++ci) {
+        const int cc = ci == o0 ? 0 : int(range_lo(unsigned(ci), tot, gr) - unsigned(base));
+        if (cc <= last_cc) continue;  // CTAs with empty ranges share a start
+        last_cc = cc;
 #pragma unroll
         for (int g = 0; g < GQA; ++g) {
           const float* pp = a.part + ((pbase + cc) * GQA + g) * 130;
@@ -733,10 +742,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       ll[g] = 0.f;
       oo[g] = 0.f;
     }
-    for (int cc = 0; cc < prev.nch; ++cc) {
-      const bool st = cc == 0 || owner_of(base + cc, total, gridDim.x) !=
-                                     owner_of(base + cc - 1, total, gridDim.x);
-      if (!st) continue;
+    // the pair's parts in chunk order: chunk 0 and each later CTA's range start in the pair
+    const unsigned tot = unsigned(total), gr = gridDim.x;
+    const int o0 = owner_of(unsigned(base), tot, gr);
+    const int o1 = owner_of(unsigned(base + prev.nch - 1), tot, gr);
+    int last_cc = -1;
+    for (int ci = o0; ci <= o1; ++ci) {
+      const int cc = ci == o0 ? 0 : int(range_lo(unsigned(ci), tot, gr) - unsigned(base));
+      if (cc <= last_cc) continue;  // CTAs with empty ranges share a start
+      last_cc = cc;
 #pragma unroll
       for (int g = 0; g < GQA; ++g) {
         float cm, cl, ov;
@@ -991,6 +1005,10 @@ cudaError_t launch_attn(const AttnRequest& r, const AttnWorkspace& w, cudaStream
   }
   const long long items = (long long)r.lanes * r.n_kv * chunks;
   const int grid = int(std::min<long long>(num_sms(dev), items));
+  if ((items + 1) * grid >= (1ll << 31)) {  // the work split's 32-bit arithmetic
+    set_error("decode_attention: lanes x kv heads x chunks too large for one call");
+    return cudaErrorInvalidValue;
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
