@@ -279,9 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     first.b = n > 0 ? l : 0;
     first.lr = lane_range(S.span[first.b], a.window);
-    const long long rel = n > 0 ? lo - S.prefix[first.b] : 0;
-    first.h = int(rel / first.lr.nch);
-    first.c = int(rel % first.lr.nch);
+    const int rel = n > 0 ? int(lo - S.prefix[first.b]) : 0;  // 32-bit: a lane's items
+    first.h = rel / first.lr.nch;
+    first.c = rel % first.lr.nch;
     first.seg = 0;
   }
 
