@@ -592,6 +592,27 @@ int max_active_clusters(int device, int splits, size_t smem) {
   return n;
 }
 
+// CTAs of the plain decode GEMM that fit on one SM with `smem` bytes of shared memory (its
+// registers decide as much as its shared memory), cached per (device, smem).
+int ctas_per_sm(int device, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::pair<int, size_t>, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_pair(device, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaFuncSetAttribute(gemm_decode_kernel<false, -1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       227 * 1024);
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemm_decode_kernel<false, -1>, kThreads,
+                                                    smem) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[key] = n;
+  return n;
+}
+
 // Tile plan for y[m, n] = x[m, k] W[n, k]^T. The grid is one wave: every CTA (and every
 // cluster of split-K CTAs) resident at once, so no tile waits for a second wave.
 // TTS_GEMM_STAGES / TTS_GEMM_SPLITS override the choice for A/B measurement.
@@ -612,10 +633,12 @@ Plan plan_gemm(int m, int k, int n, int device, int force_splits) {
   const int stage = kWBytes + cols * 128;
   const int tiles = n / kTileM;
   const int sms = num_sms(device);
-  // Many tiles (the heads): two CTAs per SM, one stage per pipeline. Otherwise one CTA per SM
-  // with as many stages as 216 KB of rings hold (two per pipeline at decode sizes; three of
-  // 72 KB for 448 rows, whose single pipeline otherwise waits on each stage's load).
-  const bool two = tiles > sms;
+  // Many tiles (the heads): two CTAs per SM with one stage per pipeline, where two fit (at
+  // decode sizes the kernel's registers allow one CTA per SM: then the tiles run in waves of
+  // one CTA per SM, each with deeper rings). Otherwise one CTA per SM with as many stages as
+  // 216 KB of rings hold (two per pipeline at decode sizes; three of 72 KB for 448 rows, whose
+  // single pipeline otherwise waits on each stage's load).
+  const bool two = tiles > sms && ctas_per_sm(device, size_t(100 + 2) * 1024) >= 2;
   const int budget = two ? 100 * 1024 : 216 * 1024;
   p.stages = std::max(1, std::min(4, budget / (stage * p.pipes)));
   p.stages = std::max(1, std::min(8, env_int("TTS_GEMM_STAGES", p.stages)));
