@@ -200,10 +200,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- weight tiles: global step g = (tile, cb, tap)
     const int total = my_tiles * steps;
+    // the ring slot and phase of step g, and its (tile, cb, tap), kept as running counters (a
+    // division by a run-time divisor is a long instruction sequence)
+    int s = 0, tile_i = 0, cb = 0, t = 0;
+    uint32_t ph = 0;
     for (int g = 0; g < total; ++g) {
-      const int s = g % kBStages;
       tl_t = TTS_TL_NOW();
-      const bool ok_e = g < kBStages || mbar_wait_warp(&empty_b[s], ((g / kBStages) + 1) & 1);
+      const bool ok_e = g < kBStages || mbar_wait_warp(&empty_b[s], ph ^ 1u);
       tl_w0 += TTS_TL_NOW() - tl_t;
       if (!ok_e) {
         if (lane == 0) atomicOr(a.err, 16);
@@ -211,8 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (elect_one()) {
         int l0, bb, co0;
-        tile_of(g / steps, l0, bb, co0);
-        const int i = g % steps, cb = i / a.k, t = i % a.k;
+        tile_of(tile_i, l0, bb, co0);
         uint8_t* dst = b_base + s * b_bytes;
         if constexpr (kPair) {
           // this CTA's half of the tile's rows; both halves count on the leader's barrier,
@@ -230,6 +232,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __syncwarp();
+      if (++t == a.k) {
+        t = 0;
+        if (++cb == ncb) {
+          cb = 0;
+          ++tile_i;
+        }
+      }
+      if (++s == kBStages) {
+        s = 0;
+        ph ^= 1u;
+      }
     }
   } else if (warp == 1 && (!kPair || leader)) {
     // ---------------- MMA issuer: the accumulators of one tile at a time (in a pair, M = 256:
@@ -244,7 +257,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     const uint32_t slab = uint32_t(a.R) * 16;
     bool ok = true;
-    int gc = 0, g = 0;  // global halo and step counters
+    // the halo and weight ring slots of the next step and their phases, as running counters
+    int sa = 0, sb = 0;
+    uint32_t pa = 0, pb = 0;
     for (int tl = 0; tl < my_tiles && ok; ++tl) {
       // accumulator set tl % nbuf, used for the (tl / nbuf)-th time
       const int buf = tl % a.nbuf, use = tl / a.nbuf;
@@ -257,10 +272,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      for (int cb = 0; cb < ncb && ok; ++cb, ++gc) {
-        const int sa = gc % kAStages;
+      for (int cb = 0; cb < ncb && ok; ++cb) {
         tl_t = TTS_TL_NOW();
-        const bool ok_a = mbar_wait_warp(&ready_a[sa], (gc / kAStages) & 1);
+        const bool ok_a = mbar_wait_warp(&ready_a[sa], pa);
         tl_w1 += TTS_TL_NOW() - tl_t;
         if (!ok_a) {
           if (lane == 0) atomicOr(a.err, 32);
@@ -268,11 +282,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const uint32_t ha = smem_u32(a_base + sa * a_bytes);
-        for (int t = 0; t < a.k; ++t, ++g) {
+        for (int t = 0; t < a.k; ++t) {
           const int i = cb * a.k + t;
-          const int sb = g % kBStages;
           tl_t = TTS_TL_NOW();
-          const bool ok_b = mbar_wait_warp(&full_b[sb], (g / kBStages) & 1);
+          const bool ok_b = mbar_wait_warp(&full_b[sb], pb);
           tl_w2 += TTS_TL_NOW() - tl_t;
           if (!ok_b) {
             if (lane == 0) atomicOr(a.err, 64);
@@ -334,10 +347,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             commit(&empty_b[sb]);
           }
           __syncwarp();
+          if (++sb == kBStages) {
+            sb = 0;
+            pb ^= 1u;
+          }
         }
         if (ok) {
           if (elect_one()) commit(&empty_a[sa]);
           __syncwarp();
+        }
+        if (++sa == kAStages) {
+          sa = 0;
+          pa ^= 1u;
         }
       }
       if (ok) {
