@@ -263,10 +263,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
 
-  const long long total = S.prefix[a.lanes];
-  const long long lo = range_lo(blockIdx.x, unsigned(total), gridDim.x);
-  const long long hi = range_lo(blockIdx.x + 1, unsigned(total), gridDim.x);
-  const long long n = hi - lo;  // items of this CTA
+  const int total = S.prefix[a.lanes];
+  const int lo = range_lo(blockIdx.x, unsigned(total), gridDim.x);
+  const int hi = range_lo(blockIdx.x + 1, unsigned(total), gridDim.x);
+  const int n = hi - lo;  // items of this CTA
   const uint32_t tmem = S.tmem;
 
   // the first item: lane b with prefix[b] <= lo < prefix[b + 1]
@@ -339,8 +339,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tl_rel = TTS_TL_NOW();
     }
     bool ok = true;
-    long long nk = 0, nv = 0;  // tiles issued
-    for (long long k = 0; k <= n && ok; ++k) {
+    int nk = 0, nv = 0;  // tiles issued
+    for (int k = 0; k <= n && ok; ++k) {
       Boxes cur{};
       if (k < n) {
         const int s = int(k % kStages);
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (k + 1 < n) next = lookup(x);  // read ahead: used next round
       }
       if (k >= 1) {
-        const long long kv = k - 1;
+        const int kv = k - 1;
         const int s = int(kv % kStages);
         if (kv >= kStages) ok = mbar_wait(&S.empty_v[s], uint32_t((kv / kStages) - 1) & 1);
         ok = __all_sync(0xffffffffu, ok);
@@ -370,9 +370,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     if (!ok && a.err && lane == 0) atomicOr(a.err, kFlagAttnWait);
     // Leave no copy in flight: wait (bounded) for the last tiles issued to land.
-    for (long long j = max(0ll, nk - kStages); j < nk; ++j)
+    for (int j = max(0, nk - kStages); j < nk; ++j)
       mbar_wait(&S.full_k[j % kStages], uint32_t(j / kStages) & 1);
-    for (long long j = max(0ll, nv - kStages); j < nv; ++j)
+    for (int j = max(0, nv - kStages); j < nv; ++j)
       mbar_wait(&S.full_v[j % kStages], uint32_t(j / kStages) & 1);
     return;
   }
@@ -381,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t idesc_o = idesc_f16_f32(128, kN) | (1u << 15);  // A (V^T) MN-major
 
   // O(i) = V(i)^T . P(i)^T, issued by the O warp when P(i) and V(i) are in place
-  auto do_o = [&](long long i, bool& ok, long long& no) {
+  auto do_o = [&](int i, bool& ok, int& no) {
     const int s = int(i % kStages);
     ok = mbar_wait(&S.p_full[i & 1], uint32_t(i >> 1) & 1) && ok;
     ok = mbar_wait(&S.full_v[s], uint32_t(i / kStages) & 1) && ok;
@@ -413,8 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // run side by side (different TMEM columns and operands), so neither chain waits for the
     // other's issue.
     bool ok = true;
-    long long no = 0;
-    for (long long i = 0; i < n && ok; ++i) do_o(i, ok, no);
+    int no = 0;
+    for (int i = 0; i < n && ok; ++i) do_o(i, ok, no);
     if (!ok && a.err && lane == 0) atomicOr(a.err, kFlagAttnWait);
     if (!ok && no > 0) mbar_wait(&S.o_full[(no - 1) & 1], uint32_t((no - 1) >> 1) & 1, 100000000ull);
     tc_fence_before();
@@ -425,10 +425,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kMmaWarp) {
     // ================= score warp: S(j) = K(j) . Q^T when K(j) and its segment's q are in place
     bool ok = true;
-    long long ns = 0;  // MMA groups issued
+    int ns = 0;  // MMA groups issued
     [[maybe_unused]] unsigned long long tl_s0 = 0;
     Cursor x = first;
-    for (long long j = 0; j < n && ok; ++j) {
+    for (int j = 0; j < n && ok; ++j) {
       const int s = int(j % kStages);
       if (j == 0 || x.c == 0) ok = mbar_wait(&S.q_full[x.seg & 1], uint32_t(x.seg >> 1) & 1) && ok;
       ok = mbar_wait(&S.full_k[s], uint32_t(j / kStages) & 1) && ok;
@@ -490,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int expect = 0;
     if (n > 0) {
       Cursor x = first;
-      for (long long j = 1; j < n; ++j) cursor_next(x, S.span, a);
+      for (int j = 1; j < n; ++j) cursor_next(x, S.span, a);
       const bool first_part = first.c != 0;
       const bool last_part = x.c + 1 != x.lr.nch;
       expect = (x.seg == 0) ? ((first_part || last_part) ? 1 : 0)
@@ -608,7 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) mbar_arrive(&S.q_full[seg & 1]);
   };
   // the first item of the segment after the one `x` is in (x itself if none follows)
-  auto next_segment = [&](Cursor x, long long& at) -> Cursor {
+  auto next_segment = [&](Cursor x, int& at) -> Cursor {
     const int left = x.lr.nch - x.c;  // items of x's segment from x on
     at += left;
     x.c = x.lr.nch - 1;
@@ -618,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   Cursor cur = first;
   // q of segments 0 and 1 now; registers then hold segment 2's
-  long long pos1 = 0, pos2 = 0;
+  int pos1 = 0, pos2 = 0;
   Cursor seg1 = cur, seg2 = cur;
   if (n > 0) {
     load_q(cur);
@@ -663,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   int c_first = cur.c;
 
   // folds item i's sum and O into a state (l, acc) at the previous item's scale
-  auto fold = [&](long long i, float* l, float* o_acc) {
+  auto fold = [&](int i, float* l, float* o_acc) {
     ok = mbar_wait(&S.o_full[i & 1], uint32_t(i >> 1) & 1) && ok;
     tc_fence_after();
     float ov[16];
@@ -785,14 +785,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     ++n_partial;
   };
 
-  for (long long j = 0; j < n; ++j) {
+  for (int j = 0; j < n; ++j) {
     const int s = int(j % kStages);
     // first item of a segment after the first: the segment after next gets its q now (its
     // buffer was last read by scores that are complete)
     if (j > 0 && cur.c == 0 && pos2 < n) {
       store_q(cur.seg + 1);
       Cursor nx = seg2;
-      long long at = pos2;
+      int at = pos2;
       seg2 = next_segment(nx, at);
       pos2 = at;
       if (pos2 < n) load_q(seg2);
