@@ -194,9 +194,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __syncwarp();
+      // ring slot and phase of k-block i as running counters (no division by the run-time SP)
+      int s = pre % SP;
+      uint32_t ph = uint32_t(pre / SP) & 1u;
       for (int i = pre; i < cnt; ++i) {
-        const int s = i % SP;
-        if (!mbar_wait_warp(&em[s], ((i / SP) + 1) & 1)) {
+        if (!mbar_wait_warp(&em[s], ph ^ 1u)) {
           if (lane == 0) atomicOr(a.err, 1);
           break;
         }
@@ -209,6 +211,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(st + kWBytes + g * a.ng * 128, &tmX, &fl[s], kb * kBlockK, g * a.ng);
         }
         __syncwarp();
+        if (++s == SP) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       // this pipeline's weights are all requested: start on the next GEMM's
       if (pp == 0 && elect_one())
@@ -225,9 +231,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* fl = full + pp * SP;
       uint64_t* em = empty + pp * SP;
       const uint32_t acc = tmem + uint32_t(pp * a.acc_cols);
+      int s = 0;  // ring slot and phase of k-block i
+      uint32_t ph = 0;
       for (int i = 0; i < cnt; ++i) {
-        const int s = i % SP;
-        if (!mbar_wait_warp(&fl[s], (i / SP) & 1)) {
+        if (!mbar_wait_warp(&fl[s], ph)) {
           if (lane == 0) atomicOr(a.err, 2);
           break;
         }
@@ -246,6 +253,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&em[s]);
         }
         __syncwarp();
+        if (++s == SP) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       if (elect_one()) umma_commit(done);  // no MMA issued: arrives at once (zero partial)
       __syncwarp();

@@ -85,12 +85,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool ok = true;
-  long issued = 0;  // producer: K blocks whose loads were issued
+  int issued = 0;  // producer: K blocks whose loads were issued (32-bit: tiles x K blocks)
 
   if (warp == 0) {
     // ---------------- producer
     const uint64_t pol_w = l2_policy_evict_last();  // every m tile of this n tile reads it
-    long g = 0;  // K blocks issued over all tiles
+    int g = 0;  // K blocks issued over all tiles
     for (int i = 0; i < my_tiles && ok; ++i) {
       const int t = blockIdx.x + i * gridDim.x;
       const int m0 = (t % a.m_tiles) * kPfM;
@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer
     const uint32_t idesc = idesc_f16_f32(kPfM, kPfN);
-    long g = 0;
+    int g = 0;
     for (int i = 0; i < my_tiles && ok; ++i) {
       const int b = i & 1;
       if (i >= 2) ok = mbar_wait_warp(&tempty[b], uint32_t((i >> 1) - 1) & 1);
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       __syncwarp();
       mbar_wait(drain, 0, 100000000ull);
     } else if (warp == 0 && lane == 0) {
-      for (long gg = issued > kPfStages ? issued - kPfStages : 0; gg < issued; ++gg)
+      for (int gg = issued > kPfStages ? issued - kPfStages : 0; gg < issued; ++gg)
         mbar_wait(&full[gg % kPfStages], uint32_t(gg / kPfStages) & 1, 100000000ull);
     }
   }
